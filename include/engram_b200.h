@@ -1,0 +1,225 @@
+/*
+ * engram_b200.h -- C ABI of the B200 (sm_100a) Engram/PLE table path.
+ *
+ * The reference (fulvian/engraft-ngram) is Python; the FFI it would bind for
+ * this path is ctypes (INTEGRATION.md shows the stub).  Every entry point:
+ *   - takes plain pointers and sizes (device pointers unless noted "host");
+ *   - is enqueued on the caller's CUDA stream (`stream`, a cudaStream_t; NULL =
+ *     the legacy default stream), makes no host synchronisation and allocates
+ *     no memory (scratch space is passed in);
+ *   - returns 0 on success or a negative ENGRAM_ERR_* code; nothing is launched
+ *     when an argument check fails.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   engram_table_init / engram_table_pack  <- PleTable.__init__ + read_rows_raw
+ *       (engraft/table.py:48-104): the table's addressing constants, and the
+ *       per-head IQ4_NL rows made resident in HBM instead of read per row.
+ *   engram_hash            <- PleTable.ngram_addresses (engraft/table.py:111-144),
+ *       damage.ngram_rows (engraft/damage.py:68-104), lens.local_to_global
+ *       (engraft/lens.py:108-110).
+ *   engram_overlay_map_build <- the row_map dict membership test
+ *       (engraft/replica/seq.py:401-417, engraft/replica/distill.py:401-457).
+ *   engram_forward         <- OverlayEmb.build (engraft/replica/seq.py:372-444) with
+ *       RowSet.from_position + dequant_iq4nl (engraft/lens.py:127-136,
+ *       engraft/table.py:147-169) and dequant_iq4_xs (engraft/replica/dequant.py:150-189).
+ *   engram_backward        <- autograd of rows_var[idx_r] / index_put
+ *       (engraft/replica/seq.py:433-441): row gradients, duplicates summed.
+ *   engram_adam_step       <- reg.backward() + torch.optim.Adam.step()
+ *       (engraft/descend_corpus.py:921-947).
+ */
+#ifndef ENGRAM_B200_H
+#define ENGRAM_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ENGRAM_API __attribute__((visibility("default")))
+#else
+#define ENGRAM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define ENGRAM_OK 0
+#define ENGRAM_ERR_ARG (-1)       /* null pointer, negative size, bad enum      */
+#define ENGRAM_ERR_FORMAT (-2)    /* unsupported fmt / dim / mode combination   */
+#define ENGRAM_ERR_RANGE (-3)     /* table geometry or a size out of range      */
+#define ENGRAM_ERR_WORKSPACE (-4) /* scratch buffer too small                   */
+#define ENGRAM_ERR_CUDA (-5)      /* a launch failed (cudaGetLastError)         */
+
+/* ---- row formats of the resident table ---------------------------------- */
+#define ENGRAM_FMT_F32 0    /* dim floats per row                              */
+#define ENGRAM_FMT_IQ4_NL 1 /* ggml IQ4_NL, dim/32 blocks (the reference table) */
+#define ENGRAM_FMT_IQ4_XS 2 /* ggml IQ4_XS, dim/256 superblocks                 */
+
+/* ---- output modes of engram_forward ------------------------------------- */
+/* out float [n, n_heads, dim]: the reference's emb (row h of position t at
+ * out[t, h, :], engraft/replica/seq.py:444 reshapes it to [n, n_heads*dim]).  */
+#define ENGRAM_MODE_CONCAT_F32 0
+/* out bf16 [n, heads_per_ngram*dim], updated in place:
+ *   out[t, g*dim+c] = bf16_rn(float(out[t, g*dim+c]) + (row[g][c] + row[hpn+g][c]))
+ * i.e. the bigram and trigram rows of group g summed into the residual stream.
+ * Builder-defined; requires ngram_size == 3.                                  */
+#define ENGRAM_MODE_PAIRSUM_ADD_BF16 1
+
+#define ENGRAM_MAX_HEADS 32
+#define ENGRAM_MAX_CTX 4
+
+/*
+ * Table descriptor, filled by engram_table_init.  Plain data in host memory,
+ * owned by the caller; passed by pointer and copied by value into launches.
+ */
+typedef struct engram_table {
+    const void* rows;      /* device, resident rows (layout: engram_table_pack) */
+    int64_t n_rows;
+    int64_t row_stride;    /* bytes between rows                               */
+    int32_t fmt;
+    int32_t dim;
+    int32_t ngram_size;    /* context length N (2..ENGRAM_MAX_CTX)             */
+    int32_t heads_per_ngram;
+    int32_t n_heads;       /* (N-1) * heads_per_ngram                          */
+    int32_t reserved;
+    int64_t eos_token_id;
+    uint64_t mult[ENGRAM_MAX_CTX];              /* layer_multipliers[0..N-1]  */
+    uint64_t head_magic[ENGRAM_MAX_HEADS];      /* x % p_h by multiplication   */
+    uint32_t head_size[ENGRAM_MAX_HEADS];       /* p_h                        */
+    uint32_t head_shift[ENGRAM_MAX_HEADS];
+    int64_t head_offset[ENGRAM_MAX_HEADS];      /* head_offsets[h]            */
+} engram_table;
+
+/*
+ * Overlay descriptor: the trainable rows and the device map global id -> slot
+ * built by engram_overlay_map_build.  R == 0 means "no overlay".
+ */
+typedef struct engram_overlay {
+    const float* rows;      /* device [R, dim] fp32 (rows_var)                 */
+    int64_t n_rows;         /* R                                               */
+    const int32_t* map_keys;  /* device [capacity]; -1 = empty                 */
+    const int32_t* map_slots; /* device [capacity]                             */
+    int64_t capacity;       /* power of two >= 2R (0 when R == 0)              */
+} engram_overlay;
+
+/* dim: 1..1024; F32 needs dim % 4 == 0 (dim % 8 == 0 for PAIRSUM_ADD_BF16),
+ * IQ4_NL dim % 32 == 0, IQ4_XS dim % 256 == 0. */
+
+/* Bytes per resident row: F32 dim*4; IQ4_NL round_up(dim/32*18, 16);
+ * IQ4_XS dim/256*144.  Negative on an unsupported fmt/dim.                    */
+ENGRAM_API int64_t engram_row_stride(int32_t fmt, int32_t dim);
+
+/* Bytes per row of the reference's own (GGUF) layout: F32 dim*4; IQ4_NL
+ * dim/32*18; IQ4_XS dim/256*136.                                              */
+ENGRAM_API int64_t engram_raw_row_bytes(int32_t fmt, int32_t dim);
+
+/*
+ * Fills *t (host memory).  head_sizes/head_offsets/mult are HOST arrays of
+ * n_heads = (ngram_size-1)*heads_per_ngram, n_heads and ngram_size entries
+ * (mult may hold more; the first ngram_size are used).  Checks 1 <= p_h,
+ * head_offsets[h] + p_h <= n_rows <= 2^31-1, and computes the per-head
+ * division magic (Granlund & Montgomery, PLDI 1994, unsigned case).
+ * Replaces PleTable.__init__ (engraft/table.py:48-88).
+ */
+ENGRAM_API int engram_table_init(engram_table* t, const void* rows, int64_t n_rows, int32_t fmt, int32_t dim,
+                      int32_t ngram_size, int32_t heads_per_ngram, const int64_t* head_sizes,
+                      const int64_t* head_offsets, const uint64_t* mult, int32_t n_mult,
+                      int64_t eos_token_id);
+
+/*
+ * Repacks rows from the reference's layout (src: device, n_rows *
+ * engram_raw_row_bytes) into the resident layout (dst: device, n_rows *
+ * engram_row_stride).  Resident layouts (16-byte aligned rows):
+ *   F32:    unchanged.
+ *   IQ4_NL: [qs of the dim/32 blocks, 16 B each][fp16 d of each block][zero pad].
+ *   IQ4_XS: per superblock 144 B = [qs 128 B][d 2 B][scales_h 2 B][scales_l 4 B][8 zero B].
+ * Replaces PleTable.read_rows_raw (engraft/table.py:90-104) as the row source.
+ */
+ENGRAM_API int engram_table_pack(int32_t fmt, int32_t dim, const uint8_t* src, int64_t n_rows, void* dst, void* stream);
+
+/*
+ * Builds the open-addressing map global id -> slot for the overlay rows:
+ * map[ids[k]] = k.  keys/slots: device [capacity], capacity a power of two
+ * >= 2R; the kernel clears them first.  ids must be distinct and >= 0 (the
+ * keys of the reference's row_map, engraft/replica/distill.py:452-453).
+ */
+ENGRAM_API int engram_overlay_map_build(const int32_t* ids, int64_t R, int32_t* keys, int32_t* slots,
+                             int64_t capacity, void* stream);
+
+/*
+ * K1 alone: global row ids [n, n_heads] (int32) of positions t0..t0+n-1 of
+ * `tokens` (device int32; tokens before t0 are read as context).  seg_start
+ * (device int32 [t0+n] or NULL): seg_start[t] = first index of t's segment;
+ * a predecessor before it counts as missing (engraft/replica/seq.py:393-399).
+ * Bit-identical to PleTable.ngram_addresses + local_to_global.
+ */
+ENGRAM_API int engram_hash(const engram_table* t, const int32_t* tokens, const int32_t* seg_start, int64_t t0,
+                int64_t n, int32_t* ids_out, void* stream);
+
+/*
+ * Fused hash -> overlay lookup -> gather/dequant -> emit, one launch.
+ * out: see ENGRAM_MODE_*.  ids_out (nullable) int32 [n, n_heads] global ids;
+ * slots_out (nullable) int32 [n, n_heads] overlay slot or -1 (the input of
+ * engram_backward); hit_count (nullable) device int64[1] += number of
+ * (position, head) pairs served by the overlay (OverlayEmb.n_id_hits).
+ */
+ENGRAM_API int engram_forward(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                   const int32_t* seg_start, int64_t t0, int64_t n, int32_t mode, void* out,
+                   int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream);
+
+/*
+ * Dequantised rows by global id: out float [n, dim] = row ids[k] of the table
+ * (no overlay).  Replaces distill._read_true_rows (engraft/replica/distill.py:378-396)
+ * and PleTable.read_rows (engraft/table.py:106-109) on the resident table.
+ * Ids must lie in [0, n_rows); an id outside that range gives a zero row.
+ */
+ENGRAM_API int engram_gather_rows(const engram_table* t, const int32_t* ids, int64_t n, float* out, void* stream);
+
+/* Scratch bytes engram_backward needs for n positions of n_heads heads and R
+ * overlay rows. */
+ENGRAM_API int64_t engram_backward_workspace_bytes(int64_t n, int32_t n_heads, int64_t R);
+
+/*
+ * Row gradients of the overlay: grad_rows[r, :] = sum over (t,h) with
+ * slots[t,h] == r of the upstream gradient at (t,h), added from +0 in
+ * ascending t*n_heads+h order -- the order in which the reference's
+ * index_put_(accumulate=True) adds duplicates (serially on one CPU thread,
+ * after a stable sort on CUDA), so the result is bit-identical to it and
+ * deterministic.  Every row of grad_rows [R, dim] is written (zero where no
+ * hit).  mode CONCAT_F32: grad float [n, n_heads, dim]; mode PAIRSUM_ADD_BF16:
+ * grad bf16 [n, hpn*dim] (the term of (t,h) is grad[t, (h%hpn)*dim : +dim]).
+ * workspace: device scratch of engram_backward_workspace_bytes(n, n_heads, R).
+ */
+ENGRAM_API int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram,
+                    int32_t mode, const void* grad, int32_t dim, int64_t R, float* grad_rows,
+                    void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * One optimizer step over numel fp32 elements, in place on p, m, v:
+ *   g  = g_in + reg_scale * (2*(p - p0))        (p0 NULL: g = g_in)
+ *   m  = fma(1-beta1, g-m, m)                   (torch lerp)
+ *   v  = v*beta2 + ((1-beta2)*g)*g
+ *   p  = p + (-(lr/(1-beta1^step)) * m) / (sqrt(v)/sqrt(1-beta2^step) + eps)
+ * reg_scale = float(mu) / max(sum(p0^2), 1e-12): the factor autograd applies
+ * to the descent's regulariser (engraft/descend_corpus.py:935-937); step >= 1
+ * is the step count after this update (torch.optim.Adam, no weight decay).
+ */
+ENGRAM_API int engram_adam_step(float* p, const float* g, float* m, float* v, const float* p0, int64_t numel,
+                     int64_t step, double lr, double beta1, double beta2, double eps, float reg_scale,
+                     void* stream);
+
+/* Host self-test of the division magic: out[i] = x[i] % d using exactly the
+ * device code path (host arrays).  Lets CPU-only tests check it. */
+ENGRAM_API int engram_selftest_mod(const uint64_t* x, int64_t count, uint32_t d, uint64_t* out);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * entry points, all devices); lets callers verify that the CUDA path ran. */
+ENGRAM_API int64_t engram_launch_count(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+ENGRAM_API int engram_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ENGRAM_B200_H */

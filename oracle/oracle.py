@@ -1,0 +1,194 @@
+"""ctypes wrapper of the CPU oracle (engram_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: the checker for the CUDA path.  Imported by tests/,
+__graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference leg;
+never by the product package.  Each function names the reference code that the
+C restatement follows (paths inside the fulvian/engraft-ngram project).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "liboracle.so"
+
+FMT_F32, FMT_IQ4_NL, FMT_IQ4_XS = 0, 1, 2
+MODE_CONCAT_F32, MODE_PAIRSUM_ADD_BF16 = 0, 1
+
+_lib = None
+
+
+def build() -> Path:
+    """Compile liboracle.so with the committed Makefile (gcc)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        src = HERE / "engram_oracle.c"
+        if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+            build()
+        L = C.CDLL(str(LIB_PATH))
+        p, i32, i64, u64p = C.c_void_p, C.c_int32, C.c_int64, C.c_void_p
+        L.orc_hash.argtypes = [p, p, i64, i64, i32, i32, u64p, p, p, i64, p]
+        L.orc_hash.restype = None
+        L.orc_raw_row_bytes.argtypes = [i32, i32]
+        L.orc_raw_row_bytes.restype = i64
+        L.orc_dequant.argtypes = [i32, i32, p, i64, p]
+        L.orc_dequant.restype = None
+        L.orc_forward.argtypes = [i32, i32, p, i64, p, i64, i32, i32, p, p, p, i64, i32, p, p]
+        L.orc_forward.restype = None
+        L.orc_backward.argtypes = [p, i64, i32, i32, i32, p, i32, i64, p]
+        L.orc_backward.restype = None
+        L.orc_adam.argtypes = [p, p, p, p, p, i64, i64, C.c_double, C.c_double, C.c_double, C.c_double, C.c_float]
+        L.orc_adam.restype = None
+        L.orc_pack.argtypes = [i32, i32, p, i64, p, i64]
+        L.orc_pack.restype = None
+        L.orc_num_threads.restype = C.c_int
+        L.orc_set_num_threads.argtypes = [C.c_int]
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def set_num_threads(n: int) -> None:
+    lib().orc_set_num_threads(int(n))
+
+
+def num_threads() -> int:
+    return int(lib().orc_num_threads())
+
+
+def raw_row_bytes(fmt: int, dim: int) -> int:
+    return int(lib().orc_raw_row_bytes(fmt, dim))
+
+
+def resident_row_bytes(fmt: int, dim: int) -> int:
+    """Bytes per row of the device-resident layout (the C ABI's engram_row_stride)."""
+    if fmt == FMT_F32:
+        return dim * 4
+    if fmt == FMT_IQ4_NL:
+        return ((dim // 32) * 18 + 15) // 16 * 16
+    return (dim // 256) * 144
+
+
+def hash_ids(tokens, ngram_size, hpn, mult, head_sizes, head_offsets, eos, seg_start=None, t0=0, n=None):
+    """Global row ids [n, n_heads] of positions t0..t0+n-1 (engraft/table.py:111-144,
+    global ids per engraft/lens.py:108-110; segments per engraft/replica/seq.py:393-399)."""
+    tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+    if n is None:
+        n = tokens.shape[0] - t0
+    n_heads = (ngram_size - 1) * hpn
+    out = np.empty((n, n_heads), dtype=np.int32)
+    if n == 0:
+        return out
+    m = np.zeros(8, dtype=np.uint64)
+    m[:len(mult)] = np.asarray([int(x) for x in mult], dtype=np.uint64)
+    sizes = np.ascontiguousarray(head_sizes, dtype=np.int64)
+    offs = np.ascontiguousarray(head_offsets, dtype=np.int64)
+    ss = None if seg_start is None else np.ascontiguousarray(seg_start, dtype=np.int32)
+    lib().orc_hash(_ptr(tokens), _ptr(ss), t0, n, ngram_size, hpn, _ptr(m), _ptr(sizes), _ptr(offs),
+                   int(eos), _ptr(out))
+    return out
+
+
+def dequant(fmt: int, dim: int, raw) -> np.ndarray:
+    """float32 [n, dim] from the reference's raw row bytes (engraft/table.py:147-169,
+    engraft/replica/dequant.py:127-189)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    n = raw.shape[0]
+    out = np.empty((n, dim), dtype=np.float32)
+    if n:
+        lib().orc_dequant(fmt, dim, _ptr(raw), n, _ptr(out))
+    return out
+
+
+def forward(fmt, dim, table_raw, ids, hpn, ov_rows, ov_ids, mode=MODE_CONCAT_F32, residual=None):
+    """OverlayEmb.build on rows (engraft/replica/seq.py:372-444).  Returns
+    (out, slots): CONCAT -> float32 [n, n_heads, dim]; PAIRSUM_ADD_BF16 ->
+    uint16 (bf16 bits) [n, hpn*dim] = residual + pair sums.  ov_ids[k] is the
+    global id of overlay row k (row_map = {ov_ids[k]: k})."""
+    table_raw = np.ascontiguousarray(table_raw, dtype=np.uint8)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    n, n_heads = ids.shape
+    ov_rows = np.ascontiguousarray(ov_rows, dtype=np.float32).reshape(-1, dim)
+    ov_ids = np.asarray(ov_ids, dtype=np.int32)
+    order = np.argsort(ov_ids, kind="stable")
+    keys = np.ascontiguousarray(ov_ids[order])
+    vals = np.ascontiguousarray(order.astype(np.int32))
+    slots = np.empty((n, n_heads), dtype=np.int32)
+    if mode == MODE_CONCAT_F32:
+        out = np.empty((n, n_heads, dim), dtype=np.float32)
+    else:
+        out = np.array(residual, dtype=np.uint16, copy=True).reshape(n, hpn * dim)
+    if n:
+        lib().orc_forward(fmt, dim, _ptr(table_raw), table_raw.shape[0], _ptr(ids), n, n_heads, hpn,
+                          _ptr(ov_rows), _ptr(keys), _ptr(vals), keys.shape[0], mode, _ptr(out), _ptr(slots))
+    return out, slots
+
+
+def backward(slots, hpn, grad, dim, R, mode=MODE_CONCAT_F32) -> np.ndarray:
+    """Row gradients [R, dim], duplicates summed from +0 in ascending (t,h)
+    order (autograd of engraft/replica/seq.py:433-441)."""
+    slots = np.ascontiguousarray(slots, dtype=np.int32)
+    n, n_heads = slots.shape
+    if mode == MODE_CONCAT_F32:
+        grad = np.ascontiguousarray(grad, dtype=np.float32)
+    else:
+        grad = np.ascontiguousarray(grad, dtype=np.uint16)
+    out = np.empty((R, dim), dtype=np.float32)
+    lib().orc_backward(_ptr(slots), n, n_heads, hpn, mode, _ptr(grad), dim, R, _ptr(out))
+    return out
+
+
+def adam_(p, g, m, v, step, lr, beta1=0.9, beta2=0.999, eps=1e-8, p0=None, reg_scale=0.0) -> None:
+    """In-place Adam step with the descent's regulariser gradient
+    (engraft/descend_corpus.py:921-947; torch.optim.Adam single-tensor rule)."""
+    for a in (p, m, v):
+        assert a.dtype == np.float32 and a.flags.c_contiguous
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    p0c = None if p0 is None else np.ascontiguousarray(p0, dtype=np.float32)
+    lib().orc_adam(_ptr(p), _ptr(g), _ptr(m), _ptr(v), _ptr(p0c), p.size, int(step), float(lr),
+                   float(beta1), float(beta2), float(eps), float(np.float32(reg_scale)))
+
+
+def reg_scale(mu: float, rows0) -> np.float32:
+    """float(mu) / max(sum(p0^2), 1e-12) in fp32, the factor autograd applies to
+    2*(p-p0) (engraft/descend_corpus.py:936).  The sum is taken in float64 then
+    rounded; torch's own fp32 reduction order may differ in the last bit."""
+    S = np.float32(max(float(np.square(np.asarray(rows0, dtype=np.float64)).sum()), 1e-12))
+    return np.float32(np.float32(mu) / S)
+
+
+def pack(fmt: int, dim: int, raw) -> np.ndarray:
+    """Reference raw rows -> device-resident row layout (uint8 [n, stride])."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    n = raw.shape[0]
+    stride = resident_row_bytes(fmt, dim)
+    out = np.empty((n, stride), dtype=np.uint8)
+    if n:
+        lib().orc_pack(fmt, dim, _ptr(raw), n, _ptr(out), stride)
+    return out
+
+
+def bf16_bits(x) -> np.ndarray:
+    """float32 -> bf16 bit patterns, round to nearest even (uint16)."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (b & 0x7FFFFFFF) > 0x7F800000
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((b[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_to_f32(bits) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)

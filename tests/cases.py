@@ -1,0 +1,71 @@
+"""Rebuilds the inputs of each golden overlay case (tests/golden) so the oracle
+and the CUDA path can be run on exactly the data the reference saw."""
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+
+import numpy as np
+
+import fixtures as FX
+from oracle import oracle as O
+
+
+def sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@dataclasses.dataclass
+class TableSpec:
+    fmt: int
+    dim: int
+    raw: np.ndarray          # reference raw row bytes [n_rows, raw_row_bytes]
+    params: dict             # mult, head_sizes, head_offsets, eos, ngram_size, hpn
+
+    @property
+    def n_heads(self) -> int:
+        return (self.params["ngram_size"] - 1) * self.params["hpn"]
+
+    def ids(self, tokens, seg_start=None, t0=0, n=None):
+        p = self.params
+        return O.hash_ids(tokens, p["ngram_size"], p["hpn"], p["mult"], p["head_sizes"], p["head_offsets"],
+                          p["eos"], seg_start=seg_start, t0=t0, n=n)
+
+    def true_rows(self, ids) -> np.ndarray:
+        return O.dequant(self.fmt, self.dim, self.raw[np.asarray(ids, dtype=np.int64)])
+
+
+def syn_table() -> TableSpec:
+    return TableSpec(O.FMT_IQ4_NL, 160, FX.syn_table_raw(), FX.syn_params())
+
+
+def fake_table(rows_f32: np.ndarray, seed: int = 1) -> TableSpec:
+    return TableSpec(O.FMT_F32, 160, rows_f32.view(np.uint8).reshape(rows_f32.shape[0], -1),
+                     FX.fake_table_params(seed=seed))
+
+
+@dataclasses.dataclass
+class OverlayCase:
+    table: TableSpec
+    tokens: np.ndarray
+    seg_start: np.ndarray | None
+    t0: int
+    n: int
+    row_ids: np.ndarray
+    rows_init: np.ndarray
+    grad: np.ndarray
+    golden: dict
+
+
+def overlay_case(golden, prefix: str, table: TableSpec) -> OverlayCase:
+    g = {k[len(prefix):]: golden[k] for k in golden.files if k.startswith(prefix)}
+    tokens = g["tokens"]
+    n_prefix = int(g["n_prefix"])
+    start = int(g["start"])
+    seg_start = FX.seg_starts(g["segment_ids"]) if int(g["use_segments"]) else None
+    row_ids = g["row_ids"]
+    rows_init = (table.true_rows(row_ids) + FX.overlay_noise(int(g["seed"]), (len(row_ids), table.dim))).astype(np.float32)
+    assert sha(rows_init) == str(g["rows_init_sha"]), "fixture regeneration drifted from the reference's inputs"
+    n = n_prefix - start
+    grad = FX.overlay_grad(int(g["seed"]), (n, table.n_heads * table.dim))
+    return OverlayCase(table, tokens, seg_start, start, n, row_ids, rows_init, grad, g)

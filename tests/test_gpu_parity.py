@@ -1,0 +1,286 @@
+"""Parity of the CUDA path (called through the C ABI of libengram_b200.so) with
+the CPU oracle and with the reference's golden vectors.
+
+Integer and byte work (row ids, slots, gathered rows, dequantised values,
+the bf16 pair-sum epilogue) and the row gradients (summed in the reference's
+order) must be bit-identical.  Adam must match the oracle bit for bit and the
+reference's torch trajectory within 1e-6 of the row norm (the north-star
+tolerance is 1e-5 of the row norm).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import fixtures as FX
+from cases import fake_table, overlay_case, sha, syn_table
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def eb():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    import engraft_ngram_b200 as eb
+    eb.load_library()
+    return eb
+
+
+def hash_only_table(eb, params, dim=4):
+    n_rows = max(o + s for o, s in zip(params["head_offsets"], params["head_sizes"]))
+    rows = torch.zeros(n_rows * dim * 4, dtype=torch.uint8, device=DEV)
+    return eb.DeviceTable(rows, eb.FMT_F32, dim, params["head_sizes"], params["head_offsets"], params["mult"],
+                          params["eos"], params["ngram_size"], params["hpn"], n_rows=n_rows)
+
+
+def device_table(eb, spec):
+    p = spec.params
+    return eb.DeviceTable.from_raw(spec.raw, spec.fmt, spec.dim, p["head_sizes"], p["head_offsets"], p["mult"],
+                                   p["eos"], p["ngram_size"], p["hpn"], device=DEV)
+
+
+# ------------------------------------------------------------------ K1: hash
+def test_hash_matches_reference_golden(eb, golden):
+    t = hash_only_table(eb, FX.fake_table_params(seed=7))
+    assert np.array_equal(t.global_ids(golden["hash_fake_tokens"]).cpu().numpy(), golden["hash_fake_ids"])
+    t = hash_only_table(eb, FX.syn_params())
+    assert np.array_equal(t.global_ids(golden["hash_syn_tokens"]).cpu().numpy(), golden["hash_syn_ids"])
+    for k in range(9):
+        toks = golden[f"edge{k}_tokens"]
+        got = t.global_ids(toks).cpu().numpy() if len(toks) else np.zeros((0, 16), np.int32)
+        assert np.array_equal(got, golden[f"edge{k}_ids"].reshape(-1, 16)), k
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_hash_large_random_with_segments_vs_oracle(eb, seed):
+    rng = np.random.default_rng(seed)
+    sizes = [int(x) for x in rng.integers(2, 40_000_000, size=16)]
+    sizes[3] = 1
+    sizes[5] = 1 << 20  # a power of two
+    params = dict(mult=[int(x) for x in rng.integers(0, 2**64 - 1, size=4, dtype=np.uint64)],
+                  head_sizes=sizes, head_offsets=FX.head_offsets(sizes), eos=248044, ngram_size=3, hpn=8)
+    T = 131_072
+    toks = rng.integers(-5, 2**31 - 1, size=T).astype(np.int32)
+    toks[rng.integers(0, T, size=3000)] = 248044
+    seg = np.sort(rng.integers(0, 60, size=T))
+    ss = FX.seg_starts(seg)
+    t = hash_only_table(eb, params, dim=4)
+    for t0, n in ((0, T), (777, T - 777 - 5)):
+        got = t.global_ids(toks, seg_start=ss, t0=t0, n=n).cpu().numpy()
+        ref = O.hash_ids(toks, 3, 8, params["mult"], sizes, params["head_offsets"], 248044, seg_start=ss, t0=t0, n=n)
+        assert np.array_equal(got, ref)
+
+
+# --------------------------------------------- K2 + K3 on the reference's cases
+def _golden_case_on_gpu(eb, c):
+    dt = device_table(eb, c.table)
+    omap = eb.OverlayMap(torch.from_numpy(c.row_ids), DEV)
+    rows_var = torch.from_numpy(c.rows_init).to(DEV).requires_grad_(True)
+    hits = torch.zeros(1, dtype=torch.int64, device=DEV)
+    ss = None if c.seg_start is None else torch.from_numpy(c.seg_start)
+    emb = eb.engram_embed(dt, c.tokens, rows_var, omap, ss, c.t0, c.n, hits)
+    emb.backward(torch.from_numpy(c.grad).to(DEV))
+    return emb.detach().cpu().numpy(), rows_var.grad.cpu().numpy(), int(hits.item())
+
+
+@pytest.mark.parametrize("prefix", ["ov_syn_", "ov_synnoseg_"])
+def test_overlay_emb_iq4nl_matches_reference_bit_exact(eb, golden, prefix):
+    c = overlay_case(golden, prefix, syn_table())
+    emb, grad_rows, hits = _golden_case_on_gpu(eb, c)
+    assert sha(emb) == str(c.golden["emb_sha"])
+    assert np.array_equal(emb[1], c.golden["emb_row1"])
+    assert hits == int(c.golden["n_id_hits"])
+    assert np.array_equal(grad_rows.view(np.uint32), c.golden["grad_rows"].view(np.uint32))
+
+
+def test_overlay_emb_fake_table_matches_reference_bit_exact(eb, golden, fake1_rows):
+    c = overlay_case(golden, "ov_fake_", fake_table(fake1_rows, seed=1))
+    emb, grad_rows, hits = _golden_case_on_gpu(eb, c)
+    assert sha(emb) == str(c.golden["emb_sha"])
+    assert hits == int(c.golden["n_id_hits"])
+    assert np.array_equal(grad_rows.view(np.uint32), c.golden["grad_rows"].view(np.uint32))
+
+
+def test_drop_in_overlay_emb_class(eb, golden):
+    """The drop-in class, built exactly as the reference's callers build it
+    (engraft/replica/seq.py:1430-1432), reproduces the reference's emb."""
+    c = overlay_case(golden, "ov_syn_", syn_table())
+    dt = device_table(eb, c.table)
+    row_map = {int(g): i for i, g in enumerate(c.row_ids.tolist())}
+    rows_var = torch.from_numpy(c.rows_init).to(DEV).requires_grad_(True)
+    seg = torch.from_numpy(c.golden["segment_ids"].astype(np.int64))
+    ov = eb.OverlayEmb(dt, c.tokens.tolist(), rows_var, row_map, segment_ids=seg, overlay_cache={})
+    emb = ov.build(int(c.golden["n_prefix"]))
+    assert emb.shape == (c.n, 16 * 160) and emb.dtype == torch.float32 and emb.requires_grad
+    assert sha(emb.detach().cpu().numpy()) == str(c.golden["emb_sha"])
+    assert ov.n_id_hits == int(c.golden["n_id_hits"]) and ov.n_key_hits == 0
+    emb.backward(torch.from_numpy(c.grad).to(DEV))
+    assert np.array_equal(rows_var.grad.cpu().numpy().view(np.uint32), c.golden["grad_rows"].view(np.uint32))
+
+
+def test_device_table_duck_type_matches_table_reads(eb, golden):
+    spec = syn_table()
+    dt = device_table(eb, spec)
+    got = dt.read_rows(3, 0, 64)
+    assert np.array_equal(got.view(np.uint32), golden["dq_nl_out"].view(np.uint32))
+    toks = golden["hash_syn_tokens"][:50].tolist()
+    loc = dt.ngram_addresses(toks)
+    ids = golden["hash_syn_ids"][:50] - np.asarray(spec.params["head_offsets"])[None, :]
+    assert loc == ids.tolist()
+
+
+# ------------------------------------------------ random tables vs the oracle
+def zipf_tokens(rng, n, vocab=151_936, s=1.1):
+    ranks = np.arange(1, vocab + 1, dtype=np.float64)
+    cdf = np.cumsum(ranks ** -s)
+    cdf /= cdf[-1]
+    return np.searchsorted(cdf, rng.random(n)).astype(np.int32)
+
+
+def random_spec(fmt, dim, n_rows, seed):
+    rng = np.random.default_rng(seed)
+    if fmt == O.FMT_F32:
+        raw = (rng.standard_normal((n_rows, dim)) * 0.0085).astype(np.float32).view(np.uint8).reshape(n_rows, -1)
+    elif fmt == O.FMT_IQ4_NL:
+        raw = FX.iq4nl_raw(n_rows, seed, dim)
+    else:
+        raw = FX.iq4xs_raw(n_rows, seed, dim)
+    sizes = [n_rows // 16 - 3 * h for h in range(16)]
+    sizes[-1] += n_rows - sum(sizes)
+    params = dict(mult=[int(x) | 1 for x in rng.integers(1, 2**63, size=4, dtype=np.uint64)], head_sizes=sizes,
+                  head_offsets=FX.head_offsets(sizes), eos=151_935, ngram_size=3, hpn=8)
+    from cases import TableSpec
+    return TableSpec(fmt, dim, raw, params)
+
+
+FORMATS = [(O.FMT_F32, 128), (O.FMT_F32, 160), (O.FMT_IQ4_NL, 160), (O.FMT_IQ4_XS, 256), (O.FMT_IQ4_XS, 512)]
+
+
+@pytest.mark.parametrize("fmt,dim", FORMATS)
+@pytest.mark.parametrize("mode", [O.MODE_CONCAT_F32, O.MODE_PAIRSUM_ADD_BF16])
+def test_forward_backward_random_vs_oracle(eb, fmt, dim, mode):
+    seed = 100 * fmt + dim + mode
+    rng = np.random.default_rng(seed)
+    spec = random_spec(fmt, dim, 40_000, seed)
+    T = 3000
+    toks = zipf_tokens(rng, T)
+    toks[rng.integers(0, T, size=30)] = 151_935
+    seg = np.sort(rng.integers(0, 12, size=T))
+    ss = FX.seg_starts(seg)
+    ids = spec.ids(toks, seg_start=ss)
+    read = np.unique(ids)
+    ov_ids = np.unique(np.concatenate([rng.choice(read, size=min(len(read), 900), replace=False),
+                                       rng.integers(0, 40_000, size=200)])).astype(np.int32)
+    rng.shuffle(ov_ids)
+    R = len(ov_ids)
+    rows_init = (rng.standard_normal((R, dim)) * 0.01).astype(np.float32)
+
+    dt = device_table(eb, spec)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    rows_var = torch.from_numpy(rows_init).to(DEV).requires_grad_(True)
+    hits = torch.zeros(1, dtype=torch.int64, device=DEV)
+    if mode == O.MODE_CONCAT_F32:
+        out_ref, slots = O.forward(fmt, dim, spec.raw, ids, 8, rows_init, ov_ids, mode)
+        out = eb.engram_embed(dt, toks, rows_var, omap, torch.from_numpy(ss), 0, T, hits)
+        assert np.array_equal(out.detach().cpu().numpy().view(np.uint32), out_ref.reshape(T, -1).view(np.uint32))
+        grad = (rng.standard_normal(out.shape) * 1e-3).astype(np.float32)
+        out.backward(torch.from_numpy(grad).to(DEV))
+    else:
+        res0 = (rng.standard_normal((T, 8 * dim)) * 0.5).astype(np.float32)
+        res_bits = O.bf16_bits(res0)
+        out_ref, slots = O.forward(fmt, dim, spec.raw, ids, 8, rows_init, ov_ids, mode, residual=res_bits)
+        res = torch.from_numpy(res_bits.view(np.int16)).to(DEV).view(torch.bfloat16)
+        out = eb.engram_residual_add(res, dt, toks, rows_var, omap, torch.from_numpy(ss), 0, hits)
+        assert np.array_equal(out.detach().view(torch.int16).cpu().numpy().view(np.uint16), out_ref)
+        grad = O.bf16_bits((rng.standard_normal((T, 8 * dim)) * 1e-2).astype(np.float32))
+        out.backward(torch.from_numpy(grad.view(np.int16)).to(DEV).view(torch.bfloat16))
+    assert int(hits.item()) == int((slots >= 0).sum())
+    gref = O.backward(slots, 8, grad, dim, R, mode)
+    assert np.array_equal(rows_var.grad.cpu().numpy().view(np.uint32), gref.view(np.uint32))
+
+
+def test_backward_heavy_duplicates_and_large_R_bit_exact(eb):
+    """A few slots hit thousands of times (sequential order matters) and
+    R > 2^16 (three radix passes)."""
+    rng = np.random.default_rng(7)
+    T, nh, dim = 20_000, 16, 128
+    R = 70_000
+    slots = np.full((T, nh), -1, dtype=np.int32)
+    m = rng.random((T, nh)) < 0.6
+    hot = rng.integers(0, 5, size=(T, nh))
+    cold = rng.integers(0, R, size=(T, nh))
+    slots[m] = np.where(rng.random((T, nh)) < 0.5, hot, cold)[m]
+    slots[:, 3] = R - 1
+    grad = (rng.standard_normal((T, nh, dim)) * 1e-3).astype(np.float32)
+    import engraft_ngram_b200 as ebm
+    got = ebm.row_gradients(torch.from_numpy(slots).to(DEV), torch.from_numpy(grad).to(DEV), nh, 8, dim, R,
+                            ebm.MODE_CONCAT_F32).cpu().numpy()
+    ref = O.backward(slots, 8, grad, dim, R)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    again = ebm.row_gradients(torch.from_numpy(slots).to(DEV), torch.from_numpy(grad).to(DEV), nh, 8, dim, R,
+                              ebm.MODE_CONCAT_F32).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+
+
+def test_backward_no_hits_gives_zero_rows(eb):
+    slots = torch.full((100, 16), -1, dtype=torch.int32, device=DEV)
+    grad = torch.randn(100, 16, 128, device=DEV)
+    g = eb.row_gradients(slots, grad, 16, 8, 128, 33, eb.MODE_CONCAT_F32)
+    assert g.shape == (33, 128) and bool((g == 0).all())
+
+
+# ---------------------------------------------------------------- K4: Adam
+def test_adam_matches_oracle_bit_exact_and_reference_within_tolerance(eb, golden):
+    rows0 = golden["adam_rows0"]
+    p = torch.from_numpy(rows0.copy()).to(DEV).requires_grad_(True)
+    opt = eb.OverlayAdam([p], lr=float(golden["adam_lr"]), reg_ref=torch.from_numpy(rows0).to(DEV),
+                         reg_mu=float(golden["adam_mu"]))
+    po, mo, vo = rows0.copy(), np.zeros_like(rows0), np.zeros_like(rows0)
+    rs = np.float32(opt._reg_scale)
+    for k in range(golden["adam_grads"].shape[0]):
+        p.grad = torch.from_numpy(golden["adam_grads"][k]).to(DEV)
+        opt.step()
+        O.adam_(po, golden["adam_grads"][k], mo, vo, k + 1, float(golden["adam_lr"]), p0=rows0, reg_scale=rs)
+        got = p.detach().cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), po.view(np.uint32))
+        ref = golden["adam_traj"][k]
+        norm = np.linalg.norm(ref, axis=1, keepdims=True)
+        assert (np.abs(got - ref) <= 1e-6 * norm).all()
+
+
+def test_adam_random_sizes_and_misaligned_views(eb):
+    rng = np.random.default_rng(3)
+    for numel in (1, 7, 4096, 1_000_003):
+        p = rng.standard_normal(numel).astype(np.float32) * 0.01
+        g = rng.standard_normal(numel).astype(np.float32) * 1e-3
+        p0 = rng.standard_normal(numel).astype(np.float32) * 0.01
+        m = np.zeros(numel, np.float32)
+        v = np.zeros(numel, np.float32)
+        big = torch.zeros(numel + 1, device=DEV)
+        pd = big[1:]  # 4-byte aligned only: the scalar path
+        pd.copy_(torch.from_numpy(p))
+        md, vd = torch.zeros(numel, device=DEV), torch.zeros(numel, device=DEV)
+        gd, p0d = torch.from_numpy(g).to(DEV), torch.from_numpy(p0).to(DEV)
+        lib = eb.load_library()
+        for step in (1, 2, 3):
+            st = lib.engram_adam_step(pd.data_ptr(), gd.data_ptr(), md.data_ptr(), vd.data_ptr(), p0d.data_ptr(),
+                                      numel, step, 1e-3, 0.9, 0.999, 1e-8, 0.37, torch.cuda.current_stream().cuda_stream)
+            assert st == 0
+            O.adam_(p, g, m, v, step, 1e-3, p0=p0, reg_scale=np.float32(0.37))
+        assert np.array_equal(pd.cpu().numpy().view(np.uint32), p.view(np.uint32))
+        assert np.array_equal(vd.cpu().numpy().view(np.uint32), v.view(np.uint32))
+
+
+# ----------------------------------------------------------- pack kernel
+@pytest.mark.parametrize("fmt,dim", [(O.FMT_IQ4_NL, 160), (O.FMT_IQ4_NL, 64), (O.FMT_IQ4_XS, 256),
+                                     (O.FMT_IQ4_XS, 768), (O.FMT_F32, 12)])
+def test_pack_kernel_matches_oracle_layout(eb, fmt, dim):
+    spec = random_spec(fmt, dim, 4096, 11)
+    dt = device_table(eb, spec)
+    got = dt.rows.cpu().numpy().reshape(4096, -1)
+    assert np.array_equal(got, O.pack(fmt, dim, spec.raw))

@@ -1,0 +1,74 @@
+"""Host-side logic of the product package (no GPU): segment starts, row_map
+validation, .pleo files, the install seam."""
+from __future__ import annotations
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import fixtures as FX
+import engraft_ngram_b200 as eb
+from engraft_ngram_b200.overlay import OverlayMap
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_seg_starts_match_reference_rule(seed):
+    rng = np.random.default_rng(seed)
+    seg = np.sort(rng.integers(0, 20, size=500))
+    if seed == 4:  # non-contiguous repeats follow the reference's first-occurrence rule
+        seg = rng.integers(0, 6, size=300)
+    assert np.array_equal(eb.seg_starts_from_segment_ids(torch.from_numpy(seg)), FX.seg_starts(seg))
+    assert eb.seg_starts_from_segment_ids(np.zeros(0, np.int64)).shape == (0,)
+
+
+def test_packed_segment_ids_example():
+    # engraft/replica/pack.py example from the reference's tests/test_seq.py:55
+    seg = torch.tensor([0, 0, 0, 0, 0, 1, 1, 1])
+    assert eb.seg_starts_from_segment_ids(seg).tolist() == [0, 0, 0, 0, 0, 5, 5, 5]
+
+
+def test_row_map_validation():
+    with pytest.raises(NotImplementedError):
+        OverlayMap.from_row_map({((1, 2, 3), 0): 0}, "cpu")
+    with pytest.raises(ValueError):
+        OverlayMap.from_row_map({5: 0, 6: 2}, "cpu")
+    with pytest.raises(ValueError):
+        OverlayMap.from_row_map({-3: 0}, "cpu")
+    with pytest.raises(ValueError):
+        OverlayMap.from_row_map({2**31: 0}, "cpu")
+
+
+def test_pleo_bytes_identical_to_reference(golden, tmp_path):
+    p = tmp_path / "x.pleo"
+    eb.write_pleo(p, golden["pleo_rows"], golden["pleo_data"], strict_160=True)
+    assert np.array_equal(np.frombuffer(p.read_bytes(), dtype=np.uint8), golden["pleo_bytes"])
+    rows, data = eb.read_pleo(p)
+    assert np.array_equal(rows, golden["pleo_rows"]) and np.array_equal(data, golden["pleo_data"])
+
+
+def test_pleo_rejects_bad_magic_and_shapes(tmp_path):
+    p = tmp_path / "bad.pleo"
+    p.write_bytes(b"XXXX" + b"\0" * 8)
+    with pytest.raises(ValueError):
+        eb.read_pleo(p)
+    with pytest.raises(ValueError):
+        eb.write_pleo(tmp_path / "a.pleo", np.zeros(2, np.int32), np.zeros((2, 128), np.float32), strict_160=True)
+    eb.write_pleo(tmp_path / "b.pleo", np.array([9, 3], np.int32), np.ones((2, 256), np.float32))
+    rows, data = eb.read_pleo(tmp_path / "b.pleo")
+    assert data.shape == (2, 256) and rows.tolist() == [9, 3]
+
+
+def test_install_replaces_module_attribute():
+    seq = types.SimpleNamespace(OverlayEmb="reference-class")
+    eb.install(seq)
+    assert seq.OverlayEmb is eb.OverlayEmb
+    eb.uninstall(seq)
+    assert seq.OverlayEmb == "reference-class"
+
+
+def test_overlay_emb_refuses_cpu_tensors():
+    ov = eb.OverlayEmb(object(), [1, 2, 3], torch.zeros(0, 160), {})
+    with pytest.raises(RuntimeError):
+        ov.build(3)

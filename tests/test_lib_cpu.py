@@ -1,0 +1,122 @@
+"""CPU-only checks of the C-ABI library: it loads, exports every entry point
+include/engram_b200.h declares, rejects bad arguments with the documented
+status codes before touching the GPU, and its per-head division magic equals
+Python's % on edge and random values."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import engraft_ngram_b200 as eb
+from engraft_ngram_b200 import _lib as L
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from engraft_ngram_b200 import build
+    build.build()
+    return L.load()
+
+
+def header_functions() -> list[str]:
+    text = (ROOT / "include" / "engram_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:ENGRAM_API\s+)?(?:int|int64_t)\s+(engram_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = header_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(L.SIGNATURES), "ctypes binding and header disagree"
+
+
+def test_version_and_layout_helpers(lib):
+    assert lib.engram_version() >= 100
+    assert lib.engram_row_stride(L.FMT_F32, 128) == 512
+    assert lib.engram_row_stride(L.FMT_IQ4_NL, 160) == 96
+    assert lib.engram_row_stride(L.FMT_IQ4_XS, 256) == 144
+    assert lib.engram_raw_row_bytes(L.FMT_IQ4_NL, 160) == 90
+    assert lib.engram_raw_row_bytes(L.FMT_IQ4_XS, 256) == 136
+    assert lib.engram_row_stride(L.FMT_IQ4_XS, 200) == L.ERR_FORMAT
+    assert lib.engram_row_stride(L.FMT_F32, 2048) == L.ERR_FORMAT
+    assert lib.engram_row_stride(7, 128) == L.ERR_FORMAT
+    assert C.sizeof(L.EngramTable) == 8 * 3 + 4 * 6 + 8 + 8 * 4 + 8 * 32 + 4 * 32 * 2 + 8 * 32
+
+
+def _init(lib, **kw):
+    args = dict(rows=0x1000, n_rows=1000, fmt=L.FMT_F32, dim=128, ngram_size=3, hpn=8,
+                sizes=[50] * 16, offs=[50 * h for h in range(16)], mult=[3, 5, 7, 9], eos=7)
+    args.update(kw)
+    t = L.EngramTable()
+    s = np.asarray(args["sizes"], dtype=np.int64)
+    o = np.asarray(args["offs"], dtype=np.int64)
+    m = np.asarray(args["mult"], dtype=np.uint64)
+    st = lib.engram_table_init(C.byref(t), args["rows"], args["n_rows"], args["fmt"], args["dim"],
+                               args["ngram_size"], args["hpn"], s.ctypes.data, o.ctypes.data, m.ctypes.data,
+                               len(m), args["eos"])
+    return st, t
+
+
+def test_table_init_validates(lib):
+    st, t = _init(lib)
+    assert st == 0 and t.n_heads == 16 and t.row_stride == 512 and t.head_size[3] == 50
+    assert _init(lib, n_rows=0)[0] == L.ERR_RANGE
+    assert _init(lib, offs=[50 * h + 1 for h in range(16)], n_rows=800)[0] == L.ERR_RANGE
+    assert _init(lib, sizes=[0] + [50] * 15)[0] == L.ERR_RANGE
+    assert _init(lib, rows=0x1004)[0] == L.ERR_ARG  # not 16-byte aligned
+    assert _init(lib, ngram_size=5)[0] == L.ERR_ARG
+    assert _init(lib, dim=100, fmt=L.FMT_IQ4_NL)[0] == L.ERR_FORMAT
+    assert _init(lib, mult=[3, 5])[0] == L.ERR_ARG
+
+
+def test_entry_points_reject_bad_arguments_without_launching(lib):
+    st, t = _init(lib)
+    ov = L.EngramOverlay(None, 0, None, None, 0)
+    # negative sizes / null buffers / bad modes are rejected before any launch
+    assert lib.engram_forward(C.byref(t), C.byref(ov), 0x1000, None, 0, -1, 0, 0x1000, None, None, None, None) == L.ERR_ARG
+    assert lib.engram_forward(C.byref(t), C.byref(ov), None, None, 0, 5, 0, 0x1000, None, None, None, None) == L.ERR_ARG
+    assert lib.engram_forward(C.byref(t), C.byref(ov), 0x1000, None, 0, 5, 9, 0x1000, None, None, None, None) == L.ERR_ARG
+    assert lib.engram_forward(C.byref(t), C.byref(ov), 0x1000, None, 0, 5, 0, 0x1008, None, None, None, None) == L.ERR_ARG
+    bad_ov = L.EngramOverlay(0x2000, 10, 0x3000, 0x4000, 12)  # capacity not a power of two
+    assert lib.engram_forward(C.byref(t), C.byref(bad_ov), 0x1000, None, 0, 5, 0, 0x1000, None, None, None, None) == L.ERR_RANGE
+    assert lib.engram_forward(C.byref(t), C.byref(ov), None, None, 0, 0, 0, None, None, None, None, None) == 0
+    assert lib.engram_hash(C.byref(t), None, None, 0, 3, 0x1000, None) == L.ERR_ARG
+    assert lib.engram_overlay_map_build(0x1000, 10, 0x2000, 0x3000, 16, None) == L.ERR_RANGE
+    assert lib.engram_backward(0x1000, 10, 16, 8, 0, 0x2000, 128, 5, 0x3000, 0x4000, 0, None) == L.ERR_WORKSPACE
+    assert lib.engram_backward(0x1000, 10, 16, 4, 1, 0x2000, 128, 5, 0x3000, 0x4000, 1 << 20, None) == L.ERR_FORMAT
+    assert lib.engram_adam_step(0x1000, 0x1000, 0x1000, 0x1000, None, 10, 0, 1e-3, 0.9, 0.999, 1e-8, 0.0, None) == L.ERR_ARG
+    assert lib.engram_backward_workspace_bytes(2048, 16, 40000) > 4 * 4 * 2048 * 16
+
+
+def test_error_mapping():
+    with pytest.raises(ValueError):
+        L.check(L.ERR_RANGE, "x")
+    with pytest.raises(RuntimeError):
+        L.check(L.ERR_CUDA, "x")
+    L.check(0, "x")
+
+
+def test_division_magic_equals_python_mod(lib):
+    rng = np.random.default_rng(0)
+    divisors = [1, 2, 3, 7, 1 << 20, (1 << 20) + 1, 65521, 5000, 20_000_096, 2**31 - 1, 2**31 - 2,
+                *[int(x) for x in rng.integers(1, 2**31, size=40)]]
+    xs = np.concatenate([
+        np.array([0, 1, 2, 2**63, 2**63 - 1, 2**64 - 1, 2**64 - 2, 2**32, 2**32 - 1], dtype=np.uint64),
+        rng.integers(0, 2**64 - 1, size=20000, dtype=np.uint64, endpoint=True),
+    ])
+    out = np.empty_like(xs)
+    for d in divisors:
+        edge = np.array([d - 1, d, d + 1, 2 * d, (2**64 - 1) // d * d, (2**64 - 1) // d * d - 1],
+                        dtype=np.uint64)
+        x = np.concatenate([xs, edge])
+        o = np.empty_like(x)
+        assert lib.engram_selftest_mod(x.ctypes.data, len(x), d, o.ctypes.data) == 0
+        assert np.array_equal(o, x % np.uint64(d)), d

@@ -1,0 +1,108 @@
+"""Pins the CPU oracle to the reference: every function is checked against the
+golden vectors that tests/golden/make_golden.py produced by running the
+reference (fulvian/engraft-ngram) itself."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import fixtures as FX
+from cases import fake_table, overlay_case, sha, syn_table
+from oracle import oracle as O
+
+
+def test_hash_fake_table_matches_reference(golden):
+    # engraft/testing/fake_table.py:41-66 on the damage-test corpus shape
+    p = FX.fake_table_params(seed=7)
+    ids = O.hash_ids(golden["hash_fake_tokens"], p["ngram_size"], p["hpn"], p["mult"], p["head_sizes"],
+                     p["head_offsets"], p["eos"])
+    assert np.array_equal(ids, golden["hash_fake_ids"])
+
+
+def test_hash_synthetic_pletable_matches_reference(golden):
+    # engraft/table.py:111-144 through the real PleTable reader on a GGUF
+    t = syn_table()
+    assert np.array_equal(t.ids(golden["hash_syn_tokens"]), golden["hash_syn_ids"])
+
+
+@pytest.mark.parametrize("k", range(9))
+def test_hash_edge_cases_match_reference(golden, k):
+    t = syn_table()
+    toks = golden[f"edge{k}_tokens"]
+    assert np.array_equal(t.ids(toks), golden[f"edge{k}_ids"].reshape(-1, 16))
+
+
+def test_dequant_iq4nl_bit_exact(golden):
+    got = O.dequant(O.FMT_IQ4_NL, 160, golden["dq_nl_raw"])
+    assert np.array_equal(got.view(np.uint32), golden["dq_nl_out"].view(np.uint32))
+
+
+def test_dequant_iq4xs_bit_exact(golden):
+    got = O.dequant(O.FMT_IQ4_XS, 256, golden["dq_xs_raw"])
+    assert np.array_equal(got.view(np.uint32), golden["dq_xs_out"].view(np.uint32))
+
+
+def _run_overlay(c):
+    ids = c.table.ids(c.tokens, seg_start=c.seg_start, t0=c.t0, n=c.n)
+    emb, slots = O.forward(c.table.fmt, c.table.dim, c.table.raw, ids, 8, c.rows_init, c.row_ids)
+    grad_rows = O.backward(slots, 8, c.grad, c.table.dim, len(c.row_ids))
+    return emb, slots, grad_rows
+
+
+@pytest.mark.parametrize("prefix", ["ov_syn_", "ov_synnoseg_"])
+def test_overlay_forward_backward_iq4nl_bit_exact(golden, prefix):
+    c = overlay_case(golden, prefix, syn_table())
+    emb, slots, grad_rows = _run_overlay(c)
+    assert sha(emb) == str(c.golden["emb_sha"])
+    assert int((slots >= 0).sum()) == int(c.golden["n_id_hits"])
+    assert np.array_equal(grad_rows.view(np.uint32), c.golden["grad_rows"].view(np.uint32))
+
+
+def test_overlay_forward_backward_fake_table_bit_exact(golden, fake1_rows):
+    c = overlay_case(golden, "ov_fake_", fake_table(fake1_rows, seed=1))
+    emb, slots, grad_rows = _run_overlay(c)
+    assert sha(emb) == str(c.golden["emb_sha"])
+    assert int((slots >= 0).sum()) == int(c.golden["n_id_hits"])
+    assert np.array_equal(grad_rows.view(np.uint32), c.golden["grad_rows"].view(np.uint32))
+
+
+def test_backward_order_independent_of_threads(golden):
+    c = overlay_case(golden, "ov_syn_", syn_table())
+    n0 = O.num_threads()
+    try:
+        O.set_num_threads(1)
+        a = _run_overlay(c)[2]
+        O.set_num_threads(max(3, n0))
+        b = _run_overlay(c)[2]
+    finally:
+        O.set_num_threads(n0)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_adam_with_regulariser_matches_torch_adam(golden):
+    # engraft/descend_corpus.py:921-947 with torch.optim.Adam defaults
+    rows0 = golden["adam_rows0"]
+    p = rows0.copy()
+    m = np.zeros_like(p)
+    v = np.zeros_like(p)
+    rs = np.float32(np.float32(golden["adam_mu"]) / golden["adam_S"])
+    for k in range(golden["adam_grads"].shape[0]):
+        O.adam_(p, golden["adam_grads"][k], m, v, k + 1, float(golden["adam_lr"]), p0=rows0, reg_scale=rs)
+        norm = np.linalg.norm(golden["adam_traj"][k], axis=1, keepdims=True)
+        err = np.abs(p - golden["adam_traj"][k])
+        assert (err <= 1e-6 * norm).all(), float((err / norm).max())
+        assert np.allclose(m, golden["adam_m"][k], rtol=1e-5, atol=1e-12)
+        assert np.allclose(v, golden["adam_v"][k], rtol=1e-5, atol=1e-15)
+
+
+def test_pack_layouts_roundtrip(golden):
+    # the resident layouts hold the same bytes as the reference rows
+    raw = golden["dq_nl_raw"]
+    pk = O.pack(O.FMT_IQ4_NL, 160, raw)
+    assert pk.shape == (64, 96)
+    assert np.array_equal(pk[:, :80].reshape(64, 5, 16), raw.reshape(64, 5, 18)[:, :, 2:])
+    assert np.array_equal(pk[:, 80:90].reshape(64, 5, 2), raw.reshape(64, 5, 18)[:, :, :2])
+    xs = golden["dq_xs_raw"]
+    pk = O.pack(O.FMT_IQ4_XS, 256, xs)
+    assert pk.shape == (48, 144)
+    assert np.array_equal(pk[:, :128], xs[:, 8:]) and np.array_equal(pk[:, 128:136], xs[:, :8])

@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--table-rows", type=int, default=None, help="override (profiling a small case)")
+    ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU")
     return ap.parse_args()
 
 
@@ -235,7 +237,11 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
-        self.idx = gpu_index
+        import torch
+        try:
+            self.idx = "GPU-" + str(torch.cuda.get_device_properties(gpu_index).uuid)
+        except Exception:
+            self.idx = str(gpu_index)
         self.proc = None
 
     def __enter__(self):
@@ -291,7 +297,7 @@ def cpu_oracle_step_time(cfg, seed, frac=None, budget_s=20.0):
     from engraft_ngram_b200.table import synthetic_head_sizes, synthetic_multipliers
     fmt = {"f32": O.FMT_F32, "iq4_nl": O.FMT_IQ4_NL, "iq4_xs": O.FMT_IQ4_XS}[cfg["fmt"]]
     dim = cfg["dim"]
-    n_rows = min(cfg["rows"], 1 << 24)
+    n_rows = min(cfg["rows"], 1 << 22)
     rb = O.raw_row_bytes(fmt, dim)
     rng = np.random.default_rng(seed)
     raw = np.frombuffer(rng.bytes(n_rows * rb), dtype=np.uint8).reshape(n_rows, rb).copy()
@@ -412,7 +418,11 @@ START = time.perf_counter()
 
 def main():
     args = parse()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.table_rows:
+        cfg["rows"] = args.table_rows
+    if args.seqs:
+        cfg["seqs"] = args.seqs
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -524,10 +534,10 @@ def run_e2e(wl, args, device, ddist, world):
     hit_h = torch.zeros(1, dtype=torch.int64).pin_memory()
     rows_var = wl.p0.clone().requires_grad_(True)
     opt = eb.OverlayAdam([rows_var], lr=wl.lr, reg_ref=wl.p0, reg_mu=wl.mu)
-    residual = wl.out
     hits = torch.zeros(1, dtype=torch.int64, device=device)
 
     def one():
+        residual = wl.out.detach()
         tok = tok_h.to(device, non_blocking=True)
         ss = ss_h.to(device, non_blocking=True)
         hits.zero_()

@@ -76,6 +76,8 @@ SIGNATURES = {
     "engram_backward_workspace_bytes": (C.c_int64, [C.c_int64, C.c_int32, C.c_int64]),
     "engram_backward": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
                                   C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
+    "engram_backward_noalloc": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                          C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),
     "engram_adam_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                    C.c_double, C.c_double, C.c_double, C.c_double, C.c_float, C.c_void_p]),
     "engram_selftest_mod": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),

@@ -13,6 +13,8 @@
 //   2. segment starts per slot from the sorted keys;
 //   3. one warp per slot adds its terms in that order, from +0, in fp32.
 // The result is bit-identical to the reference and independent of scheduling.
+#include <mutex>
+
 #include "engram_common.cuh"
 
 using namespace engram;
@@ -433,4 +435,45 @@ extern "C" int engram_adam_step(float* p, const float* g, float* m, float* v, co
         count_launches(1);
     }
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+// ---- engram_backward_noalloc ---------------------------------------------------
+// The same row-gradient computation for callers that cannot allocate device
+// memory on their hot path: the scratch comes from this file-scope array
+// instead of a caller workspace.  Host code must not pass the array's name to
+// a kernel (on the host it is only a stand-in symbol); its device address is
+// looked up once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ENGRAM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device (set-up on first use).
+int noalloc_scratch(void** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ENGRAM_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return ENGRAM_ERR_CUDA;
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return ENGRAM_OK;
+}
+}  // namespace
+
+extern "C" int engram_backward_noalloc(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram,
+                                       int32_t mode, const void* grad, int32_t dim, int64_t R, float* grad_rows,
+                                       void* stream) {
+    if (n < 0 || R < 0 || n_heads < 1 || n_heads > ENGRAM_MAX_HEADS) return ENGRAM_ERR_ARG;
+    if (R >= (1LL << 24) || n * n_heads >= (1LL << 31)) return ENGRAM_ERR_RANGE;
+    if (layout(nullptr, n * n_heads, R).bytes > ENGRAM_NOALLOC_SCRATCH_BYTES) return ENGRAM_ERR_WORKSPACE;
+    void* scratch = nullptr;
+    const int st = noalloc_scratch(&scratch);
+    if (st != ENGRAM_OK) return st;
+    return engram_backward(slots, n, n_heads, heads_per_ngram, mode, grad, dim, R, grad_rows, scratch,
+                           ENGRAM_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -194,6 +194,35 @@ ENGRAM_API int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
                     int32_t mode, const void* grad, int32_t dim, int64_t R, float* grad_rows,
                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Size of the library's own scratch array used by engram_backward_noalloc. */
+#define ENGRAM_NOALLOC_SCRATCH_BYTES (12LL << 20)
+
+/*
+ * engram_backward without a workspace argument, for callers that cannot
+ * allocate device memory when they need the row gradients: a host engine
+ * that reserves all of its GPU memory up front and forbids allocation on the
+ * serving/training path (the llama.cpp-style engines that consume .pleo
+ * overlays work this way), or code that must not pay cudaMalloc's implicit
+ * device-wide synchronisation in the middle of a step.  It has no counterpart
+ * in the reference, which always lets torch allocate.
+ *
+ * The caller still passes every input and output; the scratch lives in one
+ * file-scope device array of ENGRAM_NOALLOC_SCRATCH_BYTES (12 MiB) that every
+ * GPU which loads the library keeps until the process exits.  Sizes whose
+ * engram_backward_workspace_bytes(n, n_heads, R) exceeds that return
+ * ENGRAM_ERR_WORKSPACE and launch nothing (about n*n_heads <= 500,000 entries
+ * with R <= 500,000 rows fits).  The first call on a device looks up the
+ * array's device address with that device current, so make that first call
+ * before any stream capture.  All calls share the array: two calls whose
+ * kernels overlap on the GPU (different streams, or different host threads on
+ * one device) race and corrupt each other's results, so serialise them.
+ * Nothing in the array needs to start at zero: each call writes every scratch
+ * byte it later reads.  Results are bit-identical to engram_backward.
+ */
+ENGRAM_API int engram_backward_noalloc(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram,
+                                       int32_t mode, const void* grad, int32_t dim, int64_t R, float* grad_rows,
+                                       void* stream);
+
 /*
  * One optimizer step over numel fp32 elements, in place on p, m, v:
  *   g  = g_in + reg_scale * (2*(p - p0))        (p0 NULL: g = g_in)

@@ -1,0 +1,102 @@
+// engram_adam.cu -- K4: the optimizer step over the overlay rows, fused with the
+// gradient of the descent's regulariser (engraft/descend_corpus.py:921-947).
+// The update follows torch.optim.Adam's single-tensor rule op for op (lerp as
+// one fma, then v*b2 + ((1-b2)*g)*g, sqrt(v)/sqrt(bc2) + eps, p + (-ss*m)/den)
+// with IEEE-rounded sqrt and division, so it matches the CPU oracle bit for bit.
+#include "engram_common.cuh"
+
+using namespace engram;
+
+namespace {
+
+struct AdamScalars {
+    float w1, b2, w2, eps, neg_step_size, bc2_sqrt, reg_scale;
+};
+
+__device__ __forceinline__ float adam_elem(float& p, float g, float& m, float& v, float p0, bool reg,
+                                           const AdamScalars& a) {
+    if (reg) g = __fadd_rn(g, __fmul_rn(a.reg_scale, __fmul_rn(2.0f, __fsub_rn(p, p0))));
+    const float mi = __fmaf_rn(a.w1, __fsub_rn(g, m), m);
+    const float vi = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(__fmul_rn(a.w2, g), g));
+    const float den = __fadd_rn(__fdiv_rn(__fsqrt_rn(vi), a.bc2_sqrt), a.eps);
+    p = __fadd_rn(p, __fdiv_rn(__fmul_rn(a.neg_step_size, mi), den));
+    m = mi;
+    v = vi;
+    return p;
+}
+
+__global__ void __launch_bounds__(256) k_adam_vec4(float4* __restrict__ p, const float4* __restrict__ g,
+                                                   float4* __restrict__ m, float4* __restrict__ v,
+                                                   const float4* __restrict__ p0, int64_t n4, AdamScalars a) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        float4 pp = p[i], mm = m[i], vv = v[i];
+        const float4 gg = __ldcs(g + i);
+        const float4 q = p0 ? __ldg(p0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const bool reg = p0 != nullptr;
+        adam_elem(pp.x, gg.x, mm.x, vv.x, q.x, reg, a);
+        adam_elem(pp.y, gg.y, mm.y, vv.y, q.y, reg, a);
+        adam_elem(pp.z, gg.z, mm.z, vv.z, q.z, reg, a);
+        adam_elem(pp.w, gg.w, mm.w, vv.w, q.w, reg, a);
+        p[i] = pp;
+        m[i] = mm;
+        v[i] = vv;
+    }
+}
+
+__global__ void k_adam_scalar(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                              float* __restrict__ v, const float* __restrict__ p0, int64_t lo, int64_t n,
+                              AdamScalars a) {
+    for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float pp = p[i], mm = m[i], vv = v[i];
+        adam_elem(pp, g[i], mm, vv, p0 ? p0[i] : 0.f, p0 != nullptr, a);
+        p[i] = pp;
+        m[i] = mm;
+        v[i] = vv;
+    }
+}
+
+int grid_for(int64_t work, int threads, int per_sm) {
+    const int64_t want = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count() * per_sm;
+    const int64_t g = want < cap ? want : cap;
+    return (int)(g > 0 ? g : 1);
+}
+
+}  // namespace
+
+extern "C" int engram_adam_step(float* p, const float* g, float* m, float* v, const float* p0, int64_t numel,
+                                int64_t step, double lr, double beta1, double beta2, double eps, float reg_scale,
+                                void* stream) {
+    if (numel < 0 || step < 1) return ENGRAM_ERR_ARG;
+    if (numel == 0) return ENGRAM_OK;
+    if (!p || !g || !m || !v) return ENGRAM_ERR_ARG;
+    AdamScalars a;
+    const double bc1 = 1.0 - pow(beta1, (double)step);
+    const double bc2 = 1.0 - pow(beta2, (double)step);
+    a.w1 = (float)(1.0 - beta1);
+    a.b2 = (float)beta2;
+    a.w2 = (float)(1.0 - beta2);
+    a.eps = (float)eps;
+    a.neg_step_size = -(float)(lr / bc1);
+    a.bc2_sqrt = (float)sqrt(bc2);
+    a.reg_scale = reg_scale;
+    cudaStream_t s = (cudaStream_t)stream;
+    const bool vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v) && (!p0 || aligned16(p0));
+    int64_t done = 0;
+    if (vec) {
+        const int64_t n4 = numel / 4;
+        if (n4 > 0)
+        {
+            k_adam_vec4<<<grid_for(n4, 256, 8), 256, 0, s>>>((float4*)p, (const float4*)g, (float4*)m, (float4*)v,
+                                                             (const float4*)p0, n4, a);
+            count_launches(1);
+        }
+        done = n4 * 4;
+    }
+    if (done < numel) {
+        k_adam_scalar<<<grid_for(numel - done, 256, 8), 256, 0, s>>>(p, g, m, v, p0, done, numel, a);
+        count_launches(1);
+    }
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+

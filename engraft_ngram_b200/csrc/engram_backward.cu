@@ -1,18 +1,23 @@
-// engram_backward.cu -- K3 (row gradients of the overlay) and K4 (Adam + the
-// descent's regulariser).
+// engram_backward.cu -- K3: row gradients of the overlay.
 //
-// K3 reproduces the reference's accumulation order exactly.  The reference
-// sums duplicate rows with index_put_(accumulate=True) over idx lists built in
-// ascending (t, h) order (engraft/replica/seq.py:401-441): serially on one CPU
-// thread, and after a stable sort of the indices on CUDA.  Here:
-//   1. a stable LSD radix sort (8-bit digits) of the hit entries keyed by
-//      overlay slot; entry values are flat indices t*n_heads+h, so each slot's
-//      entries come out in ascending (t, h) order.  Ranks inside a tile come
-//      from warp __match_any_sync groups plus per-warp digit counts, so no
-//      comparison sort is needed;
-//   2. segment starts per slot from the sorted keys;
-//   3. one warp per slot adds its terms in that order, from +0, in fp32.
-// The result is bit-identical to the reference and independent of scheduling.
+// The result reproduces the reference's accumulation order exactly.  The
+// reference sums duplicate rows with index_put_(accumulate=True) over idx lists
+// built in ascending (t, h) order (engraft/replica/seq.py:401-441): serially on
+// one CPU thread, and after a stable sort of the indices on CUDA.  Here:
+//   1. a stable LSD radix sort (8-bit digits) of the hit entries keyed by overlay
+//      slot; entry values are flat indices t*n_heads+h, so each slot's entries
+//      come out in ascending (t, h) order.  Ranks inside a tile come from warp
+//      __match_any_sync groups plus per-warp digit counts (no comparison sort);
+//      block offsets come from a per-digit row scan (256 blocks);
+//   2. segment starts per slot from the sorted keys; segments longer than
+//      kHeavy entries are listed for block-wide reduction;
+//   3. one reduce kernel, scheduled dynamically: each block first takes heavy
+//      segments (the longest chains), streaming their rows through a
+//      kStages-deep cp.async shared-memory pipeline while every thread adds its
+//      own columns in order; then warps take the remaining slots, one per warp.
+// Every term is added from +0 in ascending (t, h) order in fp32, so the result
+// is bit-identical to the reference and independent of scheduling.
+#include <algorithm>
 #include <mutex>
 
 #include "engram_common.cuh"
@@ -27,6 +32,14 @@ constexpr int kRsWarps = kRsThreads / 32;
 constexpr int kRsItems = 16;
 constexpr int kRsTile = kRsThreads * kRsItems;
 constexpr int kScanThreads = 1024;
+constexpr int kHeavy = 64;            // segments with more entries are reduced by a whole block
+constexpr int kRedThreads = 256;
+constexpr int kStageBytes = 16384;    // rows staged per pipeline stage (>= 4 rows of <= 4 KB)
+constexpr int kStages = 6;
+constexpr int kRedSmem = kStages * kStageBytes;
+
+// counters[] in the workspace
+constexpr int kCntHits = 0, kCntHeavy = 1, kCntHeavyNext = 2, kCntLightNext = 3;
 
 inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
@@ -34,7 +47,9 @@ struct Workspace {
     int32_t* keys[2];
     int32_t* vals[2];
     uint32_t* block_hist;
+    uint32_t* digit_tot;
     int32_t* seg_begin;
+    int32_t* heavy;
     int32_t* counters;
     int64_t bytes;
     int nblk;
@@ -44,6 +59,7 @@ Workspace layout(void* base, int64_t N, int64_t R) {
     Workspace w{};
     const int64_t nblk = (N + kRsTile - 1) / kRsTile;
     w.nblk = (int)(nblk > 0 ? nblk : 1);
+    const int64_t max_heavy = std::min<int64_t>(R, N / (kHeavy + 1) + 1);
     char* p = static_cast<char*>(base);
     int64_t off = 0;
     auto take = [&](int64_t bytes) {
@@ -56,17 +72,54 @@ Workspace layout(void* base, int64_t N, int64_t R) {
         w.vals[k] = reinterpret_cast<int32_t*>(take(4 * N));
     }
     w.block_hist = reinterpret_cast<uint32_t*>(take(4 * 256 * (int64_t)w.nblk));
+    w.digit_tot = reinterpret_cast<uint32_t*>(take(4 * 256));
     w.seg_begin = reinterpret_cast<int32_t*>(take(4 * (R + 1)));
+    w.heavy = reinterpret_cast<int32_t*>(take(4 * max_heavy));
     w.counters = reinterpret_cast<int32_t*>(take(64));
     w.bytes = off;
     return w;
 }
 
+// Exclusive scan of one value per thread over a block of `nthreads` (multiple of
+// 32, <= 1024); returns the exclusive prefix, *total gets the block sum.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sums, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFull, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t s = lane < nwarps ? warp_sums[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(kFull, s, o);
+            if (lane >= o) s += y;
+        }
+        if (lane < nwarps) warp_sums[lane] = s;  // inclusive over warps
+    }
+    __syncthreads();
+    const uint32_t before = warp == 0 ? 0u : warp_sums[warp - 1];
+    if (total) *total = warp_sums[nwarps - 1];
+    const uint32_t res = before + x - v;
+    __syncthreads();  // warp_sums may be reused by the caller
+    return res;
+}
+
 // Pass histogram: digit counts of this block's tile, stored digit-major.
 __global__ void __launch_bounds__(kRsThreads) k_rs_hist(const int32_t* __restrict__ keys, const int32_t* n_dev,
-                                                        int64_t n_static, int shift, uint32_t* block_hist, int nblk) {
+                                                        int64_t n_static, int shift, uint32_t* block_hist, int nblk,
+                                                        int32_t* counters) {
     __shared__ uint32_t h[256];
     for (int d = threadIdx.x; d < 256; d += kRsThreads) h[d] = 0;
+    if (counters && blockIdx.x == 0 && threadIdx.x == 0) {
+        counters[kCntHeavy] = 0;
+        counters[kCntHeavyNext] = 0;
+        counters[kCntLightNext] = 0;
+    }
     __syncthreads();
     const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
     const int64_t begin = (int64_t)blockIdx.x * kRsTile;
@@ -81,42 +134,42 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_hist(const int32_t* __restric
     for (int d = threadIdx.x; d < 256; d += kRsThreads) block_hist[(int64_t)d * nblk + blockIdx.x] = h[d];
 }
 
-// Exclusive scan in place over len entries (one block).  *total = sum.
-__global__ void __launch_bounds__(kScanThreads) k_scan(uint32_t* a, int64_t len, int32_t* total) {
-    __shared__ uint32_t part[kScanThreads];
-    const int tid = threadIdx.x;
-    const int64_t per = (len + kScanThreads - 1) / kScanThreads;
-    const int64_t lo = tid * per, hi = (lo + per < len) ? lo + per : len;
-    uint32_t s = 0;
-    for (int64_t i = lo; i < hi; i++) s += a[i];
-    part[tid] = s;
-    __syncthreads();
-    for (int off = 1; off < kScanThreads; off <<= 1) {
-        const uint32_t v = tid >= off ? part[tid - off] : 0u;
-        __syncthreads();
-        part[tid] += v;
-        __syncthreads();
+// Block d: exclusive scan, in place, of digit d's counts over the blocks; digit_tot[d] = total.
+__global__ void __launch_bounds__(kScanThreads) k_rs_rowscan(uint32_t* block_hist, int nblk, uint32_t* digit_tot) {
+    __shared__ uint32_t wsum[32];
+    uint32_t* row = block_hist + (int64_t)blockIdx.x * nblk;
+    uint32_t carry = 0;
+    for (int base = 0; base < nblk; base += kScanThreads) {
+        const int i = base + threadIdx.x;
+        const uint32_t v = i < nblk ? row[i] : 0u;
+        uint32_t tot;
+        const uint32_t ex = block_exclusive_scan(v, wsum, &tot);
+        if (i < nblk) row[i] = carry + ex;
+        carry += tot;
     }
-    uint32_t run = part[tid] - s;  // exclusive prefix of this thread's chunk
-    for (int64_t i = lo; i < hi; i++) {
-        const uint32_t x = a[i];
-        a[i] = run;
-        run += x;
-    }
-    if (tid == kScanThreads - 1 && total) *total = (int32_t)part[tid];
+    if (threadIdx.x == 0) digit_tot[blockIdx.x] = carry;
 }
 
 // Stable scatter of one pass.  vals_in == nullptr: the value is the index.
+// total_out (nullable): receives the number of entries sorted (the hit count).
 __global__ void __launch_bounds__(kRsThreads) k_rs_scatter(const int32_t* __restrict__ keys_in,
                                                            const int32_t* __restrict__ vals_in, const int32_t* n_dev,
                                                            int64_t n_static, int shift,
-                                                           const uint32_t* __restrict__ block_off, int nblk,
+                                                           const uint32_t* __restrict__ block_off,
+                                                           const uint32_t* __restrict__ digit_tot, int nblk,
                                                            int32_t* __restrict__ keys_out,
-                                                           int32_t* __restrict__ vals_out) {
+                                                           int32_t* __restrict__ vals_out, int32_t* total_out) {
     __shared__ uint32_t wcnt[kRsWarps][256];
     __shared__ uint32_t run[256];
+    __shared__ uint32_t wsum[32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int d = tid; d < 256; d += kRsThreads) run[d] = block_off[(int64_t)d * nblk + blockIdx.x];
+    {
+        const uint32_t dt = digit_tot[tid];  // kRsThreads == 256 digits
+        uint32_t tot;
+        const uint32_t base = block_exclusive_scan(dt, wsum, &tot);
+        run[tid] = base + block_off[(int64_t)tid * nblk + blockIdx.x];
+        if (total_out && blockIdx.x == 0 && tid == 0) *total_out = (int32_t)tot;
+    }
     const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
     const int64_t begin = (int64_t)blockIdx.x * kRsTile;
     const unsigned lt = (1u << lane) - 1u;
@@ -131,7 +184,8 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_scatter(const int32_t* __rest
         const int rank = __popc(peers & lt);
         if (valid && rank == 0) wcnt[warp][digit] = (uint32_t)__popc(peers);
         __syncthreads();
-        for (int d = tid; d < 256; d += kRsThreads) {
+        {
+            const int d = tid;
             uint32_t acc = run[d];
 #pragma unroll
             for (int w = 0; w < kRsWarps; w++) {
@@ -151,10 +205,11 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_scatter(const int32_t* __rest
     }
 }
 
-// seg_begin[s] = number of sorted entries with key < s, for s in [0, R].
-__global__ void k_seg_begin(const int32_t* __restrict__ keys, const int32_t* n_dev, int64_t R,
-                            int32_t* __restrict__ seg_begin) {
-    const int64_t n = *n_dev;
+// seg_begin[s] = number of sorted entries with key < s, for s in [0, R]; segments
+// longer than kHeavy are appended to heavy[] (their order does not matter).
+__global__ void k_seg_begin(const int32_t* __restrict__ keys, int32_t* counters, int64_t R,
+                            int32_t* __restrict__ seg_begin, int32_t* __restrict__ heavy) {
+    const int64_t n = counters[kCntHits];
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (n == 0) {
@@ -164,105 +219,139 @@ __global__ void k_seg_begin(const int32_t* __restrict__ keys, const int32_t* n_d
     for (int64_t i = tid; i < n; i += stride) {
         const int32_t k = keys[i];
         const int32_t prev = i == 0 ? -1 : keys[i - 1];
-        for (int64_t s = (int64_t)prev + 1; s <= k; s++) seg_begin[s] = (int32_t)i;
+        if (k != prev) {
+            for (int64_t s = (int64_t)prev + 1; s <= k; s++) seg_begin[s] = (int32_t)i;
+            int64_t lo = i, hi = n;  // first index > i whose key differs (upper bound of k)
+            while (lo < hi) {
+                const int64_t mid = (lo + hi) >> 1;
+                if (keys[mid] <= k) lo = mid + 1; else hi = mid;
+            }
+            if (lo - i > kHeavy) heavy[atomicAdd(counters + kCntHeavy, 1)] = k;
+        }
         if (i == n - 1)
             for (int64_t s = (int64_t)k + 1; s <= R; s++) seg_begin[s] = (int32_t)n;
     }
 }
 
-// One warp per slot: grad_rows[s] = sum of its terms in sorted (ascending) order.
-// CONCAT: term = grad[i, :] (fp32, i = t*n_heads+h); CPL = float4 chunks per lane.
-template <int CPL>
-__global__ void __launch_bounds__(256) k_reduce_concat(const int32_t* __restrict__ seg_begin,
-                                                       const int32_t* __restrict__ vals, int64_t R, int dim,
-                                                       const float* __restrict__ grad, float* __restrict__ grad_rows) {
-    const int lane = threadIdx.x & 31;
-    const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    const int cpr = dim >> 2;
-    const float4* g4 = reinterpret_cast<const float4*>(grad);
-    for (int64_t s = warp0; s < R; s += nwarps) {
-        const int b = __ldg(seg_begin + s), e = __ldg(seg_begin + s + 1);
-        float4 acc[CPL];
-#pragma unroll
-        for (int j = 0; j < CPL; j++) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        constexpr int P = 4;
-        for (int k = b; k < e; k += P) {
-            float4 x[P][CPL];
-#pragma unroll
-            for (int p = 0; p < P; p++) {
-                if (k + p < e) {
-                    const int64_t i = __ldg(vals + k + p);
-#pragma unroll
-                    for (int j = 0; j < CPL; j++) {
-                        const int c = lane + 32 * j;
-                        if (c < cpr) x[p][j] = __ldg(g4 + i * cpr + c);
-                    }
-                }
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Address of the upstream-gradient row of flat entry i = t*n_heads + h.
+template <int MODE>
+__device__ __forceinline__ const uint8_t* grad_row(const uint8_t* grad, int64_t i, int dim, int n_heads, int hpn) {
+    if (MODE == ENGRAM_MODE_CONCAT_F32) return grad + i * (int64_t)dim * 4;
+    const int64_t t = i / n_heads;
+    const int h = (int)(i - t * n_heads);
+    return grad + (t * hpn * dim + (int64_t)(h % hpn) * dim) * 2;
+}
+
+// One heavy segment [b, e) of slot s, reduced by the whole block.
+template <int MODE>
+__device__ void reduce_heavy(int64_t s, int b, int e, const int32_t* __restrict__ vals, int dim, int n_heads, int hpn,
+                             const uint8_t* __restrict__ grad, float* __restrict__ grad_rows, uint8_t* smem) {
+    constexpr int ES = MODE == ENGRAM_MODE_CONCAT_F32 ? 4 : 2;
+    const int row_bytes = dim * ES;
+    const int chunks = row_bytes >> 4;
+    const int rps = kStageBytes / row_bytes;  // rows per stage
+    const int n = e - b;
+    const int nst = (n + rps - 1) / rps;
+    const int tid = threadIdx.x;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // columns tid + 256*j (dim <= 1024)
+
+    auto issue = [&](int st) {
+        if (st < nst) {
+            uint8_t* buf = smem + (st % kStages) * kStageBytes;
+            const int r0 = st * rps;
+            const int nr = min(rps, n - r0);
+            for (int c = tid; c < nr * chunks; c += kRedThreads) {
+                const int r = c / chunks, p = c - r * chunks;
+                const int64_t i = __ldg(vals + b + r0 + r);
+                cp_async16(buf + r * row_bytes + p * 16, grad_row<MODE>(grad, i, dim, n_heads, hpn) + p * 16);
             }
+        }
+        cp_async_commit();
+    };
+#pragma unroll 1
+    for (int st = 0; st < kStages - 1; st++) issue(st);
+#pragma unroll 1
+    for (int st = 0; st < nst; st++) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();
+        issue(st + kStages - 1);
+        const uint8_t* buf = smem + (st % kStages) * kStageBytes;
+        const int nr = min(rps, n - st * rps);
+#pragma unroll 1
+        for (int r = 0; r < nr; r++) {
 #pragma unroll
-            for (int p = 0; p < P; p++) {
-                if (k + p < e) {
-#pragma unroll
-                    for (int j = 0; j < CPL; j++) {
-                        acc[j].x = __fadd_rn(acc[j].x, x[p][j].x);
-                        acc[j].y = __fadd_rn(acc[j].y, x[p][j].y);
-                        acc[j].z = __fadd_rn(acc[j].z, x[p][j].z);
-                        acc[j].w = __fadd_rn(acc[j].w, x[p][j].w);
-                    }
+            for (int j = 0; j < 4; j++) {
+                const int c = tid + kRedThreads * j;
+                if (c < dim) {
+                    float x;
+                    if (MODE == ENGRAM_MODE_CONCAT_F32)
+                        x = reinterpret_cast<const float*>(buf + r * row_bytes)[c];
+                    else
+                        x = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(buf + r * row_bytes)[c] << 16);
+                    acc[j] = __fadd_rn(acc[j], x);
                 }
             }
         }
-        float4* dst = reinterpret_cast<float4*>(grad_rows + s * (int64_t)dim);
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the next segment reuses the stage buffers
 #pragma unroll
-        for (int j = 0; j < CPL; j++) {
-            const int c = lane + 32 * j;
-            if (c < cpr) dst[c] = acc[j];
-        }
+    for (int j = 0; j < 4; j++) {
+        const int c = tid + kRedThreads * j;
+        if (c < dim) grad_rows[s * dim + c] = acc[j];
     }
 }
 
-// PAIRSUM: term of (t,h) = bf16 grad[t, (h%hpn)*dim : +dim]; CPL = 8-value chunks per lane.
-template <int CPL>
-__global__ void __launch_bounds__(256) k_reduce_pairsum(const int32_t* __restrict__ seg_begin,
-                                                        const int32_t* __restrict__ vals, int64_t R, int dim,
-                                                        int n_heads, int hpn, const uint16_t* __restrict__ grad,
-                                                        float* __restrict__ grad_rows) {
-    const int lane = threadIdx.x & 31;
-    const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    const int cpr = dim >> 3;
-    const int64_t row_elems = (int64_t)hpn * dim;
-    for (int64_t s = warp0; s < R; s += nwarps) {
-        const int b = __ldg(seg_begin + s), e = __ldg(seg_begin + s + 1);
-        float acc[CPL][8];
+// One light segment (<= kHeavy entries) of slot s, reduced by one warp.
+// CPL = 16-byte chunks of the row per lane; P rows are loaded before they are added.
+template <int MODE, int CPL>
+__device__ __forceinline__ void reduce_light(int64_t s, int b, int e, const int32_t* __restrict__ vals, int dim,
+                                             int n_heads, int hpn, const uint8_t* __restrict__ grad,
+                                             float* __restrict__ grad_rows, int lane) {
+    constexpr int P = (8 / CPL) > 0 ? 8 / CPL : 1;
+    constexpr int VPC = MODE == ENGRAM_MODE_CONCAT_F32 ? 4 : 8;  // values per 16-byte chunk
+    const int cpr = dim / VPC;
+    const int n = e - b;
+    const int32_t idx0 = lane < n ? __ldg(vals + b + lane) : 0;
+    const int32_t idx1 = lane + 32 < n ? __ldg(vals + b + 32 + lane) : 0;
+    float acc[CPL][VPC];
 #pragma unroll
-        for (int j = 0; j < CPL; j++)
+    for (int j = 0; j < CPL; j++)
 #pragma unroll
-            for (int q = 0; q < 8; q++) acc[j][q] = 0.f;
-        constexpr int P = 4;
-        for (int k = b; k < e; k += P) {
-            uint4 x[P][CPL];
+        for (int q = 0; q < VPC; q++) acc[j][q] = 0.f;
+    for (int k0 = 0; k0 < n; k0 += P) {
+        uint4 x[P][CPL];
 #pragma unroll
-            for (int p = 0; p < P; p++) {
-                if (k + p < e) {
-                    const int32_t i = __ldg(vals + k + p);
-                    const int64_t t = i / n_heads;
-                    const int h = i - (int)(t * n_heads);
-                    const uint4* src = reinterpret_cast<const uint4*>(grad + t * row_elems + (int64_t)(h % hpn) * dim);
+        for (int p = 0; p < P; p++) {
+            const int k = k0 + p;
+            const int32_t i = __shfl_sync(kFull, k < 32 ? idx0 : idx1, k & 31);
+            if (k < n) {
+                const uint4* src = reinterpret_cast<const uint4*>(grad_row<MODE>(grad, i, dim, n_heads, hpn));
 #pragma unroll
-                    for (int j = 0; j < CPL; j++) {
-                        const int c = lane + 32 * j;
-                        if (c < cpr) x[p][j] = __ldg(src + c);
-                    }
+                for (int j = 0; j < CPL; j++) {
+                    const int c = lane + 32 * j;
+                    if (c < cpr) x[p][j] = __ldg(src + c);
                 }
             }
+        }
 #pragma unroll
-            for (int p = 0; p < P; p++) {
-                if (k + p < e) {
+        for (int p = 0; p < P; p++) {
+            if (k0 + p < n) {
 #pragma unroll
-                    for (int j = 0; j < CPL; j++) {
-                        const uint32_t w[4] = {x[p][j].x, x[p][j].y, x[p][j].z, x[p][j].w};
+                for (int j = 0; j < CPL; j++) {
+                    const uint32_t w[4] = {x[p][j].x, x[p][j].y, x[p][j].z, x[p][j].w};
+                    if (MODE == ENGRAM_MODE_CONCAT_F32) {
+#pragma unroll
+                        for (int q = 0; q < 4; q++) acc[j][q] = __fadd_rn(acc[j][q], __uint_as_float(w[q]));
+                    } else {
 #pragma unroll
                         for (int q = 0; q < 4; q++) {
                             acc[j][2 * q] = __fadd_rn(acc[j][2 * q], __uint_as_float(w[q] << 16));
@@ -272,62 +361,69 @@ __global__ void __launch_bounds__(256) k_reduce_pairsum(const int32_t* __restric
                 }
             }
         }
-        float4* dst = reinterpret_cast<float4*>(grad_rows + s * (int64_t)dim);
+    }
+    float4* dst = reinterpret_cast<float4*>(grad_rows + s * (int64_t)dim);
 #pragma unroll
-        for (int j = 0; j < CPL; j++) {
-            const int c = lane + 32 * j;
-            if (c < cpr) {
-                dst[2 * c] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
-                dst[2 * c + 1] = make_float4(acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
-            }
+    for (int j = 0; j < CPL; j++) {
+        const int c = lane + 32 * j;
+        if (c < cpr) {
+#pragma unroll
+            for (int q = 0; q < VPC; q += 4)
+                dst[c * (VPC / 4) + q / 4] = make_float4(acc[j][q], acc[j][q + 1], acc[j][q + 2], acc[j][q + 3]);
         }
     }
 }
 
-struct AdamScalars {
-    float w1, b2, w2, eps, neg_step_size, bc2_sqrt, reg_scale;
-};
-
-__device__ __forceinline__ float adam_elem(float& p, float g, float& m, float& v, float p0, bool reg,
-                                           const AdamScalars& a) {
-    if (reg) g = __fadd_rn(g, __fmul_rn(a.reg_scale, __fmul_rn(2.0f, __fsub_rn(p, p0))));
-    const float mi = __fmaf_rn(a.w1, __fsub_rn(g, m), m);
-    const float vi = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(__fmul_rn(a.w2, g), g));
-    const float den = __fadd_rn(__fdiv_rn(__fsqrt_rn(vi), a.bc2_sqrt), a.eps);
-    p = __fadd_rn(p, __fdiv_rn(__fmul_rn(a.neg_step_size, mi), den));
-    m = mi;
-    v = vi;
-    return p;
-}
-
-__global__ void __launch_bounds__(256) k_adam_vec4(float4* __restrict__ p, const float4* __restrict__ g,
-                                                   float4* __restrict__ m, float4* __restrict__ v,
-                                                   const float4* __restrict__ p0, int64_t n4, AdamScalars a) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-        float4 pp = p[i], mm = m[i], vv = v[i];
-        const float4 gg = __ldcs(g + i);
-        const float4 q = p0 ? __ldg(p0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        const bool reg = p0 != nullptr;
-        adam_elem(pp.x, gg.x, mm.x, vv.x, q.x, reg, a);
-        adam_elem(pp.y, gg.y, mm.y, vv.y, q.y, reg, a);
-        adam_elem(pp.z, gg.z, mm.z, vv.z, q.z, reg, a);
-        adam_elem(pp.w, gg.w, mm.w, vv.w, q.w, reg, a);
-        p[i] = pp;
-        m[i] = mm;
-        v[i] = vv;
+template <int MODE, int CPL>
+__global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restrict__ seg_begin,
+                                                        const int32_t* __restrict__ vals, int64_t R, int dim,
+                                                        int n_heads, int hpn, const uint8_t* __restrict__ grad,
+                                                        float* __restrict__ grad_rows,
+                                                        const int32_t* __restrict__ heavy, int32_t* counters) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ int s_job;
+    const int lane = threadIdx.x & 31;
+    const int n_heavy = counters[kCntHeavy];
+    // heavy segments first: the longest sequential chains start earliest
+    while (true) {
+        if (threadIdx.x == 0) s_job = atomicAdd(counters + kCntHeavyNext, 1);
+        __syncthreads();
+        const int j = s_job;
+        __syncthreads();
+        if (j >= n_heavy) break;
+        const int64_t s = heavy[j];
+        reduce_heavy<MODE>(s, __ldg(seg_begin + s), __ldg(seg_begin + s + 1), vals, dim, n_heads, hpn, grad,
+                           grad_rows, smem);
+    }
+    // then every other slot, eight at a time per warp
+    constexpr int kGrab = 8;
+    while (true) {
+        int64_t base = 0;
+        if (lane == 0) base = atomicAdd(counters + kCntLightNext, kGrab);
+        base = __shfl_sync(kFull, base, 0);
+        if (base >= R) break;
+        const int64_t end = base + kGrab < R ? base + kGrab : R;
+        for (int64_t s = base; s < end; s++) {
+            const int b = __ldg(seg_begin + s), e = __ldg(seg_begin + s + 1);
+            if (e - b <= kHeavy) reduce_light<MODE, CPL>(s, b, e, vals, dim, n_heads, hpn, grad, grad_rows, lane);
+        }
     }
 }
 
-__global__ void k_adam_scalar(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
-                              float* __restrict__ v, const float* __restrict__ p0, int64_t lo, int64_t n,
-                              AdamScalars a) {
-    for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        float pp = p[i], mm = m[i], vv = v[i];
-        adam_elem(pp, g[i], mm, vv, p0 ? p0[i] : 0.f, p0 != nullptr, a);
-        p[i] = pp;
-        m[i] = mm;
-        v[i] = vv;
+template <int MODE, int CPL>
+void launch_reduce(const Workspace& w, const int32_t* vals, int64_t R, int dim, int n_heads, int hpn,
+                   const void* grad, float* grad_rows, cudaStream_t s) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaFuncSetAttribute(k_reduce<MODE, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRedSmem);
+        configured[dev] = true;
     }
+    const int grid = sm_count() * 2;
+    k_reduce<MODE, CPL><<<grid, kRedThreads, kRedSmem, s>>>(w.seg_begin, vals, R, dim, n_heads, hpn,
+                                                           static_cast<const uint8_t*>(grad), grad_rows, w.heavy,
+                                                           w.counters);
 }
 
 int grid_for(int64_t work, int threads, int per_sm) {
@@ -367,73 +463,35 @@ extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
     int bits = 0;
     while ((1LL << bits) < R) bits++;
     const int passes = bits <= 8 ? 1 : (bits + 7) / 8;
-    const int64_t hist_len = 256LL * w.nblk;
     int cur = 0;
     for (int pass = 0; pass < passes; pass++) {
         const int shift = 8 * pass;
         const int32_t* kin = pass == 0 ? slots : w.keys[cur];
         const int32_t* vin = pass == 0 ? nullptr : w.vals[cur];
-        const int32_t* n_dev = pass == 0 ? nullptr : w.counters;
+        const int32_t* n_dev = pass == 0 ? nullptr : w.counters + kCntHits;
         const int out = pass == 0 ? 0 : 1 - cur;
-        k_rs_hist<<<w.nblk, kRsThreads, 0, s>>>(kin, n_dev, N, shift, w.block_hist, w.nblk);
-        k_scan<<<1, kScanThreads, 0, s>>>(w.block_hist, hist_len, pass == 0 ? w.counters : w.counters + 1);
-        k_rs_scatter<<<w.nblk, kRsThreads, 0, s>>>(kin, vin, n_dev, N, shift, w.block_hist, w.nblk, w.keys[out],
-                                                     w.vals[out]);
+        k_rs_hist<<<w.nblk, kRsThreads, 0, s>>>(kin, n_dev, N, shift, w.block_hist, w.nblk,
+                                                pass == 0 ? w.counters : nullptr);
+        k_rs_rowscan<<<256, kScanThreads, 0, s>>>(w.block_hist, w.nblk, w.digit_tot);
+        k_rs_scatter<<<w.nblk, kRsThreads, 0, s>>>(kin, vin, n_dev, N, shift, w.block_hist, w.digit_tot, w.nblk,
+                                                     w.keys[out], w.vals[out],
+                                                     pass == 0 ? w.counters + kCntHits : nullptr);
         cur = out;
     }
-    count_launches(3 * passes + 2);
-    k_seg_begin<<<grid_for(N, 256, 8), 256, 0, s>>>(w.keys[cur], w.counters, R, w.seg_begin);
-    const int rblocks = grid_for(R * 32, 256, 8);
+    k_seg_begin<<<grid_for(N, 256, 8), 256, 0, s>>>(w.keys[cur], w.counters, R, w.seg_begin, w.heavy);
     if (mode == ENGRAM_MODE_CONCAT_F32) {
         const int cpl = (dim / 4 + 31) / 32;
-        const float* g = static_cast<const float*>(grad);
-        if (cpl <= 1) k_reduce_concat<1><<<rblocks, 256, 0, s>>>(w.seg_begin, w.vals[cur], R, dim, g, grad_rows);
-        else if (cpl <= 2) k_reduce_concat<2><<<rblocks, 256, 0, s>>>(w.seg_begin, w.vals[cur], R, dim, g, grad_rows);
-        else if (cpl <= 4) k_reduce_concat<4><<<rblocks, 256, 0, s>>>(w.seg_begin, w.vals[cur], R, dim, g, grad_rows);
-        else k_reduce_concat<8><<<rblocks, 256, 0, s>>>(w.seg_begin, w.vals[cur], R, dim, g, grad_rows);
+        if (cpl <= 1) launch_reduce<ENGRAM_MODE_CONCAT_F32, 1>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else if (cpl <= 2) launch_reduce<ENGRAM_MODE_CONCAT_F32, 2>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else if (cpl <= 4) launch_reduce<ENGRAM_MODE_CONCAT_F32, 4>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else launch_reduce<ENGRAM_MODE_CONCAT_F32, 8>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
     } else {
         const int cpl = (dim / 8 + 31) / 32;
-        const uint16_t* g = static_cast<const uint16_t*>(grad);
-        if (cpl <= 1) k_reduce_pairsum<1><<<rblocks, 256, 0, s>>>(w.seg_begin, w.vals[cur], R, dim, n_heads, heads_per_ngram, g, grad_rows);
-        else if (cpl <= 2) k_reduce_pairsum<2><<<rblocks, 256, 0, s>>>(w.seg_begin, w.vals[cur], R, dim, n_heads, heads_per_ngram, g, grad_rows);
-        else k_reduce_pairsum<4><<<rblocks, 256, 0, s>>>(w.seg_begin, w.vals[cur], R, dim, n_heads, heads_per_ngram, g, grad_rows);
+        if (cpl <= 1) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 1>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else if (cpl <= 2) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 2>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 4>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
     }
-    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
-}
-
-extern "C" int engram_adam_step(float* p, const float* g, float* m, float* v, const float* p0, int64_t numel,
-                                int64_t step, double lr, double beta1, double beta2, double eps, float reg_scale,
-                                void* stream) {
-    if (numel < 0 || step < 1) return ENGRAM_ERR_ARG;
-    if (numel == 0) return ENGRAM_OK;
-    if (!p || !g || !m || !v) return ENGRAM_ERR_ARG;
-    AdamScalars a;
-    const double bc1 = 1.0 - pow(beta1, (double)step);
-    const double bc2 = 1.0 - pow(beta2, (double)step);
-    a.w1 = (float)(1.0 - beta1);
-    a.b2 = (float)beta2;
-    a.w2 = (float)(1.0 - beta2);
-    a.eps = (float)eps;
-    a.neg_step_size = -(float)(lr / bc1);
-    a.bc2_sqrt = (float)sqrt(bc2);
-    a.reg_scale = reg_scale;
-    cudaStream_t s = (cudaStream_t)stream;
-    const bool vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v) && (!p0 || aligned16(p0));
-    int64_t done = 0;
-    if (vec) {
-        const int64_t n4 = numel / 4;
-        if (n4 > 0)
-        {
-            k_adam_vec4<<<grid_for(n4, 256, 8), 256, 0, s>>>((float4*)p, (const float4*)g, (float4*)m, (float4*)v,
-                                                             (const float4*)p0, n4, a);
-            count_launches(1);
-        }
-        done = n4 * 4;
-    }
-    if (done < numel) {
-        k_adam_scalar<<<grid_for(numel - done, 256, 8), 256, 0, s>>>(p, g, m, v, p0, done, numel, a);
-        count_launches(1);
-    }
+    count_launches(3 * passes + 2);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
 

@@ -54,22 +54,36 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)bits16));
 }
 
+// The tokens one position's hash reads: x[s] = token at t-s (unread when t-s < 0)
+// and lo = the first index of t's segment.  Loaded ahead of the hash so the
+// loads of the next position overlap the current one's row reads.
+struct TokCtx {
+    int32_t x[ENGRAM_MAX_CTX];
+    int32_t lo;
+};
+
+__device__ __forceinline__ TokCtx load_ctx(const engram_table& T, const int32_t* __restrict__ tokens,
+                                           const int32_t* __restrict__ seg_start, int64_t t) {
+    TokCtx c;
+    c.lo = seg_start ? __ldg(seg_start + t) : 0;
+#pragma unroll
+    for (int s = 0; s < ENGRAM_MAX_CTX; s++) c.x[s] = (s < T.ngram_size && t - s >= 0) ? __ldg(tokens + t - s) : 0;
+    return c;
+}
+
 // Global row id of head `h` at position t (engraft/table.py:111-144 + engraft/lens.py:108-110).
 // ctx[0] = x_t; ctx[s] = x_{t-s}, or EOS once a predecessor is missing (before
-// `lo`, the start of t's segment) or is itself EOS; the current token never cuts.
-__device__ __forceinline__ int32_t hash_row(const engram_table& T, const int32_t* __restrict__ tokens, int64_t t,
-                                            int64_t lo, int h) {
+// lo, the start of t's segment) or is itself EOS; the current token never cuts.
+__device__ __forceinline__ int32_t hash_ctx(const engram_table& T, const TokCtx& c, int64_t t, int h) {
     const int N = T.ngram_size;
     int64_t ctx[ENGRAM_MAX_CTX];
-    ctx[0] = (int64_t)__ldg(tokens + t);
+    ctx[0] = (int64_t)c.x[0];
     bool cut = false;
 #pragma unroll
     for (int s = 1; s < ENGRAM_MAX_CTX; s++) {
         if (s < N) {
-            const int64_t pos = t - s;
-            int64_t tok = T.eos_token_id;
-            const bool have = (pos >= lo) && !cut;
-            if (have) tok = (int64_t)__ldg(tokens + pos);
+            const bool have = (t - s >= (int64_t)c.lo) && !cut;
+            int64_t tok = have ? (int64_t)c.x[s] : T.eos_token_id;
             if (!have || tok == T.eos_token_id) {
                 cut = true;
                 tok = T.eos_token_id;
@@ -84,6 +98,11 @@ __device__ __forceinline__ int32_t hash_row(const engram_table& T, const int32_t
         if (j < n) mixed ^= (uint64_t)ctx[j] * T.mult[j];
     const uint64_t local = mod_by_magic(mixed, T.head_size[h], T.head_magic[h], T.head_shift[h]);
     return (int32_t)(T.head_offset[h] + (int64_t)local);
+}
+
+__device__ __forceinline__ int32_t hash_row(const engram_table& T, const int32_t* __restrict__ tokens,
+                                            const int32_t* __restrict__ seg_start, int64_t t, int h) {
+    return hash_ctx(T, load_ctx(T, tokens, seg_start, t), t, h);
 }
 
 // Overlay map probe (open addressing, linear probing; built by

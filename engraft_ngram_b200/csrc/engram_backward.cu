@@ -9,12 +9,12 @@
 //      come out in ascending (t, h) order.  Ranks inside a tile come from warp
 //      __match_any_sync groups plus per-warp digit counts (no comparison sort);
 //      block offsets come from a per-digit row scan (256 blocks);
-//   2. segment starts per slot from the sorted keys; segments longer than
-//      kHeavy entries are listed for block-wide reduction;
-//   3. one reduce kernel, scheduled dynamically: each block first takes heavy
-//      segments (the longest chains), streaming their rows through a
-//      kStages-deep cp.async shared-memory pipeline while every thread adds its
-//      own columns in order; then warps take the remaining slots, one per warp.
+//   2. segment starts per slot from the sorted keys;
+//   3. one streaming segmented reduction: blocks take segment-aligned chunks
+//      of the sorted entries (dynamically), stage their row offsets in shared
+//      memory, stream the rows through a kStages-deep cp.async ring, and every
+//      thread adds its own columns in order, writing a slot's row when its
+//      segment ends.
 // Every term is added from +0 in ascending (t, h) order in fp32, so the result
 // is bit-identical to the reference and independent of scheduling.
 #include <algorithm>
@@ -32,14 +32,17 @@ constexpr int kRsWarps = kRsThreads / 32;
 constexpr int kRsItems = 16;
 constexpr int kRsTile = kRsThreads * kRsItems;
 constexpr int kScanThreads = 1024;
-constexpr int kHeavy = 64;            // segments with more entries are reduced by a whole block
 constexpr int kRedThreads = 256;
-constexpr int kStageBytes = 16384;    // rows staged per pipeline stage (>= 4 rows of <= 4 KB)
-constexpr int kStages = 6;
-constexpr int kRedSmem = kStages * kStageBytes;
+constexpr int kChunk = 256;           // nominal sorted entries per work chunk (snapped to segment starts)
+constexpr int kMetaCap = 4096;        // entries whose row offsets and keys a block stages at a time
+constexpr int kStageBytes = 16384;    // rows per pipeline stage (>= 4 rows of <= 4 KB)
+constexpr int kStages = 4;
+constexpr int kRedSmem = kStages * kStageBytes + kMetaCap * 4 + (kMetaCap + 1) * 4;
+
+constexpr int kBigChunk = 4 * kChunk;  // chunks longer than this (long segments) are scheduled first
 
 // counters[] in the workspace
-constexpr int kCntHits = 0, kCntHeavy = 1, kCntHeavyNext = 2, kCntLightNext = 3;
+constexpr int kCntHits = 0, kCntChunkNext = 1, kCntBig = 2, kCntBigNext = 3;
 
 inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
@@ -49,7 +52,8 @@ struct Workspace {
     uint32_t* block_hist;
     uint32_t* digit_tot;
     int32_t* seg_begin;
-    int32_t* heavy;
+    int32_t* chunk_lo;  // [max_chunks + 1] segment-aligned chunk bounds
+    int32_t* big;       // [max_chunks] ids of long chunks
     int32_t* counters;
     int64_t bytes;
     int nblk;
@@ -59,7 +63,6 @@ Workspace layout(void* base, int64_t N, int64_t R) {
     Workspace w{};
     const int64_t nblk = (N + kRsTile - 1) / kRsTile;
     w.nblk = (int)(nblk > 0 ? nblk : 1);
-    const int64_t max_heavy = std::min<int64_t>(R, N / (kHeavy + 1) + 1);
     char* p = static_cast<char*>(base);
     int64_t off = 0;
     auto take = [&](int64_t bytes) {
@@ -74,7 +77,9 @@ Workspace layout(void* base, int64_t N, int64_t R) {
     w.block_hist = reinterpret_cast<uint32_t*>(take(4 * 256 * (int64_t)w.nblk));
     w.digit_tot = reinterpret_cast<uint32_t*>(take(4 * 256));
     w.seg_begin = reinterpret_cast<int32_t*>(take(4 * (R + 1)));
-    w.heavy = reinterpret_cast<int32_t*>(take(4 * max_heavy));
+    const int64_t max_chunks = N / kChunk + 1;
+    w.chunk_lo = reinterpret_cast<int32_t*>(take(4 * (max_chunks + 1)));
+    w.big = reinterpret_cast<int32_t*>(take(4 * max_chunks));
     w.counters = reinterpret_cast<int32_t*>(take(64));
     w.bytes = off;
     return w;
@@ -116,20 +121,22 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_hist(const int32_t* __restric
     __shared__ uint32_t h[256];
     for (int d = threadIdx.x; d < 256; d += kRsThreads) h[d] = 0;
     if (counters && blockIdx.x == 0 && threadIdx.x == 0) {
-        counters[kCntHeavy] = 0;
-        counters[kCntHeavyNext] = 0;
-        counters[kCntLightNext] = 0;
+        counters[kCntChunkNext] = 0;
+        counters[kCntBig] = 0;
+        counters[kCntBigNext] = 0;
     }
     __syncthreads();
     const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
     const int64_t begin = (int64_t)blockIdx.x * kRsTile;
-    for (int k = threadIdx.x; k < kRsTile; k += kRsThreads) {
-        const int64_t i = begin + k;
-        if (i < n) {
-            const int32_t key = keys[i];
-            if (key >= 0) atomicAdd(&h[(key >> shift) & 255], 1u);
-        }
+    int32_t kr[kRsItems];
+#pragma unroll
+    for (int sub = 0; sub < kRsItems; sub++) {
+        const int64_t i = begin + (int64_t)sub * kRsThreads + threadIdx.x;
+        kr[sub] = i < n ? __ldg(keys + i) : -1;
     }
+#pragma unroll
+    for (int sub = 0; sub < kRsItems; sub++)
+        if (kr[sub] >= 0) atomicAdd(&h[(kr[sub] >> shift) & 255], 1u);
     __syncthreads();
     for (int d = threadIdx.x; d < 256; d += kRsThreads) block_hist[(int64_t)d * nblk + blockIdx.x] = h[d];
 }
@@ -152,6 +159,9 @@ __global__ void __launch_bounds__(kScanThreads) k_rs_rowscan(uint32_t* block_his
 
 // Stable scatter of one pass.  vals_in == nullptr: the value is the index.
 // total_out (nullable): receives the number of entries sorted (the hit count).
+// The tile's keys (and values) are loaded into registers up front, so the 16
+// sub-tiles cost one memory latency; per-warp digit counts alternate between
+// two shared buffers so each sub-tile needs two block barriers.
 __global__ void __launch_bounds__(kRsThreads) k_rs_scatter(const int32_t* __restrict__ keys_in,
                                                            const int32_t* __restrict__ vals_in, const int32_t* n_dev,
                                                            int64_t n_static, int shift,
@@ -159,56 +169,62 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_scatter(const int32_t* __rest
                                                            const uint32_t* __restrict__ digit_tot, int nblk,
                                                            int32_t* __restrict__ keys_out,
                                                            int32_t* __restrict__ vals_out, int32_t* total_out) {
-    __shared__ uint32_t wcnt[kRsWarps][256];
+    __shared__ uint32_t wcnt[2][kRsWarps][256];
     __shared__ uint32_t run[256];
     __shared__ uint32_t wsum[32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
+    const int64_t begin = (int64_t)blockIdx.x * kRsTile;
+    int32_t kr[kRsItems], vr[kRsItems];
+#pragma unroll
+    for (int sub = 0; sub < kRsItems; sub++) {
+        const int64_t i = begin + (int64_t)sub * kRsThreads + tid;
+        kr[sub] = i < n ? __ldg(keys_in + i) : -1;
+        vr[sub] = vals_in ? (i < n ? __ldg(vals_in + i) : 0) : (int32_t)i;
+    }
+    for (int k = tid; k < 2 * kRsWarps * 256; k += kRsThreads) (&wcnt[0][0][0])[k] = 0;
     {
         const uint32_t dt = digit_tot[tid];  // kRsThreads == 256 digits
         uint32_t tot;
-        const uint32_t base = block_exclusive_scan(dt, wsum, &tot);
+        const uint32_t base = block_exclusive_scan(dt, wsum, &tot);  // contains a barrier
         run[tid] = base + block_off[(int64_t)tid * nblk + blockIdx.x];
         if (total_out && blockIdx.x == 0 && tid == 0) *total_out = (int32_t)tot;
     }
-    const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
-    const int64_t begin = (int64_t)blockIdx.x * kRsTile;
     const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
     for (int sub = 0; sub < kRsItems; sub++) {
-        for (int k = tid; k < kRsWarps * 256; k += kRsThreads) (&wcnt[0][0])[k] = 0;
-        __syncthreads();
-        const int64_t i = begin + (int64_t)sub * kRsThreads + tid;
-        const int32_t key = (i < n) ? keys_in[i] : -1;
+        const int B = sub & 1;
+        const int32_t key = kr[sub];
         const bool valid = key >= 0;
         const int digit = valid ? ((key >> shift) & 255) : (256 + lane);
         const unsigned peers = __match_any_sync(kFull, digit);
         const int rank = __popc(peers & lt);
-        if (valid && rank == 0) wcnt[warp][digit] = (uint32_t)__popc(peers);
+        if (valid && rank == 0) wcnt[B][warp][digit] = (uint32_t)__popc(peers);
         __syncthreads();
         {
             const int d = tid;
             uint32_t acc = run[d];
 #pragma unroll
             for (int w = 0; w < kRsWarps; w++) {
-                const uint32_t c = wcnt[w][d];
-                wcnt[w][d] = acc;
+                const uint32_t c = wcnt[B][w][d];
+                wcnt[B][w][d] = acc;
+                wcnt[B ^ 1][w][d] = 0;  // ready for the next sub-tile
                 acc += c;
             }
             run[d] = acc;
         }
         __syncthreads();
         if (valid) {
-            const uint32_t pos = wcnt[warp][digit] + (uint32_t)rank;
+            const uint32_t pos = wcnt[B][warp][digit] + (uint32_t)rank;
             keys_out[pos] = key;
-            vals_out[pos] = vals_in ? vals_in[i] : (int32_t)i;
+            vals_out[pos] = vr[sub];
         }
-        __syncthreads();
     }
 }
 
-// seg_begin[s] = number of sorted entries with key < s, for s in [0, R]; segments
-// longer than kHeavy are appended to heavy[] (their order does not matter).
-__global__ void k_seg_begin(const int32_t* __restrict__ keys, int32_t* counters, int64_t R,
-                            int32_t* __restrict__ seg_begin, int32_t* __restrict__ heavy) {
+// seg_begin[s] = number of sorted entries with key < s, for s in [0, R].
+__global__ void k_seg_begin(const int32_t* __restrict__ keys, const int32_t* counters, int64_t R,
+                            int32_t* __restrict__ seg_begin) {
     const int64_t n = counters[kCntHits];
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -219,15 +235,7 @@ __global__ void k_seg_begin(const int32_t* __restrict__ keys, int32_t* counters,
     for (int64_t i = tid; i < n; i += stride) {
         const int32_t k = keys[i];
         const int32_t prev = i == 0 ? -1 : keys[i - 1];
-        if (k != prev) {
-            for (int64_t s = (int64_t)prev + 1; s <= k; s++) seg_begin[s] = (int32_t)i;
-            int64_t lo = i, hi = n;  // first index > i whose key differs (upper bound of k)
-            while (lo < hi) {
-                const int64_t mid = (lo + hi) >> 1;
-                if (keys[mid] <= k) lo = mid + 1; else hi = mid;
-            }
-            if (lo - i > kHeavy) heavy[atomicAdd(counters + kCntHeavy, 1)] = k;
-        }
+        for (int64_t s = (int64_t)prev + 1; s <= k; s++) seg_begin[s] = (int32_t)i;
         if (i == n - 1)
             for (int64_t s = (int64_t)k + 1; s <= R; s++) seg_begin[s] = (int32_t)n;
     }
@@ -241,189 +249,190 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// Address of the upstream-gradient row of flat entry i = t*n_heads + h.
+// Offset, in 16-byte units, of the upstream-gradient row of flat entry i = t*n_heads + h.
 template <int MODE>
-__device__ __forceinline__ const uint8_t* grad_row(const uint8_t* grad, int64_t i, int dim, int n_heads, int hpn) {
-    if (MODE == ENGRAM_MODE_CONCAT_F32) return grad + i * (int64_t)dim * 4;
+__device__ __forceinline__ uint32_t grad_row16(int64_t i, int dim, int n_heads, int hpn) {
+    if (MODE == ENGRAM_MODE_CONCAT_F32) return (uint32_t)((i * (int64_t)dim) >> 2);
     const int64_t t = i / n_heads;
     const int h = (int)(i - t * n_heads);
-    return grad + (t * hpn * dim + (int64_t)(h % hpn) * dim) * 2;
+    return (uint32_t)((t * hpn * dim + (int64_t)(h % hpn) * dim) >> 3);
 }
 
-// One heavy segment [b, e) of slot s, reduced by the whole block.
-template <int MODE>
-__device__ void reduce_heavy(int64_t s, int b, int e, const int32_t* __restrict__ vals, int dim, int n_heads, int hpn,
-                             const uint8_t* __restrict__ grad, float* __restrict__ grad_rows, uint8_t* smem) {
+// First segment start at or after sorted entry e (e in [0, n]).
+__device__ __forceinline__ int64_t snap_to_segment(const int32_t* __restrict__ keys,
+                                                   const int32_t* __restrict__ seg_begin, int64_t e, int64_t n) {
+    if (e <= 0) return 0;
+    if (e >= n) return n;
+    const int32_t k = __ldg(keys + e);
+    if (__ldg(keys + e - 1) != k) return e;
+    return __ldg(seg_begin + k + 1);
+}
+
+// chunk_lo[j] = first segment start at or after j*kChunk, j in [0, n_chunks];
+// chunks longer than kBigChunk are listed in big[] so they start first.
+__global__ void k_chunks(const int32_t* __restrict__ keys, const int32_t* __restrict__ seg_begin, int32_t* counters,
+                         int32_t* __restrict__ chunk_lo, int32_t* __restrict__ big) {
+    const int64_t n = counters[kCntHits];
+    const int64_t nchunks = (n + kChunk - 1) / kChunk;
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j <= nchunks; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t lo = snap_to_segment(keys, seg_begin, j * kChunk, n);
+        chunk_lo[j] = (int32_t)lo;
+        if (j < nchunks) {
+            const int64_t hi = snap_to_segment(keys, seg_begin, (j + 1) * kChunk, n);
+            if (hi - lo > kBigChunk) big[atomicAdd(counters + kCntBig, 1)] = (int32_t)j;
+        }
+    }
+}
+
+// Streaming segmented reduction over the slot-sorted entries.  Blocks take
+// chunks of ~kChunk entries whose bounds are snapped to segment starts (so a
+// segment never spans two blocks; a long segment makes one long chunk).  A
+// chunk's row offsets and keys are staged in shared memory, then its rows
+// stream through a kStages-deep cp.async ring while thread c adds column c of
+// every row in order and writes the slot's row when its segment ends.  Slots
+// without entries get zero rows.  NJ = columns per thread (dim <= 256*NJ).
+template <int MODE, int NJ>
+__global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restrict__ keys,
+                                                        const int32_t* __restrict__ vals,
+                                                        const int32_t* __restrict__ seg_begin,
+                                                        const int32_t* __restrict__ chunk_lo,
+                                                        const int32_t* __restrict__ big, int32_t* counters,
+                                                        int64_t R, int dim, int n_heads, int hpn,
+                                                        const uint8_t* __restrict__ grad,
+                                                        float* __restrict__ grad_rows) {
     constexpr int ES = MODE == ENGRAM_MODE_CONCAT_F32 ? 4 : 2;
-    const int row_bytes = dim * ES;
-    const int chunks = row_bytes >> 4;
-    const int rps = kStageBytes / row_bytes;  // rows per stage
-    const int n = e - b;
-    const int nst = (n + rps - 1) / rps;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t* m_off = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes);
+    int32_t* m_key = reinterpret_cast<int32_t*>(m_off + kMetaCap);
+    __shared__ int s_job;
     const int tid = threadIdx.x;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // columns tid + 256*j (dim <= 1024)
+    const int64_t n = counters[kCntHits];
+    const int64_t nchunks = (n + kChunk - 1) / kChunk;
+    const int row_bytes = dim * ES;
+    const int chunks16 = row_bytes >> 4;
+    const int rps = kStageBytes / row_bytes;  // rows per stage
+    const uint4* g16 = reinterpret_cast<const uint4*>(grad);
 
-    auto issue = [&](int st) {
-        if (st < nst) {
-            uint8_t* buf = smem + (st % kStages) * kStageBytes;
-            const int r0 = st * rps;
-            const int nr = min(rps, n - r0);
-            for (int c = tid; c < nr * chunks; c += kRedThreads) {
-                const int r = c / chunks, p = c - r * chunks;
-                const int64_t i = __ldg(vals + b + r0 + r);
-                cp_async16(buf + r * row_bytes + p * 16, grad_row<MODE>(grad, i, dim, n_heads, hpn) + p * 16);
+    const int n_big = counters[kCntBig];
+    while (true) {
+        // long chunks first (their sequential chains are the critical path), then the rest in order
+        if (tid == 0) {
+            int j = -1;
+            const int b = atomicAdd(counters + kCntBigNext, 1);
+            if (b < n_big) {
+                j = big[b];
+            } else {
+                while (true) {
+                    const int c = atomicAdd(counters + kCntChunkNext, 1);
+                    if (c >= nchunks) break;
+                    if (chunk_lo[c + 1] - chunk_lo[c] <= kBigChunk) { j = c; break; }
+                }
             }
+            s_job = j;
         }
-        cp_async_commit();
-    };
-#pragma unroll 1
-    for (int st = 0; st < kStages - 1; st++) issue(st);
-#pragma unroll 1
-    for (int st = 0; st < nst; st++) {
-        cp_async_wait<kStages - 2>();
         __syncthreads();
-        issue(st + kStages - 1);
-        const uint8_t* buf = smem + (st % kStages) * kStageBytes;
-        const int nr = min(rps, n - st * rps);
+        const int64_t j = s_job;
+        __syncthreads();
+        if (j < 0) break;
+        const int64_t lo = chunk_lo[j];
+        const int64_t hi = chunk_lo[j + 1];
+        float acc[NJ];
+#pragma unroll
+        for (int q = 0; q < NJ; q++) acc[q] = 0.f;
+        for (int64_t m0 = lo; m0 < hi; m0 += kMetaCap) {
+            const int mn = (int)(hi - m0 < kMetaCap ? hi - m0 : kMetaCap);
+            for (int e = tid; e <= mn; e += kRedThreads) {
+                if (e < mn) {
+                    m_off[e] = grad_row16<MODE>(__ldg(vals + m0 + e), dim, n_heads, hpn);
+                    m_key[e] = __ldg(keys + m0 + e);
+                } else {
+                    m_key[e] = (m0 + e < hi) ? __ldg(keys + m0 + e) : -1;  // key after the last staged entry
+                }
+            }
+            __syncthreads();
+            const int nst = (mn + rps - 1) / rps;
+            auto issue = [&](int st) {
+                if (st < nst) {
+                    uint8_t* buf = smem + (st % kStages) * kStageBytes;
+                    const int r0 = st * rps;
+                    const int nr = min(rps, mn - r0);
+                    for (int c = tid; c < nr * chunks16; c += kRedThreads) {
+                        const int r = c / chunks16, p = c - r * chunks16;
+                        cp_async16(buf + r * row_bytes + p * 16, g16 + m_off[r0 + r] + p);
+                    }
+                }
+                cp_async_commit();
+            };
 #pragma unroll 1
-        for (int r = 0; r < nr; r++) {
+            for (int st = 0; st < kStages - 1; st++) issue(st);
+#pragma unroll 1
+            for (int st = 0; st < nst; st++) {
+                cp_async_wait<kStages - 2>();
+                __syncthreads();
+                issue(st + kStages - 1);
+                const uint8_t* buf = smem + (st % kStages) * kStageBytes;
+                const int r0 = st * rps;
+                const int nr = min(rps, mn - r0);
+#pragma unroll 1
+                for (int r = 0; r < nr; r++) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int c = tid + kRedThreads * j;
-                if (c < dim) {
-                    float x;
-                    if (MODE == ENGRAM_MODE_CONCAT_F32)
-                        x = reinterpret_cast<const float*>(buf + r * row_bytes)[c];
-                    else
-                        x = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(buf + r * row_bytes)[c] << 16);
-                    acc[j] = __fadd_rn(acc[j], x);
-                }
-            }
-        }
-    }
-    cp_async_wait<0>();
-    __syncthreads();  // the next segment reuses the stage buffers
+                    for (int q = 0; q < NJ; q++) {
+                        const int c = tid + kRedThreads * q;
+                        if (c < dim) {
+                            float x;
+                            if (MODE == ENGRAM_MODE_CONCAT_F32)
+                                x = reinterpret_cast<const float*>(buf + r * row_bytes)[c];
+                            else
+                                x = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(buf + r * row_bytes)[c] << 16);
+                            acc[q] = __fadd_rn(acc[q], x);
+                        }
+                    }
+                    const int e = r0 + r;
+                    const int32_t key = m_key[e];
+                    if (m_key[e + 1] != key) {  // last entry of its segment
+                        float* dst = grad_rows + (int64_t)key * dim;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int c = tid + kRedThreads * j;
-        if (c < dim) grad_rows[s * dim + c] = acc[j];
-    }
-}
-
-// One light segment (<= kHeavy entries) of slot s, reduced by one warp.
-// CPL = 16-byte chunks of the row per lane; P rows are loaded before they are added.
-template <int MODE, int CPL>
-__device__ __forceinline__ void reduce_light(int64_t s, int b, int e, const int32_t* __restrict__ vals, int dim,
-                                             int n_heads, int hpn, const uint8_t* __restrict__ grad,
-                                             float* __restrict__ grad_rows, int lane) {
-    constexpr int P = (8 / CPL) > 0 ? 8 / CPL : 1;
-    constexpr int VPC = MODE == ENGRAM_MODE_CONCAT_F32 ? 4 : 8;  // values per 16-byte chunk
-    const int cpr = dim / VPC;
-    const int n = e - b;
-    const int32_t idx0 = lane < n ? __ldg(vals + b + lane) : 0;
-    const int32_t idx1 = lane + 32 < n ? __ldg(vals + b + 32 + lane) : 0;
-    float acc[CPL][VPC];
-#pragma unroll
-    for (int j = 0; j < CPL; j++)
-#pragma unroll
-        for (int q = 0; q < VPC; q++) acc[j][q] = 0.f;
-    for (int k0 = 0; k0 < n; k0 += P) {
-        uint4 x[P][CPL];
-#pragma unroll
-        for (int p = 0; p < P; p++) {
-            const int k = k0 + p;
-            const int32_t i = __shfl_sync(kFull, k < 32 ? idx0 : idx1, k & 31);
-            if (k < n) {
-                const uint4* src = reinterpret_cast<const uint4*>(grad_row<MODE>(grad, i, dim, n_heads, hpn));
-#pragma unroll
-                for (int j = 0; j < CPL; j++) {
-                    const int c = lane + 32 * j;
-                    if (c < cpr) x[p][j] = __ldg(src + c);
-                }
-            }
-        }
-#pragma unroll
-        for (int p = 0; p < P; p++) {
-            if (k0 + p < n) {
-#pragma unroll
-                for (int j = 0; j < CPL; j++) {
-                    const uint32_t w[4] = {x[p][j].x, x[p][j].y, x[p][j].z, x[p][j].w};
-                    if (MODE == ENGRAM_MODE_CONCAT_F32) {
-#pragma unroll
-                        for (int q = 0; q < 4; q++) acc[j][q] = __fadd_rn(acc[j][q], __uint_as_float(w[q]));
-                    } else {
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            acc[j][2 * q] = __fadd_rn(acc[j][2 * q], __uint_as_float(w[q] << 16));
-                            acc[j][2 * q + 1] = __fadd_rn(acc[j][2 * q + 1], __uint_as_float(w[q] & 0xffff0000u));
+                        for (int q = 0; q < NJ; q++) {
+                            const int c = tid + kRedThreads * q;
+                            if (c < dim) dst[c] = acc[q];
+                            acc[q] = 0.f;
                         }
                     }
                 }
             }
+            cp_async_wait<0>();
+            __syncthreads();  // stage buffers and metadata are reused next
         }
     }
-    float4* dst = reinterpret_cast<float4*>(grad_rows + s * (int64_t)dim);
-#pragma unroll
-    for (int j = 0; j < CPL; j++) {
-        const int c = lane + 32 * j;
-        if (c < cpr) {
-#pragma unroll
-            for (int q = 0; q < VPC; q += 4)
-                dst[c * (VPC / 4) + q / 4] = make_float4(acc[j][q], acc[j][q + 1], acc[j][q + 2], acc[j][q + 3]);
-        }
-    }
-}
-
-template <int MODE, int CPL>
-__global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restrict__ seg_begin,
-                                                        const int32_t* __restrict__ vals, int64_t R, int dim,
-                                                        int n_heads, int hpn, const uint8_t* __restrict__ grad,
-                                                        float* __restrict__ grad_rows,
-                                                        const int32_t* __restrict__ heavy, int32_t* counters) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ int s_job;
-    const int lane = threadIdx.x & 31;
-    const int n_heavy = counters[kCntHeavy];
-    // heavy segments first: the longest sequential chains start earliest
-    while (true) {
-        if (threadIdx.x == 0) s_job = atomicAdd(counters + kCntHeavyNext, 1);
-        __syncthreads();
-        const int j = s_job;
-        __syncthreads();
-        if (j >= n_heavy) break;
-        const int64_t s = heavy[j];
-        reduce_heavy<MODE>(s, __ldg(seg_begin + s), __ldg(seg_begin + s + 1), vals, dim, n_heads, hpn, grad,
-                           grad_rows, smem);
-    }
-    // then every other slot, eight at a time per warp
-    constexpr int kGrab = 8;
-    while (true) {
-        int64_t base = 0;
-        if (lane == 0) base = atomicAdd(counters + kCntLightNext, kGrab);
-        base = __shfl_sync(kFull, base, 0);
-        if (base >= R) break;
-        const int64_t end = base + kGrab < R ? base + kGrab : R;
-        for (int64_t s = base; s < end; s++) {
-            const int b = __ldg(seg_begin + s), e = __ldg(seg_begin + s + 1);
-            if (e - b <= kHeavy) reduce_light<MODE, CPL>(s, b, e, vals, dim, n_heads, hpn, grad, grad_rows, lane);
+    // slots without entries
+    const int lane = tid & 31;
+    const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + tid) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t s = warp0; s < R; s += nwarps) {
+        if (__ldg(seg_begin + s) == __ldg(seg_begin + s + 1)) {
+            float4* dst = reinterpret_cast<float4*>(grad_rows + s * dim);
+            for (int c = lane; c < (dim >> 2); c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
 }
 
-template <int MODE, int CPL>
-void launch_reduce(const Workspace& w, const int32_t* vals, int64_t R, int dim, int n_heads, int hpn,
-                   const void* grad, float* grad_rows, cudaStream_t s) {
+int grid_for_chunks(const Workspace& w);
+
+template <int MODE, int NJ>
+void launch_reduce(const Workspace& w, const int32_t* keys, const int32_t* vals, int64_t R, int dim, int n_heads,
+                   int hpn, const void* grad, float* grad_rows, cudaStream_t s) {
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaFuncSetAttribute(k_reduce<MODE, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRedSmem);
+        cudaFuncSetAttribute(k_reduce<MODE, NJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRedSmem);
         configured[dev] = true;
     }
     const int grid = sm_count() * 2;
-    k_reduce<MODE, CPL><<<grid, kRedThreads, kRedSmem, s>>>(w.seg_begin, vals, R, dim, n_heads, hpn,
-                                                           static_cast<const uint8_t*>(grad), grad_rows, w.heavy,
-                                                           w.counters);
+    k_chunks<<<grid_for_chunks(w), 256, 0, s>>>(keys, w.seg_begin, w.counters, w.chunk_lo, w.big);
+    k_reduce<MODE, NJ><<<grid, kRedThreads, kRedSmem, s>>>(keys, vals, w.seg_begin, w.chunk_lo, w.big, w.counters, R,
+                                                          dim, n_heads, hpn,
+                                                          static_cast<const uint8_t*>(grad), grad_rows);
 }
 
 int grid_for(int64_t work, int threads, int per_sm) {
@@ -432,6 +441,8 @@ int grid_for(int64_t work, int threads, int per_sm) {
     const int64_t g = want < cap ? want : cap;
     return (int)(g > 0 ? g : 1);
 }
+
+int grid_for_chunks(const Workspace& w) { return grid_for((int64_t)w.nblk * kRsTile / kChunk + 2, 256, 4); }
 
 }  // namespace
 
@@ -448,6 +459,9 @@ extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
     if (dim <= 0 || dim > 1024 || (mode == ENGRAM_MODE_CONCAT_F32 ? dim % 4 : dim % 8)) return ENGRAM_ERR_FORMAT;
     if (mode == ENGRAM_MODE_PAIRSUM_ADD_BF16 && n_heads != 2 * heads_per_ngram) return ENGRAM_ERR_FORMAT;
     if (R >= (1LL << 24) || n * n_heads >= (1LL << 31)) return ENGRAM_ERR_RANGE;
+    const int64_t grad_bytes = mode == ENGRAM_MODE_CONCAT_F32 ? n * n_heads * (int64_t)dim * 4
+                                                              : n * (int64_t)heads_per_ngram * dim * 2;
+    if ((grad_bytes >> 4) >= (1LL << 32)) return ENGRAM_ERR_RANGE;
     if (R == 0) return ENGRAM_OK;
     if (!grad_rows || !aligned16(grad_rows)) return ENGRAM_ERR_ARG;
     cudaStream_t s = (cudaStream_t)stream;
@@ -478,20 +492,18 @@ extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
                                                      pass == 0 ? w.counters + kCntHits : nullptr);
         cur = out;
     }
-    k_seg_begin<<<grid_for(N, 256, 8), 256, 0, s>>>(w.keys[cur], w.counters, R, w.seg_begin, w.heavy);
+    k_seg_begin<<<grid_for(N, 256, 8), 256, 0, s>>>(w.keys[cur], w.counters, R, w.seg_begin);
+    const int nj = (dim + kRedThreads - 1) / kRedThreads;
     if (mode == ENGRAM_MODE_CONCAT_F32) {
-        const int cpl = (dim / 4 + 31) / 32;
-        if (cpl <= 1) launch_reduce<ENGRAM_MODE_CONCAT_F32, 1>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else if (cpl <= 2) launch_reduce<ENGRAM_MODE_CONCAT_F32, 2>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else if (cpl <= 4) launch_reduce<ENGRAM_MODE_CONCAT_F32, 4>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else launch_reduce<ENGRAM_MODE_CONCAT_F32, 8>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        if (nj <= 1) launch_reduce<ENGRAM_MODE_CONCAT_F32, 1>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else if (nj <= 2) launch_reduce<ENGRAM_MODE_CONCAT_F32, 2>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else launch_reduce<ENGRAM_MODE_CONCAT_F32, 4>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
     } else {
-        const int cpl = (dim / 8 + 31) / 32;
-        if (cpl <= 1) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 1>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else if (cpl <= 2) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 2>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 4>(w, w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        if (nj <= 1) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 1>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else if (nj <= 2) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 2>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        else launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 4>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
     }
-    count_launches(3 * passes + 2);
+    count_launches(3 * passes + 3);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
 

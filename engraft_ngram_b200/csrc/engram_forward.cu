@@ -348,6 +348,167 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
     flush_hits(hits, hit_count, lane);
 }
 
+// ---- PAIRSUM_ADD for IQ4 tables: shared-memory staged, double-buffered warps ----
+//
+// Each warp owns two shared-memory buffers of one position each (the bf16
+// residual row + the 16 resident table rows).  While position i is computed
+// from one buffer, position i+nw's rows are already being copied into the
+// other by cp.async, so no register holds data in flight and the hash, probe
+// and DRAM latencies of one position hide behind the work of another.  The
+// table rows are fetched even for heads the overlay serves (so the copies do
+// not wait for the map probe); overlay rows are read from global memory (they
+// stay L2-resident) when consumed.  Lane q of a group row handles values
+// {32u+4m..+3} and {32u+16+4m..+3} (u = q/4, m = q%4): the low and high
+// nibbles of the same four code bytes, decoded together through a 256-entry
+// (kv[b&15], kv[b>>4]) table, with paired fp32 multiplies and adds.
+constexpr int kStagedWarps = 4;
+constexpr int kPairTableBytes = 256 * 8;
+
+__device__ __forceinline__ void cp_async16_f(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_f() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_f() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
+// 8 values (two runs of 4) of one row at lane chunk q: v[k] = (value at 32u+4m+k, value at 32u+16+4m+k).
+template <int FMT>
+__device__ __forceinline__ void row_pairs(const uint8_t* row_smem, const float* ov_row, int q, int dim,
+                                          const float2* pair_tab, float2* v) {
+    const int u = q >> 2, m = q & 3;
+    if (ov_row != nullptr) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(ov_row + 32 * u + 4 * m));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(ov_row + 32 * u + 16 + 4 * m));
+        v[0] = make_float2(a.x, b.x);
+        v[1] = make_float2(a.y, b.y);
+        v[2] = make_float2(a.z, b.z);
+        v[3] = make_float2(a.w, b.w);
+        return;
+    }
+    uint32_t qs;
+    float d;
+    if (FMT == ENGRAM_FMT_IQ4_XS) {
+        const uint8_t* sb = row_smem + (u >> 3) * 144;
+        const int ib = u & 7;
+        qs = *reinterpret_cast<const uint32_t*>(sb + ib * 16 + 4 * m);
+        const uint2 hdr = *reinterpret_cast<const uint2*>(sb + 128);
+        d = block_scale<ENGRAM_FMT_IQ4_XS>(hdr.x, hdr.y, ib);
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = __fmul2_rn(f2(d), pair_tab[(qs >> (8 * k)) & 0xffu]);
+    } else {
+        const int nb = dim >> 5;
+        qs = *reinterpret_cast<const uint32_t*>(row_smem + u * 16 + 4 * m);
+        d = half_bits_to_float(*reinterpret_cast<const unsigned short*>(row_smem + 16 * nb + 2 * u));
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = __fmul2_rn(pair_tab[(qs >> (8 * k)) & 0xffu], f2(d));
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
+    engram_table T, engram_overlay OV, const int32_t* __restrict__ tokens, const int32_t* __restrict__ seg_start,
+    int64_t t0, int64_t n, __nv_bfloat16* __restrict__ out, int32_t* ids_out, int32_t* slots_out,
+    unsigned long long* hit_count, int buf_bytes) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    float2* pair_tab = reinterpret_cast<float2*>(smem);
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) pair_tab[b] = make_float2(kKvIq4[b & 15], kKvIq4[b >> 4]);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* wbuf = smem + kPairTableBytes + warp * 2 * buf_bytes;
+    const int64_t nw = (int64_t)gridDim.x * kStagedWarps;
+    int64_t i = (int64_t)blockIdx.x * kStagedWarps + warp;
+    if (i >= n) return;  // no block-wide barrier follows
+    const int nh = T.n_heads, hpn = T.heads_per_ngram, dim = T.dim;
+    const int res_bytes = hpn * dim * 2;
+    const int pieces = (int)(T.row_stride >> 4);
+    const int row_pieces = nh * pieces;
+    const uint8_t* rows = static_cast<const uint8_t*>(T.rows);
+
+    auto issue = [&](int64_t pos, int32_t gid, int b) {
+        uint8_t* bb = wbuf + b * buf_bytes;
+        const uint4* src = reinterpret_cast<const uint4*>(out + pos * (int64_t)hpn * dim);
+        for (int c = lane; c < (res_bytes >> 4); c += 32) cp_async16_f(bb + c * 16, src + c);
+        for (int j0 = 0; j0 < row_pieces; j0 += 32) {
+            const int j = j0 + lane;
+            const int h = j / pieces;
+            const int p = j - h * pieces;
+            const int32_t g = __shfl_sync(kFull, gid, h < nh ? h : 0);
+            if (j < row_pieces)
+                cp_async16_f(bb + res_bytes + h * T.row_stride + p * 16, rows + (int64_t)g * T.row_stride + p * 16);
+        }
+        cp_async_commit_f();
+    };
+
+    TokCtx ctx = load_ctx(T, tokens, seg_start, t0 + i);
+    int32_t gid = lane < nh ? hash_ctx(T, ctx, t0 + i, lane) : 0;
+    issue(i, gid, 0);
+    int32_t slot = lane < nh ? overlay_slot(OV, gid) : -1;
+    int64_t inext = i + nw;
+    if (inext < n) ctx = load_ctx(T, tokens, seg_start, t0 + inext);
+    unsigned long long hits = 0;
+    int b = 0;
+    for (; i < n; i += nw, inext += nw) {
+        const bool has_next = inext < n;
+        int32_t gid_n = 0;
+        if (has_next) {
+            gid_n = lane < nh ? hash_ctx(T, ctx, t0 + inext, lane) : 0;
+            issue(inext, gid_n, b ^ 1);
+            if (inext + nw < n) ctx = load_ctx(T, tokens, seg_start, t0 + inext + nw);
+        } else {
+            cp_async_commit_f();  // one group per iteration keeps the wait count uniform
+        }
+        if (lane < nh) {
+            if (ids_out) ids_out[i * nh + lane] = gid;
+            if (slots_out) slots_out[i * nh + lane] = slot;
+        }
+        hits += (unsigned long long)__popc(__ballot_sync(kFull, lane < nh && slot >= 0));
+        cp_async_wait_f<1>();
+        __syncwarp();
+        const uint8_t* bb = wbuf + b * buf_bytes;
+        __nv_bfloat16* orow = out + i * (int64_t)hpn * dim;
+        for (int g = 0; g < hpn; g++) {
+            const int32_t sa = __shfl_sync(kFull, slot, g);
+            const int32_t sb = __shfl_sync(kFull, slot, hpn + g);
+            const uint8_t* ra = bb + res_bytes + g * T.row_stride;
+            const uint8_t* rb = bb + res_bytes + (hpn + g) * T.row_stride;
+            const float* oa = sa >= 0 ? OV.rows + (int64_t)sa * dim : nullptr;
+            const float* ob = sb >= 0 ? OV.rows + (int64_t)sb * dim : nullptr;
+            for (int q = lane; q < (dim >> 3); q += 32) {
+                float2 va[4], vb[4];
+                row_pairs<FMT>(ra, oa, q, dim, pair_tab, va);
+                row_pairs<FMT>(rb, ob, q, dim, pair_tab, vb);
+                const int v0 = g * dim + 32 * (q >> 2) + 4 * (q & 3);
+                const uint2 r0 = *reinterpret_cast<const uint2*>(bb + 2 * v0);
+                const uint2 r1 = *reinterpret_cast<const uint2*>(bb + 2 * (v0 + 16));
+                const uint32_t w0[2] = {r0.x, r0.y}, w1[2] = {r1.x, r1.y};
+                uint32_t o0[2], o1[2];
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    // values v0+2k, v0+2k+1 (low halves) and v0+16+2k, v0+16+2k+1 (high halves)
+                    const float2 s_lo = __fadd2_rn(va[2 * k], vb[2 * k]);          // (v0+2k, v0+16+2k)
+                    const float2 s_hi = __fadd2_rn(va[2 * k + 1], vb[2 * k + 1]);  // (v0+2k+1, v0+16+2k+1)
+                    const float2 x0 = __fadd2_rn(make_float2(bf16_lo(w0[k]), bf16_hi(w0[k])), make_float2(s_lo.x, s_hi.x));
+                    const float2 x1 = __fadd2_rn(make_float2(bf16_lo(w1[k]), bf16_hi(w1[k])), make_float2(s_lo.y, s_hi.y));
+                    o0[k] = pack_bf16x2(x0.x, x0.y);
+                    o1[k] = pack_bf16x2(x1.x, x1.y);
+                }
+                __stcs(reinterpret_cast<uint2*>(orow + v0), make_uint2(o0[0], o0[1]));
+                __stcs(reinterpret_cast<uint2*>(orow + v0 + 16), make_uint2(o1[0], o1[1]));
+            }
+        }
+        __syncwarp();  // buffer b is refilled next iteration
+        slot = -1;
+        if (has_next && lane < nh) slot = overlay_slot(OV, gid_n);
+        gid = gid_n;
+        b ^= 1;
+    }
+    cp_async_wait_f<0>();
+    flush_hits(hits, hit_count, lane);
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(256) k_gather_rows(engram_table T, const int32_t* __restrict__ ids, int64_t n,
                                                      float* __restrict__ out) {
@@ -371,6 +532,277 @@ __global__ void __launch_bounds__(256) k_gather_rows(engram_table T, const int32
     }
 }
 
+// ---- PAIRSUM_ADD specialised for the table geometries in use --------------------
+//
+// Same staging as k_forward_pairsum_staged, with the geometry fixed at compile
+// time (8 bigram + 8 trigram heads, FMT, DIM), so every index is a constant or
+// a shift, and with the position pipeline one step deeper: while position k is
+// computed from its buffer, position k+1's rows are in flight, position k+1's
+// first overlay-map probe is in flight, and position k+2's tokens are in
+// flight.  Codes are decoded through a 16-float shared table (conflict-free:
+// the 16 entries sit in 16 banks) and scaled with paired fp32 multiplies.
+constexpr int kXsWarps = 4;
+
+struct ProbeState {
+    uint32_t pos;   // current probe position
+    int32_t key;    // key loaded at pos
+    int32_t slot;   // slot loaded at pos
+};
+
+__device__ __forceinline__ ProbeState probe_start(const engram_overlay& OV, int32_t gid) {
+    ProbeState p{0u, -1, -1};
+    if (OV.n_rows == 0) return p;
+    p.pos = map_home(gid, OV.capacity);
+    p.key = __ldg(OV.map_keys + p.pos);
+    p.slot = __ldg(OV.map_slots + p.pos);
+    return p;
+}
+
+__device__ __forceinline__ int32_t probe_finish(const engram_overlay& OV, int32_t gid, ProbeState p) {
+    if (OV.n_rows == 0) return -1;
+    const uint32_t mask = (uint32_t)OV.capacity - 1u;
+    for (int64_t probe = 0; probe < OV.capacity; probe++) {
+        if (p.key == gid) return p.slot;
+        if (p.key == -1) return -1;
+        p.pos = (p.pos + 1u) & mask;
+        p.key = __ldg(OV.map_keys + p.pos);
+        p.slot = __ldg(OV.map_slots + p.pos);
+    }
+    return -1;
+}
+
+template <int FMT, int DIM>
+struct XsGeom {
+    static constexpr int HPN = 8, NH = 16;
+    static constexpr int ROW = FMT == ENGRAM_FMT_IQ4_XS ? 144 * (DIM / 256) : ((DIM / 32) * 18 + 15) / 16 * 16;
+    static constexpr int RES = HPN * DIM * 2;
+    static constexpr int BUF = RES + NH * ROW;
+    static constexpr int PIECES = ROW / 16;
+    static constexpr int NQ = (DIM / 8 + 31) / 32;  // 8-value lane chunks per row per lane
+};
+
+// Values of lane chunk q of one row: v[k] = (value 32u+4m+k, value 32u+16+4m+k), u = q/4, m = q%4.
+template <int FMT, int DIM>
+__device__ __forceinline__ void xs_row(const uint8_t* row, const float* ov_row, int q, const float* kv, float2* v) {
+    const int u = q >> 2, m = q & 3;
+    if (ov_row != nullptr) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(ov_row + 32 * u + 4 * m));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(ov_row + 32 * u + 16 + 4 * m));
+        v[0] = make_float2(a.x, b.x);
+        v[1] = make_float2(a.y, b.y);
+        v[2] = make_float2(a.z, b.z);
+        v[3] = make_float2(a.w, b.w);
+        return;
+    }
+    uint32_t qs;
+    float d;
+    if (FMT == ENGRAM_FMT_IQ4_XS) {
+        const uint8_t* sb = row + (u >> 3) * 144;
+        const int ib = u & 7;
+        qs = *reinterpret_cast<const uint32_t*>(sb + ib * 16 + 4 * m);
+        const uint2 hdr = *reinterpret_cast<const uint2*>(sb + 128);
+        d = block_scale<ENGRAM_FMT_IQ4_XS>(hdr.x, hdr.y, ib);
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            v[k] = __fmul2_rn(f2(d), make_float2(kv[(qs >> (8 * k)) & 15u], kv[(qs >> (8 * k + 4)) & 15u]));
+    } else {
+        qs = *reinterpret_cast<const uint32_t*>(row + u * 16 + 4 * m);
+        d = half_bits_to_float(*reinterpret_cast<const unsigned short*>(row + 16 * (DIM / 32) + 2 * u));
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            v[k] = __fmul2_rn(make_float2(kv[(qs >> (8 * k)) & 15u], kv[(qs >> (8 * k + 4)) & 15u]), f2(d));
+    }
+}
+
+template <int FMT, int DIM>
+__global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
+    engram_table T, engram_overlay OV, const int32_t* __restrict__ tokens, const int32_t* __restrict__ seg_start,
+    int64_t t0, int64_t n, __nv_bfloat16* __restrict__ out, int32_t* ids_out, int32_t* slots_out,
+    unsigned long long* hit_count) {
+    using G = XsGeom<FMT, DIM>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* kv = reinterpret_cast<float*>(smem);
+    if (threadIdx.x < 16) kv[threadIdx.x] = kKvIq4[threadIdx.x];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* wbuf = smem + 64 + warp * 2 * G::BUF;
+    const int64_t nw = (int64_t)gridDim.x * kXsWarps;
+    const int64_t first = (int64_t)blockIdx.x * kXsWarps + warp;
+    if (first >= n) return;  // no block-wide barrier follows
+    const uint8_t* rows = static_cast<const uint8_t*>(T.rows);
+    const bool head_lane = lane < G::NH;
+
+    auto issue = [&](int64_t pos, int32_t gid, int b) {
+        uint8_t* bb = wbuf + b * G::BUF;
+        const uint4* src = reinterpret_cast<const uint4*>(out + pos * (G::HPN * DIM));
+#pragma unroll
+        for (int c = 0; c < G::RES / 16 / 32; c++) cp_async16_f(bb + (c * 32 + lane) * 16, src + c * 32 + lane);
+#pragma unroll
+        for (int j0 = 0; j0 < G::NH * G::PIECES; j0 += 32) {
+            const int j = j0 + lane;
+            const int h = j / G::PIECES;
+            const int p = j - h * G::PIECES;
+            const int32_t g = __shfl_sync(kFull, gid, h < G::NH ? h : 0);
+            if (j < G::NH * G::PIECES)
+                cp_async16_f(bb + G::RES + h * G::ROW + p * 16, rows + (int64_t)g * G::ROW + p * 16);
+        }
+        cp_async_commit_f();
+    };
+
+    // pipeline state: position k (gid, slot), k+1 (gid, probe in flight), k+2 (tokens in flight)
+    int64_t i = first;
+    TokCtx c0 = load_ctx(T, tokens, seg_start, t0 + i);
+    int32_t gid = head_lane ? hash_ctx(T, c0, t0 + i, lane) : 0;
+    issue(i, gid, 0);
+    int32_t slot = head_lane ? probe_finish(OV, gid, probe_start(OV, gid)) : -1;
+    int64_t i1 = i + nw;
+    int32_t gid1 = 0;
+    ProbeState pr1{0u, -1, -1};
+    if (i1 < n) {
+        const TokCtx c1 = load_ctx(T, tokens, seg_start, t0 + i1);
+        gid1 = head_lane ? hash_ctx(T, c1, t0 + i1, lane) : 0;
+        if (head_lane) pr1 = probe_start(OV, gid1);
+    }
+    TokCtx c2{};
+    if (i1 + nw < n) c2 = load_ctx(T, tokens, seg_start, t0 + i1 + nw);
+    unsigned long long hits = 0;
+    int b = 0;
+    for (; i < n; i += nw) {
+        const int64_t inext = i + nw;
+        if (inext < n) issue(inext, gid1, b ^ 1);
+        else cp_async_commit_f();
+        if (head_lane) {
+            if (ids_out) ids_out[i * G::NH + lane] = gid;
+            if (slots_out) slots_out[i * G::NH + lane] = slot;
+        }
+        hits += (unsigned long long)__popc(__ballot_sync(kFull, head_lane && slot >= 0));
+        cp_async_wait_f<1>();
+        __syncwarp();
+        const uint8_t* bb = wbuf + b * G::BUF;
+        __nv_bfloat16* orow = out + i * (G::HPN * DIM);
+#pragma unroll
+        for (int g = 0; g < G::HPN; g++) {
+            const int32_t sa = __shfl_sync(kFull, slot, g);
+            const int32_t sb = __shfl_sync(kFull, slot, G::HPN + g);
+            const float* oa = sa >= 0 ? OV.rows + (int64_t)sa * DIM : nullptr;
+            const float* ob = sb >= 0 ? OV.rows + (int64_t)sb * DIM : nullptr;
+#pragma unroll
+            for (int jq = 0; jq < G::NQ; jq++) {
+                const int q = lane + 32 * jq;
+                if (q < DIM / 8) {
+                    float2 va[4], vb[4];
+                    xs_row<FMT, DIM>(bb + G::RES + g * G::ROW, oa, q, kv, va);
+                    xs_row<FMT, DIM>(bb + G::RES + (G::HPN + g) * G::ROW, ob, q, kv, vb);
+                    const int v0 = g * DIM + 32 * (q >> 2) + 4 * (q & 3);
+                    const uint2 r0 = *reinterpret_cast<const uint2*>(bb + 2 * v0);
+                    const uint2 r1 = *reinterpret_cast<const uint2*>(bb + 2 * (v0 + 16));
+                    const uint32_t w0[2] = {r0.x, r0.y}, w1[2] = {r1.x, r1.y};
+                    uint32_t o0[2], o1[2];
+#pragma unroll
+                    for (int k = 0; k < 2; k++) {
+                        const float2 s_lo = __fadd2_rn(va[2 * k], vb[2 * k]);
+                        const float2 s_hi = __fadd2_rn(va[2 * k + 1], vb[2 * k + 1]);
+                        const float2 x0 = __fadd2_rn(make_float2(bf16_lo(w0[k]), bf16_hi(w0[k])), make_float2(s_lo.x, s_hi.x));
+                        const float2 x1 = __fadd2_rn(make_float2(bf16_lo(w1[k]), bf16_hi(w1[k])), make_float2(s_lo.y, s_hi.y));
+                        o0[k] = pack_bf16x2(x0.x, x0.y);
+                        o1[k] = pack_bf16x2(x1.x, x1.y);
+                    }
+                    __stcs(reinterpret_cast<uint2*>(orow + v0), make_uint2(o0[0], o0[1]));
+                    __stcs(reinterpret_cast<uint2*>(orow + v0 + 16), make_uint2(o1[0], o1[1]));
+                }
+            }
+        }
+        __syncwarp();  // buffer b is refilled next iteration
+        // advance the pipeline: k+1's probe resolves, k+2 is hashed and probed, k+3's tokens load
+        gid = gid1;
+        slot = (inext < n && head_lane) ? probe_finish(OV, gid1, pr1) : -1;
+        const int64_t i2 = inext + nw;
+        if (i2 < n) {
+            gid1 = head_lane ? hash_ctx(T, c2, t0 + i2, lane) : 0;
+            if (head_lane) pr1 = probe_start(OV, gid1);
+            if (i2 + nw < n) c2 = load_ctx(T, tokens, seg_start, t0 + i2 + nw);
+        }
+        b ^= 1;
+    }
+    cp_async_wait_f<0>();
+    flush_hits(hits, hit_count, lane);
+}
+
+template <int FMT, int DIM>
+void launch_pairsum_fixed(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
+                          const int32_t* seg_start, int64_t t0, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
+                          int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
+    using G = XsGeom<FMT, DIM>;
+    const int smem = 64 + kXsWarps * 2 * G::BUF;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        cudaFuncSetAttribute(k_forward_pairsum_fixed<FMT, DIM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        configured[dev] = true;
+    }
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_forward_pairsum_fixed<FMT, DIM>, kXsWarps * 32, smem);
+    if (per_sm < 1) per_sm = 1;
+    const int64_t want = (n + kXsWarps - 1) / kXsWarps;
+    const int64_t cap = (int64_t)sm_count() * per_sm;
+    const int blocks = (int)(want < cap ? want : cap);
+    k_forward_pairsum_fixed<FMT, DIM><<<blocks, kXsWarps * 32, smem, s>>>(T, OV, tokens, seg_start, t0, n, out, ids_out,
+                                                                          slots_out, hit_count);
+}
+
+// Runs the compile-time specialisation for this table if there is one.
+template <int FMT>
+bool launch_pairsum_specialised(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
+                                const int32_t* seg_start, int64_t t0, int64_t n, __nv_bfloat16* out,
+                                int32_t* ids_out, int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
+    if (T.heads_per_ngram != 8 || T.n_heads != 16) return false;
+    if (FMT == ENGRAM_FMT_IQ4_XS && T.dim == 256) {
+        launch_pairsum_fixed<ENGRAM_FMT_IQ4_XS, 256>(T, OV, tokens, seg_start, t0, n, out, ids_out, slots_out, hit_count, s);
+        return true;
+    }
+    if (FMT == ENGRAM_FMT_IQ4_XS && T.dim == 512) {
+        launch_pairsum_fixed<ENGRAM_FMT_IQ4_XS, 512>(T, OV, tokens, seg_start, t0, n, out, ids_out, slots_out, hit_count, s);
+        return true;
+    }
+    if (FMT == ENGRAM_FMT_IQ4_NL && T.dim == 160) {
+        launch_pairsum_fixed<ENGRAM_FMT_IQ4_NL, 160>(T, OV, tokens, seg_start, t0, n, out, ids_out, slots_out, hit_count, s);
+        return true;
+    }
+    return false;
+}
+
+constexpr int kMaxStagedSmem = 200 * 1024;
+
+inline int staged_buf_bytes(const engram_table& T) {
+    return (int)(T.heads_per_ngram * T.dim * 2 + T.n_heads * T.row_stride);
+}
+inline int staged_smem_bytes(const engram_table& T) {
+    return kPairTableBytes + kStagedWarps * 2 * staged_buf_bytes(T);
+}
+
+template <int FMT>
+void launch_pairsum_staged(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
+                           const int32_t* seg_start, int64_t t0, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
+                           int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
+    const int smem = staged_smem_bytes(T);
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && configured[dev] < smem) {
+        cudaFuncSetAttribute(k_forward_pairsum_staged<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxStagedSmem);
+        configured[dev] = kMaxStagedSmem;
+    }
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_forward_pairsum_staged<FMT>, kStagedWarps * 32, smem);
+    if (per_sm < 1) per_sm = 1;
+    const int64_t want = (n + kStagedWarps - 1) / kStagedWarps;
+    const int64_t cap = (int64_t)sm_count() * per_sm;
+    const int blocks = (int)(want < cap ? want : cap);
+    k_forward_pairsum_staged<FMT><<<blocks, kStagedWarps * 32, smem, s>>>(T, OV, tokens, seg_start, t0, n, out, ids_out,
+                                                                          slots_out, hit_count, staged_buf_bytes(T));
+}
+
 template <int FMT>
 void launch_forward(const engram_table& T, const engram_overlay& OV, const int32_t* tokens, const int32_t* seg_start,
                     int64_t t0, int64_t n, int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
@@ -383,6 +815,11 @@ void launch_forward(const engram_table& T, const engram_overlay& OV, const int32
     if (mode == ENGRAM_MODE_CONCAT_F32)
         k_forward_concat<FMT, FMT == ENGRAM_FMT_F32 ? 16 : 8><<<blocks, threads, 0, s>>>(T, OV, tokens, seg_start, t0, n, (float*)out, ids_out,
                                                             slots_out, hit_count);
+    else if (FMT != ENGRAM_FMT_F32 && launch_pairsum_specialised<FMT>(T, OV, tokens, seg_start, t0, n, (__nv_bfloat16*)out,
+                                                                      ids_out, slots_out, hit_count, s)) {
+    } else if (FMT != ENGRAM_FMT_F32 && staged_smem_bytes(T) <= kMaxStagedSmem)
+        launch_pairsum_staged<FMT>(T, OV, tokens, seg_start, t0, n, (__nv_bfloat16*)out, ids_out, slots_out,
+                                   hit_count, s);
     else
         k_forward_pairsum<FMT, 4><<<blocks, threads, 0, s>>>(T, OV, tokens, seg_start, t0, n, (__nv_bfloat16*)out,
                                                              ids_out, slots_out, hit_count);

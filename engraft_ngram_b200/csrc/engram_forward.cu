@@ -581,36 +581,43 @@ struct XsGeom {
     static constexpr int NQ = (DIM / 8 + 31) / 32;  // 8-value lane chunks per row per lane
 };
 
-// Values of lane chunk q of one row: v[k] = (value 32u+4m+k, value 32u+16+4m+k), u = q/4, m = q%4.
+// Values [8q, 8q+8) of one row as four float pairs (v[k] = values 8q+2k, 8q+2k+1).
 template <int FMT, int DIM>
 __device__ __forceinline__ void xs_row(const uint8_t* row, const float* ov_row, int q, const float* kv, float2* v) {
-    const int u = q >> 2, m = q & 3;
     if (ov_row != nullptr) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(ov_row + 32 * u + 4 * m));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(ov_row + 32 * u + 16 + 4 * m));
-        v[0] = make_float2(a.x, b.x);
-        v[1] = make_float2(a.y, b.y);
-        v[2] = make_float2(a.z, b.z);
-        v[3] = make_float2(a.w, b.w);
+        const float4 a = __ldg(reinterpret_cast<const float4*>(ov_row + 8 * q));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(ov_row + 8 * q) + 1);
+        v[0] = make_float2(a.x, a.y);
+        v[1] = make_float2(a.z, a.w);
+        v[2] = make_float2(b.x, b.y);
+        v[3] = make_float2(b.z, b.w);
         return;
     }
-    uint32_t qs;
+    const int u = q >> 2, k = q & 3;  // 32-value sub-block u; k selects bytes (k&1)*8.. and the nibble half k>>1
+    const int sh = (k >> 1) * 4;
+    uint2 qs;
     float d;
     if (FMT == ENGRAM_FMT_IQ4_XS) {
         const uint8_t* sb = row + (u >> 3) * 144;
         const int ib = u & 7;
-        qs = *reinterpret_cast<const uint32_t*>(sb + ib * 16 + 4 * m);
+        qs = *reinterpret_cast<const uint2*>(sb + ib * 16 + (k & 1) * 8);
         const uint2 hdr = *reinterpret_cast<const uint2*>(sb + 128);
         d = block_scale<ENGRAM_FMT_IQ4_XS>(hdr.x, hdr.y, ib);
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            v[k] = __fmul2_rn(f2(d), make_float2(kv[(qs >> (8 * k)) & 15u], kv[(qs >> (8 * k + 4)) & 15u]));
+        for (int j = 0; j < 2; j++)
+            v[j] = __fmul2_rn(f2(d), make_float2(kv[(qs.x >> (16 * j + sh)) & 15u], kv[(qs.x >> (16 * j + 8 + sh)) & 15u]));
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+            v[2 + j] = __fmul2_rn(f2(d), make_float2(kv[(qs.y >> (16 * j + sh)) & 15u], kv[(qs.y >> (16 * j + 8 + sh)) & 15u]));
     } else {
-        qs = *reinterpret_cast<const uint32_t*>(row + u * 16 + 4 * m);
+        qs = *reinterpret_cast<const uint2*>(row + u * 16 + (k & 1) * 8);
         d = half_bits_to_float(*reinterpret_cast<const unsigned short*>(row + 16 * (DIM / 32) + 2 * u));
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            v[k] = __fmul2_rn(make_float2(kv[(qs >> (8 * k)) & 15u], kv[(qs >> (8 * k + 4)) & 15u]), f2(d));
+        for (int j = 0; j < 2; j++)
+            v[j] = __fmul2_rn(make_float2(kv[(qs.x >> (16 * j + sh)) & 15u], kv[(qs.x >> (16 * j + 8 + sh)) & 15u]), f2(d));
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+            v[2 + j] = __fmul2_rn(make_float2(kv[(qs.y >> (16 * j + sh)) & 15u], kv[(qs.y >> (16 * j + 8 + sh)) & 15u]), f2(d));
     }
 }
 
@@ -693,22 +700,16 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
                     float2 va[4], vb[4];
                     xs_row<FMT, DIM>(bb + G::RES + g * G::ROW, oa, q, kv, va);
                     xs_row<FMT, DIM>(bb + G::RES + (G::HPN + g) * G::ROW, ob, q, kv, vb);
-                    const int v0 = g * DIM + 32 * (q >> 2) + 4 * (q & 3);
-                    const uint2 r0 = *reinterpret_cast<const uint2*>(bb + 2 * v0);
-                    const uint2 r1 = *reinterpret_cast<const uint2*>(bb + 2 * (v0 + 16));
-                    const uint32_t w0[2] = {r0.x, r0.y}, w1[2] = {r1.x, r1.y};
-                    uint32_t o0[2], o1[2];
+                    const int v0 = g * DIM + 8 * q;
+                    const uint4 r = *reinterpret_cast<const uint4*>(bb + 2 * v0);
+                    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+                    uint32_t o[4];
 #pragma unroll
-                    for (int k = 0; k < 2; k++) {
-                        const float2 s_lo = __fadd2_rn(va[2 * k], vb[2 * k]);
-                        const float2 s_hi = __fadd2_rn(va[2 * k + 1], vb[2 * k + 1]);
-                        const float2 x0 = __fadd2_rn(make_float2(bf16_lo(w0[k]), bf16_hi(w0[k])), make_float2(s_lo.x, s_hi.x));
-                        const float2 x1 = __fadd2_rn(make_float2(bf16_lo(w1[k]), bf16_hi(w1[k])), make_float2(s_lo.y, s_hi.y));
-                        o0[k] = pack_bf16x2(x0.x, x0.y);
-                        o1[k] = pack_bf16x2(x1.x, x1.y);
+                    for (int k = 0; k < 4; k++) {
+                        const float2 x = __fadd2_rn(make_float2(bf16_lo(w[k]), bf16_hi(w[k])), __fadd2_rn(va[k], vb[k]));
+                        o[k] = pack_bf16x2(x.x, x.y);
                     }
-                    __stcs(reinterpret_cast<uint2*>(orow + v0), make_uint2(o0[0], o0[1]));
-                    __stcs(reinterpret_cast<uint2*>(orow + v0 + 16), make_uint2(o1[0], o1[1]));
+                    __stcs(reinterpret_cast<uint4*>(orow + v0), make_uint4(o[0], o[1], o[2], o[3]));
                 }
             }
         }

@@ -155,7 +155,9 @@ class Workload:
         lib = L.load()
         self.ws_bytes = int(lib.engram_backward_workspace_bytes(self.T, nh, max(self.R, 1)))
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
-        Rs = self.R // world if self.R else 0
+        from engraft_ngram_b200.dist import shard_bounds
+        lo, hi = shard_bounds(self.R, world, rank)
+        Rs = hi - lo
         self.Rs = Rs
         self.m = torch.zeros(max(Rs, 1), self.dim, device=device)
         self.v = torch.zeros(max(Rs, 1), self.dim, device=device)
@@ -166,8 +168,6 @@ class Workload:
         self.step_count = 0
         self.stream = torch.cuda.current_stream(device).cuda_stream
         self.ov_desc = self.omap.descriptor(self.rows_var) if self.R else L.EngramOverlay(None, 0, None, None, 0)
-        if self.R and self.R % world:
-            raise SystemExit(f"R={self.R} must divide by the world size {world}")
 
     # one step through the C ABI (device-resident inputs)
     def forward(self, hit_count=None):
@@ -185,18 +185,20 @@ class Workload:
         self.L.check(st, "engram_backward")
 
     def optimizer(self, dist=None):
+        """Adam (+ regulariser) on this rank's rows; with N ranks the row gradients
+        are reduce-scattered first and the updated rows all-gathered after
+        (engraft_ngram_b200.dist)."""
+        from engraft_ngram_b200.dist import all_gather_rows, reduce_scatter_rows, shard_bounds
         self.step_count += 1
-        lo = self.rank * self.Rs
-        p = self.rows_var[lo:lo + self.Rs]
-        g = self.grad_rows[lo:lo + self.Rs] if dist is None else self.g_shard
-        if dist is not None:
-            dist.reduce_scatter_tensor(self.g_shard, self.grad_rows)
+        lo, hi = shard_bounds(self.R, self.world, self.rank)
+        p = self.rows_var[lo:hi]
+        g = self.grad_rows[lo:hi] if dist is None else reduce_scatter_rows(self.grad_rows)
         st = self.L.load().engram_adam_step(p.data_ptr(), g.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
-                                            self.p0[lo:lo + self.Rs].data_ptr(), p.numel(), self.step_count, self.lr,
+                                            self.p0[lo:hi].data_ptr(), p.numel(), self.step_count, self.lr,
                                             0.9, 0.999, 1e-8, self.reg_scale, self.stream)
         self.L.check(st, "engram_adam_step")
         if dist is not None:
-            dist.all_gather_into_tensor(self.rows_var, p)
+            all_gather_rows(self.rows_var, p)
 
     def step(self, dist=None):
         self.forward()
@@ -441,8 +443,6 @@ def main():
     wl = Workload(cfg, rank, world, args.seed, device)
     lib = wl.L.load()
     ddist = dist if world > 1 else None
-    if ddist is not None:
-        wl.g_shard = torch.empty(max(wl.Rs, 1), wl.dim, device=device)
     nbytes = wl.algorithmic_bytes()
     step_bytes = nbytes["fwd"] + nbytes["bwd"] + nbytes["adam"]
 

@@ -1,0 +1,76 @@
+"""Multi-GPU plumbing for the overlay update: one process per GPU, data-parallel
+over the token batch, the resident table replicated on every rank.
+
+The path's only exchange step is the overlay gradient.  Every rank computes
+row gradients for all R overlay rows from its own batch; the rows are then
+sharded by contiguous blocks (rank r owns rows [r*R/W, (r+1)*R/W)):
+  1. reduce-scatter of grad_rows [R, D] -> each owner's summed shard;
+  2. the owner runs the fused Adam step (with the regulariser) on its shard;
+  3. all-gather of the updated shards -> every rank's rows_var for the next
+     forward.
+Collectives go through torch.distributed (NCCL between GPUs, gloo on CPU for
+tests).  The reference has no multi-GPU code; W=1 is bit-identical to the
+single-process step, W>1 sums the per-rank gradients in rank order.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(R: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [lo, hi) of the overlay owned by `rank` (contiguous, near-equal)."""
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad rank {rank} of {world}")
+    base, extra = divmod(R, world)
+    lo = rank * base + min(rank, extra)
+    hi = lo + base + (1 if rank < extra else 0)
+    return lo, hi
+
+
+def _equal_shards(R: int, world: int) -> bool:
+    return R % world == 0
+
+
+def reduce_scatter_rows(grad_rows: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of grad_rows over ranks, restricted to this rank's shard."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    R = grad_rows.shape[0]
+    lo, hi = shard_bounds(R, world, rank)
+    if world == 1:
+        return grad_rows[lo:hi]
+    if _equal_shards(R, world) and dist.get_backend(group) == "nccl":
+        out = torch.empty_like(grad_rows[lo:hi])
+        dist.reduce_scatter_tensor(out, grad_rows.contiguous(), group=group)
+        return out
+    full = grad_rows.clone()
+    dist.all_reduce(full, group=group)  # backends without reduce-scatter (gloo), or ragged shards
+    return full[lo:hi]
+
+
+def all_gather_rows(rows_var: torch.Tensor, shard: torch.Tensor, group=None) -> None:
+    """rows_var[all] <- the owners' shards (in place)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    R = rows_var.shape[0]
+    if world == 1:
+        lo, hi = shard_bounds(R, 1, 0)
+        if shard.data_ptr() != rows_var[lo:hi].data_ptr():
+            rows_var[lo:hi].copy_(shard)
+        return
+    if _equal_shards(R, world) and dist.get_backend(group) == "nccl":
+        lo, hi = shard_bounds(R, world, rank)
+        if shard.data_ptr() != rows_var[lo:hi].data_ptr():
+            rows_var[lo:hi].copy_(shard)
+        dist.all_gather_into_tensor(rows_var, rows_var[lo:hi], group=group)
+        return
+    # ragged shards or a backend without all_gather_into_tensor: pad every shard to the largest
+    spans = [shard_bounds(R, world, r) for r in range(world)]
+    width = max(hi - lo for lo, hi in spans)
+    padded = torch.zeros((width,) + tuple(rows_var.shape[1:]), dtype=rows_var.dtype, device=rows_var.device)
+    padded[: shard.shape[0]].copy_(shard)
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded, group=group)
+    for (lo, hi), part in zip(spans, parts):
+        rows_var[lo:hi].copy_(part[: hi - lo])

@@ -45,6 +45,9 @@ CONFIGS = {
     "cfg2": dict(rows=FULL_ROWS, fmt="iq4_xs", dim=256, seqs=1, seq_len=2048, R=40_000, mode="pairsum", bwd=False),
     "cfg3": dict(rows=1 << 20, fmt="f32", dim=128, seqs=1, seq_len=2048, R=40_000, mode="concat", bwd=True),
     "cfg1": dict(rows=1 << 20, fmt="f32", dim=128, seqs=1, seq_len=2048, R=0, mode="concat", bwd=False),
+    # decode-style: 256 sequences, 3 uniform history tokens + 1 new token; rows of the new tokens only
+    "cfg4": dict(rows=1 << 20, fmt="f32", dim=128, seqs=256, seq_len=4, R=40_000, mode="concat", bwd=False,
+                 decode=True),
 }
 
 
@@ -112,6 +115,7 @@ class Workload:
         mult = synthetic_multipliers(seed)
         rows = synthetic_resident(cfg["rows"], fmt, self.dim, seed, device)
         self.table = eb.DeviceTable(rows, fmt, self.dim, sizes, offs, mult, EOS, n_rows=cfg["rows"])
+        self.decode = bool(cfg.get("decode"))
         self.T = cfg["seqs"] * cfg["seq_len"]
         cdf = zipf_cdf(torch, device)
         # the census batch (rank 0's) fixes the overlay rows identically on every rank
@@ -122,9 +126,18 @@ class Workload:
         gen.manual_seed(seed * 1000 + 17 + rank)
         self.tokens = census if rank == 0 else zipf_tokens(torch, self.T, gen, cdf)
         self.seg_start = (torch.arange(self.T, device=device, dtype=torch.int32) // cfg["seq_len"]) * cfg["seq_len"]
+        self.positions = None
+        if self.decode:  # uniform histories; output rows are the sequences' last tokens
+            census = torch.randint(0, VOCAB, (self.T,), generator=gen0, device=device, dtype=torch.int32)
+            self.tokens = census if rank == 0 else torch.randint(0, VOCAB, (self.T,), generator=gen, device=device,
+                                                                 dtype=torch.int32)
+            self.positions = torch.arange(cfg["seqs"], device=device, dtype=torch.int64) * cfg["seq_len"] + cfg["seq_len"] - 1
         R = cfg["R"]
         if R:
-            ids = self.table.global_ids(census, self.seg_start).reshape(-1).to(torch.int64)
+            ids = self.table.global_ids(census, self.seg_start)
+            if self.decode:
+                ids = ids[self.positions]
+            ids = ids.reshape(-1).to(torch.int64)
             uniq, cnt = torch.unique(ids, return_counts=True)
             order = torch.argsort(cnt, descending=True, stable=True)  # ties -> smaller id first
             top = uniq[order[:R]]
@@ -144,13 +157,14 @@ class Workload:
         self.nh, self.hpn = nh, hpn
         gg = torch.Generator(device=device)
         gg.manual_seed(seed * 1000 + 99 + rank)
+        self.n_out = self.positions.numel() if self.decode else self.T
         if self.mode == L.MODE_PAIRSUM_ADD_BF16:
             self.out = (torch.randn(self.T, hpn * self.dim, generator=gg, device=device) * 0.5).to(torch.bfloat16)
             self.dout = (torch.randn(self.T, hpn * self.dim, generator=gg, device=device) * 1e-3).to(torch.bfloat16)
         else:
-            self.out = torch.empty(self.T, nh, self.dim, device=device)
-            self.dout = torch.randn(self.T, nh, self.dim, generator=gg, device=device) * 1e-3
-        self.slots = torch.empty(self.T, nh, dtype=torch.int32, device=device)
+            self.out = torch.empty(self.n_out, nh, self.dim, device=device)
+            self.dout = torch.randn(self.n_out, nh, self.dim, generator=gg, device=device) * 1e-3
+        self.slots = torch.empty(self.n_out, nh, dtype=torch.int32, device=device)
         self.hits = torch.zeros(1, dtype=torch.int64, device=device)
         lib = L.load()
         self.ws_bytes = int(lib.engram_backward_workspace_bytes(self.T, nh, max(self.R, 1)))
@@ -172,6 +186,14 @@ class Workload:
     # one step through the C ABI (device-resident inputs)
     def forward(self, hit_count=None):
         import ctypes as C
+        if self.decode:
+            st = self.L.load().engram_forward_at(C.byref(self.table.ctable), C.byref(self.ov_desc),
+                                                 self.tokens.data_ptr(), self.T, self.seg_start.data_ptr(),
+                                                 self.positions.data_ptr(), self.n_out, self.mode, self.out.data_ptr(),
+                                                 None, self.slots.data_ptr() if self.R else None,
+                                                 None if hit_count is None else hit_count.data_ptr(), self.stream)
+            self.L.check(st, "engram_forward_at")
+            return
         st = self.L.load().engram_forward(C.byref(self.table.ctable), C.byref(self.ov_desc), self.tokens.data_ptr(),
                                           self.seg_start.data_ptr(), 0, self.T, self.mode, self.out.data_ptr(), None,
                                           self.slots.data_ptr() if self.R else None,
@@ -210,7 +232,7 @@ class Workload:
     def algorithmic_bytes(self):
         """Bytes the math must move once per step (formulas in DESIGN.md)."""
         import torch
-        T, nh, hpn, dim = self.T, self.nh, self.hpn, self.dim
+        T, nh, hpn, dim = self.n_out, self.nh, self.hpn, self.dim
         raw_row = {self.L.FMT_F32: dim * 4, self.L.FMT_IQ4_NL: dim // 32 * 18, self.L.FMT_IQ4_XS: dim // 256 * 136}[self.fmt]
         self.hits.zero_()
         self.forward(self.hits)
@@ -477,10 +499,10 @@ def main():
     if ddist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, fwd_ms = float(t[0]), float(t[1])
-    value = 16 * wl.T * world / (ms * 1e-3)
+    value = 16 * wl.n_out * world / (ms * 1e-3)
 
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and not wl.decode:
         e2e = run_e2e(wl, args, device, ddist, world)
 
     if rank == 0:
@@ -495,8 +517,9 @@ def main():
             "gbps": step_bytes * world / (ms * 1e-3) / 1e9,
             "algorithmic_bytes_per_step_per_gpu": step_bytes,
             "bytes_breakdown": nbytes,
-            "hit_fraction": nbytes["hits"] / (16 * wl.T),
-            "roofline": {"kernel": "engram_forward (k_forward_pairsum<IQ4_XS>)" if wl.mode else "engram_forward (k_forward_concat)",
+            "hit_fraction": nbytes["hits"] / (16 * wl.n_out),
+            "us_per_step": ms * 1e3,
+            "roofline": {"kernel": "engram_forward (k_forward_pairsum_fixed<IQ4_XS,256>)" if wl.mode else "engram_forward (k_forward_concat)",
                          "bound": "hbm", "achieved": fwd_gbs, "peak": peak, "unit": "GB/s", "frac": fwd_gbs / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s",
                          "traffic": traffic, "traffic_source": tfile, "algorithmic_bytes_per_launch": nbytes["fwd"],

@@ -16,14 +16,14 @@ from __future__ import annotations
 from . import _lib
 from ._lib import FMT_F32, FMT_IQ4_NL, FMT_IQ4_XS, MODE_CONCAT_F32, MODE_PAIRSUM_ADD_BF16
 from .optim import OverlayAdam, reg_scale
-from .overlay import (OverlayEmb, OverlayMap, engram_embed, engram_residual_add, row_gradients,
+from .overlay import (OverlayEmb, OverlayMap, engram_embed, engram_embed_at, engram_residual_add, row_gradients,
                       seg_starts_from_segment_ids)
 from .patch import install, uninstall
 from .pleo import read_pleo, read_pleo_device, write_pleo
 from .table import DeviceTable
 
 __all__ = [
-    "DeviceTable", "OverlayEmb", "OverlayMap", "OverlayAdam", "engram_embed", "engram_residual_add",
+    "DeviceTable", "OverlayEmb", "OverlayMap", "OverlayAdam", "engram_embed", "engram_embed_at", "engram_residual_add",
     "row_gradients", "seg_starts_from_segment_ids", "reg_scale", "install", "uninstall", "read_pleo",
     "write_pleo", "read_pleo_device", "FMT_F32", "FMT_IQ4_NL", "FMT_IQ4_XS", "MODE_CONCAT_F32",
     "MODE_PAIRSUM_ADD_BF16", "load_library",

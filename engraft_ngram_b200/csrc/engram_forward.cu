@@ -21,6 +21,19 @@ struct PosHeads {
     int32_t slot;  // overlay slot or -1
 };
 
+// Output row i -> token position: pm.at(i), or pos[i] for an explicit position
+// list (decode-style calls), clamped into [0, n_tokens).
+struct PosMap {
+    int64_t t0;
+    const int64_t* pos;
+    int64_t n_tokens;
+    __device__ __forceinline__ int64_t at(int64_t i) const {
+        if (pos == nullptr) return t0 + i;
+        const int64_t p = __ldg(pos + i);
+        return p < 0 ? 0 : (p >= n_tokens ? n_tokens - 1 : p);
+    }
+};
+
 __device__ __forceinline__ PosHeads heads_of(const engram_table& T, const engram_overlay& OV, const TokCtx& c,
                                              int64_t t, int lane) {
     PosHeads r{0, -1};
@@ -46,14 +59,14 @@ __device__ __forceinline__ void flush_hits(unsigned long long hits, unsigned lon
 }
 
 __global__ void __launch_bounds__(256) k_hash(engram_table T, const int32_t* __restrict__ tokens,
-                                              const int32_t* __restrict__ seg_start, int64_t t0, int64_t n,
+                                              const int32_t* __restrict__ seg_start, PosMap pm, int64_t n,
                                               int32_t* __restrict__ ids_out) {
     const int nh = T.n_heads;
     const int64_t total = n * nh;
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = k / nh;
         const int h = (int)(k - i * nh);
-        ids_out[k] = hash_row(T, tokens, seg_start, t0 + i, h);
+        ids_out[k] = hash_row(T, tokens, seg_start, pm.at(i), h);
     }
 }
 
@@ -159,7 +172,7 @@ __device__ __forceinline__ void ld_f8(const float* __restrict__ src, float* v) {
 template <int FMT, int U>
 __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engram_overlay OV,
                                                            const int32_t* __restrict__ tokens,
-                                                           const int32_t* __restrict__ seg_start, int64_t t0,
+                                                           const int32_t* __restrict__ seg_start, PosMap pm,
                                                            int64_t n, float* __restrict__ out, int32_t* ids_out,
                                                            int32_t* slots_out, unsigned long long* hit_count) {
     __shared__ float s_kv[16];
@@ -175,12 +188,12 @@ __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engra
     const float* ovr = OV.rows;
     unsigned long long hits = 0;
     TokCtx nxt{};
-    if (warp0 < n) nxt = load_ctx(T, tokens, seg_start, t0 + warp0);
+    if (warp0 < n) nxt = load_ctx(T, tokens, seg_start, pm.at(warp0));
     for (int64_t i = warp0; i < n; i += nwarps) {
         const TokCtx cur = nxt;
-        const PosHeads ph = heads_of(T, OV, cur, t0 + i, lane);
+        const PosHeads ph = heads_of(T, OV, cur, pm.at(i), lane);
         write_heads(ph, i, nh, lane, ids_out, slots_out, hits);
-        if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, t0 + i + nwarps);
+        if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, pm.at(i + nwarps));
         float4* dst = reinterpret_cast<float4*>(out + i * (int64_t)nh * dim);
         for (int base = 0; base < cpp; base += 32 * U) {
             float4 v[U];
@@ -250,7 +263,7 @@ __device__ __forceinline__ uint4 pair_add(const uint4& r, const float* a, const 
 template <int FMT, int U>
 __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engram_overlay OV,
                                                             const int32_t* __restrict__ tokens,
-                                                            const int32_t* __restrict__ seg_start, int64_t t0,
+                                                            const int32_t* __restrict__ seg_start, PosMap pm,
                                                             int64_t n, __nv_bfloat16* __restrict__ out,
                                                             int32_t* ids_out, int32_t* slots_out,
                                                             unsigned long long* hit_count) {
@@ -267,7 +280,7 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
     const float* ovr = OV.rows;
     unsigned long long hits = 0;
     TokCtx nxt{};
-    if (warp0 < n) nxt = load_ctx(T, tokens, seg_start, t0 + warp0);
+    if (warp0 < n) nxt = load_ctx(T, tokens, seg_start, pm.at(warp0));
     for (int64_t i = warp0; i < n; i += nwarps) {
         const TokCtx cur = nxt;
         uint4* res = reinterpret_cast<uint4*>(out + i * (int64_t)hpn * dim);
@@ -280,9 +293,9 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                 if (c < cpp) r[u] = __ldcs(res + c);
             }
             if (base == 0) {
-                ph = heads_of(T, OV, cur, t0 + i, lane);
+                ph = heads_of(T, OV, cur, pm.at(i), lane);
                 write_heads(ph, i, nh, lane, ids_out, slots_out, hits);
-                if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, t0 + i + nwarps);
+                if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, pm.at(i + nwarps));
             }
             if constexpr (FMT == ENGRAM_FMT_F32) {
                 float fa[U][8], fb[U][8];
@@ -410,7 +423,7 @@ __device__ __forceinline__ void row_pairs(const uint8_t* row_smem, const float* 
 template <int FMT>
 __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
     engram_table T, engram_overlay OV, const int32_t* __restrict__ tokens, const int32_t* __restrict__ seg_start,
-    int64_t t0, int64_t n, __nv_bfloat16* __restrict__ out, int32_t* ids_out, int32_t* slots_out,
+    PosMap pm, int64_t n, __nv_bfloat16* __restrict__ out, int32_t* ids_out, int32_t* slots_out,
     unsigned long long* hit_count, int buf_bytes) {
     extern __shared__ __align__(16) uint8_t smem[];
     float2* pair_tab = reinterpret_cast<float2*>(smem);
@@ -442,21 +455,21 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
         cp_async_commit_f();
     };
 
-    TokCtx ctx = load_ctx(T, tokens, seg_start, t0 + i);
-    int32_t gid = lane < nh ? hash_ctx(T, ctx, t0 + i, lane) : 0;
+    TokCtx ctx = load_ctx(T, tokens, seg_start, pm.at(i));
+    int32_t gid = lane < nh ? hash_ctx(T, ctx, pm.at(i), lane) : 0;
     issue(i, gid, 0);
     int32_t slot = lane < nh ? overlay_slot(OV, gid) : -1;
     int64_t inext = i + nw;
-    if (inext < n) ctx = load_ctx(T, tokens, seg_start, t0 + inext);
+    if (inext < n) ctx = load_ctx(T, tokens, seg_start, pm.at(inext));
     unsigned long long hits = 0;
     int b = 0;
     for (; i < n; i += nw, inext += nw) {
         const bool has_next = inext < n;
         int32_t gid_n = 0;
         if (has_next) {
-            gid_n = lane < nh ? hash_ctx(T, ctx, t0 + inext, lane) : 0;
+            gid_n = lane < nh ? hash_ctx(T, ctx, pm.at(inext), lane) : 0;
             issue(inext, gid_n, b ^ 1);
-            if (inext + nw < n) ctx = load_ctx(T, tokens, seg_start, t0 + inext + nw);
+            if (inext + nw < n) ctx = load_ctx(T, tokens, seg_start, pm.at(inext + nw));
         } else {
             cp_async_commit_f();  // one group per iteration keeps the wait count uniform
         }
@@ -624,7 +637,7 @@ __device__ __forceinline__ void xs_row(const uint8_t* row, const float* ov_row, 
 template <int FMT, int DIM>
 __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     engram_table T, engram_overlay OV, const int32_t* __restrict__ tokens, const int32_t* __restrict__ seg_start,
-    int64_t t0, int64_t n, __nv_bfloat16* __restrict__ out, int32_t* ids_out, int32_t* slots_out,
+    PosMap pm, int64_t n, __nv_bfloat16* __restrict__ out, int32_t* ids_out, int32_t* slots_out,
     unsigned long long* hit_count) {
     using G = XsGeom<FMT, DIM>;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -658,20 +671,20 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
 
     // pipeline state: position k (gid, slot), k+1 (gid, probe in flight), k+2 (tokens in flight)
     int64_t i = first;
-    TokCtx c0 = load_ctx(T, tokens, seg_start, t0 + i);
-    int32_t gid = head_lane ? hash_ctx(T, c0, t0 + i, lane) : 0;
+    TokCtx c0 = load_ctx(T, tokens, seg_start, pm.at(i));
+    int32_t gid = head_lane ? hash_ctx(T, c0, pm.at(i), lane) : 0;
     issue(i, gid, 0);
     int32_t slot = head_lane ? probe_finish(OV, gid, probe_start(OV, gid)) : -1;
     int64_t i1 = i + nw;
     int32_t gid1 = 0;
     ProbeState pr1{0u, -1, -1};
     if (i1 < n) {
-        const TokCtx c1 = load_ctx(T, tokens, seg_start, t0 + i1);
-        gid1 = head_lane ? hash_ctx(T, c1, t0 + i1, lane) : 0;
+        const TokCtx c1 = load_ctx(T, tokens, seg_start, pm.at(i1));
+        gid1 = head_lane ? hash_ctx(T, c1, pm.at(i1), lane) : 0;
         if (head_lane) pr1 = probe_start(OV, gid1);
     }
     TokCtx c2{};
-    if (i1 + nw < n) c2 = load_ctx(T, tokens, seg_start, t0 + i1 + nw);
+    if (i1 + nw < n) c2 = load_ctx(T, tokens, seg_start, pm.at(i1 + nw));
     unsigned long long hits = 0;
     int b = 0;
     for (; i < n; i += nw) {
@@ -719,9 +732,9 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         slot = (inext < n && head_lane) ? probe_finish(OV, gid1, pr1) : -1;
         const int64_t i2 = inext + nw;
         if (i2 < n) {
-            gid1 = head_lane ? hash_ctx(T, c2, t0 + i2, lane) : 0;
+            gid1 = head_lane ? hash_ctx(T, c2, pm.at(i2), lane) : 0;
             if (head_lane) pr1 = probe_start(OV, gid1);
-            if (i2 + nw < n) c2 = load_ctx(T, tokens, seg_start, t0 + i2 + nw);
+            if (i2 + nw < n) c2 = load_ctx(T, tokens, seg_start, pm.at(i2 + nw));
         }
         b ^= 1;
     }
@@ -731,7 +744,7 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
 
 template <int FMT, int DIM>
 void launch_pairsum_fixed(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
-                          const int32_t* seg_start, int64_t t0, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
+                          const int32_t* seg_start, PosMap pm, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
                           int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
     using G = XsGeom<FMT, DIM>;
     const int smem = 64 + kXsWarps * 2 * G::BUF;
@@ -748,26 +761,26 @@ void launch_pairsum_fixed(const engram_table& T, const engram_overlay& OV, const
     const int64_t want = (n + kXsWarps - 1) / kXsWarps;
     const int64_t cap = (int64_t)sm_count() * per_sm;
     const int blocks = (int)(want < cap ? want : cap);
-    k_forward_pairsum_fixed<FMT, DIM><<<blocks, kXsWarps * 32, smem, s>>>(T, OV, tokens, seg_start, t0, n, out, ids_out,
+    k_forward_pairsum_fixed<FMT, DIM><<<blocks, kXsWarps * 32, smem, s>>>(T, OV, tokens, seg_start, pm, n, out, ids_out,
                                                                           slots_out, hit_count);
 }
 
 // Runs the compile-time specialisation for this table if there is one.
 template <int FMT>
 bool launch_pairsum_specialised(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
-                                const int32_t* seg_start, int64_t t0, int64_t n, __nv_bfloat16* out,
+                                const int32_t* seg_start, PosMap pm, int64_t n, __nv_bfloat16* out,
                                 int32_t* ids_out, int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
     if (T.heads_per_ngram != 8 || T.n_heads != 16) return false;
     if (FMT == ENGRAM_FMT_IQ4_XS && T.dim == 256) {
-        launch_pairsum_fixed<ENGRAM_FMT_IQ4_XS, 256>(T, OV, tokens, seg_start, t0, n, out, ids_out, slots_out, hit_count, s);
+        launch_pairsum_fixed<ENGRAM_FMT_IQ4_XS, 256>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out, hit_count, s);
         return true;
     }
     if (FMT == ENGRAM_FMT_IQ4_XS && T.dim == 512) {
-        launch_pairsum_fixed<ENGRAM_FMT_IQ4_XS, 512>(T, OV, tokens, seg_start, t0, n, out, ids_out, slots_out, hit_count, s);
+        launch_pairsum_fixed<ENGRAM_FMT_IQ4_XS, 512>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out, hit_count, s);
         return true;
     }
     if (FMT == ENGRAM_FMT_IQ4_NL && T.dim == 160) {
-        launch_pairsum_fixed<ENGRAM_FMT_IQ4_NL, 160>(T, OV, tokens, seg_start, t0, n, out, ids_out, slots_out, hit_count, s);
+        launch_pairsum_fixed<ENGRAM_FMT_IQ4_NL, 160>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out, hit_count, s);
         return true;
     }
     return false;
@@ -784,7 +797,7 @@ inline int staged_smem_bytes(const engram_table& T) {
 
 template <int FMT>
 void launch_pairsum_staged(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
-                           const int32_t* seg_start, int64_t t0, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
+                           const int32_t* seg_start, PosMap pm, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
                            int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
     const int smem = staged_smem_bytes(T);
     static int configured[64] = {0};
@@ -800,13 +813,13 @@ void launch_pairsum_staged(const engram_table& T, const engram_overlay& OV, cons
     const int64_t want = (n + kStagedWarps - 1) / kStagedWarps;
     const int64_t cap = (int64_t)sm_count() * per_sm;
     const int blocks = (int)(want < cap ? want : cap);
-    k_forward_pairsum_staged<FMT><<<blocks, kStagedWarps * 32, smem, s>>>(T, OV, tokens, seg_start, t0, n, out, ids_out,
+    k_forward_pairsum_staged<FMT><<<blocks, kStagedWarps * 32, smem, s>>>(T, OV, tokens, seg_start, pm, n, out, ids_out,
                                                                           slots_out, hit_count, staged_buf_bytes(T));
 }
 
 template <int FMT>
 void launch_forward(const engram_table& T, const engram_overlay& OV, const int32_t* tokens, const int32_t* seg_start,
-                    int64_t t0, int64_t n, int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                    PosMap pm, int64_t n, int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
                     unsigned long long* hit_count, cudaStream_t s) {
     const int threads = 256;
     const int64_t warps_needed = n;
@@ -814,15 +827,15 @@ void launch_forward(const engram_table& T, const engram_overlay& OV, const int32
     const int64_t cap = (int64_t)sm_count() * 2;  // persistent: the two blocks per SM that fit
     const int blocks = (int)(blocks_needed < cap ? blocks_needed : cap);
     if (mode == ENGRAM_MODE_CONCAT_F32)
-        k_forward_concat<FMT, FMT == ENGRAM_FMT_F32 ? 16 : 8><<<blocks, threads, 0, s>>>(T, OV, tokens, seg_start, t0, n, (float*)out, ids_out,
+        k_forward_concat<FMT, FMT == ENGRAM_FMT_F32 ? 16 : 8><<<blocks, threads, 0, s>>>(T, OV, tokens, seg_start, pm, n, (float*)out, ids_out,
                                                             slots_out, hit_count);
-    else if (FMT != ENGRAM_FMT_F32 && launch_pairsum_specialised<FMT>(T, OV, tokens, seg_start, t0, n, (__nv_bfloat16*)out,
+    else if (FMT != ENGRAM_FMT_F32 && launch_pairsum_specialised<FMT>(T, OV, tokens, seg_start, pm, n, (__nv_bfloat16*)out,
                                                                       ids_out, slots_out, hit_count, s)) {
     } else if (FMT != ENGRAM_FMT_F32 && staged_smem_bytes(T) <= kMaxStagedSmem)
-        launch_pairsum_staged<FMT>(T, OV, tokens, seg_start, t0, n, (__nv_bfloat16*)out, ids_out, slots_out,
+        launch_pairsum_staged<FMT>(T, OV, tokens, seg_start, pm, n, (__nv_bfloat16*)out, ids_out, slots_out,
                                    hit_count, s);
     else
-        k_forward_pairsum<FMT, 4><<<blocks, threads, 0, s>>>(T, OV, tokens, seg_start, t0, n, (__nv_bfloat16*)out,
+        k_forward_pairsum<FMT, 4><<<blocks, threads, 0, s>>>(T, OV, tokens, seg_start, pm, n, (__nv_bfloat16*)out,
                                                              ids_out, slots_out, hit_count);
 }
 
@@ -836,15 +849,17 @@ extern "C" int engram_hash(const engram_table* t, const int32_t* tokens, const i
     const int64_t total = n * t->n_heads;
     const int threads = 256;
     const int64_t want = (total + threads - 1) / threads, cap = (int64_t)sm_count() * 16;
-    k_hash<<<(int)(want < cap ? want : cap), threads, 0, (cudaStream_t)stream>>>(*t, tokens, seg_start, t0, n, ids_out);
+    k_hash<<<(int)(want < cap ? want : cap), threads, 0, (cudaStream_t)stream>>>(*t, tokens, seg_start,
+                                                                                PosMap{t0, nullptr, 0}, n, ids_out);
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
 
-extern "C" int engram_forward(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
-                              const int32_t* seg_start, int64_t t0, int64_t n, int32_t mode, void* out,
-                              int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream) {
-    if (!t || t0 < 0 || n < 0) return ENGRAM_ERR_ARG;
+namespace {
+int forward_impl(const engram_table* t, const engram_overlay* ov, const int32_t* tokens, const int32_t* seg_start,
+                 PosMap pm, int64_t n, int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                 int64_t* hit_count, void* stream) {
+    if (!t || n < 0) return ENGRAM_ERR_ARG;
     if (mode != ENGRAM_MODE_CONCAT_F32 && mode != ENGRAM_MODE_PAIRSUM_ADD_BF16) return ENGRAM_ERR_ARG;
     if (mode == ENGRAM_MODE_PAIRSUM_ADD_BF16) {
         if (t->ngram_size != 3 || t->dim % 8) return ENGRAM_ERR_FORMAT;
@@ -865,13 +880,31 @@ extern "C" int engram_forward(const engram_table* t, const engram_overlay* ov, c
     cudaStream_t s = (cudaStream_t)stream;
     unsigned long long* hc = reinterpret_cast<unsigned long long*>(hit_count);
     switch (t->fmt) {
-        case ENGRAM_FMT_F32: launch_forward<ENGRAM_FMT_F32>(*t, OV, tokens, seg_start, t0, n, mode, out, ids_out, slots_out, hc, s); break;
-        case ENGRAM_FMT_IQ4_NL: launch_forward<ENGRAM_FMT_IQ4_NL>(*t, OV, tokens, seg_start, t0, n, mode, out, ids_out, slots_out, hc, s); break;
-        case ENGRAM_FMT_IQ4_XS: launch_forward<ENGRAM_FMT_IQ4_XS>(*t, OV, tokens, seg_start, t0, n, mode, out, ids_out, slots_out, hc, s); break;
+        case ENGRAM_FMT_F32: launch_forward<ENGRAM_FMT_F32>(*t, OV, tokens, seg_start, pm, n, mode, out, ids_out, slots_out, hc, s); break;
+        case ENGRAM_FMT_IQ4_NL: launch_forward<ENGRAM_FMT_IQ4_NL>(*t, OV, tokens, seg_start, pm, n, mode, out, ids_out, slots_out, hc, s); break;
+        case ENGRAM_FMT_IQ4_XS: launch_forward<ENGRAM_FMT_IQ4_XS>(*t, OV, tokens, seg_start, pm, n, mode, out, ids_out, slots_out, hc, s); break;
         default: return ENGRAM_ERR_FORMAT;
     }
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+}  // namespace
+
+extern "C" int engram_forward(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                              const int32_t* seg_start, int64_t t0, int64_t n, int32_t mode, void* out,
+                              int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream) {
+    if (t0 < 0) return ENGRAM_ERR_ARG;
+    return forward_impl(t, ov, tokens, seg_start, PosMap{t0, nullptr, 0}, n, mode, out, ids_out, slots_out, hit_count,
+                        stream);
+}
+
+extern "C" int engram_forward_at(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                 int64_t n_tokens, const int32_t* seg_start, const int64_t* positions, int64_t n,
+                                 int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out, int64_t* hit_count,
+                                 void* stream) {
+    if (n_tokens < 1 || (n > 0 && !positions)) return ENGRAM_ERR_ARG;
+    return forward_impl(t, ov, tokens, seg_start, PosMap{0, positions, n_tokens}, n, mode, out, ids_out, slots_out,
+                        hit_count, stream);
 }
 
 extern "C" int engram_gather_rows(const engram_table* t, const int32_t* ids, int64_t n, float* out, void* stream) {

@@ -187,6 +187,53 @@ def engram_embed(dtable: DeviceTable, tokens, rows_var: torch.Tensor, omap: Over
     return _ConcatFn.apply(rows_var, dtable, omap, tokens, ss, t0, n, hit_count)
 
 
+class _ConcatAtFn(torch.autograd.Function):
+    """CONCAT rows at an explicit position list (decode-style)."""
+
+    @staticmethod
+    def forward(ctx, rows_var, dtable: DeviceTable, omap: OverlayMap, tokens, seg_start, positions, hit_count):
+        dev = dtable.device
+        nh, dim = dtable.n_heads, dtable.dim
+        n = positions.numel()
+        rv = rows_var.detach().contiguous()
+        out = torch.empty(n, nh * dim, dtype=torch.float32, device=dev)
+        need_grad = rows_var.requires_grad and omap.R > 0
+        slots = torch.empty(n, nh, dtype=torch.int32, device=dev) if need_grad else None
+        ov = omap.descriptor(rv)
+        st = L.load().engram_forward_at(C.byref(dtable.ctable), C.byref(ov), tokens.data_ptr(), tokens.numel(),
+                                        L.ptr(seg_start), positions.data_ptr(), n, L.MODE_CONCAT_F32, out.data_ptr(),
+                                        None, L.ptr(slots), L.ptr(hit_count), L.stream_of(dev))
+        L.check(st, "engram_forward_at")
+        ctx.meta = (nh, dtable.heads_per_ngram, dim, omap.R, n)
+        ctx.save_for_backward(slots if slots is not None else torch.empty(0, dtype=torch.int32, device=dev))
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        (slots,) = ctx.saved_tensors
+        nh, hpn, dim, R, n = ctx.meta
+        if not ctx.needs_input_grad[0] or R == 0 or slots.numel() == 0:
+            return (None,) * 7
+        grad_rows = row_gradients(slots, grad_out.contiguous().to(torch.float32), nh, hpn, dim, R, L.MODE_CONCAT_F32)
+        return (grad_rows,) + (None,) * 6
+
+
+def engram_embed_at(dtable: DeviceTable, tokens, positions, rows_var: torch.Tensor, omap: OverlayMap,
+                    seg_start=None, hit_count: torch.Tensor | None = None) -> torch.Tensor:
+    """emb [len(positions), n_heads*dim] for an explicit position list: the
+    decode-style lookup (one new token per sequence; the reference computes it
+    position by position with Replica.ple_true_emb, engraft/replica/model.py:473-495)."""
+    dev = dtable.device
+    _check_rows_var(rows_var, dtable.dim)
+    tokens = _as_i32(tokens, dev)
+    pos = torch.as_tensor(positions, dtype=torch.int64)
+    if pos.numel() and (int(pos.min()) < 0 or int(pos.max()) >= tokens.numel()):
+        raise ValueError("positions must lie in [0, len(tokens))")
+    pos = pos.to(dev, non_blocking=True).contiguous()
+    ss = None if seg_start is None else _as_i32(seg_start, dev)
+    return _ConcatAtFn.apply(rows_var, dtable, omap, tokens, ss, pos, hit_count)
+
+
 def engram_residual_add(residual: torch.Tensor, dtable: DeviceTable, tokens, rows_var: torch.Tensor,
                         omap: OverlayMap, seg_start=None, t0: int = 0,
                         hit_count: torch.Tensor | None = None) -> torch.Tensor:

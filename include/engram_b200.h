@@ -168,6 +168,19 @@ ENGRAM_API int engram_forward(const engram_table* t, const engram_overlay* ov, c
                    int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream);
 
 /*
+ * engram_forward for an explicit list of positions (decode-style lookups: one
+ * new token per sequence, each sequence's recent tokens laid out in `tokens`
+ * with seg_start marking where each sequence starts).  Output row k is
+ * position positions[k] (device int64 [n]; values are clamped into
+ * [0, n_tokens)).  Replaces the per-position Replica.ple_true_emb
+ * (engraft/replica/model.py:473-495), overlay substituted as there.
+ */
+ENGRAM_API int engram_forward_at(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                 int64_t n_tokens, const int32_t* seg_start, const int64_t* positions, int64_t n,
+                                 int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out, int64_t* hit_count,
+                                 void* stream);
+
+/*
  * Dequantised rows by global id: out float [n, dim] = row ids[k] of the table
  * (no overlay).  Replaces distill._read_true_rows (engraft/replica/distill.py:378-396)
  * and PleTable.read_rows (engraft/table.py:106-109) on the resident table.

@@ -284,3 +284,30 @@ def test_pack_kernel_matches_oracle_layout(eb, fmt, dim):
     dt = device_table(eb, spec)
     got = dt.rows.cpu().numpy().reshape(4096, -1)
     assert np.array_equal(got, O.pack(fmt, dim, spec.raw))
+
+
+# ---------------------------------------------------- decode-style positions
+def test_forward_at_positions_decode_style_vs_oracle(eb):
+    """256 sequences x (3 history + 1 new token); rows of the new tokens only."""
+    rng = np.random.default_rng(44)
+    spec = random_spec(O.FMT_F32, 128, 1 << 16, 44)
+    B = 256
+    toks = rng.integers(0, 151_935, size=(B, 4)).astype(np.int32)
+    toks[::17, 1] = 151_935  # an EOS in some histories
+    flat = toks.reshape(-1)
+    ss = np.repeat(np.arange(B) * 4, 4).astype(np.int32)
+    positions = np.arange(B) * 4 + 3
+    ids_all = spec.ids(flat, seg_start=ss)
+    ids = ids_all[positions]
+    ov_ids = np.unique(ids)[::3].astype(np.int32)
+    rows_init = (rng.standard_normal((len(ov_ids), 128)) * 0.01).astype(np.float32)
+    out_ref, slots = O.forward(spec.fmt, 128, spec.raw, ids, 8, rows_init, ov_ids)
+    dt = device_table(eb, spec)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    rows_var = torch.from_numpy(rows_init).to(DEV).requires_grad_(True)
+    out = eb.engram_embed_at(dt, flat, positions, rows_var, omap, torch.from_numpy(ss))
+    assert np.array_equal(out.detach().cpu().numpy().view(np.uint32), out_ref.reshape(B, -1).view(np.uint32))
+    grad = (rng.standard_normal(out.shape) * 1e-3).astype(np.float32)
+    out.backward(torch.from_numpy(grad).to(DEV))
+    gref = O.backward(slots, 8, grad, 128, len(ov_ids))
+    assert np.array_equal(rows_var.grad.cpu().numpy().view(np.uint32), gref.view(np.uint32))

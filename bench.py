@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--table-rows", type=int, default=None, help="override (profiling a small case)")
     ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU")
+    ap.add_argument("--shard", action="store_true",
+                    help="row-sharded table: each rank holds rows g with g %% N == rank; rows move by NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -113,8 +115,17 @@ class Workload:
         sizes = synthetic_head_sizes(cfg["rows"])
         offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
         mult = synthetic_multipliers(seed)
-        rows = synthetic_resident(cfg["rows"], fmt, self.dim, seed, device)
-        self.table = eb.DeviceTable(rows, fmt, self.dim, sizes, offs, mult, EOS, n_rows=cfg["rows"])
+        self.shard = None
+        if cfg.get("shard"):
+            from engraft_ngram_b200.shard import ShardedTable, local_exchange, nccl_exchange
+            n_local = (cfg["rows"] - rank + world - 1) // world
+            rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device)
+            self.shard = ShardedTable(rows, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"])
+            self.exchange = nccl_exchange() if world > 1 else local_exchange([self.shard])
+            self.table = self.shard
+        else:
+            rows = synthetic_resident(cfg["rows"], fmt, self.dim, seed, device)
+            self.table = eb.DeviceTable(rows, fmt, self.dim, sizes, offs, mult, EOS, n_rows=cfg["rows"])
         self.decode = bool(cfg.get("decode"))
         self.T = cfg["seqs"] * cfg["seq_len"]
         cdf = zipf_cdf(torch, device)
@@ -150,10 +161,15 @@ class Workload:
             self.ov_ids = torch.zeros(0, dtype=torch.int32, device=device)
         self.R = int(self.ov_ids.numel())
         self.omap = eb.OverlayMap(self.ov_ids, device)
-        self.p0 = self.table.gather_rows(self.ov_ids) if self.R else torch.zeros(0, self.dim, device=device)
+        if self.shard is not None:  # true rows live on their owners; start from seeded values instead
+            gp = torch.Generator(device=device)
+            gp.manual_seed(seed * 1000 + 5)
+            self.p0 = torch.randn(self.R, self.dim, generator=gp, device=device) * 0.0085
+        else:
+            self.p0 = self.table.gather_rows(self.ov_ids) if self.R else torch.zeros(0, self.dim, device=device)
         self.rows_var = self.p0.clone()
         self.grad_rows = torch.zeros_like(self.p0)
-        nh, hpn = self.table.n_heads, self.table.heads_per_ngram
+        nh, hpn = self.table.n_heads, 8
         self.nh, self.hpn = nh, hpn
         gg = torch.Generator(device=device)
         gg.manual_seed(seed * 1000 + 99 + rank)
@@ -186,6 +202,10 @@ class Workload:
     # one step through the C ABI (device-resident inputs)
     def forward(self, hit_count=None):
         import ctypes as C
+        if self.shard is not None:
+            self.shard.forward(self.tokens, self.seg_start, self.omap, self.rows_var, self.out, self.mode,
+                               self.exchange, slots_out=self.slots if self.R else None, hit_count=hit_count)
+            return
         if self.decode:
             st = self.L.load().engram_forward_at(C.byref(self.table.ctable), C.byref(self.ov_desc),
                                                  self.tokens.data_ptr(), self.T, self.seg_start.data_ptr(),
@@ -433,7 +453,8 @@ def config_json(cfg, args):
                         f"{cfg['rows']}-row x {cfg['dim']} {cfg['fmt']} table, R={cfg['R']} overlay rows, "
                         f"{cfg['mode']} emit, {'fwd+bwd+Adam' if cfg['bwd'] else 'fwd only'}",
             "table_rows": cfg["rows"], "dim": cfg["dim"], "format": cfg["fmt"], "positions_per_gpu": cfg["seqs"] * cfg["seq_len"],
-            "overlay_rows": cfg["R"], "emit": cfg["mode"], "parallelism": f"dp{args.gpus}",
+            "overlay_rows": cfg["R"], "emit": cfg["mode"],
+            "parallelism": f"dp{args.gpus}" + ("+row-sharded table (id mod N, NCCL all-to-all of ids and rows)" if cfg.get("shard") else ""),
             "l2": "inputs larger than L2 (residual and upstream gradient 537 MB each, table 46 GB)"}
 
 
@@ -447,6 +468,7 @@ def main():
         cfg["rows"] = args.table_rows
     if args.seqs:
         cfg["seqs"] = args.seqs
+    cfg["shard"] = bool(args.shard)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

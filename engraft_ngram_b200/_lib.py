@@ -68,6 +68,7 @@ SIGNATURES = {
                                     C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int64]),
     "engram_table_pack": (C.c_int, [C.c_int32, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
     "engram_overlay_map_build": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
+    "engram_overlay_lookup": (C.c_int, [C.POINTER(EngramOverlay), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
     "engram_hash": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
                               C.c_void_p]),
     "engram_forward": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p, C.c_int64,
@@ -75,6 +76,13 @@ SIGNATURES = {
     "engram_forward_at": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_int64,
                                     C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_void_p]),
+    "engram_forward_indirect": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
+                                          C.c_int64, C.c_int64, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_shard_requests": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p,
+                                        C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_shard_gather": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p,
+                                      C.c_void_p]),
     "engram_gather_rows": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
     "engram_backward_workspace_bytes": (C.c_int64, [C.c_int64, C.c_int32, C.c_int64]),
     "engram_backward": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,

@@ -19,6 +19,7 @@ constexpr unsigned kFull = 0xffffffffu;
 struct PosHeads {
     int32_t gid;   // this lane's head: global row id
     int32_t slot;  // overlay slot or -1
+    int32_t row;   // row in T.rows serving it (the global id, or an index into gathered rows)
 };
 
 // Output row i -> token position: pm.at(i), or pos[i] for an explicit position
@@ -27,6 +28,14 @@ struct PosMap {
     int64_t t0;
     const int64_t* pos;
     int64_t n_tokens;
+    const int32_t* rix;  // nullable: row of (output row i, head h) in T.rows is rix[i*n_heads + h]
+    // Row number in T.rows that serves head h of output row i (the global id
+    // unless the rows were gathered into a local buffer, see engram_forward_indirect).
+    __device__ __forceinline__ int32_t row(int64_t i, int h, int nh, int32_t gid) const {
+        if (rix == nullptr) return gid;
+        const int32_t r = __ldg(rix + i * nh + h);
+        return r < 0 ? 0 : r;
+    }
     __device__ __forceinline__ int64_t at(int64_t i) const {
         if (pos == nullptr) return t0 + i;
         const int64_t p = __ldg(pos + i);
@@ -35,11 +44,12 @@ struct PosMap {
 };
 
 __device__ __forceinline__ PosHeads heads_of(const engram_table& T, const engram_overlay& OV, const TokCtx& c,
-                                             int64_t t, int lane) {
-    PosHeads r{0, -1};
+                                             const PosMap& pm, int64_t i, int lane) {
+    PosHeads r{0, -1, 0};
     if (lane < T.n_heads) {
-        r.gid = hash_ctx(T, c, t, lane);
+        r.gid = hash_ctx(T, c, pm.at(i), lane);
         r.slot = overlay_slot(OV, r.gid);
+        r.row = pm.row(i, lane, T.n_heads, r.gid);
     }
     return r;
 }
@@ -191,7 +201,7 @@ __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engra
     if (warp0 < n) nxt = load_ctx(T, tokens, seg_start, pm.at(warp0));
     for (int64_t i = warp0; i < n; i += nwarps) {
         const TokCtx cur = nxt;
-        const PosHeads ph = heads_of(T, OV, cur, pm.at(i), lane);
+        const PosHeads ph = heads_of(T, OV, cur, pm, i, lane);
         write_heads(ph, i, nh, lane, ids_out, slots_out, hits);
         if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, pm.at(i + nwarps));
         float4* dst = reinterpret_cast<float4*>(out + i * (int64_t)nh * dim);
@@ -205,7 +215,7 @@ __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engra
                 const int h = c / cpr;
                 const int cc = c - h * cpr;
                 const int hs = h < nh ? h : 0;
-                const int32_t g = __shfl_sync(kFull, ph.gid, hs);
+                const int32_t g = __shfl_sync(kFull, ph.row, hs);
                 const int32_t s = __shfl_sync(kFull, ph.slot, hs);
                 sl[u] = s;
                 if (c < cpp) {
@@ -293,7 +303,7 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                 if (c < cpp) r[u] = __ldcs(res + c);
             }
             if (base == 0) {
-                ph = heads_of(T, OV, cur, pm.at(i), lane);
+                ph = heads_of(T, OV, cur, pm, i, lane);
                 write_heads(ph, i, nh, lane, ids_out, slots_out, hits);
                 if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, pm.at(i + nwarps));
             }
@@ -305,9 +315,9 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                     const int g = c / cpr;
                     const int cc = c - g * cpr;
                     const int gs = g < hpn ? g : 0;
-                    const int32_t ga = __shfl_sync(kFull, ph.gid, gs);
+                    const int32_t ga = __shfl_sync(kFull, ph.row, gs);
                     const int32_t s0 = __shfl_sync(kFull, ph.slot, gs);
-                    const int32_t gb = __shfl_sync(kFull, ph.gid, hpn + gs);
+                    const int32_t gb = __shfl_sync(kFull, ph.row, hpn + gs);
                     const int32_t s1 = __shfl_sync(kFull, ph.slot, hpn + gs);
                     if (c < cpp) {
                         ld_f8(s0 >= 0 ? ovr + (int64_t)s0 * dim + 8 * cc
@@ -329,9 +339,9 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                     const int g = c / cpr;
                     const int cc = c - g * cpr;
                     const int gs = g < hpn ? g : 0;
-                    const int32_t ga = __shfl_sync(kFull, ph.gid, gs);
+                    const int32_t ga = __shfl_sync(kFull, ph.row, gs);
                     const int32_t s0 = __shfl_sync(kFull, ph.slot, gs);
-                    const int32_t gb = __shfl_sync(kFull, ph.gid, hpn + gs);
+                    const int32_t gb = __shfl_sync(kFull, ph.row, hpn + gs);
                     const int32_t s1 = __shfl_sync(kFull, ph.slot, hpn + gs);
                     if (c < cpp) {
                         if (s0 < 0) ra[u] = raw8<FMT>(rows + (int64_t)ga * T.row_stride, cc, dim);
@@ -457,7 +467,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
 
     TokCtx ctx = load_ctx(T, tokens, seg_start, pm.at(i));
     int32_t gid = lane < nh ? hash_ctx(T, ctx, pm.at(i), lane) : 0;
-    issue(i, gid, 0);
+    issue(i, lane < nh ? pm.row(i, lane, nh, gid) : 0, 0);
     int32_t slot = lane < nh ? overlay_slot(OV, gid) : -1;
     int64_t inext = i + nw;
     if (inext < n) ctx = load_ctx(T, tokens, seg_start, pm.at(inext));
@@ -468,7 +478,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
         int32_t gid_n = 0;
         if (has_next) {
             gid_n = lane < nh ? hash_ctx(T, ctx, pm.at(inext), lane) : 0;
-            issue(inext, gid_n, b ^ 1);
+            issue(inext, lane < nh ? pm.row(inext, lane, nh, gid_n) : 0, b ^ 1);
             if (inext + nw < n) ctx = load_ctx(T, tokens, seg_start, pm.at(inext + nw));
         } else {
             cp_async_commit_f();  // one group per iteration keeps the wait count uniform
@@ -673,7 +683,7 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     int64_t i = first;
     TokCtx c0 = load_ctx(T, tokens, seg_start, pm.at(i));
     int32_t gid = head_lane ? hash_ctx(T, c0, pm.at(i), lane) : 0;
-    issue(i, gid, 0);
+    issue(i, head_lane ? pm.row(i, lane, G::NH, gid) : 0, 0);
     int32_t slot = head_lane ? probe_finish(OV, gid, probe_start(OV, gid)) : -1;
     int64_t i1 = i + nw;
     int32_t gid1 = 0;
@@ -689,7 +699,7 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     int b = 0;
     for (; i < n; i += nw) {
         const int64_t inext = i + nw;
-        if (inext < n) issue(inext, gid1, b ^ 1);
+        if (inext < n) issue(inext, head_lane ? pm.row(inext, lane, G::NH, gid1) : 0, b ^ 1);
         else cp_async_commit_f();
         if (head_lane) {
             if (ids_out) ids_out[i * G::NH + lane] = gid;
@@ -850,7 +860,7 @@ extern "C" int engram_hash(const engram_table* t, const int32_t* tokens, const i
     const int threads = 256;
     const int64_t want = (total + threads - 1) / threads, cap = (int64_t)sm_count() * 16;
     k_hash<<<(int)(want < cap ? want : cap), threads, 0, (cudaStream_t)stream>>>(*t, tokens, seg_start,
-                                                                                PosMap{t0, nullptr, 0}, n, ids_out);
+                                                                                PosMap{t0, nullptr, 0, nullptr}, n, ids_out);
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
@@ -894,8 +904,17 @@ extern "C" int engram_forward(const engram_table* t, const engram_overlay* ov, c
                               const int32_t* seg_start, int64_t t0, int64_t n, int32_t mode, void* out,
                               int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream) {
     if (t0 < 0) return ENGRAM_ERR_ARG;
-    return forward_impl(t, ov, tokens, seg_start, PosMap{t0, nullptr, 0}, n, mode, out, ids_out, slots_out, hit_count,
+    return forward_impl(t, ov, tokens, seg_start, PosMap{t0, nullptr, 0, nullptr}, n, mode, out, ids_out, slots_out, hit_count,
                         stream);
+}
+
+extern "C" int engram_forward_indirect(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                       const int32_t* seg_start, int64_t t0, int64_t n, const int32_t* row_index,
+                                       int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                                       int64_t* hit_count, void* stream) {
+    if (t0 < 0 || (n > 0 && !row_index)) return ENGRAM_ERR_ARG;
+    return forward_impl(t, ov, tokens, seg_start, PosMap{t0, nullptr, 0, row_index}, n, mode, out, ids_out, slots_out,
+                        hit_count, stream);
 }
 
 extern "C" int engram_forward_at(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
@@ -903,7 +922,7 @@ extern "C" int engram_forward_at(const engram_table* t, const engram_overlay* ov
                                  int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out, int64_t* hit_count,
                                  void* stream) {
     if (n_tokens < 1 || (n > 0 && !positions)) return ENGRAM_ERR_ARG;
-    return forward_impl(t, ov, tokens, seg_start, PosMap{0, positions, n_tokens}, n, mode, out, ids_out, slots_out,
+    return forward_impl(t, ov, tokens, seg_start, PosMap{0, positions, n_tokens, nullptr}, n, mode, out, ids_out, slots_out,
                         hit_count, stream);
 }
 

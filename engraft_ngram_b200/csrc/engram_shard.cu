@@ -1,0 +1,183 @@
+// engram_shard.cu -- the row-sharded table across W GPUs (owner(id) = id mod W).
+//
+// Each rank keeps only the rows it owns (global id g lives on rank g % W at local
+// index g / W).  Per step a rank:
+//   1. hashes its positions (engram_hash) and probes the overlay;
+//   2. engram_shard_requests: inserts every table row it needs (overlay hits
+//      excluded) into a hash set -- one request per distinct row --, groups the
+//      distinct ids by owner (send_ids, per-owner counts) and records, for every
+//      (position, head), where that row will sit in the reply buffer (row_index);
+//   3. exchanges ids with NCCL all-to-all-v (host code); each owner copies the
+//      requested rows out of its shard with engram_shard_gather; the quantised
+//      rows travel back with a second all-to-all-v;
+//   4. runs the forward with row_index pointing into the received rows
+//      (engram_forward_indirect).
+// No kernel here reads another GPU's memory: remote rows arrive in local HBM
+// through NCCL before any kernel touches them.
+#include "engram_common.cuh"
+
+using namespace engram;
+
+namespace {
+
+constexpr int kMaxWorld = 64;
+
+__device__ __forceinline__ uint32_t set_home(int32_t key, int64_t capacity) { return map_home(key, capacity); }
+
+__global__ void k_set_clear(int32_t* keys, int64_t capacity, int64_t* counts, int world) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < capacity; i += stride) keys[i] = -1;
+    if (blockIdx.x == 0 && threadIdx.x < 2 * world) counts[threadIdx.x] = 0;  // counts[world] + cursors[world]
+}
+
+// Inserts the ids that the table must serve (slot < 0) into the set.
+__global__ void k_set_insert(const int32_t* __restrict__ ids, const int32_t* __restrict__ slots, int64_t n,
+                             int32_t* keys, int64_t capacity) {
+    const uint32_t mask = (uint32_t)capacity - 1u;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += stride) {
+        if (slots && slots[k] >= 0) continue;
+        const int32_t g = ids[k];
+        uint32_t pos = set_home(g, capacity);
+        for (int64_t probe = 0; probe < capacity; probe++) {
+            // a plain read first: repeated ids (Zipf-hot rows) then need no atomic
+            const int32_t seen = *reinterpret_cast<volatile int32_t*>(keys + pos);
+            if (seen == g) break;
+            if (seen == -1) {
+                const int32_t prev = atomicCAS(keys + pos, -1, g);
+                if (prev == -1 || prev == g) break;
+            }
+            pos = (pos + 1u) & mask;
+        }
+    }
+}
+
+// Per-owner counts of the distinct ids, aggregated per block in shared memory
+// (one global atomic per owner per block; the ids of a hot table would
+// otherwise serialise on W counters).
+__global__ void k_owner_count(const int32_t* __restrict__ keys, int64_t capacity, int world,
+                              unsigned long long* counts) {
+    __shared__ unsigned int c[kMaxWorld];
+    for (int o = threadIdx.x; o < world; o += blockDim.x) c[o] = 0;
+    __syncthreads();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < capacity; e += stride) {
+        const int32_t g = keys[e];
+        if (g >= 0) atomicAdd(c + (g % world), 1u);
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < world; o += blockDim.x)
+        if (c[o]) atomicAdd(counts + o, (unsigned long long)c[o]);
+}
+
+// send_ids grouped by owner; vals[e] = the entry's position in send_ids (= in the
+// reply).  Each block reserves one range per owner, then places its entries
+// inside the ranges with shared-memory counters.
+__global__ void k_owner_scatter(const int32_t* __restrict__ keys, int32_t* __restrict__ vals, int64_t capacity,
+                                int world, const unsigned long long* counts, unsigned long long* cursors,
+                                int32_t* __restrict__ send_ids) {
+    __shared__ unsigned long long off[kMaxWorld];
+    __shared__ unsigned int c[kMaxWorld];
+    __shared__ unsigned long long base[kMaxWorld];
+    if (threadIdx.x == 0) {
+        unsigned long long acc = 0;
+        for (int o = 0; o < world; o++) {
+            off[o] = acc;
+            acc += counts[o];
+        }
+    }
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t e0 = (int64_t)blockIdx.x * blockDim.x; e0 < capacity; e0 += stride) {
+        for (int o = threadIdx.x; o < world; o += blockDim.x) c[o] = 0;
+        __syncthreads();
+        const int64_t e = e0 + threadIdx.x;
+        const int32_t g = e < capacity ? keys[e] : -1;
+        unsigned int local = 0;
+        if (g >= 0) local = atomicAdd(c + (g % world), 1u);
+        __syncthreads();
+        for (int o = threadIdx.x; o < world; o += blockDim.x)
+            base[o] = c[o] ? off[o] + atomicAdd(cursors + o, (unsigned long long)c[o]) : 0ull;
+        __syncthreads();
+        if (g >= 0) {
+            const unsigned long long pos = base[g % world] + local;
+            send_ids[pos] = g;
+            vals[e] = (int32_t)pos;
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void k_row_index(const int32_t* __restrict__ ids, const int32_t* __restrict__ slots, int64_t n,
+                            const int32_t* __restrict__ keys, const int32_t* __restrict__ vals, int64_t capacity,
+                            int32_t* __restrict__ row_index) {
+    const uint32_t mask = (uint32_t)capacity - 1u;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += stride) {
+        int32_t r = -1;
+        if (!(slots && slots[k] >= 0)) {
+            const int32_t g = ids[k];
+            uint32_t pos = set_home(g, capacity);
+            for (int64_t probe = 0; probe < capacity; probe++) {
+                const int32_t key = keys[pos];
+                if (key == g) {
+                    r = vals[pos];
+                    break;
+                }
+                if (key == -1) break;
+                pos = (pos + 1u) & mask;
+            }
+        }
+        row_index[k] = r;
+    }
+}
+
+// out[k] = shard row (ids[k] / world); one thread per 16-byte word.
+__global__ void k_shard_gather(const uint8_t* __restrict__ shard, int64_t stride, int64_t n_local,
+                               const int32_t* __restrict__ ids, int64_t n, int world, uint8_t* __restrict__ out) {
+    const int64_t words = stride >> 4;
+    const int64_t total = n * words;
+    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total; w += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t k = w / words, p = w - k * words;
+        const int64_t local = (int64_t)ids[k] / world;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (ids[k] >= 0 && local < n_local) v = __ldg(reinterpret_cast<const uint4*>(shard + local * stride) + p);
+        reinterpret_cast<uint4*>(out + k * stride)[p] = v;
+    }
+}
+
+int grid(int64_t work) {
+    const int64_t want = (work + 255) / 256, cap = (int64_t)sm_count() * 8;
+    return (int)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+}  // namespace
+
+extern "C" int engram_shard_requests(const int32_t* ids, const int32_t* slots, int64_t n, int32_t world,
+                                     int32_t* set_keys, int32_t* set_vals, int64_t capacity, int32_t* send_ids,
+                                     int64_t* counts, int32_t* row_index, void* stream) {
+    if (n < 0 || world < 1 || world > kMaxWorld) return ENGRAM_ERR_ARG;
+    if (!set_keys || !set_vals || !send_ids || !counts || !row_index) return ENGRAM_ERR_ARG;
+    if (n > 0 && !ids) return ENGRAM_ERR_ARG;
+    if ((capacity & (capacity - 1)) != 0 || capacity < 2 * n || capacity < 2 || capacity > (1LL << 31))
+        return ENGRAM_ERR_RANGE;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(counts);
+    k_set_clear<<<grid(capacity), 256, 0, s>>>(set_keys, capacity, counts, world);
+    k_set_insert<<<grid(n), 256, 0, s>>>(ids, slots, n, set_keys, capacity);
+    k_owner_count<<<grid(capacity), 256, 0, s>>>(set_keys, capacity, world, cnt);
+    k_owner_scatter<<<grid(capacity), 256, 0, s>>>(set_keys, set_vals, capacity, world, cnt, cnt + world, send_ids);
+    k_row_index<<<grid(n), 256, 0, s>>>(ids, slots, n, set_keys, set_vals, capacity, row_index);
+    count_launches(5);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int engram_shard_gather(const void* shard_rows, int64_t stride, int64_t n_local, const int32_t* ids,
+                                   int64_t n, int32_t world, void* out, void* stream) {
+    if (n < 0 || world < 1 || stride <= 0 || (stride & 15) || n_local < 0) return ENGRAM_ERR_ARG;
+    if (n == 0) return ENGRAM_OK;
+    if (!shard_rows || !ids || !out || !aligned16(shard_rows) || !aligned16(out)) return ENGRAM_ERR_ARG;
+    k_shard_gather<<<grid(n * (stride >> 4)), 256, 0, (cudaStream_t)stream>>>(
+        static_cast<const uint8_t*>(shard_rows), stride, n_local, ids, n, world, static_cast<uint8_t*>(out));
+    count_launches(1);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}

@@ -160,3 +160,24 @@ extern "C" int engram_overlay_map_build(const int32_t* ids, int64_t R, int32_t* 
     count_launches(2);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
+
+// ---- overlay lookup: slots of a batch of global ids (-1 when not an overlay row)
+__global__ void k_overlay_lookup(engram_overlay OV, const int32_t* __restrict__ ids, int64_t n, int32_t* slots) {
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x)
+        slots[k] = overlay_slot(OV, ids[k]);
+}
+
+extern "C" int engram_overlay_lookup(const engram_overlay* ov, const int32_t* ids, int64_t n, int32_t* slots_out,
+                                     void* stream) {
+    if (!ov || n < 0) return ENGRAM_ERR_ARG;
+    if (n == 0) return ENGRAM_OK;
+    if (!ids || !slots_out) return ENGRAM_ERR_ARG;
+    const engram_overlay OV = *ov;
+    if (OV.n_rows < 0 || (OV.n_rows > 0 && (!OV.map_keys || !OV.map_slots))) return ENGRAM_ERR_ARG;
+    if (OV.n_rows > 0 && ((OV.capacity & (OV.capacity - 1)) != 0 || OV.capacity < 2 * OV.n_rows)) return ENGRAM_ERR_RANGE;
+    const int threads = 256;
+    const int64_t want = (n + threads - 1) / threads, cap = (int64_t)sm_count() * 16;
+    k_overlay_lookup<<<(int)(want < cap ? want : cap), threads, 0, (cudaStream_t)stream>>>(OV, ids, n, slots_out);
+    count_launches(1);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}

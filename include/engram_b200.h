@@ -147,6 +147,13 @@ ENGRAM_API int engram_overlay_map_build(const int32_t* ids, int64_t R, int32_t* 
                              int64_t capacity, void* stream);
 
 /*
+ * Overlay membership of a batch of global ids: slots_out[k] = row_map[ids[k]]
+ * or -1 (the reference's `g in row_map`, engraft/replica/seq.py:411-417).
+ */
+ENGRAM_API int engram_overlay_lookup(const engram_overlay* ov, const int32_t* ids, int64_t n, int32_t* slots_out,
+                                     void* stream);
+
+/*
  * K1 alone: global row ids [n, n_heads] (int32) of positions t0..t0+n-1 of
  * `tokens` (device int32; tokens before t0 are read as context).  seg_start
  * (device int32 [t0+n] or NULL): seg_start[t] = first index of t's segment;
@@ -166,6 +173,45 @@ ENGRAM_API int engram_hash(const engram_table* t, const int32_t* tokens, const i
 ENGRAM_API int engram_forward(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
                    const int32_t* seg_start, int64_t t0, int64_t n, int32_t mode, void* out,
                    int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream);
+
+/*
+ * engram_forward with the table rows taken from a gathered buffer: t->rows
+ * points at rows laid out like the resident table (t->row_stride bytes each)
+ * and row_index (device int32 [n, n_heads]) gives, for each (output row, head),
+ * the row to read; entries for heads the overlay serves are ignored (-1).
+ * The hash and the overlay probe still use t's addressing constants, so ids_out,
+ * slots_out and hit_count are those of engram_forward.  Used by the row-sharded
+ * table after the all-to-all of rows (engram_shard_requests / _gather).
+ */
+ENGRAM_API int engram_forward_indirect(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                       const int32_t* seg_start, int64_t t0, int64_t n, const int32_t* row_index,
+                                       int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                                       int64_t* hit_count, void* stream);
+
+/*
+ * Row-sharded table (owner(g) = g mod world, local index g / world), step 1 of
+ * the exchange: from the global ids [n] (n = positions * heads) and the overlay
+ * slots (nullable; entries with slot >= 0 need no table row), builds
+ *   send_ids  (device int32 [<= n]): the distinct ids, grouped by owner rank;
+ *   counts    (device int64 [2*world]): counts[o] = ids for owner o (the rest
+ *             is scratch);
+ *   row_index (device int32 [n]): position of each entry's id in send_ids
+ *             (= its row in the reply), -1 for overlay entries.
+ * set_keys/set_vals: device int32 [capacity] scratch, capacity a power of two
+ * >= 2n.  The order inside an owner's group is unspecified; results do not
+ * depend on it.  No reference counterpart: the reference is single-process.
+ */
+ENGRAM_API int engram_shard_requests(const int32_t* ids, const int32_t* slots, int64_t n, int32_t world,
+                                     int32_t* set_keys, int32_t* set_vals, int64_t capacity, int32_t* send_ids,
+                                     int64_t* counts, int32_t* row_index, void* stream);
+
+/*
+ * Owner side: out[k] = the resident row of global id ids[k] from this rank's
+ * shard (local index ids[k] / world; stride bytes per row, 16-byte multiple).
+ * Ids outside the shard give zero rows.
+ */
+ENGRAM_API int engram_shard_gather(const void* shard_rows, int64_t stride, int64_t n_local, const int32_t* ids,
+                                   int64_t n, int32_t world, void* out, void* stream);
 
 /*
  * engram_forward for an explicit list of positions (decode-style lookups: one

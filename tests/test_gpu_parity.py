@@ -311,3 +311,39 @@ def test_forward_at_positions_decode_style_vs_oracle(eb):
     out.backward(torch.from_numpy(grad).to(DEV))
     gref = O.backward(slots, 8, grad, 128, len(ov_ids))
     assert np.array_equal(rows_var.grad.cpu().numpy().view(np.uint32), gref.view(np.uint32))
+
+
+# ------------------------------------------------------- row-sharded table
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("fmt,dim,mode", [(O.FMT_IQ4_XS, 256, O.MODE_PAIRSUM_ADD_BF16),
+                                          (O.FMT_IQ4_NL, 160, O.MODE_CONCAT_F32),
+                                          (O.FMT_F32, 128, O.MODE_CONCAT_F32)])
+def test_row_sharded_table_matches_resident_table(eb, world, fmt, dim, mode):
+    """W ranks emulated on one GPU: each rank's forward over rows fetched from
+    the owners (id mod W) equals the forward over the whole resident table."""
+    from engraft_ngram_b200.shard import ShardedTable, local_exchange
+    rng = np.random.default_rng(world * 7 + fmt)
+    spec = random_spec(fmt, dim, 30_001, 5 + world)
+    full = device_table(eb, spec)
+    shards = [ShardedTable.from_full(full, world, r) for r in range(world)]
+    ex = local_exchange(shards)
+    T = 1500
+    ov_ids = np.unique(rng.integers(0, 30_001, size=700)).astype(np.int32)
+    rows_var = torch.from_numpy((rng.standard_normal((len(ov_ids), dim)) * 0.01).astype(np.float32)).to(DEV)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    for r in range(world):
+        toks = zipf_tokens(rng, T)
+        ss = FX.seg_starts(np.sort(rng.integers(0, 5, size=T)))
+        ids = spec.ids(toks, seg_start=ss)
+        ov_ids_local = ov_ids
+        if mode == O.MODE_CONCAT_F32:
+            ref, _ = O.forward(fmt, dim, spec.raw, ids, 8, rows_var.cpu().numpy(), ov_ids_local, mode)
+            out = torch.empty(T, 16, dim, device=DEV)
+        else:
+            res = O.bf16_bits((rng.standard_normal((T, 8 * dim)) * 0.5).astype(np.float32))
+            ref, _ = O.forward(fmt, dim, spec.raw, ids, 8, rows_var.cpu().numpy(), ov_ids_local, mode, residual=res)
+            out = torch.from_numpy(res.view(np.int16)).to(DEV).view(torch.bfloat16)
+        shards[r].forward(toks, torch.from_numpy(ss), omap, rows_var, out, mode, ex)
+        got = out.view(torch.int32).cpu().numpy() if mode == O.MODE_CONCAT_F32 else out.view(torch.int16).cpu().numpy()
+        want = ref.reshape(T, -1).view(np.int32) if mode == O.MODE_CONCAT_F32 else ref.view(np.int16)
+        assert np.array_equal(got.reshape(want.shape), want), r

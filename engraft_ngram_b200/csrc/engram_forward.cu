@@ -693,13 +693,19 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         gid1 = head_lane ? hash_ctx(T, c1, pm.at(i1), lane) : 0;
         if (head_lane) pr1 = probe_start(OV, gid1);
     }
+    int32_t row1 = head_lane && i1 < n ? pm.row(i1, lane, G::NH, gid1) : 0;
+    // tokens (and gathered-row indices) of position k+2 load one iteration ahead
     TokCtx c2{};
-    if (i1 + nw < n) c2 = load_ctx(T, tokens, seg_start, pm.at(i1 + nw));
+    int32_t r2 = 0;
+    if (i1 + nw < n) {
+        c2 = load_ctx(T, tokens, seg_start, pm.at(i1 + nw));
+        if (pm.rix && head_lane) r2 = __ldg(pm.rix + (i1 + nw) * G::NH + lane);
+    }
     unsigned long long hits = 0;
     int b = 0;
     for (; i < n; i += nw) {
         const int64_t inext = i + nw;
-        if (inext < n) issue(inext, head_lane ? pm.row(inext, lane, G::NH, gid1) : 0, b ^ 1);
+        if (inext < n) issue(inext, row1, b ^ 1);
         else cp_async_commit_f();
         if (head_lane) {
             if (ids_out) ids_out[i * G::NH + lane] = gid;
@@ -744,7 +750,11 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         if (i2 < n) {
             gid1 = head_lane ? hash_ctx(T, c2, pm.at(i2), lane) : 0;
             if (head_lane) pr1 = probe_start(OV, gid1);
-            if (i2 + nw < n) c2 = load_ctx(T, tokens, seg_start, pm.at(i2 + nw));
+            row1 = pm.rix ? (r2 < 0 ? 0 : r2) : gid1;
+            if (i2 + nw < n) {
+                c2 = load_ctx(T, tokens, seg_start, pm.at(i2 + nw));
+                if (pm.rix && head_lane) r2 = __ldg(pm.rix + (i2 + nw) * G::NH + lane);
+            }
         }
         b ^= 1;
     }

@@ -91,6 +91,10 @@ SIGNATURES = {
                                           C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),
     "engram_adam_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                    C.c_double, C.c_double, C.c_double, C.c_double, C.c_float, C.c_void_p]),
+    "engram_scan_hits_workspace_bytes": (C.c_int64, [C.c_int64]),
+    "engram_scan_hits": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32,
+                                   C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
     "engram_selftest_mod": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),
     "engram_launch_count": (C.c_int64, []),
 }

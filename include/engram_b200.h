@@ -296,6 +296,27 @@ ENGRAM_API int engram_adam_step(float* p, const float* g, float* m, float* v, co
                      int64_t step, double lr, double beta1, double beta2, double eps, float reg_scale,
                      void* stream);
 
+/* Scratch bytes engram_scan_hits needs for n positions. */
+ENGRAM_API int64_t engram_scan_hits_workspace_bytes(int64_t n);
+
+/*
+ * Bulk hash + overlay hit scan over positions t0..t0+n-1 of `tokens` (no
+ * segments; tokens before t0 are context), replacing damage.scan_hits +
+ * ngram_rows (engraft/damage.py:68-104,168-224).  ov: the map of the overlay
+ * rows sorted ascending (slot k = overlay_sorted[k]; ov->rows is not read);
+ * dnorm: device float [R].  For every position whose rows include at least one
+ * overlay row (and which is not the last one when exclude_last != 0), in
+ * position order: pos_out (int64, pos_base + t), nhit_out (rows matched),
+ * dmax_out / dsum_out (max and numpy-pairwise float32 sum over heads of
+ * matched ? dnorm : 0).  *n_hits (device int64) = number listed; read_count
+ * (device int64 [R]) += reads of each overlay row (all positions).  Outputs
+ * are sized n.  Requires n_heads <= 16.
+ */
+ENGRAM_API int engram_scan_hits(const engram_table* t, const int32_t* tokens, int64_t t0, int64_t n, int64_t pos_base,
+                                int32_t exclude_last, const engram_overlay* ov, const float* dnorm, int64_t* pos_out,
+                                int32_t* nhit_out, float* dmax_out, float* dsum_out, int64_t* n_hits,
+                                int64_t* read_count, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Host self-test of the division magic: out[i] = x[i] % d using exactly the
  * device code path (host arrays).  Lets CPU-only tests check it. */
 ENGRAM_API int engram_selftest_mod(const uint64_t* x, int64_t count, uint32_t d, uint64_t* out);

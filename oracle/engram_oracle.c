@@ -362,3 +362,74 @@ void orc_set_num_threads(int n) {
     (void)n;
 #endif
 }
+
+/* numpy's float32 pairwise sum of a short row (the reduction of
+ * `matched_dnorm.sum(axis=1)`): fewer than 8 terms are added in order from 0;
+ * otherwise 8 running partial sums over strides of 8, combined as
+ * ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the remaining terms in order. */
+static float np_pairwise_sum_f32(const float* a, int n) {
+    if (n < 8) {
+        float res = 0.0f;
+        for (int i = 0; i < n; i++) res = res + a[i];
+        return res;
+    }
+    float r[8];
+    for (int k = 0; k < 8; k++) r[k] = a[k];
+    int i = 8;
+    for (; i + 8 <= n; i += 8)
+        for (int k = 0; k < 8; k++) r[k] = r[k] + a[i + k];
+    float res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+    for (; i < n; i++) res = res + a[i];
+    return res;
+}
+
+/*
+ * Bulk hash + overlay hit scan, engraft/damage.py:168-224 (with ngram_rows
+ * :68-104 over the whole token array: the reference's 8M-token blocks carry 2
+ * tokens of overlap, iter_blocks :107-121, so the ids are those of one pass).
+ * For every position: its n_heads global rows; matched = row in the sorted
+ * overlay; read_count[overlay index] += 1 for every match (all positions);
+ * positions with >= 1 match, except the last one (t = n-1), are listed with
+ * n_hit_rows, dnorm_max = max over heads of (matched ? dnorm : 0) and
+ * dnorm_sum = numpy's pairwise float32 sum of the same row.  Returns the number
+ * of listed positions.
+ */
+int64_t orc_scan_hits(const int32_t* tokens, int64_t n, int32_t ngram_size, int32_t hpn, const uint64_t* mult,
+                      const int64_t* head_sizes, const int64_t* head_offsets, int64_t eos,
+                      const int32_t* ov_sorted, const float* dnorm_sorted, int64_t R, int64_t* pos_out,
+                      int32_t* nhit_out, float* dmax_out, float* dsum_out, int64_t* read_count) {
+    const int n_heads = (ngram_size - 1) * hpn;
+    int32_t* ids = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n > 0 ? n : 1) * n_heads);
+    orc_hash(tokens, NULL, 0, n, ngram_size, hpn, mult, head_sizes, head_offsets, eos, ids);
+    memset(read_count, 0, sizeof(int64_t) * (size_t)R);
+    int64_t m = 0;
+    float v[32];
+    for (int64_t t = 0; t < n; t++) {
+        int nh = 0;
+        float dmax = 0.0f;
+        for (int h = 0; h < n_heads; h++) {
+            const int32_t g = ids[t * n_heads + h];
+            int64_t lo = 0, hi = R;
+            while (lo < hi) {
+                int64_t mid = (lo + hi) / 2;
+                if (ov_sorted[mid] < g) lo = mid + 1; else hi = mid;
+            }
+            const int match = lo < R && ov_sorted[lo] == g;
+            v[h] = match ? dnorm_sorted[lo] : 0.0f;
+            if (match) {
+                read_count[lo] += 1;
+                nh++;
+            }
+            if (v[h] > dmax || h == 0) dmax = (h == 0) ? v[h] : (v[h] > dmax ? v[h] : dmax);
+        }
+        if (nh > 0 && t < n - 1) {
+            pos_out[m] = t;
+            nhit_out[m] = nh;
+            dmax_out[m] = dmax;
+            dsum_out[m] = np_pairwise_sum_f32(v, n_heads);
+            m++;
+        }
+    }
+    free(ids);
+    return m;
+}

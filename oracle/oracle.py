@@ -192,3 +192,31 @@ def bf16_bits(x) -> np.ndarray:
 
 def bf16_to_f32(bits) -> np.ndarray:
     return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def scan_hits(tokens, ngram_size, hpn, mult, head_sizes, head_offsets, eos, overlay_sorted, dnorm_sorted) -> dict:
+    """engraft/damage.py:168-224 restated: hit positions of the overlay rows and
+    per-row read counts (dict with the reference's keys)."""
+    L = lib()
+    if not hasattr(L, "_scan_typed"):
+        p, i32, i64 = C.c_void_p, C.c_int32, C.c_int64
+        L.orc_scan_hits.argtypes = [p, i64, i32, i32, p, p, p, i64, p, p, i64, p, p, p, p, p]
+        L.orc_scan_hits.restype = i64
+        L._scan_typed = True
+    tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+    n = tokens.shape[0]
+    ov = np.ascontiguousarray(overlay_sorted, dtype=np.int32)
+    dn = np.ascontiguousarray(dnorm_sorted, dtype=np.float32)
+    m = np.zeros(8, dtype=np.uint64)
+    m[:len(mult)] = np.asarray([int(x) for x in mult], dtype=np.uint64)
+    sizes = np.ascontiguousarray(head_sizes, dtype=np.int64)
+    offs = np.ascontiguousarray(head_offsets, dtype=np.int64)
+    pos = np.empty(max(n, 1), np.int64)
+    nh = np.empty(max(n, 1), np.int32)
+    dmax = np.empty(max(n, 1), np.float32)
+    dsum = np.empty(max(n, 1), np.float32)
+    rc = np.empty(max(len(ov), 1), np.int64)
+    k = L.orc_scan_hits(_ptr(tokens), n, ngram_size, hpn, _ptr(m), _ptr(sizes), _ptr(offs), int(eos), _ptr(ov),
+                        _ptr(dn), len(ov), _ptr(pos), _ptr(nh), _ptr(dmax), _ptr(dsum), _ptr(rc))
+    return {"pos": pos[:k], "n_hit_rows": nh[:k], "dnorm_max": dmax[:k], "dnorm_sum": dsum[:k],
+            "read_count": rc[:len(ov)], "n_tokens": n}

@@ -237,6 +237,23 @@ def main(ref_root: str) -> None:
         out["pleo_data"] = data
         out["pleo_bytes"] = np.frombuffer(pth.read_bytes(), dtype=np.uint8).copy()
 
+    # ---- 7. bulk hash + overlay hit scan (engraft/damage.py:168-224) -------
+    ft7 = FakeTable(seed=7)
+    toks = FX.synthetic_corpus(20_000, seed=1, eos=ft7.eos_token_id)
+    big, tri = damage.ngram_rows(toks, ft7)
+    rows16 = np.concatenate([big, tri], axis=1)
+    rng = np.random.default_rng(77)
+    picks = rows16[rng.integers(0, 19_999, size=60), rng.integers(0, 16, size=60)]
+    overlay_sorted = np.unique(np.concatenate([picks, rng.integers(0, 80_000, size=40)])).astype(np.int32)
+    dnorm_sorted = (rng.random(len(overlay_sorted)) * 0.3).astype(np.float32)
+    dnorm_sorted[::7] = 0.0  # unchanged rows
+    hits = damage.scan_hits(toks, ft7, overlay_sorted, dnorm_sorted, block=4_000)
+    out["scan_tokens"] = toks
+    out["scan_overlay"] = overlay_sorted
+    out["scan_dnorm"] = dnorm_sorted
+    for k in ("pos", "n_hit_rows", "dnorm_max", "dnorm_sum", "read_count"):
+        out[f"scan_{k}"] = hits[k]
+
     meta = dict(reference_root=str(ref_root), torch=torch.__version__, numpy=np.__version__,
                 gguf=getattr(gguf, "__version__", "0.19.0"))
     out["meta"] = np.array(repr(meta))

@@ -347,3 +347,33 @@ def test_row_sharded_table_matches_resident_table(eb, world, fmt, dim, mode):
         got = out.view(torch.int32).cpu().numpy() if mode == O.MODE_CONCAT_F32 else out.view(torch.int16).cpu().numpy()
         want = ref.reshape(T, -1).view(np.int32) if mode == O.MODE_CONCAT_F32 else ref.view(np.int16)
         assert np.array_equal(got.reshape(want.shape), want), r
+
+
+# ------------------------------------------------- bulk hash + overlay hit scan
+def test_scan_hits_matches_reference_golden(eb, golden):
+    p = FX.fake_table_params(seed=7)
+    t = hash_only_table(eb, p)
+    for block in (20_000, 4_000, 777):
+        got = eb.scan_hits(golden["scan_tokens"], t, golden["scan_overlay"], golden["scan_dnorm"], block=block)
+        assert np.array_equal(got["pos"], golden["scan_pos"]), block
+        assert np.array_equal(got["n_hit_rows"], golden["scan_n_hit_rows"])
+        assert np.array_equal(got["dnorm_max"].view(np.uint32), golden["scan_dnorm_max"].view(np.uint32))
+        assert np.array_equal(got["dnorm_sum"].view(np.uint32), golden["scan_dnorm_sum"].view(np.uint32))
+        assert np.array_equal(got["read_count"], golden["scan_read_count"])
+
+
+def test_scan_hits_large_corpus_vs_oracle(eb):
+    rng = np.random.default_rng(9)
+    p = FX.syn_params()
+    t = hash_only_table(eb, p)
+    toks = zipf_tokens(rng, 2_000_000)
+    toks[rng.integers(0, toks.size, size=5000)] = p["eos"]
+    ids = O.hash_ids(toks[:200_000], 3, 8, p["mult"], p["head_sizes"], p["head_offsets"], p["eos"])
+    ov = np.unique(np.concatenate([np.unique(ids)[::50], rng.integers(0, sum(FX.SYN_HEAD_SIZES), size=300)]))
+    dn = (rng.random(len(ov)) * 0.2).astype(np.float32)
+    got = eb.scan_hits(toks, t, ov, dn, block=300_000)
+    ref = O.scan_hits(toks, 3, 8, p["mult"], p["head_sizes"], p["head_offsets"], p["eos"], ov, dn)
+    for k in ("pos", "n_hit_rows", "read_count"):
+        assert np.array_equal(got[k], ref[k]), k
+    for k in ("dnorm_max", "dnorm_sum"):
+        assert np.array_equal(got[k].view(np.uint32), ref[k].view(np.uint32)), k

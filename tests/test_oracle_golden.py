@@ -106,3 +106,15 @@ def test_pack_layouts_roundtrip(golden):
     pk = O.pack(O.FMT_IQ4_XS, 256, xs)
     assert pk.shape == (48, 144)
     assert np.array_equal(pk[:, :128], xs[:, 8:]) and np.array_equal(pk[:, 128:136], xs[:, :8])
+
+
+def test_scan_hits_matches_reference(golden):
+    # engraft/damage.py:168-224 on the reference's own test corpus shape
+    p = FX.fake_table_params(seed=7)
+    got = O.scan_hits(golden["scan_tokens"], p["ngram_size"], p["hpn"], p["mult"], p["head_sizes"],
+                      p["head_offsets"], p["eos"], golden["scan_overlay"], golden["scan_dnorm"])
+    assert np.array_equal(got["pos"], golden["scan_pos"])
+    assert np.array_equal(got["n_hit_rows"], golden["scan_n_hit_rows"])
+    assert np.array_equal(got["dnorm_max"].view(np.uint32), golden["scan_dnorm_max"].view(np.uint32))
+    assert np.array_equal(got["dnorm_sum"].view(np.uint32), golden["scan_dnorm_sum"].view(np.uint32))
+    assert np.array_equal(got["read_count"], golden["scan_read_count"])

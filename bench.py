@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=DEFAULT_STEPS)
     ap.add_argument("--warmup", type=int, default=DEFAULT_WARMUP)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS) + ["scan"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -448,6 +448,62 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_scan(args, device):
+    """Throughput of the bulk hash + overlay hit scan (engraft/damage.py:168-224) on
+    a device-resident Zipf corpus: positions/s (16 rows each)."""
+    import ctypes as C
+    import torch
+    import engraft_ngram_b200 as eb
+    from engraft_ngram_b200 import _lib as L
+    from engraft_ngram_b200.table import synthetic_head_sizes, synthetic_multipliers
+    n = 64 * 1024 * 1024
+    sizes = synthetic_head_sizes(FULL_ROWS)
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
+    dt = eb.DeviceTable(torch.zeros(64, dtype=torch.uint8, device=device), L.FMT_F32, 4, sizes, offs,
+                        synthetic_multipliers(args.seed), EOS, n_rows=FULL_ROWS, hash_only=True)
+    g = torch.Generator(device=device)
+    g.manual_seed(args.seed)
+    toks = zipf_tokens(torch, n, g, zipf_cdf(torch, device))
+    ids = dt.global_ids(toks[: 1 << 20]).reshape(-1)
+    ov = torch.unique(ids)[::7][:14_032].to(torch.int32)  # s0b-sized overlay of rows the corpus reads
+    R = ov.numel()
+    omap = eb.OverlayMap(ov, device)
+    ovd = L.EngramOverlay(None, R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
+    dnorm = torch.rand(R, generator=g, device=device) * 0.2
+    lib = L.load()
+    wsb = int(lib.engram_scan_hits_workspace_bytes(n))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=device)
+    pos = torch.empty(n, dtype=torch.int64, device=device)
+    nh = torch.empty(n, dtype=torch.int32, device=device)
+    dmax = torch.empty(n, dtype=torch.float32, device=device)
+    dsum = torch.empty(n, dtype=torch.float32, device=device)
+    nhits = torch.zeros(1, dtype=torch.int64, device=device)
+    rc = torch.zeros(R, dtype=torch.int64, device=device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+
+    def once():
+        st = lib.engram_scan_hits(C.byref(dt.ctable), toks.data_ptr(), 0, n, 0, 1, C.byref(ovd), dnorm.data_ptr(),
+                                  pos.data_ptr(), nh.data_ptr(), dmax.data_ptr(), dsum.data_ptr(), nhits.data_ptr(),
+                                  rc.data_ptr(), ws.data_ptr(), wsb, stream)
+        L.check(st, "engram_scan_hits")
+
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    K = max(1, min(args.steps, 50))
+    e0.record()
+    for _ in range(K):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    line = {"metric": "overlay hit scan positions/s (damage.scan_hits, 64M-token Zipf corpus, 320M-row table)",
+            "value": n / (ms * 1e-3), "unit": "positions/s", "ms_per_scan": ms, "n_hits": int(nhits.item()),
+            "overlay_rows": R, "config": {"workload": "scan: 67,108,864 tokens resident, 16 rows each"}}
+    print(json.dumps(line), flush=True)
+
+
 def config_json(cfg, args):
     return {"workload": f"{args.config}: {cfg['seqs']}x{cfg['seq_len']} tokens/GPU, Zipf(1.1) over {VOCAB}, "
                         f"{cfg['rows']}-row x {cfg['dim']} {cfg['fmt']} table, R={cfg['R']} overlay rows, "
@@ -463,6 +519,10 @@ START = time.perf_counter()
 
 def main():
     args = parse()
+    if args.config == "scan":
+        import torch
+        run_scan(args, torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
+        return
     cfg = dict(CONFIGS[args.config])
     if args.table_rows:
         cfg["rows"] = args.table_rows

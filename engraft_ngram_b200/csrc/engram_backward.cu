@@ -312,6 +312,12 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restric
     const int chunks16 = row_bytes >> 4;
     const int rps = kStageBytes / row_bytes;  // rows per stage
     const uint4* g16 = reinterpret_cast<const uint4*>(grad);
+    // when the 16-byte pieces of a row divide the block, every thread copies one
+    // fixed piece of every r_step-th row (no division in the copy loop)
+    const bool fixed_piece = chunks16 <= kRedThreads && (kRedThreads % chunks16) == 0;
+    const int my_p = fixed_piece ? tid % chunks16 : 0;
+    const int my_r = fixed_piece ? tid / chunks16 : 0;
+    const int r_step = fixed_piece ? kRedThreads / chunks16 : 1;
 
     const int n_big = counters[kCntBig];
     while (true) {
@@ -356,9 +362,14 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restric
                     uint8_t* buf = smem + (st % kStages) * kStageBytes;
                     const int r0 = st * rps;
                     const int nr = min(rps, mn - r0);
-                    for (int c = tid; c < nr * chunks16; c += kRedThreads) {
-                        const int r = c / chunks16, p = c - r * chunks16;
-                        cp_async16(buf + r * row_bytes + p * 16, g16 + m_off[r0 + r] + p);
+                    if (fixed_piece) {  // thread copies piece my_p of rows my_r, my_r + r_step, ...
+                        for (int r = my_r; r < nr; r += r_step)
+                            cp_async16(buf + r * row_bytes + my_p * 16, g16 + m_off[r0 + r] + my_p);
+                    } else {
+                        for (int c = tid; c < nr * chunks16; c += kRedThreads) {
+                            const int r = c / chunks16, p = c - r * chunks16;
+                            cp_async16(buf + r * row_bytes + p * 16, g16 + m_off[r0 + r] + p);
+                        }
                     }
                 }
                 cp_async_commit();

@@ -746,6 +746,12 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         // advance the pipeline: k+1's probe resolves, k+2 is hashed and probed, k+3's tokens load
         gid = gid1;
         slot = (inext < n && head_lane) ? probe_finish(OV, gid1, pr1) : -1;
+        if (slot >= 0) {  // next position's overlay row: pull it into L1 while this iteration's copies land
+            const char* orow_p = reinterpret_cast<const char*>(OV.rows + (int64_t)slot * DIM);
+#pragma unroll
+            for (int l = 0; l < DIM * 4 / 128; l++)
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(orow_p + 128 * l));
+        }
         const int64_t i2 = inext + nw;
         if (i2 < n) {
             gid1 = head_lane ? hash_ctx(T, c2, pm.at(i2), lane) : 0;

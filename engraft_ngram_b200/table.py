@@ -21,8 +21,11 @@ from . import _lib as L
 
 class DeviceTable:
     def __init__(self, rows: torch.Tensor, fmt: int, dim: int, head_sizes, head_offsets, mult, eos_token_id: int,
-                 ngram_size: int = 3, heads_per_ngram: int = 8, n_rows: int | None = None, source=None):
-        """rows: uint8 CUDA tensor holding n_rows resident rows (engram_row_stride bytes each)."""
+                 ngram_size: int = 3, heads_per_ngram: int = 8, n_rows: int | None = None, source=None,
+                 hash_only: bool = False):
+        """rows: uint8 CUDA tensor holding n_rows resident rows (engram_row_stride bytes each).
+        hash_only=True: the table's addressing constants only (for hashing and
+        scans); rows may be any small CUDA buffer and must never be gathered."""
         if not rows.is_cuda:
             raise RuntimeError("DeviceTable rows must live on a CUDA device")
         lib = L.load()
@@ -34,7 +37,8 @@ class DeviceTable:
         self.dim = int(dim)
         self.row_stride = stride
         self.n_rows = int(n_rows if n_rows is not None else rows.numel() // stride)
-        if rows.numel() < self.n_rows * stride:
+        self.hash_only = bool(hash_only)
+        if not hash_only and rows.numel() < self.n_rows * stride:
             raise ValueError(f"rows holds {rows.numel()} bytes, need {self.n_rows * stride}")
         self.ngram_size = int(ngram_size)
         self.heads_per_ngram = int(heads_per_ngram)
@@ -159,6 +163,8 @@ class DeviceTable:
 
     def gather_rows(self, ids) -> torch.Tensor:
         """float32 [n, dim] dequantised rows by global id (engram_gather_rows)."""
+        if self.hash_only:
+            raise RuntimeError("this DeviceTable holds addressing constants only (hash_only=True)")
         ids = _as_i32(ids, self.device).reshape(-1)
         if ids.numel():
             lo, hi = int(ids.min()), int(ids.max())

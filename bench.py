@@ -556,6 +556,7 @@ def main():
     K = args.steps
     f0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     f1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    b1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         if ddist is not None:
@@ -569,6 +570,7 @@ def main():
             f1[k].record()
             if cfg["bwd"] and wl.R:
                 wl.backward()
+                b1[k].record()
                 wl.optimizer(ddist)
         e1.record()
         torch.cuda.synchronize()
@@ -577,6 +579,7 @@ def main():
             dist.barrier()
     ms = e0.elapsed_time(e1) / K
     fwd_ms = sum(a.elapsed_time(b) for a, b in zip(f0, f1)) / K
+    bwd_ms = sum(a.elapsed_time(b) for a, b in zip(f1, b1)) / K if cfg["bwd"] and wl.R else 0.0
     t = torch.tensor([ms, fwd_ms], device=device, dtype=torch.float64)
     if ddist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -600,6 +603,7 @@ def main():
             "algorithmic_bytes_per_step_per_gpu": step_bytes,
             "bytes_breakdown": nbytes,
             "hit_fraction": nbytes["hits"] / (16 * wl.n_out),
+            "phase_ms": {"forward": fwd_ms, "backward": bwd_ms, "optimizer_and_exchange": ms - fwd_ms - bwd_ms},
             "us_per_step": ms * 1e3,
             "roofline": {"kernel": "engram_forward (k_forward_pairsum_fixed<IQ4_XS,256>)" if wl.mode else "engram_forward (k_forward_concat)",
                          "bound": "hbm", "achieved": fwd_gbs, "peak": peak, "unit": "GB/s", "frac": fwd_gbs / peak,

@@ -33,12 +33,15 @@ def needs_build() -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(verbose: bool = False, force: bool = False) -> Path:
-    if not force and not needs_build():
+def build(verbose: bool = False, force: bool = False, out: Path | None = None, defines=()) -> Path:
+    """Compiles the library (to `out`, default the in-tree libengram_b200.so);
+    `defines` are extra -D tuning macros."""
+    target = Path(out) if out is not None else LIB
+    if out is None and not force and not needs_build():
         return LIB
-    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
+    cmd = [nvcc(), *ARCH, *(f"-D{d}" for d in defines), "-lineinfo", "-O3", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "-I", str(INCLUDE), "-I", str(CSRC),
-           *(str(CSRC / s) for s in SOURCES), "-o", str(LIB) + ".tmp", "-lcudart"]
+           *(str(CSRC / s) for s in SOURCES), "-o", str(target) + ".tmp", "-lcudart"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -46,8 +49,8 @@ def build(verbose: bool = False, force: bool = False) -> Path:
         raise RuntimeError(f"nvcc failed:\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
     if verbose:
         sys.stderr.write(res.stderr)
-    os.replace(str(LIB) + ".tmp", LIB)
-    return LIB
+    os.replace(str(target) + ".tmp", target)
+    return target
 
 
 if __name__ == "__main__":

@@ -33,10 +33,16 @@ constexpr int kRsItems = 16;
 constexpr int kRsTile = kRsThreads * kRsItems;
 constexpr int kScanThreads = 1024;
 constexpr int kRedThreads = 256;
-constexpr int kChunk = 256;           // nominal sorted entries per work chunk (snapped to segment starts)
-constexpr int kMetaCap = 4096;        // entries whose row offsets and keys a block stages at a time
-constexpr int kStageBytes = 16384;    // rows per pipeline stage (>= 4 rows of <= 4 KB)
-constexpr int kStages = 4;
+#ifndef ENGRAM_RED_CHUNK
+#define ENGRAM_RED_CHUNK 256
+#endif
+#ifndef ENGRAM_RED_STAGES
+#define ENGRAM_RED_STAGES 4
+#endif
+constexpr int kChunk = ENGRAM_RED_CHUNK;  // nominal sorted entries per work chunk (snapped to segment starts)
+constexpr int kMetaCap = 4096;            // entries whose row offsets and keys a block stages at a time
+constexpr int kStageBytes = 16384;        // rows per pipeline stage (>= 4 rows of <= 4 KB)
+constexpr int kStages = ENGRAM_RED_STAGES;
 constexpr int kRedSmem = kStages * kStageBytes + kMetaCap * 4 + (kMetaCap + 1) * 4;
 
 constexpr int kBigChunk = 4 * kChunk;  // chunks longer than this (long segments) are scheduled first
@@ -384,29 +390,43 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restric
                 const uint8_t* buf = smem + (st % kStages) * kStageBytes;
                 const int r0 = st * rps;
                 const int nr = min(rps, mn - r0);
+                // 4 rows per step: their shared-memory loads issue together, the adds stay in row order
+                constexpr int U = 4;
 #pragma unroll 1
-                for (int r = 0; r < nr; r++) {
+                for (int r = 0; r < nr; r += U) {
+                    float x[U][NJ];
+                    int32_t kk[U + 1];
 #pragma unroll
-                    for (int q = 0; q < NJ; q++) {
-                        const int c = tid + kRedThreads * q;
-                        if (c < dim) {
-                            float x;
-                            if (MODE == ENGRAM_MODE_CONCAT_F32)
-                                x = reinterpret_cast<const float*>(buf + r * row_bytes)[c];
-                            else
-                                x = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(buf + r * row_bytes)[c] << 16);
-                            acc[q] = __fadd_rn(acc[q], x);
-                        }
-                    }
-                    const int e = r0 + r;
-                    const int32_t key = m_key[e];
-                    if (m_key[e + 1] != key) {  // last entry of its segment
-                        float* dst = grad_rows + (int64_t)key * dim;
+                    for (int u = 0; u <= U; u++) kk[u] = (r + u <= nr) ? m_key[r0 + r + u] : -2;
+#pragma unroll
+                    for (int u = 0; u < U; u++) {
 #pragma unroll
                         for (int q = 0; q < NJ; q++) {
                             const int c = tid + kRedThreads * q;
-                            if (c < dim) dst[c] = acc[q];
-                            acc[q] = 0.f;
+                            x[u][q] = 0.f;
+                            if (r + u < nr && c < dim) {
+                                const uint8_t* row = buf + (r + u) * row_bytes;
+                                if (MODE == ENGRAM_MODE_CONCAT_F32)
+                                    x[u][q] = reinterpret_cast<const float*>(row)[c];
+                                else
+                                    x[u][q] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(row)[c] << 16);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < U; u++) {
+                        if (r + u < nr) {
+#pragma unroll
+                            for (int q = 0; q < NJ; q++) acc[q] = __fadd_rn(acc[q], x[u][q]);
+                            if (kk[u + 1] != kk[u]) {  // last entry of its segment
+                                float* dst = grad_rows + (int64_t)kk[u] * dim;
+#pragma unroll
+                                for (int q = 0; q < NJ; q++) {
+                                    const int c = tid + kRedThreads * q;
+                                    if (c < dim) dst[c] = acc[q];
+                                    acc[q] = 0.f;
+                                }
+                            }
                         }
                     }
                 }

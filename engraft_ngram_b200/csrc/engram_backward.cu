@@ -10,11 +10,12 @@
 //      __match_any_sync groups plus per-warp digit counts (no comparison sort);
 //      block offsets come from a per-digit row scan (256 blocks);
 //   2. segment starts per slot from the sorted keys;
-//   3. one streaming segmented reduction: blocks take segment-aligned chunks
-//      of the sorted entries (dynamically), stage their row offsets in shared
-//      memory, stream the rows through a kStages-deep cp.async ring, and every
-//      thread adds its own columns in order, writing a slot's row when its
-//      segment ends.
+//   3. one segmented reduction in which every warp runs its own jobs.  A short
+//      job is a chunk of whole segments: lane l copies and adds its own 16-byte
+//      column vectors of every row through a private cp.async ring, and writes
+//      a slot's row when its segment ends.  A segment longer than the chunk
+//      size is split by columns instead: one job per 64-byte slice, so the
+//      slices of a hot slot stream on many SMs at once.
 // Every term is added from +0 in ascending (t, h) order in fp32, so the result
 // is bit-identical to the reference and independent of scheduling.
 #include <algorithm>
@@ -32,23 +33,36 @@ constexpr int kRsWarps = kRsThreads / 32;
 constexpr int kRsItems = 16;
 constexpr int kRsTile = kRsThreads * kRsItems;
 constexpr int kScanThreads = 1024;
-constexpr int kRedThreads = 256;
-#ifndef ENGRAM_RED_CHUNK
-#define ENGRAM_RED_CHUNK 256
-#endif
-#ifndef ENGRAM_RED_STAGES
-#define ENGRAM_RED_STAGES 4
-#endif
-constexpr int kChunk = ENGRAM_RED_CHUNK;  // nominal sorted entries per work chunk (snapped to segment starts)
-constexpr int kMetaCap = 4096;            // entries whose row offsets and keys a block stages at a time
-constexpr int kStageBytes = 16384;        // rows per pipeline stage (>= 4 rows of <= 4 KB)
-constexpr int kStages = ENGRAM_RED_STAGES;
-constexpr int kRedSmem = kStages * kStageBytes + kMetaCap * 4 + (kMetaCap + 1) * 4;
+// segmented reduction
+constexpr int kRedWarps = 2;         // warps per block; each warp runs its own jobs
+constexpr int kWarpSmem = 20480;     // shared memory per warp
+constexpr int kRedSmem = kRedWarps * kWarpSmem;
+constexpr int kMinChunk = 64, kMaxChunk = 2048;  // short-chunk size bounds (entries)
+constexpr int kSliceBytes = 64;      // column slice of a long-segment job
+constexpr int kLongGI = 7;           // 32-row groups in flight in a long job
+constexpr int kLongRingGroups = kLongGI + 1;
+constexpr int kLongValSlots = 2 * kLongGI + 1;
+static_assert(kLongRingGroups * 32 * kSliceBytes + kLongValSlots * 32 * 4 <= kWarpSmem, "long-job ring");
 
-constexpr int kBigChunk = 4 * kChunk;  // chunks longer than this (long segments) are scheduled first
+// Short-chunk ring: lane-owned 16-byte column vectors, NV per lane.
+template <int NV>
+struct ShortRing {
+    static constexpr int D = 32 / NV;                           // rows in flight
+    static constexpr int U = NV <= 2 ? 4 : (NV == 4 ? 2 : 1);  // rows per commit group
+    static constexpr int GI = D / U;                            // commit groups in flight
+    static constexpr int ROWS = D + U;                          // ring rows: one spare batch
+    static_assert(ROWS * NV * 512 <= kWarpSmem, "short-chunk ring");
+};
 
 // counters[] in the workspace
-constexpr int kCntHits = 0, kCntChunkNext = 1, kCntBig = 2, kCntBigNext = 3;
+constexpr int kCntHits = 0, kCntJobNext = 1, kCntLong = 2, kCntChunks = 3;
+
+// Entries per short chunk: about two chunks per warp of the reduce grid.
+__host__ __device__ inline int64_t chunk_size(int64_t n, int total_warps) {
+    const int64_t per = (n + 2LL * total_warps - 1) / (2LL * total_warps);
+    const int64_t k = (per + 31) / 32 * 32;
+    return k < kMinChunk ? kMinChunk : (k > kMaxChunk ? kMaxChunk : k);
+}
 
 inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
@@ -58,8 +72,9 @@ struct Workspace {
     uint32_t* block_hist;
     uint32_t* digit_tot;
     int32_t* seg_begin;
-    int32_t* chunk_lo;  // [max_chunks + 1] segment-aligned chunk bounds
-    int32_t* big;       // [max_chunks] ids of long chunks
+    int32_t* chunk_lo;  // [max_chunks] short entries of each chunk: [chunk_lo, chunk_hi)
+    int32_t* chunk_hi;
+    int32_t* long_seg;  // [max_chunks] slots with long segments
     int32_t* counters;
     int64_t bytes;
     int nblk;
@@ -83,9 +98,10 @@ Workspace layout(void* base, int64_t N, int64_t R) {
     w.block_hist = reinterpret_cast<uint32_t*>(take(4 * 256 * (int64_t)w.nblk));
     w.digit_tot = reinterpret_cast<uint32_t*>(take(4 * 256));
     w.seg_begin = reinterpret_cast<int32_t*>(take(4 * (R + 1)));
-    const int64_t max_chunks = N / kChunk + 1;
-    w.chunk_lo = reinterpret_cast<int32_t*>(take(4 * (max_chunks + 1)));
-    w.big = reinterpret_cast<int32_t*>(take(4 * max_chunks));
+    const int64_t max_chunks = N / kMinChunk + 2;
+    w.chunk_lo = reinterpret_cast<int32_t*>(take(4 * max_chunks));
+    w.chunk_hi = reinterpret_cast<int32_t*>(take(4 * max_chunks));
+    w.long_seg = reinterpret_cast<int32_t*>(take(4 * max_chunks));
     w.counters = reinterpret_cast<int32_t*>(take(64));
     w.bytes = off;
     return w;
@@ -127,9 +143,9 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_hist(const int32_t* __restric
     __shared__ uint32_t h[256];
     for (int d = threadIdx.x; d < 256; d += kRsThreads) h[d] = 0;
     if (counters && blockIdx.x == 0 && threadIdx.x == 0) {
-        counters[kCntChunkNext] = 0;
-        counters[kCntBig] = 0;
-        counters[kCntBigNext] = 0;
+        counters[kCntJobNext] = 0;
+        counters[kCntLong] = 0;
+        counters[kCntChunks] = 0;
     }
     __syncthreads();
     const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
@@ -274,170 +290,307 @@ __device__ __forceinline__ int64_t snap_to_segment(const int32_t* __restrict__ k
     return __ldg(seg_begin + k + 1);
 }
 
-// chunk_lo[j] = first segment start at or after j*kChunk, j in [0, n_chunks];
-// chunks longer than kBigChunk are listed in big[] so they start first.
+// Work split of the segmented reduction.  With K = the chunk size chosen from
+// the hit count, a segment longer than K entries is "long"; every other entry
+// belongs to a short chunk.  Chunk j spans [first segment start >= j*K, first
+// segment start >= (j+1)*K); a long segment can only sit at a chunk's head or
+// tail (one strictly inside would be shorter than K), so trimming those gives
+// the chunk's short entries [chunk_lo[j], chunk_hi[j]), and each long segment
+// is listed once in long_seg[] by the chunk that holds it.
 __global__ void k_chunks(const int32_t* __restrict__ keys, const int32_t* __restrict__ seg_begin, int32_t* counters,
-                         int32_t* __restrict__ chunk_lo, int32_t* __restrict__ big) {
+                         int total_warps, int32_t* __restrict__ chunk_lo, int32_t* __restrict__ chunk_hi,
+                         int32_t* __restrict__ long_seg) {
     const int64_t n = counters[kCntHits];
-    const int64_t nchunks = (n + kChunk - 1) / kChunk;
-    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j <= nchunks; j += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t lo = snap_to_segment(keys, seg_begin, j * kChunk, n);
-        chunk_lo[j] = (int32_t)lo;
-        if (j < nchunks) {
-            const int64_t hi = snap_to_segment(keys, seg_begin, (j + 1) * kChunk, n);
-            if (hi - lo > kBigChunk) big[atomicAdd(counters + kCntBig, 1)] = (int32_t)j;
+    const int64_t K = chunk_size(n, total_warps);
+    const int64_t nchunks = (n + K - 1) / K;
+    if (blockIdx.x == 0 && threadIdx.x == 0) counters[kCntChunks] = (int32_t)nchunks;
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < nchunks; j += (int64_t)gridDim.x * blockDim.x) {
+        int64_t lo = snap_to_segment(keys, seg_begin, j * K, n);
+        int64_t hi = snap_to_segment(keys, seg_begin, (j + 1) * K, n);
+        if (lo < hi) {  // head segment (it starts at lo)
+            const int32_t k = __ldg(keys + lo);
+            const int64_t end = __ldg(seg_begin + k + 1);
+            if (end - lo > K) {
+                long_seg[atomicAdd(counters + kCntLong, 1)] = k;
+                lo = end;
+            }
         }
+        if (lo < hi) {  // tail segment (it ends at hi)
+            const int32_t k = __ldg(keys + hi - 1);
+            const int64_t begin = __ldg(seg_begin + k);
+            if (hi - begin > K) {
+                long_seg[atomicAdd(counters + kCntLong, 1)] = k;
+                hi = begin;
+            }
+        }
+        chunk_lo[j] = (int32_t)lo;
+        chunk_hi[j] = (int32_t)(hi > lo ? hi : lo);
     }
 }
 
-// Streaming segmented reduction over the slot-sorted entries.  Blocks take
-// chunks of ~kChunk entries whose bounds are snapped to segment starts (so a
-// segment never spans two blocks; a long segment makes one long chunk).  A
-// chunk's row offsets and keys are staged in shared memory, then its rows
-// stream through a kStages-deep cp.async ring while thread c adds column c of
-// every row in order and writes the slot's row when its segment ends.  Slots
-// without entries get zero rows.  NJ = columns per thread (dim <= 256*NJ).
-template <int MODE, int NJ>
-__global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restrict__ keys,
-                                                        const int32_t* __restrict__ vals,
-                                                        const int32_t* __restrict__ seg_begin,
-                                                        const int32_t* __restrict__ chunk_lo,
-                                                        const int32_t* __restrict__ big, int32_t* counters,
-                                                        int64_t R, int dim, int n_heads, int hpn,
-                                                        const uint8_t* __restrict__ grad,
-                                                        float* __restrict__ grad_rows) {
+template <bool F32>
+__device__ __forceinline__ void add_vec16(float2* acc, const uint4 w) {
+    if (F32) {
+        acc[0] = __fadd2_rn(acc[0], make_float2(__uint_as_float(w.x), __uint_as_float(w.y)));
+        acc[1] = __fadd2_rn(acc[1], make_float2(__uint_as_float(w.z), __uint_as_float(w.w)));
+    } else {
+        acc[0] = __fadd2_rn(acc[0], make_float2(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u)));
+        acc[1] = __fadd2_rn(acc[1], make_float2(__uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u)));
+        acc[2] = __fadd2_rn(acc[2], make_float2(__uint_as_float(w.z << 16), __uint_as_float(w.z & 0xffff0000u)));
+        acc[3] = __fadd2_rn(acc[3], make_float2(__uint_as_float(w.w << 16), __uint_as_float(w.w & 0xffff0000u)));
+    }
+}
+
+// One short chunk [lo, hi) of whole segments, by one warp.  Lane l owns the
+// 16-byte column vectors l, l+32, ... (NV of them) of every row: it copies
+// exactly those bytes into its part of the ring and adds exactly those, so the
+// ring needs no cross-lane synchronisation.  D rows are in flight; rows are
+// committed in batches of U.  Row offsets, keys and segment-end flags come in
+// 32-row windows (lane i holds row i of the window), fetched two windows ahead.
+template <int MODE, int NV>
+__device__ __forceinline__ void reduce_short(uint8_t* __restrict__ ring, const int lane, const int64_t lo,
+                                             const int64_t hi, const int32_t* __restrict__ keys,
+                                             const int32_t* __restrict__ vals, const int dim, const int n_heads,
+                                             const int hpn, const uint4* __restrict__ g16,
+                                             float* __restrict__ grad_rows) {
+    using RG = ShortRing<NV>;
+    constexpr int D = RG::D, U = RG::U, GI = RG::GI, ROWS = RG::ROWS;
+    constexpr bool F32 = MODE == ENGRAM_MODE_CONCAT_F32;
+    constexpr int CPV = F32 ? 4 : 8;  // columns per 16-byte vector
+    const int nvec = dim / CPV;
+    const int n = (int)(hi - lo);
+    auto slot = [&](int s, int q) { return ring + (s * NV + q) * 512 + lane * 16; };
+    auto fetch = [&](int w, int32_t& k, int32_t& kn, int32_t& v) {
+        const int64_t e = lo + 32LL * w + lane;
+        k = -1;
+        kn = -1;
+        v = 0;
+        if (e < hi) {
+            k = __ldg(keys + e);
+            v = __ldg(vals + e);
+            if (e + 1 < hi) kn = __ldg(keys + e + 1);
+        }
+    };
+    auto finish = [&](int32_t k, int32_t kn, int32_t v, uint32_t& off, int32_t& key, unsigned& last) {
+        off = k >= 0 ? grad_row16<MODE>(v, dim, n_heads, hpn) : 0u;
+        key = k;
+        last = __ballot_sync(kFull, k >= 0 && k != kn);
+    };
+    // A = window being consumed, B = the next one, C = raw loads of the one after
+    uint32_t offA, offB;
+    int32_t keyA, keyB, ck, ckn, cv;
+    unsigned lastA, lastB;
+    {
+        int32_t k0, kn0, v0, k1, kn1, v1;
+        fetch(0, k0, kn0, v0);
+        fetch(1, k1, kn1, v1);
+        fetch(2, ck, ckn, cv);
+        finish(k0, kn0, v0, offA, keyA, lastA);
+        finish(k1, kn1, v1, offB, keyB, lastB);
+    }
+    auto issue = [&](int y, uint32_t off_src, int s) {  // row y of the chunk into ring row s
+        if (y < n) {
+            const uint32_t o = __shfl_sync(kFull, off_src, y & 31);
+#pragma unroll
+            for (int q = 0; q < NV; q++)
+                if (lane + 32 * q < nvec) cp_async16(slot(s, q), g16 + o + lane + 32 * q);
+        }
+    };
+#pragma unroll 1
+    for (int b = 0; b < GI; b++) {  // rows 0 .. D-1, all in window A
+#pragma unroll
+        for (int u = 0; u < U; u++) issue(b * U + u, offA, b * U + u);
+        cp_async_commit();
+    }
+    float2 acc[NV][CPV / 2];
+#pragma unroll
+    for (int q = 0; q < NV; q++)
+#pragma unroll
+        for (int i = 0; i < CPV / 2; i++) acc[q][i] = make_float2(0.f, 0.f);
+    int cs = 0, is = D;  // ring rows of the batch consumed / issued
+#pragma unroll 1
+    for (int x0 = 0; x0 < n; x0 += U) {
+        if (x0 > 0 && (x0 & 31) == 0) {
+            offA = offB;
+            keyA = keyB;
+            lastA = lastB;
+            finish(ck, ckn, cv, offB, keyB, lastB);
+            fetch((x0 >> 5) + 2, ck, ckn, cv);
+        }
+        cp_async_wait<GI - 1>();
+        uint4 v[U][NV];
+#pragma unroll
+        for (int u = 0; u < U; u++)
+#pragma unroll
+            for (int q = 0; q < NV; q++)
+                v[u][q] = (x0 + u < n && lane + 32 * q < nvec) ? *reinterpret_cast<const uint4*>(slot(cs + u, q))
+                                                                : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (x0 + u < n) {
+#pragma unroll
+                for (int q = 0; q < NV; q++) add_vec16<F32>(acc[q], v[u][q]);
+                const int r = (x0 + u) & 31;
+                if ((lastA >> r) & 1u) {  // the row ends its segment: write the slot's gradient row
+                    const int32_t key = __shfl_sync(kFull, keyA, r);
+                    float* dst = grad_rows + (int64_t)key * dim;
+#pragma unroll
+                    for (int q = 0; q < NV; q++) {
+                        if (lane + 32 * q < nvec) {
+                            float4* d4 = reinterpret_cast<float4*>(dst + (lane + 32 * q) * CPV);
+#pragma unroll
+                            for (int i = 0; i < CPV / 4; i++)
+                                d4[i] = make_float4(acc[q][2 * i].x, acc[q][2 * i].y, acc[q][2 * i + 1].x,
+                                                    acc[q][2 * i + 1].y);
+                        }
+#pragma unroll
+                        for (int i = 0; i < CPV / 2; i++) acc[q][i] = make_float2(0.f, 0.f);
+                    }
+                }
+            }
+        }
+        __syncwarp();  // the ring rows refilled below were read in the previous batch
+        const int y0 = x0 + D;
+        const uint32_t osrc = ((y0 >> 5) != (x0 >> 5)) ? offB : offA;
+#pragma unroll
+        for (int u = 0; u < U; u++) issue(y0 + u, osrc, is + u);
+        cp_async_commit();
+        cs += U;
+        if (cs == ROWS) cs = 0;
+        is += U;
+        if (is == ROWS) is = 0;
+    }
+    cp_async_wait<0>();
+}
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+
+// One kSliceBytes column slice of one long segment [a, b) (slot `key`), by one
+// warp.  Lane l copies the slice of rows 32g+l (group g); lane w < words adds
+// 4-byte word w of every row in order.  kLongGI groups are in flight; the flat
+// indices of the rows travel through a per-lane shared-memory queue filled by
+// cp.async 2*kLongGI groups ahead, so no load latency sits on the issue path.
+template <int MODE>
+__device__ __forceinline__ void reduce_long(uint8_t* __restrict__ ws, const int lane, const int64_t a, const int64_t b,
+                                            const int32_t key, const int slice, const int32_t* __restrict__ vals,
+                                            const int dim, const int n_heads, const int hpn,
+                                            const uint4* __restrict__ g16, float* __restrict__ grad_rows) {
+    constexpr bool F32 = MODE == ENGRAM_MODE_CONCAT_F32;
+    constexpr int GI = kLongGI, RG = kLongRingGroups, VS = kLongValSlots, SB = kSliceBytes;
+    uint8_t* ring = ws;
+    int32_t* vq = reinterpret_cast<int32_t*>(ws + RG * 32 * SB);
+    const int row_bytes = F32 ? dim * 4 : dim * 2;
+    const int p0 = slice * (SB / 16);
+    const int np = min(SB / 16, row_bytes / 16 - p0);  // 16-byte pieces in this slice
+    const int words = np * 4;
+    const int n = (int)(b - a);
+    const int ngroups = (n + 31) >> 5;
+    auto load_val = [&](int g) {
+        if (32 * g + lane < n) cp_async4(vq + (g % VS) * 32 + lane, vals + a + 32LL * g + lane);
+    };
+    auto issue_rows = [&](int g) {
+        if (32 * g + lane < n) {
+            const uint32_t o = grad_row16<MODE>(vq[(g % VS) * 32 + lane], dim, n_heads, hpn);
+            uint8_t* dst = ring + ((g % RG) * 32 + lane) * SB;
+            for (int p = 0; p < np; p++) cp_async16(dst + p * 16, g16 + o + p0 + p);
+        }
+    };
+#pragma unroll 1
+    for (int g = 0; g < 2 * GI; g++) load_val(g);
+    cp_async_commit();
+    cp_async_wait<0>();
+#pragma unroll 1
+    for (int g = 0; g < GI; g++) {
+        issue_rows(g);
+        cp_async_commit();
+    }
+    float2 acc = make_float2(0.f, 0.f);
+    float accf = 0.f;
+#pragma unroll 1
+    for (int it = 0; it < ngroups; it++) {
+        cp_async_wait<GI - 1>();
+        __syncwarp();  // other lanes' copies of group it are visible; group it-1's ring rows are free
+        const uint8_t* gp = ring + (it % RG) * 32 * SB + lane * 4;
+        const int nr = min(32, n - 32 * it);
+        if (lane < words) {
+            int r = 0;
+#pragma unroll 1
+            for (; r + 8 <= nr; r += 8) {
+                uint32_t w[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) w[u] = *reinterpret_cast<const uint32_t*>(gp + (r + u) * SB);
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    if (F32) accf = __fadd_rn(accf, __uint_as_float(w[u]));
+                    else acc = __fadd2_rn(acc, make_float2(__uint_as_float(w[u] << 16), __uint_as_float(w[u] & 0xffff0000u)));
+                }
+            }
+#pragma unroll 1
+            for (; r < nr; r++) {
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(gp + r * SB);
+                if (F32) accf = __fadd_rn(accf, __uint_as_float(w));
+                else acc = __fadd2_rn(acc, make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)));
+            }
+        }
+        __syncwarp();
+        issue_rows(it + GI);
+        load_val(it + 2 * GI);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+    if (lane < words) {
+        const int word = p0 * 4 + lane;
+        if (F32) grad_rows[(int64_t)key * dim + word] = accf;
+        else reinterpret_cast<float2*>(grad_rows + (int64_t)key * dim)[word] = acc;
+    }
+}
+
+// Segmented reduction over the slot-sorted entries.  Every warp takes jobs
+// (an atomic counter): first the column slices of the long segments, then the
+// short chunks.  Slots without entries get zero rows.  NV = 16-byte column
+// vectors per lane in short chunks (row bytes <= 512*NV).
+template <int MODE, int NV>
+__global__ void __launch_bounds__(kRedWarps * 32) k_reduce(const int32_t* __restrict__ keys,
+                                                           const int32_t* __restrict__ vals,
+                                                           const int32_t* __restrict__ seg_begin,
+                                                           const int32_t* __restrict__ chunk_lo,
+                                                           const int32_t* __restrict__ chunk_hi,
+                                                           const int32_t* __restrict__ long_seg, int32_t* counters,
+                                                           int64_t R, int dim, int n_heads, int hpn,
+                                                           const uint8_t* __restrict__ grad,
+                                                           float* __restrict__ grad_rows) {
     constexpr int ES = MODE == ENGRAM_MODE_CONCAT_F32 ? 4 : 2;
     extern __shared__ __align__(16) uint8_t smem[];
-    uint32_t* m_off = reinterpret_cast<uint32_t*>(smem + kStages * kStageBytes);
-    int32_t* m_key = reinterpret_cast<int32_t*>(m_off + kMetaCap);
-    __shared__ int s_job;
-    const int tid = threadIdx.x;
-    const int64_t n = counters[kCntHits];
-    const int64_t nchunks = (n + kChunk - 1) / kChunk;
-    const int row_bytes = dim * ES;
-    const int chunks16 = row_bytes >> 4;
-    const int rps = kStageBytes / row_bytes;  // rows per stage
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t* ws = smem + warp * kWarpSmem;
+    const int64_t n_long = counters[kCntLong];
+    const int64_t nchunks = counters[kCntChunks];
+    const int n_slices = (dim * ES + kSliceBytes - 1) / kSliceBytes;
+    const int64_t n_long_jobs = n_long * n_slices;
+    const int64_t n_jobs = n_long_jobs + nchunks;
     const uint4* g16 = reinterpret_cast<const uint4*>(grad);
-    // when the 16-byte pieces of a row divide the block, every thread copies one
-    // fixed piece of every r_step-th row (no division in the copy loop)
-    const bool fixed_piece = chunks16 <= kRedThreads && (kRedThreads % chunks16) == 0;
-    const int my_p = fixed_piece ? tid % chunks16 : 0;
-    const int my_r = fixed_piece ? tid / chunks16 : 0;
-    const int r_step = fixed_piece ? kRedThreads / chunks16 : 1;
-
-    const int n_big = counters[kCntBig];
     while (true) {
-        // long chunks first (their sequential chains are the critical path), then the rest in order
-        if (tid == 0) {
-            int j = -1;
-            const int b = atomicAdd(counters + kCntBigNext, 1);
-            if (b < n_big) {
-                j = big[b];
-            } else {
-                while (true) {
-                    const int c = atomicAdd(counters + kCntChunkNext, 1);
-                    if (c >= nchunks) break;
-                    if (chunk_lo[c + 1] - chunk_lo[c] <= kBigChunk) { j = c; break; }
-                }
-            }
-            s_job = j;
+        int j = 0;
+        if (lane == 0) j = atomicAdd(counters + kCntJobNext, 1);
+        j = __shfl_sync(kFull, j, 0);
+        if (j >= n_jobs) break;
+        if (j < n_long_jobs) {
+            const int32_t key = __ldg(long_seg + j / n_slices);
+            reduce_long<MODE>(ws, lane, __ldg(seg_begin + key), __ldg(seg_begin + key + 1), key, j % n_slices, vals,
+                              dim, n_heads, hpn, g16, grad_rows);
+        } else {
+            const int64_t c = j - n_long_jobs;
+            const int64_t lo = __ldg(chunk_lo + c), hi = __ldg(chunk_hi + c);
+            if (lo < hi) reduce_short<MODE, NV>(ws, lane, lo, hi, keys, vals, dim, n_heads, hpn, g16, grad_rows);
         }
-        __syncthreads();
-        const int64_t j = s_job;
-        __syncthreads();
-        if (j < 0) break;
-        const int64_t lo = chunk_lo[j];
-        const int64_t hi = chunk_lo[j + 1];
-        float acc[NJ];
-#pragma unroll
-        for (int q = 0; q < NJ; q++) acc[q] = 0.f;
-        for (int64_t m0 = lo; m0 < hi; m0 += kMetaCap) {
-            const int mn = (int)(hi - m0 < kMetaCap ? hi - m0 : kMetaCap);
-            for (int e = tid; e <= mn; e += kRedThreads) {
-                if (e < mn) {
-                    m_off[e] = grad_row16<MODE>(__ldg(vals + m0 + e), dim, n_heads, hpn);
-                    m_key[e] = __ldg(keys + m0 + e);
-                } else {
-                    m_key[e] = (m0 + e < hi) ? __ldg(keys + m0 + e) : -1;  // key after the last staged entry
-                }
-            }
-            __syncthreads();
-            const int nst = (mn + rps - 1) / rps;
-            auto issue = [&](int st) {
-                if (st < nst) {
-                    uint8_t* buf = smem + (st % kStages) * kStageBytes;
-                    const int r0 = st * rps;
-                    const int nr = min(rps, mn - r0);
-                    if (fixed_piece) {  // thread copies piece my_p of rows my_r, my_r + r_step, ...
-                        for (int r = my_r; r < nr; r += r_step)
-                            cp_async16(buf + r * row_bytes + my_p * 16, g16 + m_off[r0 + r] + my_p);
-                    } else {
-                        for (int c = tid; c < nr * chunks16; c += kRedThreads) {
-                            const int r = c / chunks16, p = c - r * chunks16;
-                            cp_async16(buf + r * row_bytes + p * 16, g16 + m_off[r0 + r] + p);
-                        }
-                    }
-                }
-                cp_async_commit();
-            };
-#pragma unroll 1
-            for (int st = 0; st < kStages - 1; st++) issue(st);
-#pragma unroll 1
-            for (int st = 0; st < nst; st++) {
-                cp_async_wait<kStages - 2>();
-                __syncthreads();
-                issue(st + kStages - 1);
-                const uint8_t* buf = smem + (st % kStages) * kStageBytes;
-                const int r0 = st * rps;
-                const int nr = min(rps, mn - r0);
-                // 4 rows per step: their shared-memory loads issue together, the adds stay in row order
-                constexpr int U = 4;
-#pragma unroll 1
-                for (int r = 0; r < nr; r += U) {
-                    float x[U][NJ];
-                    int32_t kk[U + 1];
-#pragma unroll
-                    for (int u = 0; u <= U; u++) kk[u] = (r + u <= nr) ? m_key[r0 + r + u] : -2;
-#pragma unroll
-                    for (int u = 0; u < U; u++) {
-#pragma unroll
-                        for (int q = 0; q < NJ; q++) {
-                            const int c = tid + kRedThreads * q;
-                            x[u][q] = 0.f;
-                            if (r + u < nr && c < dim) {
-                                const uint8_t* row = buf + (r + u) * row_bytes;
-                                if (MODE == ENGRAM_MODE_CONCAT_F32)
-                                    x[u][q] = reinterpret_cast<const float*>(row)[c];
-                                else
-                                    x[u][q] = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(row)[c] << 16);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < U; u++) {
-                        if (r + u < nr) {
-#pragma unroll
-                            for (int q = 0; q < NJ; q++) acc[q] = __fadd_rn(acc[q], x[u][q]);
-                            if (kk[u + 1] != kk[u]) {  // last entry of its segment
-                                float* dst = grad_rows + (int64_t)kk[u] * dim;
-#pragma unroll
-                                for (int q = 0; q < NJ; q++) {
-                                    const int c = tid + kRedThreads * q;
-                                    if (c < dim) dst[c] = acc[q];
-                                    acc[q] = 0.f;
-                                }
-                            }
-                        }
-                    }
-                }
-            }
-            cp_async_wait<0>();
-            __syncthreads();  // stage buffers and metadata are reused next
-        }
+        __syncwarp();  // the next job lays the ring out differently
     }
     // slots without entries
-    const int lane = tid & 31;
-    const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + tid) >> 5;
+    const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t s = warp0; s < R; s += nwarps) {
         if (__ldg(seg_begin + s) == __ldg(seg_begin + s + 1)) {
@@ -447,23 +600,44 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce(const int32_t* __restric
     }
 }
 
-int grid_for_chunks(const Workspace& w);
+struct ReduceLaunch {
+    int grid;
+    int total_warps;
+};
 
-template <int MODE, int NJ>
-void launch_reduce(const Workspace& w, const int32_t* keys, const int32_t* vals, int64_t R, int dim, int n_heads,
-                   int hpn, const void* grad, float* grad_rows, cudaStream_t s) {
-    static bool configured[64] = {false};
+// Grid of the reduce kernel: every block that fits at once on every SM.
+template <int MODE, int NV>
+ReduceLaunch reduce_launch() {
+    static int blocks_per_sm[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaFuncSetAttribute(k_reduce<MODE, NJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRedSmem);
-        configured[dev] = true;
+    int per_sm = 1;
+    if (dev >= 0 && dev < 64) {
+        if (blocks_per_sm[dev] == 0) {
+            cudaFuncSetAttribute(k_reduce<MODE, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRedSmem);
+            int b = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce<MODE, NV>, kRedWarps * 32, kRedSmem) !=
+                    cudaSuccess || b < 1)
+                b = 1;
+            blocks_per_sm[dev] = b;
+        }
+        per_sm = blocks_per_sm[dev];
     }
-    const int grid = sm_count() * 2;
-    k_chunks<<<grid_for_chunks(w), 256, 0, s>>>(keys, w.seg_begin, w.counters, w.chunk_lo, w.big);
-    k_reduce<MODE, NJ><<<grid, kRedThreads, kRedSmem, s>>>(keys, vals, w.seg_begin, w.chunk_lo, w.big, w.counters, R,
-                                                          dim, n_heads, hpn,
-                                                          static_cast<const uint8_t*>(grad), grad_rows);
+    const int grid = sm_count() * per_sm;
+    return {grid, grid * kRedWarps};
+}
+
+int grid_for(int64_t work, int threads, int per_sm);
+
+template <int MODE, int NV>
+void launch_reduce(const Workspace& w, const int32_t* keys, const int32_t* vals, int64_t N, int64_t R, int dim,
+                   int n_heads, int hpn, const void* grad, float* grad_rows, cudaStream_t s) {
+    const ReduceLaunch L = reduce_launch<MODE, NV>();
+    k_chunks<<<grid_for(N / kMinChunk + 2, 256, 4), 256, 0, s>>>(keys, w.seg_begin, w.counters, L.total_warps,
+                                                                   w.chunk_lo, w.chunk_hi, w.long_seg);
+    k_reduce<MODE, NV><<<L.grid, kRedWarps * 32, kRedSmem, s>>>(keys, vals, w.seg_begin, w.chunk_lo, w.chunk_hi,
+                                                                 w.long_seg, w.counters, R, dim, n_heads, hpn,
+                                                                 static_cast<const uint8_t*>(grad), grad_rows);
 }
 
 int grid_for(int64_t work, int threads, int per_sm) {
@@ -472,8 +646,6 @@ int grid_for(int64_t work, int threads, int per_sm) {
     const int64_t g = want < cap ? want : cap;
     return (int)(g > 0 ? g : 1);
 }
-
-int grid_for_chunks(const Workspace& w) { return grid_for((int64_t)w.nblk * kRsTile / kChunk + 2, 256, 4); }
 
 }  // namespace
 
@@ -524,15 +696,19 @@ extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
         cur = out;
     }
     k_seg_begin<<<grid_for(N, 256, 8), 256, 0, s>>>(w.keys[cur], w.counters, R, w.seg_begin);
-    const int nj = (dim + kRedThreads - 1) / kRedThreads;
+    const int nvec = mode == ENGRAM_MODE_CONCAT_F32 ? dim / 4 : dim / 8;  // 16-byte column vectors per row
+    const int32_t* K = w.keys[cur];
+    const int32_t* V = w.vals[cur];
+    const int hpn = heads_per_ngram;
     if (mode == ENGRAM_MODE_CONCAT_F32) {
-        if (nj <= 1) launch_reduce<ENGRAM_MODE_CONCAT_F32, 1>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else if (nj <= 2) launch_reduce<ENGRAM_MODE_CONCAT_F32, 2>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else launch_reduce<ENGRAM_MODE_CONCAT_F32, 4>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        if (nvec <= 32) launch_reduce<ENGRAM_MODE_CONCAT_F32, 1>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
+        else if (nvec <= 64) launch_reduce<ENGRAM_MODE_CONCAT_F32, 2>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
+        else if (nvec <= 128) launch_reduce<ENGRAM_MODE_CONCAT_F32, 4>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
+        else launch_reduce<ENGRAM_MODE_CONCAT_F32, 8>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
     } else {
-        if (nj <= 1) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 1>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else if (nj <= 2) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 2>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
-        else launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 4>(w, w.keys[cur], w.vals[cur], R, dim, n_heads, heads_per_ngram, grad, grad_rows, s);
+        if (nvec <= 32) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 1>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
+        else if (nvec <= 64) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 2>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
+        else launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 4>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
     }
     count_launches(3 * passes + 3);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;

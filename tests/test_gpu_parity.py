@@ -227,6 +227,31 @@ def test_backward_heavy_duplicates_and_large_R_bit_exact(eb):
     assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
 
 
+@pytest.mark.parametrize("mode,dim", [(0, 4), (0, 36), (0, 128), (0, 200), (0, 256), (0, 512), (0, 1024),
+                                      (1, 8), (1, 72), (1, 256), (1, 512), (1, 1024)])
+def test_backward_every_row_width_bit_exact(eb, mode, dim):
+    """Row widths from one 16-byte vector to 4 KB, with hot slots long enough to
+    be split into column slices, against the oracle."""
+    rng = np.random.default_rng(1000 + 10 * dim + mode)
+    T, nh, hpn = (3000 if dim <= 256 else 900), 16, 8
+    R = 5000
+    slots = np.full((T, nh), -1, dtype=np.int32)
+    m = rng.random((T, nh)) < 0.5
+    hot = rng.integers(0, 4, size=(T, nh))
+    cold = rng.integers(0, R, size=(T, nh))
+    slots[m] = np.where(rng.random((T, nh)) < 0.3, hot, cold)[m]
+    slots[rng.random(T) < 0.5, 5] = R - 1
+    if mode == O.MODE_CONCAT_F32:
+        grad = (rng.standard_normal((T, nh, dim)) * 1e-3).astype(np.float32)
+        g_dev = torch.from_numpy(grad).to(DEV)
+    else:
+        grad = O.bf16_bits((rng.standard_normal((T, hpn * dim)) * 1e-2).astype(np.float32))
+        g_dev = torch.from_numpy(grad.view(np.int16)).to(DEV).view(torch.bfloat16)
+    got = eb.row_gradients(torch.from_numpy(slots).to(DEV), g_dev, nh, hpn, dim, R, mode).cpu().numpy()
+    ref = O.backward(slots, hpn, grad, dim, R, mode)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
 def test_backward_no_hits_gives_zero_rows(eb):
     slots = torch.full((100, 16), -1, dtype=torch.int32, device=DEV)
     grad = torch.randn(100, 16, 128, device=DEV)

@@ -10,15 +10,17 @@
 //      __match_any_sync groups plus per-warp digit counts (no comparison sort);
 //      block offsets come from a per-digit row scan (256 blocks);
 //   2. segment starts per slot from the sorted keys;
-//   3. one segmented reduction in which every warp runs its own jobs.  A short
-//      job is a chunk of whole segments: lane l copies and adds its own 16-byte
-//      column vectors of every row through a private cp.async ring, and writes
-//      a slot's row when its segment ends.  A segment longer than the chunk
-//      size is split by columns instead: one job per 64-byte slice, so the
-//      slices of a hot slot stream on many SMs at once.
+//   3. one segmented reduction in which every warp runs its own jobs.  First
+//      the segments longer than kLongRows entries, split by columns: one job
+//      per 64-byte slice, so the long sequential chains of the hot slots start
+//      at once, on many SMs.  Then every warp streams the remaining entries
+//      (whole segments, taken in jobs from an atomic counter) through a private
+//      cp.async ring: lane l copies and adds its own 16-byte column vectors of
+//      every row and the warp writes a slot's row when its segment ends.
 // Every term is added from +0 in ascending (t, h) order in fp32, so the result
 // is bit-identical to the reference and independent of scheduling.
 #include <algorithm>
+#include <climits>
 #include <mutex>
 
 #include "engram_common.cuh"
@@ -34,33 +36,48 @@ constexpr int kRsItems = 16;
 constexpr int kRsTile = kRsThreads * kRsItems;
 constexpr int kScanThreads = 1024;
 // segmented reduction
-constexpr int kRedWarps = 2;         // warps per block; each warp runs its own jobs
-constexpr int kWarpSmem = 20480;     // shared memory per warp
-constexpr int kRedSmem = kRedWarps * kWarpSmem;
-constexpr int kMinChunk = 64, kMaxChunk = 2048;  // short-chunk size bounds (entries)
-constexpr int kSliceBytes = 64;      // column slice of a long-segment job
-constexpr int kLongGI = 7;           // 32-row groups in flight in a long job
+#ifndef ENGRAM_RED_ROWS
+#define ENGRAM_RED_ROWS 16
+#endif
+#ifndef ENGRAM_RED_LONG_GI
+#define ENGRAM_RED_LONG_GI 5
+#endif
+#ifndef ENGRAM_RED_CPW
+#define ENGRAM_RED_CPW 8
+#endif
+constexpr int kRedWarps = 4;                            // warps per block; each warp runs its own jobs
+constexpr int kShortRows = ENGRAM_RED_ROWS;             // 512-byte rows in flight per warp in short jobs
+constexpr int kShortWarpSmem = (kShortRows + 8) * 512;  // its ring, with one spare batch
+constexpr int kChunksPerWarp = ENGRAM_RED_CPW;          // short chunks per warp, for balance
+constexpr int kMinChunk = 32, kMaxChunk = 2048;         // short-chunk size bounds (entries)
+constexpr int kLongRows = 256;                          // segments longer than this are split by columns
+constexpr int kSliceBytes = 64;                         // column slice of a long-segment job
+constexpr int kLongGI = ENGRAM_RED_LONG_GI;             // 32-row groups in flight in a long job
 constexpr int kLongRingGroups = kLongGI + 1;
 constexpr int kLongValSlots = 2 * kLongGI + 1;
-static_assert(kLongRingGroups * 32 * kSliceBytes + kLongValSlots * 32 * 4 <= kWarpSmem, "long-job ring");
+constexpr int kLongWarpSmem = kLongRingGroups * 32 * kSliceBytes + kLongValSlots * 32 * 4;
+constexpr int kWarpSmem = kLongWarpSmem > kShortWarpSmem ? kLongWarpSmem : kShortWarpSmem;  // per warp
+constexpr int kRedSmem = kRedWarps * kWarpSmem;
 
 // Short-chunk ring: lane-owned 16-byte column vectors, NV per lane.
 template <int NV>
 struct ShortRing {
-    static constexpr int D = 32 / NV;                           // rows in flight
-    static constexpr int U = NV <= 2 ? 4 : (NV == 4 ? 2 : 1);  // rows per commit group
+    static constexpr int D = kShortRows / NV;                   // rows in flight
+    static constexpr int U = D >= 16 ? 4 : (D >= 8 ? 2 : 1);    // rows per commit group
     static constexpr int GI = D / U;                            // commit groups in flight
     static constexpr int ROWS = D + U;                          // ring rows: one spare batch
-    static_assert(ROWS * NV * 512 <= kWarpSmem, "short-chunk ring");
+    static_assert(D <= 32 && D % U == 0 && 32 % U == 0 && GI >= 2, "short-chunk ring");
+    static_assert(ROWS * NV * 512 <= kShortWarpSmem, "short-chunk ring");
 };
 
 // counters[] in the workspace
-constexpr int kCntHits = 0, kCntJobNext = 1, kCntLong = 2, kCntChunks = 3;
+constexpr int kCntHits = 0, kCntLongNext = 1, kCntLong = 2, kCntChunks = 3, kCntShortNext = 4, kCntMedium = 5;
 
-// Entries per short chunk: about two chunks per warp of the reduce grid.
-__host__ __device__ inline int64_t chunk_size(int64_t n, int total_warps) {
-    const int64_t per = (n + 2LL * total_warps - 1) / (2LL * total_warps);
-    const int64_t k = (per + 31) / 32 * 32;
+// Entries per short chunk: about kChunksPerWarp chunks per warp of the reduce grid.
+__host__ __device__ inline int64_t chunk_size(int64_t n, int warps) {
+    const int64_t parts = (int64_t)kChunksPerWarp * warps;
+    const int64_t per = (n + parts - 1) / parts;
+    const int64_t k = (per + 7) / 8 * 8;
     return k < kMinChunk ? kMinChunk : (k > kMaxChunk ? kMaxChunk : k);
 }
 
@@ -74,7 +91,8 @@ struct Workspace {
     int32_t* seg_begin;
     int32_t* chunk_lo;  // [max_chunks] short entries of each chunk: [chunk_lo, chunk_hi)
     int32_t* chunk_hi;
-    int32_t* long_seg;  // [max_chunks] slots with long segments
+    int32_t* long_seg;    // [max_chunks] slots whose segments are split by columns
+    int32_t* medium_seg;  // [max_chunks] slots whose segments are short jobs of their own
     int32_t* counters;
     int64_t bytes;
     int nblk;
@@ -102,6 +120,7 @@ Workspace layout(void* base, int64_t N, int64_t R) {
     w.chunk_lo = reinterpret_cast<int32_t*>(take(4 * max_chunks));
     w.chunk_hi = reinterpret_cast<int32_t*>(take(4 * max_chunks));
     w.long_seg = reinterpret_cast<int32_t*>(take(4 * max_chunks));
+    w.medium_seg = reinterpret_cast<int32_t*>(take(4 * max_chunks));
     w.counters = reinterpret_cast<int32_t*>(take(64));
     w.bytes = off;
     return w;
@@ -143,9 +162,11 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_hist(const int32_t* __restric
     __shared__ uint32_t h[256];
     for (int d = threadIdx.x; d < 256; d += kRsThreads) h[d] = 0;
     if (counters && blockIdx.x == 0 && threadIdx.x == 0) {
-        counters[kCntJobNext] = 0;
+        counters[kCntLongNext] = 0;
         counters[kCntLong] = 0;
         counters[kCntChunks] = 0;
+        counters[kCntShortNext] = 0;
+        counters[kCntMedium] = 0;
     }
     __syncthreads();
     const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
@@ -271,14 +292,35 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// Offset, in 16-byte units, of the upstream-gradient row of flat entry i = t*n_heads + h.
-template <int MODE>
-__device__ __forceinline__ uint32_t grad_row16(int64_t i, int dim, int n_heads, int hpn) {
-    if (MODE == ENGRAM_MODE_CONCAT_F32) return (uint32_t)((i * (int64_t)dim) >> 2);
-    const int64_t t = i / n_heads;
-    const int h = (int)(i - t * n_heads);
-    return (uint32_t)((t * hpn * dim + (int64_t)(h % hpn) * dim) >> 3);
+// Division of flat indices (< 2^31) by n_heads (<= 32) as a multiply and shift:
+// with s = 32 + ceil(log2 d) and m = ceil(2^s / d) < 2^33, (x*m) >> s == x / d
+// for every x < 2^s / d, which covers x < 2^32, and x*m stays below 2^64.
+struct HeadDiv {
+    uint64_t m;
+    int s;
+};
+
+inline HeadDiv head_div(int d) {
+    int lg = 0;
+    while ((1 << lg) < d) lg++;
+    const int s = 32 + lg;
+    return {((1ULL << s) + (uint64_t)d - 1) / (uint64_t)d, s};
 }
+
+// Offset, in 16-byte units, of the upstream-gradient row of flat entry
+// i = t*n_heads + h: CONCAT row i; PAIRSUM row t, group h % hpn (n_heads == 2*hpn).
+struct GradRows {
+    int dim, n_heads, hpn;
+    HeadDiv hd;
+    template <int MODE>
+    __device__ __forceinline__ uint32_t off16(uint32_t i) const {
+        if (MODE == ENGRAM_MODE_CONCAT_F32) return (uint32_t)(((uint64_t)i * (uint32_t)dim) >> 2);
+        const uint32_t t = (uint32_t)(((uint64_t)i * hd.m) >> hd.s);
+        const uint32_t h = i - t * (uint32_t)n_heads;
+        const uint32_t r = h >= (uint32_t)hpn ? h - (uint32_t)hpn : h;
+        return (uint32_t)(((uint64_t)(t * (uint32_t)hpn + r) * (uint32_t)dim) >> 3);
+    }
+};
 
 // First segment start at or after sorted entry e (e in [0, n]).
 __device__ __forceinline__ int64_t snap_to_segment(const int32_t* __restrict__ keys,
@@ -291,19 +333,25 @@ __device__ __forceinline__ int64_t snap_to_segment(const int32_t* __restrict__ k
 }
 
 // Work split of the segmented reduction.  With K = the chunk size chosen from
-// the hit count, a segment longer than K entries is "long"; every other entry
-// belongs to a short chunk.  Chunk j spans [first segment start >= j*K, first
-// segment start >= (j+1)*K); a long segment can only sit at a chunk's head or
+// the hit count, chunk j spans [first segment start >= j*K, first segment
+// start >= (j+1)*K).  A segment longer than K can only sit at a chunk's head or
 // tail (one strictly inside would be shorter than K), so trimming those gives
-// the chunk's short entries [chunk_lo[j], chunk_hi[j]), and each long segment
-// is listed once in long_seg[] by the chunk that holds it.
+// the chunk's short entries [chunk_lo[j], chunk_hi[j]); each trimmed segment
+// is listed once, by the chunk that holds it: in long_seg[] when it is longer
+// than max(K, kLongRows) (split by columns), else in medium_seg[] (a short job
+// of its own).
 __global__ void k_chunks(const int32_t* __restrict__ keys, const int32_t* __restrict__ seg_begin, int32_t* counters,
-                         int total_warps, int32_t* __restrict__ chunk_lo, int32_t* __restrict__ chunk_hi,
-                         int32_t* __restrict__ long_seg) {
+                         int warps, int32_t* __restrict__ chunk_lo, int32_t* __restrict__ chunk_hi,
+                         int32_t* __restrict__ long_seg, int32_t* __restrict__ medium_seg) {
     const int64_t n = counters[kCntHits];
-    const int64_t K = chunk_size(n, total_warps);
+    const int64_t K = chunk_size(n, warps);
+    const int64_t TL = K > kLongRows ? K : kLongRows;
     const int64_t nchunks = (n + K - 1) / K;
     if (blockIdx.x == 0 && threadIdx.x == 0) counters[kCntChunks] = (int32_t)nchunks;
+    auto list = [&](int32_t k, int64_t len) {
+        if (len > TL) long_seg[atomicAdd(counters + kCntLong, 1)] = k;
+        else medium_seg[atomicAdd(counters + kCntMedium, 1)] = k;
+    };
     for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < nchunks; j += (int64_t)gridDim.x * blockDim.x) {
         int64_t lo = snap_to_segment(keys, seg_begin, j * K, n);
         int64_t hi = snap_to_segment(keys, seg_begin, (j + 1) * K, n);
@@ -311,7 +359,7 @@ __global__ void k_chunks(const int32_t* __restrict__ keys, const int32_t* __rest
             const int32_t k = __ldg(keys + lo);
             const int64_t end = __ldg(seg_begin + k + 1);
             if (end - lo > K) {
-                long_seg[atomicAdd(counters + kCntLong, 1)] = k;
+                list(k, end - lo);
                 lo = end;
             }
         }
@@ -319,7 +367,7 @@ __global__ void k_chunks(const int32_t* __restrict__ keys, const int32_t* __rest
             const int32_t k = __ldg(keys + hi - 1);
             const int64_t begin = __ldg(seg_begin + k);
             if (hi - begin > K) {
-                long_seg[atomicAdd(counters + kCntLong, 1)] = k;
+                list(k, hi - begin);
                 hi = begin;
             }
         }
@@ -341,56 +389,108 @@ __device__ __forceinline__ void add_vec16(float2* acc, const uint4 w) {
     }
 }
 
-// One short chunk [lo, hi) of whole segments, by one warp.  Lane l owns the
-// 16-byte column vectors l, l+32, ... (NV of them) of every row: it copies
-// exactly those bytes into its part of the ring and adds exactly those, so the
-// ring needs no cross-lane synchronisation.  D rows are in flight; rows are
-// committed in batches of U.  Row offsets, keys and segment-end flags come in
-// 32-row windows (lane i holds row i of the window), fetched two windows ahead.
+// The short jobs (medium segments first, then the short chunks) as one
+// continuous row stream per warp.  Jobs are taken from an atomic counter while
+// the stream's 32-row metadata windows are fetched, two windows ahead of the
+// adds, so the ring never drains between jobs.  Lane l owns the 16-byte column
+// vectors l, l+32, ... (NV of them) of every row: it copies exactly those
+// bytes into its part of the ring and adds exactly those, so the ring needs no
+// cross-lane synchronisation.  D rows are in flight, committed in batches of U.
+// Every job is a run of whole segments, so a segment ends where its key
+// changes or its job ends, and the warp then writes the slot's row.
 template <int MODE, int NV>
-__device__ __forceinline__ void reduce_short(uint8_t* __restrict__ ring, const int lane, const int64_t lo,
-                                             const int64_t hi, const int32_t* __restrict__ keys,
-                                             const int32_t* __restrict__ vals, const int dim, const int n_heads,
-                                             const int hpn, const uint4* __restrict__ g16,
-                                             float* __restrict__ grad_rows) {
+__device__ __forceinline__ void reduce_stream(uint8_t* __restrict__ ring, const int lane,
+                                              const int32_t* __restrict__ keys, const int32_t* __restrict__ vals,
+                                              const int32_t* __restrict__ seg_begin,
+                                              const int32_t* __restrict__ chunk_lo,
+                                              const int32_t* __restrict__ chunk_hi,
+                                              const int32_t* __restrict__ medium_seg, int32_t* counters,
+                                              const int64_t n_medium, const int64_t n_jobs, const GradRows& G,
+                                              const uint4* __restrict__ g16, float* __restrict__ grad_rows) {
     using RG = ShortRing<NV>;
     constexpr int D = RG::D, U = RG::U, GI = RG::GI, ROWS = RG::ROWS;
     constexpr bool F32 = MODE == ENGRAM_MODE_CONCAT_F32;
     constexpr int CPV = F32 ? 4 : 8;  // columns per 16-byte vector
+    const int dim = G.dim;
     const int nvec = dim / CPV;
-    const int n = (int)(hi - lo);
     auto slot = [&](int s, int q) { return ring + (s * NV + q) * 512 + lane * 16; };
-    auto fetch = [&](int w, int32_t& k, int32_t& kn, int32_t& v) {
-        const int64_t e = lo + 32LL * w + lane;
+    // job cursor (warp-uniform): entries [jlo, jhi) of the current job not yet in a window
+    int64_t jlo = 0, jhi = 0;
+    bool exhausted = false;
+    auto next_job = [&]() {
+        while (true) {
+            int j = 0;
+            if (lane == 0) j = atomicAdd(counters + kCntShortNext, 1);
+            j = __shfl_sync(kFull, j, 0);
+            if (j >= n_jobs) return false;
+            int64_t lo, hi;
+            if (j < n_medium) {
+                const int32_t key = __ldg(medium_seg + j);
+                lo = __ldg(seg_begin + key);
+                hi = __ldg(seg_begin + key + 1);
+            } else {
+                lo = __ldg(chunk_lo + (j - n_medium));
+                hi = __ldg(chunk_hi + (j - n_medium));
+            }
+            if (lo < hi) {
+                jlo = lo;
+                jhi = hi;
+                return true;
+            }
+        }
+    };
+    // maps the next 32 stream rows to entries (taking jobs as needed); returns how many it mapped
+    auto fetch = [&](int32_t& k, int32_t& kn, int32_t& v) {
         k = -1;
         kn = -1;
         v = 0;
-        if (e < hi) {
-            k = __ldg(keys + e);
-            v = __ldg(vals + e);
-            if (e + 1 < hi) kn = __ldg(keys + e + 1);
+        int filled = 0;
+        while (filled < 32) {
+            if (jlo >= jhi) {
+                if (exhausted || !next_job()) {
+                    exhausted = true;
+                    break;
+                }
+            }
+            const int64_t avail = jhi - jlo;
+            const int take = avail < 32 - filled ? (int)avail : 32 - filled;
+            if (lane >= filled && lane < filled + take) {
+                const int64_t e = jlo + (lane - filled);
+                k = __ldg(keys + e);
+                v = __ldg(vals + e);
+                if (e + 1 < jhi) kn = __ldg(keys + e + 1);
+            }
+            filled += take;
+            jlo += take;
         }
+        return filled;
     };
     auto finish = [&](int32_t k, int32_t kn, int32_t v, uint32_t& off, int32_t& key, unsigned& last) {
-        off = k >= 0 ? grad_row16<MODE>(v, dim, n_heads, hpn) : 0u;
+        off = k >= 0 ? G.off16<MODE>((uint32_t)v) : 0u;
         key = k;
         last = __ballot_sync(kFull, k >= 0 && k != kn);
     };
-    // A = window being consumed, B = the next one, C = raw loads of the one after
+    // A = window being added, B = the next one, C = raw loads of the one after;
+    // `end` = stream length, known once a window comes back short
     uint32_t offA, offB;
     int32_t keyA, keyB, ck, ckn, cv;
     unsigned lastA, lastB;
+    int end = INT_MAX;
     {
         int32_t k0, kn0, v0, k1, kn1, v1;
-        fetch(0, k0, kn0, v0);
-        fetch(1, k1, kn1, v1);
-        fetch(2, ck, ckn, cv);
+        int f = fetch(k0, kn0, v0);
+        if (f < 32) end = f;
+        f = fetch(k1, kn1, v1);
+        if (f < 32 && end == INT_MAX) end = 32 + f;
+        f = fetch(ck, ckn, cv);
+        if (f < 32 && end == INT_MAX) end = 64 + f;
         finish(k0, kn0, v0, offA, keyA, lastA);
         finish(k1, kn1, v1, offB, keyB, lastB);
     }
-    auto issue = [&](int y, uint32_t off_src, int s) {  // row y of the chunk into ring row s
-        if (y < n) {
-            const uint32_t o = __shfl_sync(kFull, off_src, y & 31);
+    if (end == 0) return;
+    auto issue = [&](int y, uint32_t off_src, int s) {  // stream row y into ring row s
+        const uint32_t o = __shfl_sync(kFull, off_src, y & 31);
+        if (y < end) {
 #pragma unroll
             for (int q = 0; q < NV; q++)
                 if (lane + 32 * q < nvec) cp_async16(slot(s, q), g16 + o + lane + 32 * q);
@@ -407,15 +507,16 @@ __device__ __forceinline__ void reduce_short(uint8_t* __restrict__ ring, const i
     for (int q = 0; q < NV; q++)
 #pragma unroll
         for (int i = 0; i < CPV / 2; i++) acc[q][i] = make_float2(0.f, 0.f);
-    int cs = 0, is = D;  // ring rows of the batch consumed / issued
+    int cs = 0, is = D;  // ring rows of the batch added / issued
 #pragma unroll 1
-    for (int x0 = 0; x0 < n; x0 += U) {
+    for (int x0 = 0; x0 < end; x0 += U) {
         if (x0 > 0 && (x0 & 31) == 0) {
             offA = offB;
             keyA = keyB;
             lastA = lastB;
             finish(ck, ckn, cv, offB, keyB, lastB);
-            fetch((x0 >> 5) + 2, ck, ckn, cv);
+            const int f = fetch(ck, ckn, cv);
+            if (f < 32 && end == INT_MAX) end = x0 + 64 + f;
         }
         cp_async_wait<GI - 1>();
         uint4 v[U][NV];
@@ -423,16 +524,16 @@ __device__ __forceinline__ void reduce_short(uint8_t* __restrict__ ring, const i
         for (int u = 0; u < U; u++)
 #pragma unroll
             for (int q = 0; q < NV; q++)
-                v[u][q] = (x0 + u < n && lane + 32 * q < nvec) ? *reinterpret_cast<const uint4*>(slot(cs + u, q))
-                                                                : make_uint4(0u, 0u, 0u, 0u);
+                v[u][q] = (x0 + u < end && lane + 32 * q < nvec) ? *reinterpret_cast<const uint4*>(slot(cs + u, q))
+                                                                  : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            if (x0 + u < n) {
+            if (x0 + u < end) {
 #pragma unroll
                 for (int q = 0; q < NV; q++) add_vec16<F32>(acc[q], v[u][q]);
-                const int r = (x0 + u) & 31;
-                if ((lastA >> r) & 1u) {  // the row ends its segment: write the slot's gradient row
-                    const int32_t key = __shfl_sync(kFull, keyA, r);
+                const int rr = (x0 + u) & 31;
+                if ((lastA >> rr) & 1u) {  // the row ends its segment: write the slot's gradient row
+                    const int32_t key = __shfl_sync(kFull, keyA, rr);
                     float* dst = grad_rows + (int64_t)key * dim;
 #pragma unroll
                     for (int q = 0; q < NV; q++) {
@@ -476,8 +577,9 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
 template <int MODE>
 __device__ __forceinline__ void reduce_long(uint8_t* __restrict__ ws, const int lane, const int64_t a, const int64_t b,
                                             const int32_t key, const int slice, const int32_t* __restrict__ vals,
-                                            const int dim, const int n_heads, const int hpn,
-                                            const uint4* __restrict__ g16, float* __restrict__ grad_rows) {
+                                            const GradRows& G, const uint4* __restrict__ g16,
+                                            float* __restrict__ grad_rows) {
+    const int dim = G.dim;
     constexpr bool F32 = MODE == ENGRAM_MODE_CONCAT_F32;
     constexpr int GI = kLongGI, RG = kLongRingGroups, VS = kLongValSlots, SB = kSliceBytes;
     uint8_t* ring = ws;
@@ -493,7 +595,7 @@ __device__ __forceinline__ void reduce_long(uint8_t* __restrict__ ws, const int 
     };
     auto issue_rows = [&](int g) {
         if (32 * g + lane < n) {
-            const uint32_t o = grad_row16<MODE>(vq[(g % VS) * 32 + lane], dim, n_heads, hpn);
+            const uint32_t o = G.off16<MODE>((uint32_t)vq[(g % VS) * 32 + lane]);
             uint8_t* dst = ring + ((g % RG) * 32 + lane) * SB;
             for (int p = 0; p < np; p++) cp_async16(dst + p * 16, g16 + o + p0 + p);
         }
@@ -513,32 +615,31 @@ __device__ __forceinline__ void reduce_long(uint8_t* __restrict__ ws, const int 
     for (int it = 0; it < ngroups; it++) {
         cp_async_wait<GI - 1>();
         __syncwarp();  // other lanes' copies of group it are visible; group it-1's ring rows are free
-        const uint8_t* gp = ring + (it % RG) * 32 * SB + lane * 4;
-        const int nr = min(32, n - 32 * it);
-        if (lane < words) {
-            int r = 0;
-#pragma unroll 1
-            for (; r + 8 <= nr; r += 8) {
-                uint32_t w[8];
-#pragma unroll
-                for (int u = 0; u < 8; u++) w[u] = *reinterpret_cast<const uint32_t*>(gp + (r + u) * SB);
-#pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    if (F32) accf = __fadd_rn(accf, __uint_as_float(w[u]));
-                    else acc = __fadd2_rn(acc, make_float2(__uint_as_float(w[u] << 16), __uint_as_float(w[u] & 0xffff0000u)));
-                }
-            }
-#pragma unroll 1
-            for (; r < nr; r++) {
-                const uint32_t w = *reinterpret_cast<const uint32_t*>(gp + r * SB);
-                if (F32) accf = __fadd_rn(accf, __uint_as_float(w));
-                else acc = __fadd2_rn(acc, make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)));
-            }
-        }
-        __syncwarp();
+        // refill group it-1's ring rows first, so the copies' address arithmetic overlaps the adds
         issue_rows(it + GI);
         load_val(it + 2 * GI);
         cp_async_commit();
+        const uint8_t* gp = ring + (it % RG) * 32 * SB + lane * 4;
+        const int nr = min(32, n - 32 * it);
+        if (lane < words) {
+            if (nr == 32) {
+                uint32_t w[32];
+#pragma unroll
+                for (int u = 0; u < 32; u++) w[u] = *reinterpret_cast<const uint32_t*>(gp + u * SB);
+#pragma unroll
+                for (int u = 0; u < 32; u++) {
+                    if (F32) accf = __fadd_rn(accf, __uint_as_float(w[u]));
+                    else acc = __fadd2_rn(acc, make_float2(__uint_as_float(w[u] << 16), __uint_as_float(w[u] & 0xffff0000u)));
+                }
+            } else {
+#pragma unroll 1
+                for (int r = 0; r < nr; r++) {
+                    const uint32_t w = *reinterpret_cast<const uint32_t*>(gp + r * SB);
+                    if (F32) accf = __fadd_rn(accf, __uint_as_float(w));
+                    else acc = __fadd2_rn(acc, make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)));
+                }
+            }
+        }
     }
     cp_async_wait<0>();
     __syncwarp();
@@ -549,46 +650,45 @@ __device__ __forceinline__ void reduce_long(uint8_t* __restrict__ ws, const int 
     }
 }
 
-// Segmented reduction over the slot-sorted entries.  Every warp takes jobs
-// (an atomic counter): first the column slices of the long segments, then the
-// short chunks.  Slots without entries get zero rows.  NV = 16-byte column
-// vectors per lane in short chunks (row bytes <= 512*NV).
+// Segmented reduction over the slot-sorted entries.  Every warp first takes
+// column slices of the long segments (an atomic counter), so the longest
+// sequential chains start at once; then it joins the short jobs (medium
+// segments first, then the short chunks) as one row stream.  Slots without
+// entries get zero rows.  NV = 16-byte column vectors per lane in short jobs
+// (row bytes <= 512*NV).
 template <int MODE, int NV>
 __global__ void __launch_bounds__(kRedWarps * 32) k_reduce(const int32_t* __restrict__ keys,
                                                            const int32_t* __restrict__ vals,
                                                            const int32_t* __restrict__ seg_begin,
                                                            const int32_t* __restrict__ chunk_lo,
                                                            const int32_t* __restrict__ chunk_hi,
-                                                           const int32_t* __restrict__ long_seg, int32_t* counters,
-                                                           int64_t R, int dim, int n_heads, int hpn,
+                                                           const int32_t* __restrict__ long_seg,
+                                                           const int32_t* __restrict__ medium_seg,
+                                                           int32_t* counters, int64_t R, const GradRows G,
                                                            const uint8_t* __restrict__ grad,
                                                            float* __restrict__ grad_rows) {
     constexpr int ES = MODE == ENGRAM_MODE_CONCAT_F32 ? 4 : 2;
+    const int dim = G.dim;
     extern __shared__ __align__(16) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint8_t* ws = smem + warp * kWarpSmem;
-    const int64_t n_long = counters[kCntLong];
-    const int64_t nchunks = counters[kCntChunks];
-    const int n_slices = (dim * ES + kSliceBytes - 1) / kSliceBytes;
-    const int64_t n_long_jobs = n_long * n_slices;
-    const int64_t n_jobs = n_long_jobs + nchunks;
     const uint4* g16 = reinterpret_cast<const uint4*>(grad);
+    const int n_slices = (dim * ES + kSliceBytes - 1) / kSliceBytes;
+    const int64_t n_long_jobs = (int64_t)counters[kCntLong] * n_slices;
     while (true) {
         int j = 0;
-        if (lane == 0) j = atomicAdd(counters + kCntJobNext, 1);
+        if (lane == 0) j = atomicAdd(counters + kCntLongNext, 1);
         j = __shfl_sync(kFull, j, 0);
-        if (j >= n_jobs) break;
-        if (j < n_long_jobs) {
-            const int32_t key = __ldg(long_seg + j / n_slices);
-            reduce_long<MODE>(ws, lane, __ldg(seg_begin + key), __ldg(seg_begin + key + 1), key, j % n_slices, vals,
-                              dim, n_heads, hpn, g16, grad_rows);
-        } else {
-            const int64_t c = j - n_long_jobs;
-            const int64_t lo = __ldg(chunk_lo + c), hi = __ldg(chunk_hi + c);
-            if (lo < hi) reduce_short<MODE, NV>(ws, lane, lo, hi, keys, vals, dim, n_heads, hpn, g16, grad_rows);
-        }
-        __syncwarp();  // the next job lays the ring out differently
+        if (j >= n_long_jobs) break;
+        const int32_t key = __ldg(long_seg + j / n_slices);
+        reduce_long<MODE>(ws, lane, __ldg(seg_begin + key), __ldg(seg_begin + key + 1), key, j % n_slices, vals, G,
+                          g16, grad_rows);
+        __syncwarp();  // the short stream lays the ring out differently
     }
+    const int64_t n_medium = counters[kCntMedium];
+    const int64_t n_jobs = n_medium + counters[kCntChunks];
+    reduce_stream<MODE, NV>(ws, lane, keys, vals, seg_begin, chunk_lo, chunk_hi, medium_seg, counters, n_medium,
+                            n_jobs, G, g16, grad_rows);
     // slots without entries
     const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -600,31 +700,19 @@ __global__ void __launch_bounds__(kRedWarps * 32) k_reduce(const int32_t* __rest
     }
 }
 
-struct ReduceLaunch {
-    int grid;
-    int total_warps;
-};
-
-// Grid of the reduce kernel: every block that fits at once on every SM.
-template <int MODE, int NV>
-ReduceLaunch reduce_launch() {
-    static int blocks_per_sm[64] = {0};
+// Blocks of `kernel` that fit at once on one SM (set-up on first use per device).
+template <typename F>
+int blocks_per_sm(F kernel, int threads, int smem, int* cache) {
     int dev = 0;
     cudaGetDevice(&dev);
-    int per_sm = 1;
-    if (dev >= 0 && dev < 64) {
-        if (blocks_per_sm[dev] == 0) {
-            cudaFuncSetAttribute(k_reduce<MODE, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRedSmem);
-            int b = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce<MODE, NV>, kRedWarps * 32, kRedSmem) !=
-                    cudaSuccess || b < 1)
-                b = 1;
-            blocks_per_sm[dev] = b;
-        }
-        per_sm = blocks_per_sm[dev];
+    if (dev < 0 || dev >= 64) return 1;
+    if (cache[dev] == 0) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, smem) != cudaSuccess || b < 1) b = 1;
+        cache[dev] = b;
     }
-    const int grid = sm_count() * per_sm;
-    return {grid, grid * kRedWarps};
+    return cache[dev];
 }
 
 int grid_for(int64_t work, int threads, int per_sm);
@@ -632,12 +720,14 @@ int grid_for(int64_t work, int threads, int per_sm);
 template <int MODE, int NV>
 void launch_reduce(const Workspace& w, const int32_t* keys, const int32_t* vals, int64_t N, int64_t R, int dim,
                    int n_heads, int hpn, const void* grad, float* grad_rows, cudaStream_t s) {
-    const ReduceLaunch L = reduce_launch<MODE, NV>();
-    k_chunks<<<grid_for(N / kMinChunk + 2, 256, 4), 256, 0, s>>>(keys, w.seg_begin, w.counters, L.total_warps,
-                                                                   w.chunk_lo, w.chunk_hi, w.long_seg);
-    k_reduce<MODE, NV><<<L.grid, kRedWarps * 32, kRedSmem, s>>>(keys, vals, w.seg_begin, w.chunk_lo, w.chunk_hi,
-                                                                 w.long_seg, w.counters, R, dim, n_heads, hpn,
-                                                                 static_cast<const uint8_t*>(grad), grad_rows);
+    static int per_sm[64] = {0};
+    const int grid = sm_count() * blocks_per_sm(k_reduce<MODE, NV>, kRedWarps * 32, kRedSmem, per_sm);
+    k_chunks<<<grid_for(N / kMinChunk + 2, 256, 4), 256, 0, s>>>(keys, w.seg_begin, w.counters, grid * kRedWarps,
+                                                                   w.chunk_lo, w.chunk_hi, w.long_seg, w.medium_seg);
+    k_reduce<MODE, NV><<<grid, kRedWarps * 32, kRedSmem, s>>>(keys, vals, w.seg_begin, w.chunk_lo, w.chunk_hi,
+                                                               w.long_seg, w.medium_seg, w.counters, R,
+                                                               GradRows{dim, n_heads, hpn, head_div(n_heads)},
+                                                               static_cast<const uint8_t*>(grad), grad_rows);
 }
 
 int grid_for(int64_t work, int threads, int per_sm) {

@@ -6,9 +6,10 @@
 // one CPU thread, and after a stable sort of the indices on CUDA.  Here:
 //   1. a stable LSD radix sort (8-bit digits) of the hit entries keyed by overlay
 //      slot; entry values are flat indices t*n_heads+h, so each slot's entries
-//      come out in ascending (t, h) order.  Ranks inside a tile come from warp
-//      __match_any_sync groups plus per-warp digit counts (no comparison sort);
-//      block offsets come from a per-digit row scan (256 blocks);
+//      come out in ascending (t, h) order.  Ranks inside a tile come from
+//      per-warp running digit counts and, inside a warp, from one ballot per
+//      digit bit (no comparison sort); block offsets come from a per-digit
+//      row scan (256 blocks);
 //   2. segment starts per slot from the sorted keys;
 //   3. one segmented reduction in which every warp runs its own jobs.  First
 //      the segments longer than kLongRows entries, split by columns: one job
@@ -50,7 +51,10 @@ constexpr int kShortRows = ENGRAM_RED_ROWS;             // 512-byte rows in flig
 constexpr int kShortWarpSmem = (kShortRows + 8) * 512;  // its ring, with one spare batch
 constexpr int kChunksPerWarp = ENGRAM_RED_CPW;          // short chunks per warp, for balance
 constexpr int kMinChunk = 32, kMaxChunk = 2048;         // short-chunk size bounds (entries)
-constexpr int kLongRows = 256;                          // segments longer than this are split by columns
+#ifndef ENGRAM_RED_LONGROWS
+#define ENGRAM_RED_LONGROWS 256
+#endif
+constexpr int kLongRows = ENGRAM_RED_LONGROWS;          // segments longer than this are split by columns
 constexpr int kSliceBytes = 64;                         // column slice of a long-segment job
 constexpr int kLongGI = ENGRAM_RED_LONG_GI;             // 32-row groups in flight in a long job
 constexpr int kLongRingGroups = kLongGI + 1;
@@ -202,9 +206,13 @@ __global__ void __launch_bounds__(kScanThreads) k_rs_rowscan(uint32_t* block_his
 
 // Stable scatter of one pass.  vals_in == nullptr: the value is the index.
 // total_out (nullable): receives the number of entries sorted (the hit count).
-// The tile's keys (and values) are loaded into registers up front, so the 16
-// sub-tiles cost one memory latency; per-warp digit counts alternate between
-// two shared buffers so each sub-tile needs two block barriers.
+// Warp w of the block owns the tile's entries [w*512, (w+1)*512) (sub-tile s,
+// lane l -> entry w*512 + 32*s + l), so an entry's rank is: the block's offset
+// for its digit, plus the counts of that digit in the earlier warps, plus the
+// warp's running count before this sub-tile, plus its rank among the lanes of
+// this sub-tile with the same digit (found with one ballot per digit bit).  The running counts are kept per warp in
+// shared memory without block barriers; one scan over the warps per digit
+// follows the whole tile.
 __global__ void __launch_bounds__(kRsThreads) k_rs_scatter(const int32_t* __restrict__ keys_in,
                                                            const int32_t* __restrict__ vals_in, const int32_t* n_dev,
                                                            int64_t n_static, int shift,
@@ -212,53 +220,66 @@ __global__ void __launch_bounds__(kRsThreads) k_rs_scatter(const int32_t* __rest
                                                            const uint32_t* __restrict__ digit_tot, int nblk,
                                                            int32_t* __restrict__ keys_out,
                                                            int32_t* __restrict__ vals_out, int32_t* total_out) {
-    __shared__ uint32_t wcnt[2][kRsWarps][256];
+    __shared__ uint32_t wcnt[kRsWarps][256];
     __shared__ uint32_t run[256];
     __shared__ uint32_t wsum[32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t n = n_dev ? (int64_t)*n_dev : n_static;
-    const int64_t begin = (int64_t)blockIdx.x * kRsTile;
+    const int64_t wbase = (int64_t)blockIdx.x * kRsTile + (int64_t)warp * (kRsItems * 32);
     int32_t kr[kRsItems], vr[kRsItems];
 #pragma unroll
     for (int sub = 0; sub < kRsItems; sub++) {
-        const int64_t i = begin + (int64_t)sub * kRsThreads + tid;
+        const int64_t i = wbase + 32 * sub + lane;
         kr[sub] = i < n ? __ldg(keys_in + i) : -1;
         vr[sub] = vals_in ? (i < n ? __ldg(vals_in + i) : 0) : (int32_t)i;
     }
-    for (int k = tid; k < 2 * kRsWarps * 256; k += kRsThreads) (&wcnt[0][0][0])[k] = 0;
+#pragma unroll
+    for (int w = 0; w < kRsWarps; w++) wcnt[w][tid] = 0;  // kRsThreads == 256 digits
     {
-        const uint32_t dt = digit_tot[tid];  // kRsThreads == 256 digits
+        const uint32_t dt = digit_tot[tid];
         uint32_t tot;
         const uint32_t base = block_exclusive_scan(dt, wsum, &tot);  // contains a barrier
         run[tid] = base + block_off[(int64_t)tid * nblk + blockIdx.x];
         if (total_out && blockIdx.x == 0 && tid == 0) *total_out = (int32_t)tot;
     }
     const unsigned lt = (1u << lane) - 1u;
+    uint32_t* cnt = wcnt[warp];
+    uint32_t lrank[kRsItems];
 #pragma unroll
     for (int sub = 0; sub < kRsItems; sub++) {
-        const int B = sub & 1;
         const int32_t key = kr[sub];
         const bool valid = key >= 0;
-        const int digit = valid ? ((key >> shift) & 255) : (256 + lane);
-        const unsigned peers = __match_any_sync(kFull, digit);
-        const int rank = __popc(peers & lt);
-        if (valid && rank == 0) wcnt[B][warp][digit] = (uint32_t)__popc(peers);
-        __syncthreads();
-        {
-            const int d = tid;
-            uint32_t acc = run[d];
+        const int digit = (key >> shift) & 255;
+        // lanes holding the same digit: one ballot per digit bit (invalid lanes match no one)
+        unsigned peers = __ballot_sync(kFull, valid);
 #pragma unroll
-            for (int w = 0; w < kRsWarps; w++) {
-                const uint32_t c = wcnt[B][w][d];
-                wcnt[B][w][d] = acc;
-                wcnt[B ^ 1][w][d] = 0;  // ready for the next sub-tile
-                acc += c;
-            }
-            run[d] = acc;
+        for (int b = 0; b < 8; b++) {
+            const unsigned m = __ballot_sync(kFull, (digit >> b) & 1);
+            peers &= ((digit >> b) & 1) ? m : ~m;
         }
-        __syncthreads();
-        if (valid) {
-            const uint32_t pos = wcnt[B][warp][digit] + (uint32_t)rank;
+        const uint32_t rank = (uint32_t)__popc(peers & lt);
+        const uint32_t before = valid ? cnt[digit] : 0u;
+        __syncwarp();
+        if (valid && rank == 0) cnt[digit] = before + (uint32_t)__popc(peers);
+        __syncwarp();
+        lrank[sub] = before + rank;
+    }
+    __syncthreads();
+    {
+        uint32_t acc = run[tid];
+#pragma unroll
+        for (int w = 0; w < kRsWarps; w++) {
+            const uint32_t c = wcnt[w][tid];
+            wcnt[w][tid] = acc;
+            acc += c;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int sub = 0; sub < kRsItems; sub++) {
+        const int32_t key = kr[sub];
+        if (key >= 0) {
+            const uint32_t pos = cnt[(key >> shift) & 255] + lrank[sub];
             keys_out[pos] = key;
             vals_out[pos] = vr[sub];
         }

@@ -2,7 +2,9 @@
 own plugin idiom (engraft/replica/seq.py:1-17 shadows Replica attributes the
 same way): engraft.replica.seq.OverlayEmb is looked up as a module global by
 seq_forward (:907-909), seq_forward_triton (:1251-1253) and seq_step_triton
-(:1430-1432), so replacing the module attribute reroutes every caller."""
+(:1430-1432), so replacing the module attribute reroutes every caller.
+install_scan() does the same for engraft.damage.scan_hits (engraft/damage.py:168),
+which the damage report calls as a module global."""
 from __future__ import annotations
 
 import importlib
@@ -19,6 +21,25 @@ def install(seq_module=None):
         _saved.setdefault(id(seq), {})["OverlayEmb"] = seq.OverlayEmb
     seq.OverlayEmb = OverlayEmb
     return seq
+
+
+def install_scan(damage_module=None):
+    """Replaces engraft.damage.scan_hits with engraft_ngram_b200.scan_hits
+    (same arguments; the corpus is hashed and scanned on the GPU)."""
+    from .scan import scan_hits
+    dmg = damage_module or importlib.import_module("engraft.damage")
+    if "scan_hits" not in _saved.get(id(dmg), {}):
+        _saved.setdefault(id(dmg), {})["scan_hits"] = dmg.scan_hits
+    dmg.scan_hits = scan_hits
+    return dmg
+
+
+def uninstall_scan(damage_module=None):
+    dmg = damage_module or importlib.import_module("engraft.damage")
+    orig = _saved.get(id(dmg), {}).pop("scan_hits", None)
+    if orig is not None:
+        dmg.scan_hits = orig
+    return dmg
 
 
 def uninstall(seq_module=None):

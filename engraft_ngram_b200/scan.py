@@ -23,8 +23,12 @@ from .table import DeviceTable
 BLOCK_TOKENS = 8_000_000
 
 
-def scan_hits(tokens, table: DeviceTable, overlay_sorted, dnorm_sorted, block: int = BLOCK_TOKENS) -> dict:
+def scan_hits(tokens, table, overlay_sorted, dnorm_sorted, block: int = BLOCK_TOKENS, device=None) -> dict:
+    """`table`: a DeviceTable, or the reference's table object (PleTable,
+    FakeTable), of which only the addressing constants are used."""
     lib = L.load()
+    if not isinstance(table, DeviceTable):
+        table = DeviceTable.addressing_of(table, device if device is not None else "cuda")
     dev = table.device
     stream = L.stream_of(dev)
     tokens = np.asarray(tokens)

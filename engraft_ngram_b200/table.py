@@ -121,6 +121,28 @@ class DeviceTable:
         return cls.from_raw(rows, L.FMT_F32, dim, **common)
 
     _registry: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+    _addressing: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+
+    @classmethod
+    def addressing_of(cls, table, device) -> "DeviceTable":
+        """A hash-only DeviceTable with a reference table's addressing constants
+        (head sizes and offsets, multipliers, EOS, n-gram geometry), for hashing
+        and corpus scans: no rows are read or uploaded.  Cached per (table
+        object, device); a DeviceTable is returned as it is."""
+        if isinstance(table, DeviceTable):
+            return table
+        device = torch.device(device)
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        per = cls._addressing.setdefault(table, {})
+        if device not in per:
+            sizes = [int(x) for x in table.head_vocab_sizes]
+            offs = [int(x) for x in table.head_offsets]
+            per[device] = cls(torch.zeros(64, dtype=torch.uint8, device=device), L.FMT_F32, 4, sizes, offs,
+                              list(table.layer_multipliers), int(table.eos_token_id),
+                              ngram_size=int(table.ngram_size), heads_per_ngram=int(table.heads_per_ngram),
+                              n_rows=max(o + s for o, s in zip(offs, sizes)), source=table, hash_only=True)
+        return per[device]
 
     @classmethod
     def of(cls, table, device) -> "DeviceTable":

@@ -387,6 +387,36 @@ def test_scan_hits_matches_reference_golden(eb, golden):
         assert np.array_equal(got["read_count"], golden["scan_read_count"])
 
 
+class _AddressingOnly:
+    """The attributes of a reference table that hashing reads (a PleTable or
+    FakeTable without rows)."""
+
+    def __init__(self, p):
+        self.head_vocab_sizes = list(p["head_sizes"])
+        self.head_offsets = list(p["head_offsets"])
+        self.layer_multipliers = list(p["mult"])
+        self.eos_token_id = p["eos"]
+        self.ngram_size = p["ngram_size"]
+        self.heads_per_ngram = p["hpn"]
+
+
+def test_scan_hits_installed_takes_the_reference_table_object(eb, golden):
+    """install_scan reroutes engraft.damage.scan_hits; the reference passes its
+    own table object, of which only the addressing constants are used."""
+    import types
+    dmg = types.SimpleNamespace(scan_hits=None)
+    eb.install_scan(dmg)
+    try:
+        table = _AddressingOnly(FX.fake_table_params(seed=7))
+        got = dmg.scan_hits(golden["scan_tokens"], table, golden["scan_overlay"], golden["scan_dnorm"])
+    finally:
+        eb.uninstall_scan(dmg)
+    assert np.array_equal(got["pos"], golden["scan_pos"])
+    assert np.array_equal(got["n_hit_rows"], golden["scan_n_hit_rows"])
+    assert np.array_equal(got["dnorm_sum"].view(np.uint32), golden["scan_dnorm_sum"].view(np.uint32))
+    assert np.array_equal(got["read_count"], golden["scan_read_count"])
+
+
 def test_scan_hits_large_corpus_vs_oracle(eb):
     rng = np.random.default_rng(9)
     p = FX.syn_params()

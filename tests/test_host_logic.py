@@ -68,6 +68,14 @@ def test_install_replaces_module_attribute():
     assert seq.OverlayEmb == "reference-class"
 
 
+def test_install_scan_replaces_module_attribute():
+    dmg = types.SimpleNamespace(scan_hits="reference-function")
+    eb.install_scan(dmg)
+    assert dmg.scan_hits is eb.scan_hits
+    eb.uninstall_scan(dmg)
+    assert dmg.scan_hits == "reference-function"
+
+
 def test_overlay_emb_refuses_cpu_tensors():
     ov = eb.OverlayEmb(object(), [1, 2, 3], torch.zeros(0, 160), {})
     with pytest.raises(RuntimeError):

@@ -95,6 +95,18 @@ SIGNATURES = {
     "engram_scan_hits": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32,
                                    C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
+    "engram_rowset_words": (C.c_int64, [C.c_int64]),
+    "engram_rowset_mark": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                     C.c_int64, C.c_void_p, C.c_void_p]),
+    "engram_rowset_mark_ids": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]),
+    "engram_rowset_combine": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
+    "engram_rowset_workspace_bytes": (C.c_int64, [C.c_int64]),
+    "engram_rowset_extract": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                        C.c_int64, C.c_void_p]),
+    "engram_rowset_index": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                                      C.c_void_p, C.c_void_p]),
+    "engram_overlay_accumulate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
+                                            C.c_void_p]),
     "engram_selftest_mod": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),
     "engram_launch_count": (C.c_int64, []),
 }

@@ -90,6 +90,23 @@ def _check_rows_var(rows_var: torch.Tensor, dim: int) -> None:
         raise ValueError(f"rows_var must be [R, {dim}], got {tuple(rows_var.shape)}")
 
 
+def _emit(dtable, omap: OverlayMap, rv: torch.Tensor, tokens, seg_start, t0: int, n: int, mode: int,
+          out: torch.Tensor, slots, hit_count) -> None:
+    """One forward launch into `out`: engram_forward on a resident table, or the
+    row exchange plus engram_forward_indirect on a row-sharded table."""
+    if getattr(dtable, "is_sharded", False):
+        if dtable.exchange is None:
+            raise RuntimeError("this ShardedTable has no row exchange: set .exchange (e.g. nccl_exchange())")
+        dtable.forward(tokens, seg_start, omap, rv, out, mode, dtable.exchange, slots_out=slots,
+                       hit_count=hit_count, t0=t0, n=n)
+        return
+    ov = omap.descriptor(rv)
+    st = L.load().engram_forward(C.byref(dtable.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(seg_start), t0, n,
+                                 mode, out.data_ptr(), None, L.ptr(slots), L.ptr(hit_count),
+                                 L.stream_of(dtable.device))
+    L.check(st, "engram_forward")
+
+
 class _ConcatFn(torch.autograd.Function):
     """emb = gather(table, overlay=rows_var) in CONCAT mode; backward = row gradients."""
 
@@ -102,11 +119,7 @@ class _ConcatFn(torch.autograd.Function):
         out = torch.empty(n, nh * dim, dtype=torch.float32, device=dev)
         need_grad = rows_var.requires_grad and omap.R > 0
         slots = torch.empty(n, nh, dtype=torch.int32, device=dev) if need_grad else None
-        ov = omap.descriptor(rv)
-        st = L.load().engram_forward(C.byref(dtable.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(seg_start), t0, n,
-                                     L.MODE_CONCAT_F32, out.data_ptr(), None, L.ptr(slots), L.ptr(hit_count),
-                                     L.stream_of(dev))
-        L.check(st, "engram_forward")
+        _emit(dtable, omap, rv, tokens, seg_start, t0, n, L.MODE_CONCAT_F32, out, slots, hit_count)
         ctx.meta = (nh, dtable.heads_per_ngram, dim, omap.R, n)
         ctx.save_for_backward(slots if slots is not None else torch.empty(0, dtype=torch.int32, device=dev))
         return out
@@ -136,11 +149,7 @@ class _PairSumAddFn(torch.autograd.Function):
         rv = rows_var.detach().contiguous()
         need_grad = rows_var.requires_grad and omap.R > 0
         slots = torch.empty(n, nh, dtype=torch.int32, device=dev) if need_grad else None
-        ov = omap.descriptor(rv)
-        st = L.load().engram_forward(C.byref(dtable.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(seg_start), t0, n,
-                                     L.MODE_PAIRSUM_ADD_BF16, residual.data_ptr(), None, L.ptr(slots),
-                                     L.ptr(hit_count), L.stream_of(dev))
-        L.check(st, "engram_forward")
+        _emit(dtable, omap, rv, tokens, seg_start, t0, n, L.MODE_PAIRSUM_ADD_BF16, residual, slots, hit_count)
         ctx.mark_dirty(residual)
         ctx.meta = (nh, hpn, dim, omap.R, n)
         ctx.save_for_backward(slots if slots is not None else torch.empty(0, dtype=torch.int32, device=dev))

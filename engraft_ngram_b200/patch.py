@@ -4,7 +4,11 @@ same way): engraft.replica.seq.OverlayEmb is looked up as a module global by
 seq_forward (:907-909), seq_forward_triton (:1251-1253) and seq_step_triton
 (:1430-1432), so replacing the module attribute reroutes every caller.
 install_scan() does the same for engraft.damage.scan_hits (engraft/damage.py:168),
-which the damage report calls as a module global."""
+which the damage report calls as a module global, and install_rowsets() for the
+row-set builders and overlay-file operations around the descent
+(engraft.replica.distill.build_rows_var, engraft.descend_corpus's
+build_all_read_row_set / write_merged_pleo / sum_overlays, and
+engraft.replica.overlay_sum.sum_overlays)."""
 from __future__ import annotations
 
 import importlib
@@ -40,6 +44,40 @@ def uninstall_scan(damage_module=None):
     if orig is not None:
         dmg.scan_hits = orig
     return dmg
+
+
+_ROWSET_TARGETS = (
+    ("engraft.replica.distill", "build_rows_var"),
+    ("engraft.descend_corpus", "build_all_read_row_set"),
+    ("engraft.descend_corpus", "write_merged_pleo"),
+    ("engraft.descend_corpus", "sum_overlays"),
+    ("engraft.replica.overlay_sum", "sum_overlays"),
+)
+
+
+def install_rowsets(modules: dict | None = None) -> None:
+    """Replaces the row-set builders and overlay-file operations with their
+    device versions (engraft_ngram_b200.rowset; same arguments and results).
+    modules: {module name: module object} to patch instead of importing them."""
+    from . import rowset
+    for name, attr in _ROWSET_TARGETS:
+        mod = (modules or {}).get(name) if modules is not None else importlib.import_module(name)
+        if mod is None or not hasattr(mod, attr):
+            continue
+        saved = _saved.setdefault(id(mod), {})
+        if attr not in saved:
+            saved[attr] = getattr(mod, attr)
+        setattr(mod, attr, getattr(rowset, attr))
+
+
+def uninstall_rowsets(modules: dict | None = None) -> None:
+    for name, attr in _ROWSET_TARGETS:
+        mod = (modules or {}).get(name) if modules is not None else importlib.import_module(name)
+        if mod is None:
+            continue
+        orig = _saved.get(id(mod), {}).pop(attr, None)
+        if orig is not None:
+            setattr(mod, attr, orig)
 
 
 def uninstall(seq_module=None):

@@ -23,9 +23,11 @@ from .table import DeviceTable, _as_i32
 
 class ShardedTable:
     def __init__(self, shard_rows: torch.Tensor, fmt: int, dim: int, head_sizes, head_offsets, mult, eos_token_id,
-                 world: int, rank: int, n_rows: int, ngram_size: int = 3, heads_per_ngram: int = 8):
+                 world: int, rank: int, n_rows: int, ngram_size: int = 3, heads_per_ngram: int = 8, exchange=None):
         """shard_rows: uint8 CUDA tensor with this rank's rows in resident layout
-        (global rows rank, rank+W, rank+2W, ... in order)."""
+        (global rows rank, rank+W, rank+2W, ... in order).  exchange: the row
+        exchange the public API (engram_embed, engram_residual_add) uses with
+        this table, e.g. nccl_exchange(); settable later as .exchange."""
         if not (0 <= rank < world):
             raise ValueError(f"rank {rank} of {world}")
         lib = L.load()
@@ -36,7 +38,10 @@ class ShardedTable:
             raise ValueError("shard buffer too small")
         self.shard = shard_rows
         self.device = shard_rows.device
+        self.exchange = exchange
+        self.is_sharded = True
         # addressing constants of the whole table; the rows pointer is replaced per step
+        self.ngram_size, self.heads_per_ngram = int(ngram_size), int(heads_per_ngram)
         self.n_heads = (int(ngram_size) - 1) * int(heads_per_ngram)
         sizes = np.asarray([int(x) for x in head_sizes], dtype=np.int64)
         offs = np.asarray([int(x) for x in head_offsets], dtype=np.int64)
@@ -48,11 +53,11 @@ class ShardedTable:
         L.check(st, "engram_table_init")
 
     @classmethod
-    def from_full(cls, full: DeviceTable, world: int, rank: int) -> "ShardedTable":
+    def from_full(cls, full: DeviceTable, world: int, rank: int, exchange=None) -> "ShardedTable":
         """This rank's shard of a resident table (for tests and small tables)."""
         rows = full.rows.view(full.n_rows, full.row_stride)[rank::world].contiguous().reshape(-1)
         return cls(rows, full.fmt, full.dim, full.head_vocab_sizes, full.head_offsets, full.layer_multipliers,
-                   full.eos_token_id, world, rank, full.n_rows, full.ngram_size, full.heads_per_ngram)
+                   full.eos_token_id, world, rank, full.n_rows, full.ngram_size, full.heads_per_ngram, exchange)
 
     def global_ids(self, tokens, seg_start=None, t0: int = 0, n: int | None = None) -> torch.Tensor:
         """int32 [n, n_heads] global row ids (engram_hash with the table's constants)."""

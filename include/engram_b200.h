@@ -317,6 +317,58 @@ ENGRAM_API int engram_scan_hits(const engram_table* t, const int32_t* tokens, in
                                 int32_t* nhit_out, float* dmax_out, float* dsum_out, int64_t* n_hits,
                                 int64_t* read_count, void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * Row sets: sets of global table rows as device bitmaps (uint32 words, bit g%32
+ * of word g/32 = row g).  They replace the Python sets of the row-set builders:
+ * build_all_read_row_set (engraft/descend_corpus.py:1409-1430), build_rows_var
+ * (engraft/replica/distill.py:401-457) and the union of sum_overlays
+ * (engraft/replica/overlay_sum.py:36-112).  The caller zeroes a bitmap before
+ * its first use.
+ */
+/* Words of a bitmap over n_rows rows. */
+ENGRAM_API int64_t engram_rowset_words(int64_t n_rows);
+
+/* Marks the rows read at positions: for each k < n, position positions[k]
+ * (device int64; NULL: position k) of `tokens` (device int32 [n_tokens]),
+ * hashed with its context as engram_hash does, all n_heads heads
+ * (RowSet.from_position, engraft/lens.py:127-136).  Positions are clamped into
+ * [0, n_tokens). */
+ENGRAM_API int engram_rowset_mark(const engram_table* t, const int32_t* tokens, int64_t n_tokens,
+                                  const int32_t* seg_start, const int64_t* positions, int64_t n, uint32_t* bitmap,
+                                  void* stream);
+
+/* Marks the given global ids (device int32 [n]); ids outside [0, n_rows) are skipped. */
+ENGRAM_API int engram_rowset_mark_ids(const int32_t* ids, int64_t n, int64_t n_rows, uint32_t* bitmap, void* stream);
+
+/* out = a | b (op 0), a & ~b (op 1) or a & b (op 2), word by word; out may alias a or b. */
+ENGRAM_API int engram_rowset_combine(const uint32_t* a, const uint32_t* b, int64_t words, int32_t op, uint32_t* out,
+                                     void* stream);
+
+/* Scratch bytes engram_rowset_extract needs for a bitmap of `words` words. */
+ENGRAM_API int64_t engram_rowset_workspace_bytes(int64_t words);
+
+/* The members in ascending order: *count (device int64) = number of members;
+ * ids_out (device int32 [capacity], nullable when capacity == 0) receives the
+ * first min(count, capacity) of them.  The workspace then holds the bitmap's
+ * word prefixes, which engram_rowset_index reads. */
+ENGRAM_API int engram_rowset_extract(const uint32_t* bitmap, int64_t words, int32_t* ids_out, int64_t capacity,
+                                     int64_t* count, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* index_out[k] = position of ids[k] in the ascending member list, or -1 when
+ * ids[k] is not a member.  Needs the workspace of an engram_rowset_extract of
+ * the same bitmap, run before on the same stream. */
+ENGRAM_API int engram_rowset_index(const uint32_t* bitmap, int64_t words, const void* workspace,
+                                   int64_t workspace_bytes, const int32_t* ids, int64_t n, int32_t* index_out,
+                                   void* stream);
+
+/* acc[index[k]] += data[k] - base[k] for k < n (rows of dim floats, fp32
+ * subtract then add; index -1 skips a row): one .pleo file's deltas added into
+ * the sum over the union of rows (engraft/replica/overlay_sum.py:80-96).  The
+ * rows of one call must have distinct targets; repeated rows go in later calls,
+ * in file order, as np.add.at applies them. */
+ENGRAM_API int engram_overlay_accumulate(float* acc, const int32_t* index, const float* data, const float* base,
+                                         int64_t n, int32_t dim, void* stream);
+
 /* Host self-test of the division magic: out[i] = x[i] % d using exactly the
  * device code path (host arrays).  Lets CPU-only tests check it. */
 ENGRAM_API int engram_selftest_mod(const uint64_t* x, int64_t count, uint32_t d, uint64_t* out);

@@ -220,3 +220,62 @@ def scan_hits(tokens, ngram_size, hpn, mult, head_sizes, head_offsets, eos, over
                         _ptr(dn), len(ov), _ptr(pos), _ptr(nh), _ptr(dmax), _ptr(dsum), _ptr(rc))
     return {"pos": pos[:k], "n_hit_rows": nh[:k], "dnorm_max": dmax[:k], "dnorm_sum": dsum[:k],
             "read_count": rc[:len(ov)], "n_tokens": n}
+
+
+# ---------------------------------------------------------------- row sets
+def rows_read_by_prefixes(frags, ngram_size, hpn, mult, head_sizes, head_offsets, eos) -> np.ndarray:
+    """Ascending global rows read by positions 0..len-2 of each token list
+    (engraft/descend_corpus.py:1409-1430: _rows_read_by_prefix for every
+    fragment, then the sorted union)."""
+    parts = []
+    for f in frags:
+        f = np.asarray(f, dtype=np.int64).astype(np.int32)
+        if f.size > 1:
+            parts.append(hash_ids(f, ngram_size, hpn, mult, head_sizes, head_offsets, eos)[: f.size - 1].ravel())
+    return np.unique(np.concatenate(parts)) if parts else np.zeros(0, np.int32)
+
+
+def rows_var_ids(policy, sets, sequences, exclude_positions, ngram_size, hpn, mult, head_sizes, head_offsets,
+                 eos) -> np.ndarray:
+    """The ascending variable rows of build_rows_var (engraft/replica/distill.py:401-457):
+    the policy's set algebra over the census lists, minus every row read at an
+    excluded position (all heads)."""
+    a = lambda k: np.unique(np.asarray(sets[k], dtype=np.int64))  # noqa: E731
+    if policy == "all-read":
+        cand = a("all_read")
+    elif policy == "private":
+        cand = np.setdiff1d(a("all_read"), a("neutral_read"))
+    elif policy == "entity":
+        cand = np.union1d(a("entity"), a("terme"))
+    elif policy == "t8-answer":
+        cand = a("t8_answer")
+    else:
+        raise ValueError(policy)
+    excl = []
+    for s, positions in (exclude_positions or {}).items():
+        toks = np.asarray(sequences[s], dtype=np.int64).astype(np.int32)
+        ids = hash_ids(toks, ngram_size, hpn, mult, head_sizes, head_offsets, eos)
+        excl.append(ids[np.asarray(positions, dtype=np.int64)].ravel())
+    if excl:
+        cand = np.setdiff1d(cand, np.concatenate(excl))
+    return cand.astype(np.int32)
+
+
+def sum_overlays(files, true_rows_of):
+    """engraft/replica/overlay_sum.py:36-112 restated: files = [(rows, data)];
+    true_rows_of(ids) -> float32 [n, dim].  Returns (rows_union, data_merged,
+    counts) with counts = (moved_any, shared, histogram dict)."""
+    union = np.unique(np.concatenate([np.asarray(r, dtype=np.int64) for r, _ in files])).astype(np.int32)
+    n, dim = union.size, files[0][1].shape[1]
+    delta_sum = np.zeros((n, dim), dtype=np.float32)
+    moved = np.zeros(n, dtype=np.int64)
+    for rows, data in files:
+        delta = data.astype(np.float32) - true_rows_of(rows).astype(np.float32)
+        idx = np.searchsorted(union, rows)
+        np.add.at(delta_sum, idx, delta)
+        np.add.at(moved, idx[np.any(delta != 0, axis=1)], 1)
+    merged = (true_rows_of(union).astype(np.float32) + delta_sum).astype(np.float32)
+    hist = {}
+    for c in moved[moved >= 1].tolist():
+        hist[str(c)] = hist.get(str(c), 0) + 1
+    return union, merged, (int((moved >= 1).sum()), int((moved >= 2).sum()), hist)

@@ -150,3 +150,30 @@ def overlay_noise(seed: int, shape) -> np.ndarray:
 def overlay_grad(seed: int, shape) -> np.ndarray:
     """Upstream gradient fed to the overlay embedding's backward, ~N(0, 1e-3)."""
     return (np.random.default_rng((seed, 2)).standard_normal(shape) * 1e-3).astype(np.float32)
+
+
+def pleo_fact(k: int, pool: np.ndarray, pool_true_rows: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Rows and data of the k-th synthetic .pleo "fact" over a pool of global
+    rows (pool_true_rows[i] = true row of pool[i]): a seeded 40 % subset of the
+    pool at its true values, with seeded noise added to about half of the rows
+    (the others keep a delta of exactly zero).  Fact 1 lists its rows in a
+    shuffled order."""
+    rng = np.random.default_rng((k, 3))
+    pick = np.sort(rng.choice(pool.size, size=max(1, pool.size * 2 // 5), replace=False))
+    if k == 1:
+        pick = pick[rng.permutation(pick.size)]
+    rows = pool[pick].astype(np.int32)
+    data = pool_true_rows[pick].astype(np.float32).copy()
+    moved = rng.random(rows.size) < 0.5
+    data[moved] += (rng.standard_normal((int(moved.sum()), data.shape[1])) * 0.01).astype(np.float32)
+    return rows, data
+
+
+def rowset_case_sets(all_read: np.ndarray) -> dict:
+    """The census row lists of the row-set golden case, derived from all_read."""
+    a = np.asarray(all_read, dtype=np.int64)
+    return {"all_read": a.tolist(), "neutral_read": a[::3].tolist(), "entity": a[::5].tolist(),
+            "terme": a[1::7].tolist(), "t8_answer": a[2::4].tolist()}
+
+
+ROWSET_EXCLUDE = {0: [1, 2], 3: [0], 5: [4, 5, 6]}

@@ -54,6 +54,13 @@ def write_syn_gguf(path: Path, gguf) -> None:
     w.close()
 
 
+def _head_local(table, g: int) -> tuple[int, int]:
+    """(head, local index) of global row g."""
+    offs = np.asarray(table.head_offsets, dtype=np.int64)
+    h = int(np.searchsorted(offs, g, side="right") - 1)
+    return h, g - int(offs[h])
+
+
 def hash_case(table, tokens: list[int], damage) -> np.ndarray:
     from engraft.lens import local_to_global
     addr = table.ngram_addresses(tokens)
@@ -253,6 +260,38 @@ def main(ref_root: str) -> None:
     out["scan_dnorm"] = dnorm_sorted
     for k in ("pos", "n_hit_rows", "dnorm_max", "dnorm_sum", "read_count"):
         out[f"scan_{k}"] = hits[k]
+
+    # ---- 8. row sets and overlay files (descend_corpus.py:1409-1430,
+    #         distill.py:401-457, overlay_sum.py:36-112, descend_corpus.py:627-647)
+    import engraft.descend_corpus as dc
+    from engraft.replica.overlay_sum import sum_overlays
+    frags = FX.fragments(seed=31, n_frag=12, vocab=50, eos=ft7.eos_token_id, lo=3, hi=120)
+    all_read = np.asarray(dc.build_all_read_row_set(ft7, frags)["all_read"], dtype=np.int32)
+    out["rowset_all_read"] = all_read
+    sets = FX.rowset_case_sets(all_read)
+    for policy in ("all-read", "private", "entity", "t8-answer"):
+        row_map, rows_var = distill.build_rows_var(ft7, frags, policy, sets, FX.ROWSET_EXCLUDE)
+        key = policy.replace("-", "_")
+        out[f"rowset_{key}_ids"] = np.asarray(list(row_map.keys()), dtype=np.int32)
+        out[f"rowset_{key}_rows_sha"] = np.array(sha(rows_var.numpy()))
+    true_all = np.stack([ft7.read_rows(*_head_local(ft7, int(g)), 1)[0] for g in all_read]).astype(np.float32)
+    with tempfile.TemporaryDirectory() as td:
+        paths = []
+        for k in range(3):
+            rows, data = FX.pleo_fact(k, all_read, true_all)
+            pth = Path(td) / f"fact{k}.pleo"
+            write_pleo(pth, rows, data)
+            paths.append(pth)
+        union, merged, manifest = sum_overlays(ft7, paths)
+        out["sumov_union"] = union
+        out["sumov_merged_sha"] = np.array(sha(merged))
+        out["sumov_manifest"] = np.array(repr(manifest))
+        row_map, rows_var = distill.build_rows_var(ft7, frags, "private", sets, FX.ROWSET_EXCLUDE)
+        rows_var = rows_var + torch.from_numpy(FX.overlay_noise(5, tuple(rows_var.shape)))
+        mp = Path(td) / "merged.pleo"
+        info = dc.write_merged_pleo(ft7, row_map, rows_var, all_read.tolist(), mp)
+        out["merged_bytes_sha"] = np.array(hashlib.sha256(mp.read_bytes()).hexdigest())
+        out["merged_n_frozen"] = np.int64(info["n_rows_frozen"])
 
     meta = dict(reference_root=str(ref_root), torch=torch.__version__, numpy=np.__version__,
                 gguf=getattr(gguf, "__version__", "0.19.0"))

@@ -374,6 +374,41 @@ def test_row_sharded_table_matches_resident_table(eb, world, fmt, dim, mode):
         assert np.array_equal(got.reshape(want.shape), want), r
 
 
+def test_sharded_table_through_the_public_autograd_api(eb):
+    """engram_residual_add and engram_embed given a ShardedTable (W = 2
+    emulated): outputs and row gradients equal the resident table's."""
+    from engraft_ngram_b200.shard import ShardedTable, local_exchange
+    rng = np.random.default_rng(77)
+    spec = random_spec(O.FMT_IQ4_XS, 256, 30_001, 77)
+    full = device_table(eb, spec)
+    shards = [ShardedTable.from_full(full, 2, r) for r in range(2)]
+    ex = local_exchange(shards)
+    for sh in shards:
+        sh.exchange = ex
+    T = 1200
+    toks = zipf_tokens(rng, T)
+    ss = torch.from_numpy(FX.seg_starts(np.sort(rng.integers(0, 4, size=T))))
+    ov_ids = np.unique(np.concatenate([np.unique(spec.ids(toks))[::3], rng.integers(0, 30_001, size=100)]))
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids.astype(np.int32)), DEV)
+    rows0 = (rng.standard_normal((len(ov_ids), 256)) * 0.01).astype(np.float32)
+    res0 = O.bf16_bits((rng.standard_normal((T, 8 * 256)) * 0.5).astype(np.float32))
+    gout = O.bf16_bits((rng.standard_normal((T, 8 * 256)) * 1e-2).astype(np.float32))
+    results = []
+    for table in (full, shards[1]):
+        rv = torch.from_numpy(rows0).to(DEV).requires_grad_(True)
+        res = torch.from_numpy(res0.view(np.int16)).to(DEV).view(torch.bfloat16)
+        out = eb.engram_residual_add(res, table, toks, rv, omap, ss)
+        out.backward(torch.from_numpy(gout.view(np.int16)).to(DEV).view(torch.bfloat16))
+        rv2 = torch.from_numpy(rows0).to(DEV).requires_grad_(True)
+        emb = eb.engram_embed(table, toks, rv2, omap, ss)
+        results.append((out.detach().view(torch.int16).cpu().numpy(), rv.grad.cpu().numpy(),
+                        emb.detach().cpu().numpy()))
+    (o_a, g_a, e_a), (o_b, g_b, e_b) = results
+    assert np.array_equal(o_a, o_b)
+    assert np.array_equal(g_a.view(np.uint32), g_b.view(np.uint32))
+    assert np.array_equal(e_a.view(np.uint32), e_b.view(np.uint32))
+
+
 # ------------------------------------------------- bulk hash + overlay hit scan
 def test_scan_hits_matches_reference_golden(eb, golden):
     p = FX.fake_table_params(seed=7)
@@ -432,3 +467,108 @@ def test_scan_hits_large_corpus_vs_oracle(eb):
         assert np.array_equal(got[k], ref[k]), k
     for k in ("dnorm_max", "dnorm_sum"):
         assert np.array_equal(got[k].view(np.uint32), ref[k].view(np.uint32)), k
+
+
+# ------------------------------------------------- row sets and overlay files
+class _FakeTable7:
+    """FakeTable(seed=7)'s interface (engraft/testing/fake_table.py): addressing
+    constants plus read_rows, over its rows restated by the fixtures."""
+
+    def __init__(self):
+        p = FX.fake_table_params(seed=7)
+        self.rows = FX.fake_table_rows(seed=7)
+        self.head_vocab_sizes = list(p["head_sizes"])
+        self.head_offsets = list(p["head_offsets"])
+        self.layer_multipliers = list(p["mult"])
+        self.eos_token_id = p["eos"]
+        self.ngram_size = p["ngram_size"]
+        self.heads_per_ngram = p["hpn"]
+
+    def read_rows(self, h, start, n):
+        o = self.head_offsets[h] + start
+        return self.rows[o:o + n]
+
+
+@pytest.fixture(scope="module")
+def fake7():
+    return _FakeTable7()
+
+
+def _frags7():
+    return FX.fragments(seed=31, n_frag=12, vocab=50, eos=FX.fake_table_params(seed=7)["eos"], lo=3, hi=120)
+
+
+def test_build_all_read_row_set_matches_reference_golden(eb, golden, fake7):
+    from engraft_ngram_b200 import rowset
+    got = rowset.build_all_read_row_set(fake7, _frags7())
+    assert got["all_read"] == golden["rowset_all_read"].tolist()
+
+
+@pytest.mark.parametrize("policy", ["all-read", "private", "entity", "t8-answer"])
+def test_build_rows_var_matches_reference_golden(eb, golden, fake7, policy):
+    import hashlib
+    from engraft_ngram_b200 import rowset
+    sets = FX.rowset_case_sets(golden["rowset_all_read"])
+    row_map, rows_var = rowset.build_rows_var(fake7, _frags7(), policy, sets, FX.ROWSET_EXCLUDE)
+    key = policy.replace("-", "_")
+    assert list(row_map.keys()) == golden[f"rowset_{key}_ids"].tolist()
+    assert list(row_map.values()) == list(range(len(row_map)))
+    assert rows_var.device.type == "cpu" and rows_var.dtype == torch.float32
+    assert hashlib.sha256(rows_var.numpy().tobytes()).hexdigest() == str(golden[f"rowset_{key}_rows_sha"])
+
+
+def test_sum_overlays_matches_reference_golden(eb, golden, fake7, tmp_path):
+    import ast
+    import hashlib
+    from engraft_ngram_b200 import rowset
+    all_read = golden["rowset_all_read"]
+    paths = []
+    for k in range(3):
+        rows, data = FX.pleo_fact(k, all_read, fake7.rows[all_read])
+        pth = tmp_path / f"fact{k}.pleo"
+        eb.write_pleo(pth, rows, data)
+        paths.append(pth)
+    union, merged, manifest = rowset.sum_overlays(fake7, paths)
+    assert np.array_equal(union, golden["sumov_union"]) and union.dtype == np.int32
+    assert hashlib.sha256(merged.tobytes()).hexdigest() == str(golden["sumov_merged_sha"])
+    ref = ast.literal_eval(str(golden["sumov_manifest"]))
+    for k in ("n_files", "n_rows_union", "n_rows_moved_any", "n_rows_shared", "facts_per_row_histogram",
+              "quant_floor", "max_row_delta_norm_over_quant_floor"):
+        assert manifest[k] == ref[k], k
+    for k in ("shared_rows_sum_abs_norm_mean", "shared_rows_sum_abs_norm_max", "shared_rows_abs_sum_norm_mean",
+              "shared_rows_abs_sum_norm_max", "max_row_delta_norm"):
+        assert manifest[k] == pytest.approx(ref[k], rel=1e-12, abs=1e-15), k  # float64 norms, summed in another order
+
+
+def test_write_merged_pleo_matches_reference_golden(eb, golden, fake7, tmp_path):
+    import hashlib
+    from engraft_ngram_b200 import rowset
+    sets = FX.rowset_case_sets(golden["rowset_all_read"])
+    row_map, rows_var = rowset.build_rows_var(fake7, _frags7(), "private", sets, FX.ROWSET_EXCLUDE)
+    rows_var = rows_var + torch.from_numpy(FX.overlay_noise(5, tuple(rows_var.shape)))
+    out = tmp_path / "merged.pleo"
+    info = rowset.write_merged_pleo(fake7, row_map, rows_var, golden["rowset_all_read"].tolist(), out)
+    assert info["n_rows_frozen"] == int(golden["merged_n_frozen"])
+    assert hashlib.sha256(out.read_bytes()).hexdigest() == str(golden["merged_bytes_sha"])
+
+
+def test_device_row_set_algebra_and_index_vs_numpy(eb):
+    """Unions, differences, intersections, the sorted list and member indices
+    on a 320 M-row table (40 MB bitmaps), against numpy set operations."""
+    from engraft_ngram_b200.rowset import DeviceRowSet
+    rng = np.random.default_rng(3)
+    n_rows = 320_001_536
+    a_ids = np.unique(rng.integers(0, n_rows, size=200_000))
+    b_ids = np.unique(np.concatenate([a_ids[::3], rng.integers(0, n_rows, size=50_000), [0, n_rows - 1]]))
+    a = DeviceRowSet.of_ids(a_ids, n_rows, DEV)
+    b = DeviceRowSet.of_ids(b_ids, n_rows, DEV)
+    assert np.array_equal(a.ids().cpu().numpy(), a_ids)
+    assert np.array_equal((a | b).ids().cpu().numpy(), np.union1d(a_ids, b_ids))
+    assert np.array_equal((a - b).ids().cpu().numpy(), np.setdiff1d(a_ids, b_ids))
+    assert np.array_equal((a & b).ids().cpu().numpy(), np.intersect1d(a_ids, b_ids))
+    assert len(b) == b_ids.size
+    probe = np.concatenate([b_ids[::7], rng.integers(0, n_rows, size=1000)]).astype(np.int32)
+    idx = b.index(torch.from_numpy(probe)).cpu().numpy()
+    pos = np.searchsorted(b_ids, probe)
+    member = (pos < b_ids.size) & (b_ids[np.minimum(pos, b_ids.size - 1)] == probe)
+    assert np.array_equal(idx, np.where(member, pos, -1))

@@ -76,6 +76,33 @@ def test_install_scan_replaces_module_attribute():
     assert dmg.scan_hits == "reference-function"
 
 
+def test_install_rowsets_replaces_and_restores_the_builders():
+    names = ("engraft.replica.distill", "engraft.descend_corpus", "engraft.replica.overlay_sum")
+    mods = {n: types.SimpleNamespace() for n in names}
+    mods["engraft.replica.distill"].build_rows_var = "ref-brv"
+    mods["engraft.descend_corpus"].build_all_read_row_set = "ref-ars"
+    mods["engraft.descend_corpus"].write_merged_pleo = "ref-wmp"
+    mods["engraft.descend_corpus"].sum_overlays = "ref-so"
+    mods["engraft.replica.overlay_sum"].sum_overlays = "ref-so2"
+    eb.install_rowsets(mods)
+    assert mods["engraft.replica.distill"].build_rows_var is eb.build_rows_var
+    assert mods["engraft.descend_corpus"].build_all_read_row_set is eb.build_all_read_row_set
+    assert mods["engraft.descend_corpus"].write_merged_pleo is eb.write_merged_pleo
+    assert mods["engraft.descend_corpus"].sum_overlays is eb.sum_overlays
+    assert mods["engraft.replica.overlay_sum"].sum_overlays is eb.sum_overlays
+    eb.uninstall_rowsets(mods)
+    assert mods["engraft.replica.distill"].build_rows_var == "ref-brv"
+    assert mods["engraft.replica.overlay_sum"].sum_overlays == "ref-so2"
+
+
+def test_fragment_layout_of_the_row_set_builder():
+    from engraft_ngram_b200.rowset import _fragments
+    tokens, seg, pos = _fragments([[5, 6, 7], [8], [9, 10]])
+    assert tokens.tolist() == [5, 6, 7, 8, 9, 10]
+    assert seg.tolist() == [0, 0, 0, 3, 4, 4]
+    assert pos.tolist() == [0, 1, 4]  # positions 0..len-2 of each fragment
+
+
 def test_overlay_emb_refuses_cpu_tensors():
     ov = eb.OverlayEmb(object(), [1, 2, 3], torch.zeros(0, 160), {})
     with pytest.raises(RuntimeError):

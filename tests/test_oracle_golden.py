@@ -118,3 +118,38 @@ def test_scan_hits_matches_reference(golden):
     assert np.array_equal(got["dnorm_max"].view(np.uint32), golden["scan_dnorm_max"].view(np.uint32))
     assert np.array_equal(got["dnorm_sum"].view(np.uint32), golden["scan_dnorm_sum"].view(np.uint32))
     assert np.array_equal(got["read_count"], golden["scan_read_count"])
+
+
+# ---------------------------------------------------------------- row sets
+def _fake7():
+    p = FX.fake_table_params(seed=7)
+    return p, (3, 8, p["mult"], p["head_sizes"], p["head_offsets"], p["eos"])
+
+
+def test_oracle_rows_read_by_prefixes_matches_reference_golden(golden):
+    p, geo = _fake7()
+    frags = FX.fragments(seed=31, n_frag=12, vocab=50, eos=p["eos"], lo=3, hi=120)
+    got = O.rows_read_by_prefixes(frags, *geo)
+    assert np.array_equal(got, golden["rowset_all_read"])
+
+
+@pytest.mark.parametrize("policy", ["all-read", "private", "entity", "t8-answer"])
+def test_oracle_rows_var_ids_match_reference_golden(golden, policy):
+    p, geo = _fake7()
+    frags = FX.fragments(seed=31, n_frag=12, vocab=50, eos=p["eos"], lo=3, hi=120)
+    sets = FX.rowset_case_sets(golden["rowset_all_read"])
+    got = O.rows_var_ids(policy, sets, frags, FX.ROWSET_EXCLUDE, *geo)
+    assert np.array_equal(got, golden[f"rowset_{policy.replace('-', '_')}_ids"])
+
+
+def test_oracle_sum_overlays_matches_reference_golden(golden):
+    import ast
+    import hashlib
+    rows7 = FX.fake_table_rows(seed=7)
+    all_read = golden["rowset_all_read"]
+    files = [FX.pleo_fact(k, all_read, rows7[all_read]) for k in range(3)]
+    union, merged, (moved, shared, hist) = O.sum_overlays(files, lambda ids: rows7[np.asarray(ids)])
+    assert np.array_equal(union, golden["sumov_union"])
+    assert hashlib.sha256(merged.tobytes()).hexdigest() == str(golden["sumov_merged_sha"])
+    man = ast.literal_eval(str(golden["sumov_manifest"]))
+    assert (moved, shared, hist) == (man["n_rows_moved_any"], man["n_rows_shared"], man["facts_per_row_histogram"])

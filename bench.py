@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--table-rows", type=int, default=None, help="override (profiling a small case)")
     ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="N>1, replicated table: the optimizer exchange as one peer-memory kernel per rank "
+                         "(symmetric memory, engram_adam_peer_step) or as NCCL reduce-scatter + all-gather")
     ap.add_argument("--shard", action="store_true",
                     help="row-sharded table: each rank holds rows g with g %% N == rank; rows move by NCCL all-to-all")
     return ap.parse_args()
@@ -168,8 +171,22 @@ class Workload:
             self.p0 = torch.randn(self.R, self.dim, generator=gp, device=device) * 0.0085
         else:
             self.p0 = self.table.gather_rows(self.ov_ids) if self.R else torch.zeros(0, self.dim, device=device)
-        self.rows_var = self.p0.clone()
-        self.grad_rows = torch.zeros_like(self.p0)
+        self.peer = None
+        if world > 1 and self.shard is None and cfg.get("exchange", "peer") == "peer" and self.R and self.dim % 4 == 0:
+            from engraft_ngram_b200.dist import PeerRows
+            try:
+                self.peer = PeerRows(self.R, self.dim, device)
+            except Exception as exc:  # no symmetric memory here: keep the NCCL collectives, and say so
+                print(f"[bench] peer-memory exchange unavailable ({exc!r}); using NCCL collectives", file=sys.stderr)
+                cfg["exchange"] = "nccl"
+        if self.peer is not None:
+            self.peer.rows_var.copy_(self.p0)
+            self.peer.grad_rows.zero_()
+            self.rows_var = self.peer.rows_var
+            self.grad_rows = self.peer.grad_rows
+        else:
+            self.rows_var = self.p0.clone()
+            self.grad_rows = torch.zeros_like(self.p0)
         nh, hpn = self.table.n_heads, 8
         self.nh, self.hpn = nh, hpn
         gg = torch.Generator(device=device)
@@ -234,6 +251,10 @@ class Workload:
         from engraft_ngram_b200.dist import all_gather_rows, reduce_scatter_rows, shard_bounds
         self.step_count += 1
         lo, hi = shard_bounds(self.R, self.world, self.rank)
+        if self.peer is not None:  # one kernel: sum over ranks, Adam, store into every rank's rows
+            self.peer.step(self.m, self.v, self.p0[lo:hi], self.step_count, self.lr, 0.9, 0.999, 1e-8,
+                           self.reg_scale)
+            return
         p = self.rows_var[lo:hi]
         g = self.grad_rows[lo:hi] if dist is None else reduce_scatter_rows(self.grad_rows)
         st = self.L.load().engram_adam_step(p.data_ptr(), g.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
@@ -520,6 +541,9 @@ def config_json(cfg, args):
             "table_rows": cfg["rows"], "dim": cfg["dim"], "format": cfg["fmt"], "positions_per_gpu": cfg["seqs"] * cfg["seq_len"],
             "overlay_rows": cfg["R"], "emit": cfg["mode"],
             "parallelism": f"dp{args.gpus}" + ("+row-sharded table (id mod N, NCCL all-to-all of ids and rows)" if cfg.get("shard") else ""),
+            "optimizer_exchange": (None if args.gpus == 1 or cfg.get("shard") else
+                                   ("one peer-memory kernel per rank (sum over ranks + Adam + stores to every rank)"
+                                    if cfg.get("exchange", "peer") == "peer" else "NCCL reduce-scatter + all-gather")),
             "l2": "inputs larger than L2 (residual and upstream gradient 537 MB each, table 46 GB)"}
 
 
@@ -538,6 +562,7 @@ def main():
     if args.seqs:
         cfg["seqs"] = args.seqs
     cfg["shard"] = bool(args.shard)
+    cfg["exchange"] = args.exchange
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

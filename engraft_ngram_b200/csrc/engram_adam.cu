@@ -55,6 +55,55 @@ __global__ void k_adam_scalar(float* __restrict__ p, const float* __restrict__ g
     }
 }
 
+// Data-parallel optimizer step fused with its exchange, over peer memory.
+// grads[k] / rows[k]: rank k's grad_rows and rows_var ([R, dim] fp32, mapped
+// into this process over NVLink).  This rank owns the elements [lo, lo + n):
+// it sums the ranks' gradients in rank order, steps its own copy of the
+// parameter (m, v, p0 hold only the owned elements) and stores the result into
+// every rank's rows_var.  No waits inside: the caller orders the ranks around
+// the launch.
+__global__ void __launch_bounds__(256) k_adam_peer_vec4(const float4* const* __restrict__ grads,
+                                                        float4* const* __restrict__ rows, int world, int rank,
+                                                        int64_t lo4, int64_t n4, float4* __restrict__ m,
+                                                        float4* __restrict__ v, const float4* __restrict__ p0,
+                                                        AdamScalars a) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e = lo4 + i;
+        float4 gg = __ldcv(grads[0] + e);
+        for (int k = 1; k < world; k++) {
+            const float4 x = __ldcv(grads[k] + e);
+            gg.x = __fadd_rn(gg.x, x.x);
+            gg.y = __fadd_rn(gg.y, x.y);
+            gg.z = __fadd_rn(gg.z, x.z);
+            gg.w = __fadd_rn(gg.w, x.w);
+        }
+        float4 pp = rows[rank][e], mm = m[i], vv = v[i];
+        const float4 q = p0 ? __ldg(p0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const bool reg = p0 != nullptr;
+        adam_elem(pp.x, gg.x, mm.x, vv.x, q.x, reg, a);
+        adam_elem(pp.y, gg.y, mm.y, vv.y, q.y, reg, a);
+        adam_elem(pp.z, gg.z, mm.z, vv.z, q.z, reg, a);
+        adam_elem(pp.w, gg.w, mm.w, vv.w, q.w, reg, a);
+        m[i] = mm;
+        v[i] = vv;
+        for (int k = 0; k < world; k++) __stcg(rows[k] + e, pp);
+    }
+}
+
+AdamScalars adam_scalars(int64_t step, double lr, double beta1, double beta2, double eps, float reg_scale) {
+    AdamScalars a;
+    const double bc1 = 1.0 - pow(beta1, (double)step);
+    const double bc2 = 1.0 - pow(beta2, (double)step);
+    a.w1 = (float)(1.0 - beta1);
+    a.b2 = (float)beta2;
+    a.w2 = (float)(1.0 - beta2);
+    a.eps = (float)eps;
+    a.neg_step_size = -(float)(lr / bc1);
+    a.bc2_sqrt = (float)sqrt(bc2);
+    a.reg_scale = reg_scale;
+    return a;
+}
+
 int grid_for(int64_t work, int threads, int per_sm) {
     const int64_t want = (work + threads - 1) / threads;
     const int64_t cap = (int64_t)sm_count() * per_sm;
@@ -70,16 +119,7 @@ extern "C" int engram_adam_step(float* p, const float* g, float* m, float* v, co
     if (numel < 0 || step < 1) return ENGRAM_ERR_ARG;
     if (numel == 0) return ENGRAM_OK;
     if (!p || !g || !m || !v) return ENGRAM_ERR_ARG;
-    AdamScalars a;
-    const double bc1 = 1.0 - pow(beta1, (double)step);
-    const double bc2 = 1.0 - pow(beta2, (double)step);
-    a.w1 = (float)(1.0 - beta1);
-    a.b2 = (float)beta2;
-    a.w2 = (float)(1.0 - beta2);
-    a.eps = (float)eps;
-    a.neg_step_size = -(float)(lr / bc1);
-    a.bc2_sqrt = (float)sqrt(bc2);
-    a.reg_scale = reg_scale;
+    const AdamScalars a = adam_scalars(step, lr, beta1, beta2, eps, reg_scale);
     cudaStream_t s = (cudaStream_t)stream;
     const bool vec = aligned16(p) && aligned16(g) && aligned16(m) && aligned16(v) && (!p0 || aligned16(p0));
     int64_t done = 0;
@@ -100,3 +140,21 @@ extern "C" int engram_adam_step(float* p, const float* g, float* m, float* v, co
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
 
+
+extern "C" int engram_adam_peer_step(const void* grad_ptrs, const void* rows_ptrs, int32_t world, int32_t rank,
+                                     int64_t lo, int64_t n, float* m, float* v, const float* p0, int64_t step,
+                                     double lr, double beta1, double beta2, double eps, float reg_scale,
+                                     void* stream) {
+    if (world < 1 || rank < 0 || rank >= world || lo < 0 || n < 0 || step < 1) return ENGRAM_ERR_ARG;
+    if ((lo & 3) || (n & 3)) return ENGRAM_ERR_FORMAT;  // float4 elements
+    if (n == 0) return ENGRAM_OK;
+    if (!grad_ptrs || !rows_ptrs || !m || !v) return ENGRAM_ERR_ARG;
+    if (!aligned16(m) || !aligned16(v) || (p0 && !aligned16(p0))) return ENGRAM_ERR_ARG;
+    const AdamScalars a = adam_scalars(step, lr, beta1, beta2, eps, reg_scale);
+    const int64_t n4 = n / 4;
+    k_adam_peer_vec4<<<grid_for(n4, 256, 8), 256, 0, (cudaStream_t)stream>>>(
+        static_cast<const float4* const*>(grad_ptrs), static_cast<float4* const*>(rows_ptrs), world, rank, lo / 4, n4,
+        reinterpret_cast<float4*>(m), reinterpret_cast<float4*>(v), reinterpret_cast<const float4*>(p0), a);
+    count_launches(1);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}

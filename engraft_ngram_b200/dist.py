@@ -74,3 +74,54 @@ def all_gather_rows(rows_var: torch.Tensor, shard: torch.Tensor, group=None) -> 
     dist.all_gather(parts, padded, group=group)
     for (lo, hi), part in zip(spans, parts):
         rows_var[lo:hi].copy_(part[: hi - lo])
+
+
+def adam_peer_step(grad_ptrs: torch.Tensor, rows_ptrs: torch.Tensor, world: int, rank: int, R: int, dim: int,
+                   m: torch.Tensor, v: torch.Tensor, p0: torch.Tensor | None, step: int, lr: float,
+                   beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, reg_scale: float = 0.0) -> None:
+    """engram_adam_peer_step for this rank's shard_bounds rows: grad_ptrs /
+    rows_ptrs are int64 device tensors of every rank's grad_rows / rows_var
+    address; m, v, p0 hold the shard's rows only."""
+    from . import _lib as L
+    lo, hi = shard_bounds(R, world, rank)
+    st = L.load().engram_adam_peer_step(grad_ptrs.data_ptr(), rows_ptrs.data_ptr(), world, rank, lo * dim,
+                                        (hi - lo) * dim, m.data_ptr(), v.data_ptr(), L.ptr(p0), int(step),
+                                        float(lr), float(beta1), float(beta2), float(eps), float(reg_scale),
+                                        L.stream_of(m.device))
+    L.check(st, "engram_adam_peer_step")
+
+
+class PeerRows:
+    """grad_rows and rows_var [R, dim] fp32 allocated in torch symmetric memory,
+    so every rank's copies are mapped into every process over NVLink.  step()
+    is the data-parallel optimizer step as one kernel per rank
+    (engram_adam_peer_step): it replaces reduce_scatter_rows + Adam +
+    all_gather_rows, with two tiny NCCL all-reduces as the barriers around it
+    (all gradients written before any rank reads them; all rows stored before
+    any rank's next forward reads them)."""
+
+    def __init__(self, R: int, dim: int, device, group=None):
+        import torch.distributed._symmetric_memory as symm
+        if dim % 4:
+            raise ValueError("PeerRows needs dim % 4 == 0 (16-byte row pieces)")
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.R, self.dim = int(R), int(dim)
+        self.grad_rows = symm.empty(max(self.R, 1), self.dim, dtype=torch.float32, device=device)
+        self.rows_var = symm.empty(max(self.R, 1), self.dim, dtype=torch.float32, device=device)
+        self._hg = symm.rendezvous(self.grad_rows, self.group)
+        self._hr = symm.rendezvous(self.rows_var, self.group)
+        self.grad_ptrs = torch.tensor(list(self._hg.buffer_ptrs), dtype=torch.int64, device=device)
+        self.rows_ptrs = torch.tensor(list(self._hr.buffer_ptrs), dtype=torch.int64, device=device)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def barrier(self) -> None:
+        dist.all_reduce(self._flag, group=self.group)
+
+    def step(self, m: torch.Tensor, v: torch.Tensor, p0: torch.Tensor | None, step: int, lr: float,
+             beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, reg_scale: float = 0.0) -> None:
+        self.barrier()
+        adam_peer_step(self.grad_ptrs, self.rows_ptrs, self.world, self.rank, self.R, self.dim, m, v, p0, step, lr,
+                       beta1, beta2, eps, reg_scale)
+        self.barrier()

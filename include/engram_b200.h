@@ -296,6 +296,24 @@ ENGRAM_API int engram_adam_step(float* p, const float* g, float* m, float* v, co
                      int64_t step, double lr, double beta1, double beta2, double eps, float reg_scale,
                      void* stream);
 
+/*
+ * The data-parallel optimizer step fused with its exchange, over peer memory
+ * (no reference counterpart: the reference is single-process).  grad_ptrs and
+ * rows_ptrs: device arrays of `world` pointers to each rank's grad_rows and
+ * rows_var ([R, dim] fp32, each rank's buffer mapped into this process, e.g.
+ * torch symmetric memory).  This rank owns the flat elements [lo, lo + n) (lo
+ * and n multiples of 4, 16-byte aligned buffers): it sums the ranks' gradients
+ * in rank order, runs engram_adam_step's update on them (m, v, p0 hold the
+ * owned elements only) and stores the new values into every rank's rows_var.
+ * The kernel does not wait on other ranks: call it after every rank's
+ * gradients are complete, and let no rank read rows_var before every rank's
+ * call has finished (two barriers, e.g. tiny NCCL all-reduces on the stream).
+ */
+ENGRAM_API int engram_adam_peer_step(const void* grad_ptrs, const void* rows_ptrs, int32_t world, int32_t rank,
+                                     int64_t lo, int64_t n, float* m, float* v, const float* p0, int64_t step,
+                                     double lr, double beta1, double beta2, double eps, float reg_scale,
+                                     void* stream);
+
 /* Scratch bytes engram_scan_hits needs for n positions. */
 ENGRAM_API int64_t engram_scan_hits_workspace_bytes(int64_t n);
 

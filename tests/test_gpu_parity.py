@@ -572,3 +572,43 @@ def test_device_row_set_algebra_and_index_vs_numpy(eb):
     pos = np.searchsorted(b_ids, probe)
     member = (pos < b_ids.size) & (b_ids[np.minimum(pos, b_ids.size - 1)] == probe)
     assert np.array_equal(idx, np.where(member, pos, -1))
+
+
+def test_adam_peer_step_emulated_ranks_match_summed_adam(eb):
+    """engram_adam_peer_step with W = 3 ranks emulated on one GPU (separate
+    buffers, one launch per rank): every rank's rows equal Adam over the
+    rank-order sum of the gradients, and each rank's m, v shard match."""
+    from engraft_ngram_b200 import _lib as L
+    from engraft_ngram_b200.dist import adam_peer_step, shard_bounds
+    rng = np.random.default_rng(12)
+    W, R, dim = 3, 1001, 256
+    p_init = (rng.standard_normal((R, dim)) * 0.01).astype(np.float32)
+    p0 = torch.from_numpy(p_init.copy()).to(DEV)
+    grads = [torch.from_numpy((rng.standard_normal((R, dim)) * 1e-3).astype(np.float32)).to(DEV) for _ in range(W)]
+    rows = [torch.from_numpy(p_init.copy()).to(DEV) for _ in range(W)]
+    gp = torch.tensor([g.data_ptr() for g in grads], dtype=torch.int64, device=DEV)
+    rp = torch.tensor([r.data_ptr() for r in rows], dtype=torch.int64, device=DEV)
+    ms = [torch.zeros(*(shard_bounds(R, W, r)[1] - shard_bounds(R, W, r)[0], dim), device=DEV) for r in range(W)]
+    vs = [torch.zeros_like(m) for m in ms]
+    # reference: dense sum in rank order, then the single-GPU Adam kernel
+    ref_p = torch.from_numpy(p_init.copy()).to(DEV)
+    ref_m, ref_v = torch.zeros_like(ref_p), torch.zeros_like(ref_p)
+    rs = float(eb.reg_scale(0.1, p0))
+    for step in (1, 2, 3):
+        for r in range(W):
+            lo, hi = shard_bounds(R, W, r)
+            adam_peer_step(gp, rp, W, r, R, dim, ms[r], vs[r], p0[lo:hi], step, 1e-3, reg_scale=rs)
+        g = grads[0].clone()
+        for k in range(1, W):
+            g = g + grads[k]
+        st = L.load().engram_adam_step(ref_p.data_ptr(), g.data_ptr(), ref_m.data_ptr(), ref_v.data_ptr(),
+                                       p0.data_ptr(), ref_p.numel(), step, 1e-3, 0.9, 0.999, 1e-8, rs,
+                                       L.stream_of(ref_p.device))
+        L.check(st, "engram_adam_step")
+        for r in range(W):
+            assert torch.equal(rows[r].view(torch.int32), ref_p.view(torch.int32)), (step, r)
+            lo, hi = shard_bounds(R, W, r)
+            assert torch.equal(ms[r].view(torch.int32), ref_m[lo:hi].view(torch.int32))
+            assert torch.equal(vs[r].view(torch.int32), ref_v[lo:hi].view(torch.int32))
+        for gr in grads:
+            gr.mul_(0.5)

@@ -1,0 +1,80 @@
+"""Multi-GPU paths on real ranks (one process per GPU, NCCL).  Skipped with
+fewer than two GPUs; the single-GPU suite covers the same kernels with ranks
+emulated on one device."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _peer_vs_nccl(rank: int, world: int, port: int, out) -> None:
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        from engraft_ngram_b200 import _lib as L
+        from engraft_ngram_b200.dist import PeerRows, all_gather_rows, reduce_scatter_rows, shard_bounds
+        R, dim = 4000, 256
+        rng = np.random.default_rng(5)
+        p_init = torch.from_numpy((rng.standard_normal((R, dim)) * 0.01).astype(np.float32)).to(dev)
+        grads = [torch.from_numpy((rng.standard_normal((R, dim)) * 1e-3).astype(np.float32)).to(dev)
+                 for _ in range(world)]
+        lo, hi = shard_bounds(R, world, rank)
+        peer = PeerRows(R, dim, dev)
+        peer.rows_var.copy_(p_init)
+        m1, v1 = torch.zeros(hi - lo, dim, device=dev), torch.zeros(hi - lo, dim, device=dev)
+        rows2 = p_init.clone()
+        m2, v2 = torch.zeros(hi - lo, dim, device=dev), torch.zeros(hi - lo, dim, device=dev)
+        ok = True
+        for step in (1, 2, 3):
+            g = grads[rank] * (0.5 ** step)
+            peer.grad_rows.copy_(g)
+            peer.step(m1, v1, p_init[lo:hi], step, 1e-3, reg_scale=0.25)
+            shard = reduce_scatter_rows(g)
+            p = rows2[lo:hi]
+            st = L.load().engram_adam_step(p.data_ptr(), shard.data_ptr(), m2.data_ptr(), v2.data_ptr(),
+                                           p_init[lo:hi].data_ptr(), p.numel(), step, 1e-3, 0.9, 0.999, 1e-8, 0.25,
+                                           L.stream_of(dev))
+            L.check(st, "engram_adam_step")
+            all_gather_rows(rows2, p)
+            torch.cuda.synchronize()
+            ok &= torch.equal(peer.rows_var.view(torch.int32), rows2.view(torch.int32))
+            ok &= torch.equal(m1.view(torch.int32), m2.view(torch.int32))
+        out[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_matches_nccl_collectives_on_two_ranks():
+    """Two ranks: the peer-memory optimizer step equals NCCL reduce-scatter +
+    Adam + all-gather bit for bit (a two-term sum does not depend on order)."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_vs_nccl, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(out) == {0: True, 1: True}

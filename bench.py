@@ -65,7 +65,7 @@ def parse():
     ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="N>1, replicated table: the optimizer exchange as one peer-memory kernel per rank "
-                         "(symmetric memory, engram_adam_peer_step) or as NCCL reduce-scatter + all-gather")
+                         "(symmetric memory: engram_backward_to_owners + engram_adam_owner_step) or as NCCL reduce-scatter + all-gather")
     ap.add_argument("--shard", action="store_true",
                     help="row-sharded table: each rank holds rows g with g %% N == rank; rows move by NCCL all-to-all")
     return ap.parse_args()
@@ -181,9 +181,8 @@ class Workload:
                 cfg["exchange"] = "nccl"
         if self.peer is not None:
             self.peer.rows_var.copy_(self.p0)
-            self.peer.grad_rows.zero_()
             self.rows_var = self.peer.rows_var
-            self.grad_rows = self.peer.grad_rows
+            self.grad_rows = torch.zeros_like(self.p0)  # unused: the backward writes to the owners
         else:
             self.rows_var = self.p0.clone()
             self.grad_rows = torch.zeros_like(self.p0)
@@ -239,6 +238,13 @@ class Workload:
         self.L.check(st, "engram_forward")
 
     def backward(self):
+        if self.peer is not None:  # row gradients straight into their owners' receive buffers
+            st = self.L.load().engram_backward_to_owners(self.slots.data_ptr(), self.T, self.nh, self.hpn, self.mode,
+                                                         self.dout.data_ptr(), self.dim, self.R,
+                                                         self.peer.recv_ptrs.data_ptr(), self.world, self.rank,
+                                                         self.ws.data_ptr(), self.ws_bytes, self.stream)
+            self.L.check(st, "engram_backward_to_owners")
+            return
         st = self.L.load().engram_backward(self.slots.data_ptr(), self.T, self.nh, self.hpn, self.mode,
                                            self.dout.data_ptr(), self.dim, self.R, self.grad_rows.data_ptr(),
                                            self.ws.data_ptr(), self.ws_bytes, self.stream)

@@ -107,9 +107,12 @@ SIGNATURES = {
                                       C.c_void_p, C.c_void_p]),
     "engram_overlay_accumulate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
                                             C.c_void_p]),
-    "engram_adam_peer_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_int64,
-                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_double, C.c_double,
-                                        C.c_double, C.c_double, C.c_float, C.c_void_p]),
+    "engram_backward_to_owners": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                            C.c_int32, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
+                                            C.c_int64, C.c_void_p]),
+    "engram_adam_owner_step": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_int32,
+                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_double, C.c_double,
+                                         C.c_double, C.c_double, C.c_float, C.c_void_p]),
     "engram_selftest_mod": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),
     "engram_launch_count": (C.c_int64, []),
 }

@@ -55,29 +55,46 @@ __global__ void k_adam_scalar(float* __restrict__ p, const float* __restrict__ g
     }
 }
 
-// Data-parallel optimizer step fused with its exchange, over peer memory.
-// grads[k] / rows[k]: rank k's grad_rows and rows_var ([R, dim] fp32, mapped
-// into this process over NVLink).  This rank owns the elements [lo, lo + n):
-// it sums the ranks' gradients in rank order, steps its own copy of the
-// parameter (m, v, p0 hold only the owned elements) and stores the result into
-// every rank's rows_var.  No waits inside: the caller orders the ranks around
-// the launch.
-__global__ void __launch_bounds__(256) k_adam_peer_vec4(const float4* const* __restrict__ grads,
-                                                        float4* const* __restrict__ rows, int world, int rank,
-                                                        int64_t lo4, int64_t n4, float4* __restrict__ m,
-                                                        float4* __restrict__ v, const float4* __restrict__ p0,
-                                                        AdamScalars a) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t e = lo4 + i;
-        float4 gg = __ldcv(grads[0] + e);
-        for (int k = 1; k < world; k++) {
-            const float4 x = __ldcv(grads[k] + e);
-            gg.x = __fadd_rn(gg.x, x.x);
-            gg.y = __fadd_rn(gg.y, x.y);
-            gg.z = __fadd_rn(gg.z, x.z);
-            gg.w = __fadd_rn(gg.w, x.w);
+// Data-parallel optimizer step over peer memory, owner side.  recv is this
+// rank's receive buffer [world, size, dim]: block k holds rank k's row
+// gradients of the rows this rank owns (written there by the backward,
+// engram_backward_to_owners).  For each owned element: the sum of the blocks
+// in rank order, the Adam update of this rank's copy of the parameter (m, v,
+// p0 hold the owned rows only), and a store of the result into every rank's
+// rows_var (rows[k], mapped over NVLink).  No waits inside: the caller orders
+// the ranks around the launch.
+template <int W>  // W > 0: world size known at compile time; 0: any
+__global__ void __launch_bounds__(256) k_adam_owner_vec4(const float4* __restrict__ recv, int64_t shard4,
+                                                         float4* const* __restrict__ rows, int world, int rank,
+                                                         int64_t lo4, float4* __restrict__ m, float4* __restrict__ v,
+                                                         const float4* __restrict__ p0, AdamScalars a) {
+    const int nw = W > 0 ? W : world;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < shard4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float4 gg;
+        if (W > 0) {
+            float4 x[W > 0 ? W : 1];
+#pragma unroll
+            for (int k = 0; k < W; k++) x[k] = __ldcs(recv + k * shard4 + i);
+            gg = x[0];
+#pragma unroll
+            for (int k = 1; k < W; k++) {
+                gg.x = __fadd_rn(gg.x, x[k].x);
+                gg.y = __fadd_rn(gg.y, x[k].y);
+                gg.z = __fadd_rn(gg.z, x[k].z);
+                gg.w = __fadd_rn(gg.w, x[k].w);
+            }
+        } else {
+            gg = __ldcs(recv + i);
+            for (int k = 1; k < nw; k++) {
+                const float4 x = __ldcs(recv + k * shard4 + i);
+                gg.x = __fadd_rn(gg.x, x.x);
+                gg.y = __fadd_rn(gg.y, x.y);
+                gg.z = __fadd_rn(gg.z, x.z);
+                gg.w = __fadd_rn(gg.w, x.w);
+            }
         }
-        float4 pp = rows[rank][e], mm = m[i], vv = v[i];
+        float4 pp = rows[rank][lo4 + i], mm = m[i], vv = v[i];
         const float4 q = p0 ? __ldg(p0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
         const bool reg = p0 != nullptr;
         adam_elem(pp.x, gg.x, mm.x, vv.x, q.x, reg, a);
@@ -86,7 +103,7 @@ __global__ void __launch_bounds__(256) k_adam_peer_vec4(const float4* const* __r
         adam_elem(pp.w, gg.w, mm.w, vv.w, q.w, reg, a);
         m[i] = mm;
         v[i] = vv;
-        for (int k = 0; k < world; k++) __stcg(rows[k] + e, pp);
+        for (int k = 0; k < nw; k++) __stcg(rows[k] + lo4 + i, pp);
     }
 }
 
@@ -141,20 +158,34 @@ extern "C" int engram_adam_step(float* p, const float* g, float* m, float* v, co
 }
 
 
-extern "C" int engram_adam_peer_step(const void* grad_ptrs, const void* rows_ptrs, int32_t world, int32_t rank,
-                                     int64_t lo, int64_t n, float* m, float* v, const float* p0, int64_t step,
-                                     double lr, double beta1, double beta2, double eps, float reg_scale,
-                                     void* stream) {
-    if (world < 1 || rank < 0 || rank >= world || lo < 0 || n < 0 || step < 1) return ENGRAM_ERR_ARG;
-    if ((lo & 3) || (n & 3)) return ENGRAM_ERR_FORMAT;  // float4 elements
-    if (n == 0) return ENGRAM_OK;
-    if (!grad_ptrs || !rows_ptrs || !m || !v) return ENGRAM_ERR_ARG;
-    if (!aligned16(m) || !aligned16(v) || (p0 && !aligned16(p0))) return ENGRAM_ERR_ARG;
+extern "C" int engram_adam_owner_step(const float* recv, const void* rows_ptrs, int32_t world, int32_t rank,
+                                      int64_t R, int32_t dim, float* m, float* v, const float* p0, int64_t step,
+                                      double lr, double beta1, double beta2, double eps, float reg_scale,
+                                      void* stream) {
+    if (world < 1 || rank < 0 || rank >= world || R < 0 || dim <= 0 || step < 1) return ENGRAM_ERR_ARG;
+    if (dim & 3) return ENGRAM_ERR_FORMAT;  // float4 pieces
+    const int64_t base = R / world, extra = R % world;
+    const int64_t lo = rank * base + (rank < extra ? rank : extra);
+    const int64_t size = base + (rank < extra ? 1 : 0);
+    if (size == 0) return ENGRAM_OK;
+    if (!recv || !rows_ptrs || !m || !v) return ENGRAM_ERR_ARG;
+    if (!aligned16(recv) || !aligned16(m) || !aligned16(v) || (p0 && !aligned16(p0))) return ENGRAM_ERR_ARG;
     const AdamScalars a = adam_scalars(step, lr, beta1, beta2, eps, reg_scale);
-    const int64_t n4 = n / 4;
-    k_adam_peer_vec4<<<grid_for(n4, 256, 8), 256, 0, (cudaStream_t)stream>>>(
-        static_cast<const float4* const*>(grad_ptrs), static_cast<float4* const*>(rows_ptrs), world, rank, lo / 4, n4,
-        reinterpret_cast<float4*>(m), reinterpret_cast<float4*>(v), reinterpret_cast<const float4*>(p0), a);
+    const int64_t shard4 = size * dim / 4, lo4 = lo * dim / 4;
+    const int grid = grid_for(shard4, 256, 8);
+    cudaStream_t s = (cudaStream_t)stream;
+    const float4* r4 = reinterpret_cast<const float4*>(recv);
+    float4* const* rows4 = static_cast<float4* const*>(rows_ptrs);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    const float4* q4 = reinterpret_cast<const float4*>(p0);
+    switch (world) {
+        case 1: k_adam_owner_vec4<1><<<grid, 256, 0, s>>>(r4, shard4, rows4, world, rank, lo4, m4, v4, q4, a); break;
+        case 2: k_adam_owner_vec4<2><<<grid, 256, 0, s>>>(r4, shard4, rows4, world, rank, lo4, m4, v4, q4, a); break;
+        case 4: k_adam_owner_vec4<4><<<grid, 256, 0, s>>>(r4, shard4, rows4, world, rank, lo4, m4, v4, q4, a); break;
+        case 8: k_adam_owner_vec4<8><<<grid, 256, 0, s>>>(r4, shard4, rows4, world, rank, lo4, m4, v4, q4, a); break;
+        default: k_adam_owner_vec4<0><<<grid, 256, 0, s>>>(r4, shard4, rows4, world, rank, lo4, m4, v4, q4, a);
+    }
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }

@@ -353,6 +353,34 @@ __device__ __forceinline__ int64_t snap_to_segment(const int32_t* __restrict__ k
     return __ldg(seg_begin + k + 1);
 }
 
+// Where the row gradient of slot s is written: the dense [R, dim] array, or
+// (data-parallel ranks over peer memory) the receive buffer of the rank that
+// owns s.  Owners hold contiguous near-equal shards (the first R % world ranks
+// one row more); owner o's buffer is [world, size_o, dim] and this rank writes
+// block `rank` of it, so the owner finds every rank's partial row gradients in
+// its own memory.
+struct RowDst {
+    float* dense;
+    float* const* owners;  // device array [world] of receive buffers, or null
+    int64_t R;
+    int world, rank;
+    __device__ __forceinline__ float* row(int64_t s, int dim) const {
+        if (!owners) return dense + s * dim;
+        const int64_t base = R / world, extra = R % world, big = extra * (base + 1);
+        int64_t o, lo, size;
+        if (s < big) {
+            o = s / (base + 1);
+            lo = o * (base + 1);
+            size = base + 1;
+        } else {
+            o = extra + (s - big) / base;
+            lo = big + (o - extra) * base;
+            size = base;
+        }
+        return owners[o] + ((int64_t)rank * size + (s - lo)) * dim;
+    }
+};
+
 // Work split of the segmented reduction.  With K = the chunk size chosen from
 // the hit count, chunk j spans [first segment start >= j*K, first segment
 // start >= (j+1)*K).  A segment longer than K can only sit at a chunk's head or
@@ -427,7 +455,7 @@ __device__ __forceinline__ void reduce_stream(uint8_t* __restrict__ ring, const 
                                               const int32_t* __restrict__ chunk_hi,
                                               const int32_t* __restrict__ medium_seg, int32_t* counters,
                                               const int64_t n_medium, const int64_t n_jobs, const GradRows& G,
-                                              const uint4* __restrict__ g16, float* __restrict__ grad_rows) {
+                                              const uint4* __restrict__ g16, const RowDst& out) {
     using RG = ShortRing<NV>;
     constexpr int D = RG::D, U = RG::U, GI = RG::GI, ROWS = RG::ROWS;
     constexpr bool F32 = MODE == ENGRAM_MODE_CONCAT_F32;
@@ -555,7 +583,7 @@ __device__ __forceinline__ void reduce_stream(uint8_t* __restrict__ ring, const 
                 const int rr = (x0 + u) & 31;
                 if ((lastA >> rr) & 1u) {  // the row ends its segment: write the slot's gradient row
                     const int32_t key = __shfl_sync(kFull, keyA, rr);
-                    float* dst = grad_rows + (int64_t)key * dim;
+                    float* dst = out.row(key, dim);
 #pragma unroll
                     for (int q = 0; q < NV; q++) {
                         if (lane + 32 * q < nvec) {
@@ -598,8 +626,7 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
 template <int MODE>
 __device__ __forceinline__ void reduce_long(uint8_t* __restrict__ ws, const int lane, const int64_t a, const int64_t b,
                                             const int32_t key, const int slice, const int32_t* __restrict__ vals,
-                                            const GradRows& G, const uint4* __restrict__ g16,
-                                            float* __restrict__ grad_rows) {
+                                            const GradRows& G, const uint4* __restrict__ g16, const RowDst& out) {
     const int dim = G.dim;
     constexpr bool F32 = MODE == ENGRAM_MODE_CONCAT_F32;
     constexpr int GI = kLongGI, RG = kLongRingGroups, VS = kLongValSlots, SB = kSliceBytes;
@@ -666,8 +693,8 @@ __device__ __forceinline__ void reduce_long(uint8_t* __restrict__ ws, const int 
     __syncwarp();
     if (lane < words) {
         const int word = p0 * 4 + lane;
-        if (F32) grad_rows[(int64_t)key * dim + word] = accf;
-        else reinterpret_cast<float2*>(grad_rows + (int64_t)key * dim)[word] = acc;
+        if (F32) out.row(key, dim)[word] = accf;
+        else reinterpret_cast<float2*>(out.row(key, dim))[word] = acc;
     }
 }
 
@@ -686,8 +713,7 @@ __global__ void __launch_bounds__(kRedWarps * 32) k_reduce(const int32_t* __rest
                                                            const int32_t* __restrict__ long_seg,
                                                            const int32_t* __restrict__ medium_seg,
                                                            int32_t* counters, int64_t R, const GradRows G,
-                                                           const uint8_t* __restrict__ grad,
-                                                           float* __restrict__ grad_rows) {
+                                                           const uint8_t* __restrict__ grad, const RowDst out) {
     constexpr int ES = MODE == ENGRAM_MODE_CONCAT_F32 ? 4 : 2;
     const int dim = G.dim;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -703,19 +729,19 @@ __global__ void __launch_bounds__(kRedWarps * 32) k_reduce(const int32_t* __rest
         if (j >= n_long_jobs) break;
         const int32_t key = __ldg(long_seg + j / n_slices);
         reduce_long<MODE>(ws, lane, __ldg(seg_begin + key), __ldg(seg_begin + key + 1), key, j % n_slices, vals, G,
-                          g16, grad_rows);
+                          g16, out);
         __syncwarp();  // the short stream lays the ring out differently
     }
     const int64_t n_medium = counters[kCntMedium];
     const int64_t n_jobs = n_medium + counters[kCntChunks];
     reduce_stream<MODE, NV>(ws, lane, keys, vals, seg_begin, chunk_lo, chunk_hi, medium_seg, counters, n_medium,
-                            n_jobs, G, g16, grad_rows);
+                            n_jobs, G, g16, out);
     // slots without entries
     const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t s = warp0; s < R; s += nwarps) {
         if (__ldg(seg_begin + s) == __ldg(seg_begin + s + 1)) {
-            float4* dst = reinterpret_cast<float4*>(grad_rows + s * dim);
+            float4* dst = reinterpret_cast<float4*>(out.row(s, dim));
             for (int c = lane; c < (dim >> 2); c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
@@ -740,7 +766,7 @@ int grid_for(int64_t work, int threads, int per_sm);
 
 template <int MODE, int NV>
 void launch_reduce(const Workspace& w, const int32_t* keys, const int32_t* vals, int64_t N, int64_t R, int dim,
-                   int n_heads, int hpn, const void* grad, float* grad_rows, cudaStream_t s) {
+                   int n_heads, int hpn, const void* grad, const RowDst& out, cudaStream_t s) {
     static int per_sm[64] = {0};
     const int grid = sm_count() * blocks_per_sm(k_reduce<MODE, NV>, kRedWarps * 32, kRedSmem, per_sm);
     k_chunks<<<grid_for(N / kMinChunk + 2, 256, 4), 256, 0, s>>>(keys, w.seg_begin, w.counters, grid * kRedWarps,
@@ -748,7 +774,7 @@ void launch_reduce(const Workspace& w, const int32_t* keys, const int32_t* vals,
     k_reduce<MODE, NV><<<grid, kRedWarps * 32, kRedSmem, s>>>(keys, vals, w.seg_begin, w.chunk_lo, w.chunk_hi,
                                                                w.long_seg, w.medium_seg, w.counters, R,
                                                                GradRows{dim, n_heads, hpn, head_div(n_heads)},
-                                                               static_cast<const uint8_t*>(grad), grad_rows);
+                                                               static_cast<const uint8_t*>(grad), out);
 }
 
 int grid_for(int64_t work, int threads, int per_sm) {
@@ -765,9 +791,17 @@ extern "C" int64_t engram_backward_workspace_bytes(int64_t n, int32_t n_heads, i
     return layout(nullptr, n * n_heads, R).bytes;
 }
 
-extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram,
-                               int32_t mode, const void* grad, int32_t dim, int64_t R, float* grad_rows,
-                               void* workspace, int64_t workspace_bytes, void* stream) {
+namespace {
+
+__global__ void k_zero_rows(RowDst out, int64_t R, int dim) {
+    const int64_t q = dim >> 2, total = R * q;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x)
+        reinterpret_cast<float4*>(out.row(k / q, dim))[k % q] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+int backward_impl(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram, int32_t mode,
+                  const void* grad, int32_t dim, int64_t R, const RowDst& out, void* workspace,
+                  int64_t workspace_bytes, void* stream) {
     if (n < 0 || R < 0 || n_heads < 1 || n_heads > ENGRAM_MAX_HEADS || heads_per_ngram < 1) return ENGRAM_ERR_ARG;
     if (mode != ENGRAM_MODE_CONCAT_F32 && mode != ENGRAM_MODE_PAIRSUM_ADD_BF16) return ENGRAM_ERR_ARG;
     if (dim <= 0 || dim > 1024 || (mode == ENGRAM_MODE_CONCAT_F32 ? dim % 4 : dim % 8)) return ENGRAM_ERR_FORMAT;
@@ -777,11 +811,14 @@ extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
                                                               : n * (int64_t)heads_per_ngram * dim * 2;
     if ((grad_bytes >> 4) >= (1LL << 32)) return ENGRAM_ERR_RANGE;
     if (R == 0) return ENGRAM_OK;
-    if (!grad_rows || !aligned16(grad_rows)) return ENGRAM_ERR_ARG;
+    if (out.owners ? (out.world < 1 || out.rank < 0 || out.rank >= out.world)
+                   : (!out.dense || !aligned16(out.dense)))
+        return ENGRAM_ERR_ARG;
     cudaStream_t s = (cudaStream_t)stream;
     if (n == 0) {
-        return cudaMemsetAsync(grad_rows, 0, sizeof(float) * (size_t)R * dim, s) == cudaSuccess ? ENGRAM_OK
-                                                                                                 : ENGRAM_ERR_CUDA;
+        k_zero_rows<<<grid_for(R * (dim >> 2), 256, 8), 256, 0, s>>>(out, R, dim);
+        count_launches(1);
+        return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
     }
     if (!slots || !grad || !aligned16(grad)) return ENGRAM_ERR_ARG;
     const int64_t N = n * n_heads;
@@ -812,17 +849,36 @@ extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
     const int32_t* V = w.vals[cur];
     const int hpn = heads_per_ngram;
     if (mode == ENGRAM_MODE_CONCAT_F32) {
-        if (nvec <= 32) launch_reduce<ENGRAM_MODE_CONCAT_F32, 1>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
-        else if (nvec <= 64) launch_reduce<ENGRAM_MODE_CONCAT_F32, 2>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
-        else if (nvec <= 128) launch_reduce<ENGRAM_MODE_CONCAT_F32, 4>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
-        else launch_reduce<ENGRAM_MODE_CONCAT_F32, 8>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
+        if (nvec <= 32) launch_reduce<ENGRAM_MODE_CONCAT_F32, 1>(w, K, V, N, R, dim, n_heads, hpn, grad, out, s);
+        else if (nvec <= 64) launch_reduce<ENGRAM_MODE_CONCAT_F32, 2>(w, K, V, N, R, dim, n_heads, hpn, grad, out, s);
+        else if (nvec <= 128) launch_reduce<ENGRAM_MODE_CONCAT_F32, 4>(w, K, V, N, R, dim, n_heads, hpn, grad, out, s);
+        else launch_reduce<ENGRAM_MODE_CONCAT_F32, 8>(w, K, V, N, R, dim, n_heads, hpn, grad, out, s);
     } else {
-        if (nvec <= 32) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 1>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
-        else if (nvec <= 64) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 2>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
-        else launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 4>(w, K, V, N, R, dim, n_heads, hpn, grad, grad_rows, s);
+        if (nvec <= 32) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 1>(w, K, V, N, R, dim, n_heads, hpn, grad, out, s);
+        else if (nvec <= 64) launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 2>(w, K, V, N, R, dim, n_heads, hpn, grad, out, s);
+        else launch_reduce<ENGRAM_MODE_PAIRSUM_ADD_BF16, 4>(w, K, V, N, R, dim, n_heads, hpn, grad, out, s);
     }
     count_launches(3 * passes + 3);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram,
+                               int32_t mode, const void* grad, int32_t dim, int64_t R, float* grad_rows,
+                               void* workspace, int64_t workspace_bytes, void* stream) {
+    return backward_impl(slots, n, n_heads, heads_per_ngram, mode, grad, dim, R, RowDst{grad_rows, nullptr, R, 1, 0},
+                         workspace, workspace_bytes, stream);
+}
+
+extern "C" int engram_backward_to_owners(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram,
+                                         int32_t mode, const void* grad, int32_t dim, int64_t R,
+                                         const void* owner_bufs, int32_t world, int32_t rank, void* workspace,
+                                         int64_t workspace_bytes, void* stream) {
+    if (!owner_bufs) return ENGRAM_ERR_ARG;
+    return backward_impl(slots, n, n_heads, heads_per_ngram, mode, grad, dim, R,
+                         RowDst{nullptr, static_cast<float* const*>(owner_bufs), R, world, rank}, workspace,
+                         workspace_bytes, stream);
 }
 
 // ---- engram_backward_noalloc ---------------------------------------------------

@@ -76,29 +76,47 @@ def all_gather_rows(rows_var: torch.Tensor, shard: torch.Tensor, group=None) -> 
         rows_var[lo:hi].copy_(part[: hi - lo])
 
 
-def adam_peer_step(grad_ptrs: torch.Tensor, rows_ptrs: torch.Tensor, world: int, rank: int, R: int, dim: int,
-                   m: torch.Tensor, v: torch.Tensor, p0: torch.Tensor | None, step: int, lr: float,
-                   beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, reg_scale: float = 0.0) -> None:
-    """engram_adam_peer_step for this rank's shard_bounds rows: grad_ptrs /
-    rows_ptrs are int64 device tensors of every rank's grad_rows / rows_var
-    address; m, v, p0 hold the shard's rows only."""
+def backward_to_owners(slots: torch.Tensor, grad: torch.Tensor, n_heads: int, hpn: int, dim: int, R: int, mode: int,
+                       owner_ptrs: torch.Tensor, world: int, rank: int, workspace: torch.Tensor | None = None) -> None:
+    """engram_backward_to_owners: this rank's row gradients, each row stored
+    into its owner's receive buffer (block `rank`)."""
     from . import _lib as L
-    lo, hi = shard_bounds(R, world, rank)
-    st = L.load().engram_adam_peer_step(grad_ptrs.data_ptr(), rows_ptrs.data_ptr(), world, rank, lo * dim,
-                                        (hi - lo) * dim, m.data_ptr(), v.data_ptr(), L.ptr(p0), int(step),
-                                        float(lr), float(beta1), float(beta2), float(eps), float(reg_scale),
-                                        L.stream_of(m.device))
-    L.check(st, "engram_adam_peer_step")
+    lib = L.load()
+    n = slots.shape[0]
+    ws_bytes = int(lib.engram_backward_workspace_bytes(n, n_heads, R))
+    L.check(min(ws_bytes, 0), "engram_backward_workspace_bytes")
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=slots.device)
+    st = lib.engram_backward_to_owners(slots.data_ptr(), n, n_heads, hpn, mode, grad.data_ptr(), dim, R,
+                                       owner_ptrs.data_ptr(), world, rank, workspace.data_ptr(), workspace.numel(),
+                                       L.stream_of(slots.device))
+    L.check(st, "engram_backward_to_owners")
+
+
+def adam_owner_step(recv: torch.Tensor, rows_ptrs: torch.Tensor, world: int, rank: int, R: int, dim: int,
+                    m: torch.Tensor, v: torch.Tensor, p0: torch.Tensor | None, step: int, lr: float,
+                    beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, reg_scale: float = 0.0) -> None:
+    """engram_adam_owner_step: sum of the receive buffer's blocks in rank order,
+    Adam on this rank's rows (m, v, p0: the owned rows), stores into every
+    rank's rows_var."""
+    from . import _lib as L
+    st = L.load().engram_adam_owner_step(recv.data_ptr(), rows_ptrs.data_ptr(), world, rank, R, dim, m.data_ptr(),
+                                         v.data_ptr(), L.ptr(p0), int(step), float(lr), float(beta1), float(beta2),
+                                         float(eps), float(reg_scale), L.stream_of(m.device))
+    L.check(st, "engram_adam_owner_step")
 
 
 class PeerRows:
-    """grad_rows and rows_var [R, dim] fp32 allocated in torch symmetric memory,
-    so every rank's copies are mapped into every process over NVLink.  step()
-    is the data-parallel optimizer step as one kernel per rank
-    (engram_adam_peer_step): it replaces reduce_scatter_rows + Adam +
-    all_gather_rows, with two tiny NCCL all-reduces as the barriers around it
-    (all gradients written before any rank reads them; all rows stored before
-    any rank's next forward reads them)."""
+    """The data-parallel overlay update over peer memory.  rows_var [R, dim] and
+    a receive buffer [world, ceil(R/world), dim] live in torch symmetric memory,
+    so every rank's copies are mapped into every process over NVLink.  Per step:
+      backward(): the row gradients go straight to their owners' receive
+        buffers (the reduce-scatter's transfer, inside the reduction);
+      step(): barrier; each owner sums its blocks in rank order, runs Adam and
+        stores the new rows into every rank's rows_var (the all-gather's
+        transfer, inside the update); barrier.
+    The barriers are tiny NCCL all-reduces on the stream; no kernel waits on
+    another GPU."""
 
     def __init__(self, R: int, dim: int, device, group=None):
         import torch.distributed._symmetric_memory as symm
@@ -108,20 +126,31 @@ class PeerRows:
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
         self.R, self.dim = int(R), int(dim)
-        self.grad_rows = symm.empty(max(self.R, 1), self.dim, dtype=torch.float32, device=device)
+        size_max = -(-self.R // self.world)
+        self.recv = symm.empty(max(self.world * size_max, 1), self.dim, dtype=torch.float32, device=device)
         self.rows_var = symm.empty(max(self.R, 1), self.dim, dtype=torch.float32, device=device)
-        self._hg = symm.rendezvous(self.grad_rows, self.group)
+        self._hv = symm.rendezvous(self.recv, self.group)
         self._hr = symm.rendezvous(self.rows_var, self.group)
-        self.grad_ptrs = torch.tensor(list(self._hg.buffer_ptrs), dtype=torch.int64, device=device)
+        self.recv_ptrs = torch.tensor(list(self._hv.buffer_ptrs), dtype=torch.int64, device=device)
         self.rows_ptrs = torch.tensor(list(self._hr.buffer_ptrs), dtype=torch.int64, device=device)
         self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self._ws = None
 
     def barrier(self) -> None:
         dist.all_reduce(self._flag, group=self.group)
 
+    def backward(self, slots: torch.Tensor, grad: torch.Tensor, n_heads: int, hpn: int, mode: int) -> None:
+        from . import _lib as L
+        n = slots.shape[0]
+        ws_bytes = int(L.load().engram_backward_workspace_bytes(n, n_heads, self.R))
+        if self._ws is None or self._ws.numel() < ws_bytes:
+            self._ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=slots.device)
+        backward_to_owners(slots, grad, n_heads, hpn, self.dim, self.R, mode, self.recv_ptrs, self.world, self.rank,
+                           self._ws)
+
     def step(self, m: torch.Tensor, v: torch.Tensor, p0: torch.Tensor | None, step: int, lr: float,
              beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, reg_scale: float = 0.0) -> None:
         self.barrier()
-        adam_peer_step(self.grad_ptrs, self.rows_ptrs, self.world, self.rank, self.R, self.dim, m, v, p0, step, lr,
-                       beta1, beta2, eps, reg_scale)
+        adam_owner_step(self.recv, self.rows_ptrs, self.world, self.rank, self.R, self.dim, m, v, p0, step, lr,
+                        beta1, beta2, eps, reg_scale)
         self.barrier()

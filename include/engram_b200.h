@@ -297,22 +297,35 @@ ENGRAM_API int engram_adam_step(float* p, const float* g, float* m, float* v, co
                      void* stream);
 
 /*
- * The data-parallel optimizer step fused with its exchange, over peer memory
- * (no reference counterpart: the reference is single-process).  grad_ptrs and
- * rows_ptrs: device arrays of `world` pointers to each rank's grad_rows and
- * rows_var ([R, dim] fp32, each rank's buffer mapped into this process, e.g.
- * torch symmetric memory).  This rank owns the flat elements [lo, lo + n) (lo
- * and n multiples of 4, 16-byte aligned buffers): it sums the ranks' gradients
- * in rank order, runs engram_adam_step's update on them (m, v, p0 hold the
- * owned elements only) and stores the new values into every rank's rows_var.
- * The kernel does not wait on other ranks: call it after every rank's
- * gradients are complete, and let no rank read rows_var before every rank's
- * call has finished (two barriers, e.g. tiny NCCL all-reduces on the stream).
+ * Data-parallel ranks over peer memory (no reference counterpart: the reference
+ * is single-process).  The overlay rows are sharded by owner: rank o owns the
+ * contiguous rows [o*(R/W) + min(o, R%W), +size_o), size_o = R/W + (o < R%W).
+ * Each rank has a receive buffer [world, max size_o, dim] fp32 (16-byte aligned)
+ * mapped into every process (e.g. torch symmetric memory).
+ *
+ * engram_backward_to_owners: engram_backward whose row of slot s is stored into
+ * its owner's receive buffer, block `rank` (owner_bufs: device array [world] of
+ * the receive buffers); the reduce-scatter's transfer happens inside the
+ * reduction, as peer stores.
+ *
+ * engram_adam_owner_step: for the rows this rank owns, the sum of the world
+ * blocks of its receive buffer in rank order, engram_adam_step's update (m, v,
+ * p0 hold the owned rows only), and a store of the new rows into every rank's
+ * rows_var (rows_ptrs: device array [world]); the all-gather's transfer
+ * happens inside the update, as peer stores.
+ *
+ * Neither kernel waits on another GPU: every rank's backward must finish before
+ * any owner step starts, and every owner step before any rank reads rows_var
+ * (two barriers, e.g. tiny NCCL all-reduces on the stream).
  */
-ENGRAM_API int engram_adam_peer_step(const void* grad_ptrs, const void* rows_ptrs, int32_t world, int32_t rank,
-                                     int64_t lo, int64_t n, float* m, float* v, const float* p0, int64_t step,
-                                     double lr, double beta1, double beta2, double eps, float reg_scale,
-                                     void* stream);
+ENGRAM_API int engram_backward_to_owners(const int32_t* slots, int64_t n, int32_t n_heads, int32_t heads_per_ngram,
+                                         int32_t mode, const void* grad, int32_t dim, int64_t R,
+                                         const void* owner_bufs, int32_t world, int32_t rank, void* workspace,
+                                         int64_t workspace_bytes, void* stream);
+ENGRAM_API int engram_adam_owner_step(const float* recv, const void* rows_ptrs, int32_t world, int32_t rank,
+                                      int64_t R, int32_t dim, float* m, float* v, const float* p0, int64_t step,
+                                      double lr, double beta1, double beta2, double eps, float reg_scale,
+                                      void* stream);
 
 /* Scratch bytes engram_scan_hits needs for n positions. */
 ENGRAM_API int64_t engram_scan_hits_workspace_bytes(int64_t n);

@@ -574,41 +574,57 @@ def test_device_row_set_algebra_and_index_vs_numpy(eb):
     assert np.array_equal(idx, np.where(member, pos, -1))
 
 
-def test_adam_peer_step_emulated_ranks_match_summed_adam(eb):
-    """engram_adam_peer_step with W = 3 ranks emulated on one GPU (separate
-    buffers, one launch per rank): every rank's rows equal Adam over the
-    rank-order sum of the gradients, and each rank's m, v shard match."""
+def test_owner_exchange_emulated_ranks_match_summed_dense_adam(eb):
+    """The peer-memory update with W = 3 ranks emulated on one GPU (separate
+    buffers, one launch per rank): every rank's backward stores its row
+    gradients into the owners' receive buffers; each owner's step sums them in
+    rank order and runs Adam.  Every rank's rows equal Adam over the rank-order
+    sum of the dense row gradients, bit for bit; so do m and v."""
     from engraft_ngram_b200 import _lib as L
-    from engraft_ngram_b200.dist import adam_peer_step, shard_bounds
+    from engraft_ngram_b200.dist import adam_owner_step, backward_to_owners, shard_bounds
     rng = np.random.default_rng(12)
-    W, R, dim = 3, 1001, 256
+    W, R, dim, T, nh, hpn = 3, 1001, 256, 700, 16, 8
+    mode = L.MODE_PAIRSUM_ADD_BF16
     p_init = (rng.standard_normal((R, dim)) * 0.01).astype(np.float32)
     p0 = torch.from_numpy(p_init.copy()).to(DEV)
-    grads = [torch.from_numpy((rng.standard_normal((R, dim)) * 1e-3).astype(np.float32)).to(DEV) for _ in range(W)]
+    size_max = -(-R // W)
+    recv = [torch.full((W * size_max, dim), float("nan"), device=DEV) for _ in range(W)]
     rows = [torch.from_numpy(p_init.copy()).to(DEV) for _ in range(W)]
-    gp = torch.tensor([g.data_ptr() for g in grads], dtype=torch.int64, device=DEV)
-    rp = torch.tensor([r.data_ptr() for r in rows], dtype=torch.int64, device=DEV)
-    ms = [torch.zeros(*(shard_bounds(R, W, r)[1] - shard_bounds(R, W, r)[0], dim), device=DEV) for r in range(W)]
+    recv_p = torch.tensor([t.data_ptr() for t in recv], dtype=torch.int64, device=DEV)
+    rows_p = torch.tensor([t.data_ptr() for t in rows], dtype=torch.int64, device=DEV)
+    spans = [shard_bounds(R, W, r) for r in range(W)]
+    ms = [torch.zeros(hi - lo, dim, device=DEV) for lo, hi in spans]
     vs = [torch.zeros_like(m) for m in ms]
-    # reference: dense sum in rank order, then the single-GPU Adam kernel
-    ref_p = torch.from_numpy(p_init.copy()).to(DEV)
+    ref_p = p0.clone()
     ref_m, ref_v = torch.zeros_like(ref_p), torch.zeros_like(ref_p)
     rs = float(eb.reg_scale(0.1, p0))
-    for step in (1, 2, 3):
+    for step in (1, 2):
+        dense = []
         for r in range(W):
-            lo, hi = shard_bounds(R, W, r)
-            adam_peer_step(gp, rp, W, r, R, dim, ms[r], vs[r], p0[lo:hi], step, 1e-3, reg_scale=rs)
-        g = grads[0].clone()
+            slots = np.full((T, nh), -1, dtype=np.int32)
+            hit = rng.random((T, nh)) < 0.4
+            slots[hit] = rng.integers(0, R - 7, size=int(hit.sum()))  # the last rows stay without entries
+            slots[:, 2] = rng.integers(0, 3, size=T)  # hot rows: long segments
+            sl = torch.from_numpy(slots).to(DEV)
+            g = torch.from_numpy(O.bf16_bits((rng.standard_normal((T, hpn * dim)) * 1e-2).astype(np.float32))
+                                 .view(np.int16)).to(DEV).view(torch.bfloat16)
+            backward_to_owners(sl, g, nh, hpn, dim, R, mode, recv_p, W, r)
+            dense.append(eb.row_gradients(sl, g, nh, hpn, dim, R, mode))
+        for o, (lo, hi) in enumerate(spans):  # block k of owner o = rank k's rows [lo, hi)
+            for k in range(W):
+                blk = recv[o][k * (hi - lo):(k + 1) * (hi - lo)]
+                assert torch.equal(blk.view(torch.int32), dense[k][lo:hi].view(torch.int32)), (step, o, k)
+        for o, (lo, hi) in enumerate(spans):
+            adam_owner_step(recv[o], rows_p, W, o, R, dim, ms[o], vs[o], p0[lo:hi], step, 1e-3, reg_scale=rs)
+        gsum = dense[0].clone()
         for k in range(1, W):
-            g = g + grads[k]
-        st = L.load().engram_adam_step(ref_p.data_ptr(), g.data_ptr(), ref_m.data_ptr(), ref_v.data_ptr(),
+            gsum = gsum + dense[k]
+        st = L.load().engram_adam_step(ref_p.data_ptr(), gsum.data_ptr(), ref_m.data_ptr(), ref_v.data_ptr(),
                                        p0.data_ptr(), ref_p.numel(), step, 1e-3, 0.9, 0.999, 1e-8, rs,
                                        L.stream_of(ref_p.device))
         L.check(st, "engram_adam_step")
         for r in range(W):
             assert torch.equal(rows[r].view(torch.int32), ref_p.view(torch.int32)), (step, r)
-            lo, hi = shard_bounds(R, W, r)
-            assert torch.equal(ms[r].view(torch.int32), ref_m[lo:hi].view(torch.int32))
-            assert torch.equal(vs[r].view(torch.int32), ref_v[lo:hi].view(torch.int32))
-        for gr in grads:
-            gr.mul_(0.5)
+        for o, (lo, hi) in enumerate(spans):
+            assert torch.equal(ms[o].view(torch.int32), ref_m[lo:hi].view(torch.int32))
+            assert torch.equal(vs[o].view(torch.int32), ref_v[lo:hi].view(torch.int32))

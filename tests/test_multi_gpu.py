@@ -27,25 +27,31 @@ def _peer_vs_nccl(rank: int, world: int, port: int, out) -> None:
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
     try:
+        import engraft_ngram_b200 as eb
         from engraft_ngram_b200 import _lib as L
         from engraft_ngram_b200.dist import PeerRows, all_gather_rows, reduce_scatter_rows, shard_bounds
-        R, dim = 4000, 256
+        R, dim, T, nh, hpn = 4000, 256, 2048, 16, 8
+        mode = L.MODE_PAIRSUM_ADD_BF16
         rng = np.random.default_rng(5)
         p_init = torch.from_numpy((rng.standard_normal((R, dim)) * 0.01).astype(np.float32)).to(dev)
-        grads = [torch.from_numpy((rng.standard_normal((R, dim)) * 1e-3).astype(np.float32)).to(dev)
-                 for _ in range(world)]
         lo, hi = shard_bounds(R, world, rank)
         peer = PeerRows(R, dim, dev)
         peer.rows_var.copy_(p_init)
         m1, v1 = torch.zeros(hi - lo, dim, device=dev), torch.zeros(hi - lo, dim, device=dev)
         rows2 = p_init.clone()
         m2, v2 = torch.zeros(hi - lo, dim, device=dev), torch.zeros(hi - lo, dim, device=dev)
+        rr = np.random.default_rng(100 + rank)  # each rank its own batch
         ok = True
         for step in (1, 2, 3):
-            g = grads[rank] * (0.5 ** step)
-            peer.grad_rows.copy_(g)
+            slots = np.full((T, nh), -1, dtype=np.int32)
+            hit = rr.random((T, nh)) < 0.3
+            slots[hit] = rr.integers(0, R, size=int(hit.sum()))
+            sl = torch.from_numpy(slots).to(dev)
+            g = torch.from_numpy((rr.standard_normal((T, hpn * dim)) * 1e-2).astype(np.float32)).to(dev).to(
+                torch.bfloat16)
+            peer.backward(sl, g, nh, hpn, mode)
             peer.step(m1, v1, p_init[lo:hi], step, 1e-3, reg_scale=0.25)
-            shard = reduce_scatter_rows(g)
+            shard = reduce_scatter_rows(eb.row_gradients(sl, g, nh, hpn, dim, R, mode))
             p = rows2[lo:hi]
             st = L.load().engram_adam_step(p.data_ptr(), shard.data_ptr(), m2.data_ptr(), v2.data_ptr(),
                                            p_init[lo:hi].data_ptr(), p.numel(), step, 1e-3, 0.9, 0.999, 1e-8, 0.25,
@@ -62,8 +68,9 @@ def _peer_vs_nccl(rank: int, world: int, port: int, out) -> None:
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_peer_exchange_matches_nccl_collectives_on_two_ranks():
-    """Two ranks: the peer-memory optimizer step equals NCCL reduce-scatter +
-    Adam + all-gather bit for bit (a two-term sum does not depend on order)."""
+    """Two ranks: backward into the owners' buffers + the owner step equal the
+    dense backward + NCCL reduce-scatter + Adam + all-gather bit for bit (a
+    two-term sum does not depend on order)."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()

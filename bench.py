@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="N>1, replicated table: the optimizer exchange as one peer-memory kernel per rank "
                          "(symmetric memory: engram_backward_to_owners + engram_adam_owner_step) or as NCCL reduce-scatter + all-gather")
+    ap.add_argument("--shard-exchange", choices=["peer", "nccl"], default="peer",
+                    help="--shard: rows read in place from their owners over NVLink (symmetric memory) or moved by "
+                         "NCCL all-to-all of ids and rows")
     ap.add_argument("--shard", action="store_true",
                     help="row-sharded table: each rank holds rows g with g %% N == rank; rows move by NCCL all-to-all")
     return ap.parse_args()
@@ -120,12 +123,20 @@ class Workload:
         mult = synthetic_multipliers(seed)
         self.shard = None
         if cfg.get("shard"):
-            from engraft_ngram_b200.shard import ShardedTable, local_exchange, nccl_exchange
+            from engraft_ngram_b200.shard import ShardedTable, local_exchange, nccl_exchange, peer_shard_buffer
             n_local = (cfg["rows"] - rank + world - 1) // world
-            rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device)
-            self.shard = ShardedTable(rows, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"])
-            self.exchange = nccl_exchange() if world > 1 else local_exchange([self.shard])
-            self.shard.exchange = self.exchange  # the public API (run_e2e) exchanges rows the same way
+            if cfg.get("shard_exchange", "peer") == "peer" and world > 1:
+                # every rank's shard in symmetric memory: the forward reads rows in place over NVLink
+                buf, ptrs, self._shard_handle = peer_shard_buffer(cfg["rows"], fmt, self.dim, device)
+                rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device, out=buf)
+                self.shard = ShardedTable(buf, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"],
+                                          peer_ptrs=ptrs)
+                self.exchange = None
+            else:
+                rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device)
+                self.shard = ShardedTable(rows, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"])
+                self.exchange = nccl_exchange() if world > 1 else local_exchange([self.shard])
+                self.shard.exchange = self.exchange  # the public API (run_e2e) exchanges rows the same way
             self.table = self.shard
         else:
             rows = synthetic_resident(cfg["rows"], fmt, self.dim, seed, device)
@@ -172,7 +183,7 @@ class Workload:
         else:
             self.p0 = self.table.gather_rows(self.ov_ids) if self.R else torch.zeros(0, self.dim, device=device)
         self.peer = None
-        if world > 1 and self.shard is None and cfg.get("exchange", "peer") == "peer" and self.R and self.dim % 4 == 0:
+        if world > 1 and cfg.get("exchange", "peer") == "peer" and self.R and self.dim % 4 == 0:
             from engraft_ngram_b200.dist import PeerRows
             try:
                 self.peer = PeerRows(self.R, self.dim, device)
@@ -546,8 +557,11 @@ def config_json(cfg, args):
                         f"{cfg['mode']} emit, {'fwd+bwd+Adam' if cfg['bwd'] else 'fwd only'}",
             "table_rows": cfg["rows"], "dim": cfg["dim"], "format": cfg["fmt"], "positions_per_gpu": cfg["seqs"] * cfg["seq_len"],
             "overlay_rows": cfg["R"], "emit": cfg["mode"],
-            "parallelism": f"dp{args.gpus}" + ("+row-sharded table (id mod N, NCCL all-to-all of ids and rows)" if cfg.get("shard") else ""),
-            "optimizer_exchange": (None if args.gpus == 1 or cfg.get("shard") else
+            "parallelism": f"dp{args.gpus}" + (("+row-sharded table (id mod N; rows read from their owners over "
+                                                 "NVLink inside the forward)" if cfg.get("shard_exchange", "peer") == "peer"
+                                                 else "+row-sharded table (id mod N, NCCL all-to-all of ids and rows)")
+                                                if cfg.get("shard") else ""),
+            "optimizer_exchange": (None if args.gpus == 1 else
                                    ("one peer-memory kernel per rank (sum over ranks + Adam + stores to every rank)"
                                     if cfg.get("exchange", "peer") == "peer" else "NCCL reduce-scatter + all-gather")),
             "l2": "inputs larger than L2 (residual and upstream gradient 537 MB each, table 46 GB)"}
@@ -569,6 +583,7 @@ def main():
         cfg["seqs"] = args.seqs
     cfg["shard"] = bool(args.shard)
     cfg["exchange"] = args.exchange
+    cfg["shard_exchange"] = args.shard_exchange
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

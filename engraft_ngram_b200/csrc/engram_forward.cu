@@ -29,6 +29,28 @@ struct PosMap {
     const int64_t* pos;
     int64_t n_tokens;
     const int32_t* rix;  // nullable: row of (output row i, head h) in T.rows is rix[i*n_heads + h]
+    // nullable: the table is row-sharded over `world` ranks (row g at local row
+    // g / world of rank g % world's shard, shard[rank] = its address in this
+    // process, e.g. peer memory mapped over NVLink); wshift = log2(world) when
+    // world is a power of two, else -1
+    const uint8_t* const* shard = nullptr;
+    uint32_t world = 1;
+    int wshift = 0;
+    // Address of row r: T.rows + r * stride, or the row in its owner's shard.
+    __device__ __forceinline__ const uint8_t* row_ptr(const uint8_t* rows, int64_t stride, int32_t r) const {
+        if (shard == nullptr) return rows + (int64_t)r * stride;
+        uint32_t o, l;
+        if (wshift >= 0) {
+            o = (uint32_t)r & (world - 1u);
+            l = (uint32_t)r >> wshift;
+        } else {
+            l = (uint32_t)r / world;
+            o = (uint32_t)r - l * world;
+        }
+        const uint8_t* base =
+            reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(shard) + o));
+        return base + (int64_t)l * stride;
+    }
     // Row number in T.rows that serves head h of output row i (the global id
     // unless the rows were gathered into a local buffer, see engram_forward_indirect).
     __device__ __forceinline__ int32_t row(int64_t i, int h, int nh, int32_t gid) const {
@@ -220,10 +242,10 @@ __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engra
                 sl[u] = s;
                 if (c < cpp) {
                     if (FMT == ENGRAM_FMT_F32) {
-                        const float* src = s >= 0 ? ovr + (int64_t)s * dim : reinterpret_cast<const float*>(rows + (int64_t)g * T.row_stride);
+                        const float* src = s >= 0 ? ovr + (int64_t)s * dim : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, g));
                         v[u] = __ldg(reinterpret_cast<const float4*>(src) + cc);
                     } else if (s < 0) {
-                        raw[u] = raw4<FMT>(rows + (int64_t)g * T.row_stride, cc, dim);
+                        raw[u] = raw4<FMT>(pm.row_ptr(rows, T.row_stride, g), cc, dim);
                     }
                 }
             }
@@ -321,9 +343,9 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                     const int32_t s1 = __shfl_sync(kFull, ph.slot, hpn + gs);
                     if (c < cpp) {
                         ld_f8(s0 >= 0 ? ovr + (int64_t)s0 * dim + 8 * cc
-                                      : reinterpret_cast<const float*>(rows + (int64_t)ga * T.row_stride) + 8 * cc, fa[u]);
+                                      : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, ga)) + 8 * cc, fa[u]);
                         ld_f8(s1 >= 0 ? ovr + (int64_t)s1 * dim + 8 * cc
-                                      : reinterpret_cast<const float*>(rows + (int64_t)gb * T.row_stride) + 8 * cc, fb[u]);
+                                      : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, gb)) + 8 * cc, fb[u]);
                     }
                 }
 #pragma unroll
@@ -344,8 +366,8 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                     const int32_t gb = __shfl_sync(kFull, ph.row, hpn + gs);
                     const int32_t s1 = __shfl_sync(kFull, ph.slot, hpn + gs);
                     if (c < cpp) {
-                        if (s0 < 0) ra[u] = raw8<FMT>(rows + (int64_t)ga * T.row_stride, cc, dim);
-                        if (s1 < 0) rb[u] = raw8<FMT>(rows + (int64_t)gb * T.row_stride, cc, dim);
+                        if (s0 < 0) ra[u] = raw8<FMT>(pm.row_ptr(rows, T.row_stride, ga), cc, dim);
+                        if (s1 < 0) rb[u] = raw8<FMT>(pm.row_ptr(rows, T.row_stride, gb), cc, dim);
                     }
                 }
 #pragma unroll
@@ -460,7 +482,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
             const int p = j - h * pieces;
             const int32_t g = __shfl_sync(kFull, gid, h < nh ? h : 0);
             if (j < row_pieces)
-                cp_async16_f(bb + res_bytes + h * T.row_stride + p * 16, rows + (int64_t)g * T.row_stride + p * 16);
+                cp_async16_f(bb + res_bytes + h * T.row_stride + p * 16, pm.row_ptr(rows, T.row_stride, g) + p * 16);
         }
         cp_async_commit_f();
     };
@@ -644,7 +666,7 @@ __device__ __forceinline__ void xs_row(const uint8_t* row, const float* ov_row, 
     }
 }
 
-template <int FMT, int DIM>
+template <int FMT, int DIM, bool SHARD>
 __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     engram_table T, engram_overlay OV, const int32_t* __restrict__ tokens, const int32_t* __restrict__ seg_start,
     PosMap pm, int64_t n, __nv_bfloat16* __restrict__ out, int32_t* ids_out, int32_t* slots_out,
@@ -674,7 +696,8 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
             const int p = j - h * G::PIECES;
             const int32_t g = __shfl_sync(kFull, gid, h < G::NH ? h : 0);
             if (j < G::NH * G::PIECES)
-                cp_async16_f(bb + G::RES + h * G::ROW + p * 16, rows + (int64_t)g * G::ROW + p * 16);
+                cp_async16_f(bb + G::RES + h * G::ROW + p * 16,
+                             (SHARD ? pm.row_ptr(rows, G::ROW, g) : rows + (int64_t)g * G::ROW) + p * 16);
         }
         cp_async_commit_f();
     };
@@ -768,27 +791,40 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     flush_hits(hits, hit_count, lane);
 }
 
-template <int FMT, int DIM>
-void launch_pairsum_fixed(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
-                          const int32_t* seg_start, PosMap pm, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
-                          int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
+template <int FMT, int DIM, bool SHARD>
+void launch_pairsum_fixed_k(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
+                            const int32_t* seg_start, PosMap pm, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
+                            int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
     using G = XsGeom<FMT, DIM>;
     const int smem = 64 + kXsWarps * 2 * G::BUF;
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        cudaFuncSetAttribute(k_forward_pairsum_fixed<FMT, DIM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(k_forward_pairsum_fixed<FMT, DIM, SHARD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem);
         configured[dev] = true;
     }
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_forward_pairsum_fixed<FMT, DIM>, kXsWarps * 32, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_forward_pairsum_fixed<FMT, DIM, SHARD>, kXsWarps * 32,
+                                                  smem);
     if (per_sm < 1) per_sm = 1;
     const int64_t want = (n + kXsWarps - 1) / kXsWarps;
     const int64_t cap = (int64_t)sm_count() * per_sm;
     const int blocks = (int)(want < cap ? want : cap);
-    k_forward_pairsum_fixed<FMT, DIM><<<blocks, kXsWarps * 32, smem, s>>>(T, OV, tokens, seg_start, pm, n, out, ids_out,
-                                                                          slots_out, hit_count);
+    k_forward_pairsum_fixed<FMT, DIM, SHARD><<<blocks, kXsWarps * 32, smem, s>>>(T, OV, tokens, seg_start, pm, n,
+                                                                                 out, ids_out, slots_out, hit_count);
+}
+
+// The row-sharded read is a separate instantiation, so the resident-table kernel carries no shard logic.
+template <int FMT, int DIM>
+void launch_pairsum_fixed(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
+                          const int32_t* seg_start, PosMap pm, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
+                          int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
+    if (pm.shard) launch_pairsum_fixed_k<FMT, DIM, true>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out,
+                                                         hit_count, s);
+    else launch_pairsum_fixed_k<FMT, DIM, false>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out,
+                                                 hit_count, s);
 }
 
 // Runs the compile-time specialisation for this table if there is one.
@@ -931,6 +967,18 @@ extern "C" int engram_forward_indirect(const engram_table* t, const engram_overl
     if (t0 < 0 || (n > 0 && !row_index)) return ENGRAM_ERR_ARG;
     return forward_impl(t, ov, tokens, seg_start, PosMap{t0, nullptr, 0, row_index}, n, mode, out, ids_out, slots_out,
                         hit_count, stream);
+}
+
+extern "C" int engram_forward_sharded(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                      const int32_t* seg_start, int64_t t0, int64_t n, const void* shard_rows,
+                                      int32_t world, int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                                      int64_t* hit_count, void* stream) {
+    if (!shard_rows || world < 1 || world > 1024) return ENGRAM_ERR_ARG;
+    PosMap pm{t0, nullptr, 0, nullptr};
+    pm.shard = static_cast<const uint8_t* const*>(shard_rows);
+    pm.world = (uint32_t)world;
+    pm.wshift = (world & (world - 1)) == 0 ? __builtin_ctz((unsigned)world) : -1;
+    return forward_impl(t, ov, tokens, seg_start, pm, n, mode, out, ids_out, slots_out, hit_count, stream);
 }
 
 extern "C" int engram_forward_at(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,

@@ -95,8 +95,8 @@ def _emit(dtable, omap: OverlayMap, rv: torch.Tensor, tokens, seg_start, t0: int
     """One forward launch into `out`: engram_forward on a resident table, or the
     row exchange plus engram_forward_indirect on a row-sharded table."""
     if getattr(dtable, "is_sharded", False):
-        if dtable.exchange is None:
-            raise RuntimeError("this ShardedTable has no row exchange: set .exchange (e.g. nccl_exchange())")
+        if dtable.exchange is None and dtable.peer_ptrs is None:
+            raise RuntimeError("this ShardedTable has neither peer shards nor a row exchange (set .exchange)")
         dtable.forward(tokens, seg_start, omap, rv, out, mode, dtable.exchange, slots_out=slots,
                        hit_count=hit_count, t0=t0, n=n)
         return

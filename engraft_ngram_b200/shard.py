@@ -1,13 +1,17 @@
 """Row-sharded resident table across W GPUs: owner(g) = g mod W, local index g / W.
 
-Each rank holds 1/W of the table.  Per step a rank hashes its positions, skips
-the heads the overlay serves, sends the distinct remaining row ids to their
-owners (NCCL all-to-all-v), receives the quantised rows (a second
-all-to-all-v) into local HBM, and runs the forward over those rows
-(engram_forward_indirect).  The overlay itself is replicated and updated as in
-the data-parallel path (engraft_ngram_b200.dist).  The exchange is pluggable:
-`nccl_exchange` for real ranks, or any function with the same contract (the
-tests emulate W ranks on one GPU).
+Each rank holds 1/W of the table.  Two ways to read it:
+- peer memory (peer_ptrs set): every rank's shard lives in torch symmetric
+  memory, so the forward kernels copy each row straight from its owner over
+  NVLink (engram_forward_sharded); nothing runs before the forward;
+- an exchange (NCCL): a rank hashes its positions, skips the heads the overlay
+  serves, sends the distinct remaining row ids to their owners (all-to-all-v),
+  receives the quantised rows (a second all-to-all-v) into local HBM, and runs
+  the forward over those rows (engram_forward_indirect).  The exchange is
+  pluggable: `nccl_exchange` for real ranks, or any function with the same
+  contract (the tests emulate W ranks on one GPU).
+The overlay itself is replicated and updated as in the data-parallel path
+(engraft_ngram_b200.dist).
 """
 from __future__ import annotations
 
@@ -23,11 +27,15 @@ from .table import DeviceTable, _as_i32
 
 class ShardedTable:
     def __init__(self, shard_rows: torch.Tensor, fmt: int, dim: int, head_sizes, head_offsets, mult, eos_token_id,
-                 world: int, rank: int, n_rows: int, ngram_size: int = 3, heads_per_ngram: int = 8, exchange=None):
+                 world: int, rank: int, n_rows: int, ngram_size: int = 3, heads_per_ngram: int = 8, exchange=None,
+                 peer_ptrs: torch.Tensor | None = None):
         """shard_rows: uint8 CUDA tensor with this rank's rows in resident layout
         (global rows rank, rank+W, rank+2W, ... in order).  exchange: the row
         exchange the public API (engram_embed, engram_residual_add) uses with
-        this table, e.g. nccl_exchange(); settable later as .exchange."""
+        this table, e.g. nccl_exchange(); settable later as .exchange.
+        peer_ptrs: int64 device tensor [W] of every rank's shard address in
+        this process (peer_shard_buffer); when set, forward() reads rows in
+        place and needs no exchange."""
         if not (0 <= rank < world):
             raise ValueError(f"rank {rank} of {world}")
         lib = L.load()
@@ -39,6 +47,7 @@ class ShardedTable:
         self.shard = shard_rows
         self.device = shard_rows.device
         self.exchange = exchange
+        self.peer_ptrs = peer_ptrs
         self.is_sharded = True
         # addressing constants of the whole table; the rows pointer is replaced per step
         self.ngram_size, self.heads_per_ngram = int(ngram_size), int(heads_per_ngram)
@@ -104,8 +113,10 @@ class ShardedTable:
         return rows, rix
 
     def forward(self, tokens, seg_start, omap: OverlayMap, rows_var, out: torch.Tensor, mode: int,
-                exchange, slots_out=None, hit_count=None, t0: int = 0, n: int | None = None):
-        """Hash -> overlay lookup -> row exchange -> forward over the received rows."""
+                exchange=None, slots_out=None, hit_count=None, t0: int = 0, n: int | None = None):
+        """With peer_ptrs: one fused forward reading rows from their owners.
+        Otherwise: hash -> overlay lookup -> row exchange -> forward over the
+        received rows."""
         lib = L.load()
         dev = self.device
         tokens = _as_i32(tokens, dev)
@@ -113,6 +124,15 @@ class ShardedTable:
             n = tokens.numel() - t0
         ss = None if seg_start is None else _as_i32(seg_start, dev)
         stream = L.stream_of(dev)
+        if self.peer_ptrs is not None and exchange is None:
+            ov = omap.descriptor(rows_var)
+            st = lib.engram_forward_sharded(C.byref(self.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(ss), t0, n,
+                                            self.peer_ptrs.data_ptr(), self.world, mode, out.data_ptr(), None,
+                                            L.ptr(slots_out), L.ptr(hit_count), stream)
+            L.check(st, "engram_forward_sharded")
+            return out
+        if exchange is None:
+            raise RuntimeError("this ShardedTable has neither peer shards nor a row exchange")
         ids = self.global_ids(tokens, ss, t0, n)
         ov = omap.descriptor(rows_var)
         slots = None
@@ -167,3 +187,20 @@ def local_exchange(shards: list[ShardedTable]):
         return torch.cat(parts) if parts else torch.empty(0, dtype=torch.uint8, device=shard.device)
 
     return run
+
+
+def peer_shard_buffer(n_rows: int, fmt: int, dim: int, device, group=None):
+    """(this rank's shard buffer, ptrs): a uint8 buffer for ceil(n_rows / W)
+    resident rows in torch symmetric memory, and the int64 device tensor of
+    every rank's buffer address in this process (for ShardedTable's
+    peer_ptrs).  A collective: every rank of the group calls it."""
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm
+    group = group if group is not None else dist.group.WORLD
+    world = dist.get_world_size(group)
+    stride = int(L.load().engram_row_stride(fmt, dim))
+    rows_max = -(-int(n_rows) // world)
+    buf = symm.empty(max(rows_max * stride, 16), dtype=torch.uint8, device=device)
+    h = symm.rendezvous(buf, group)
+    ptrs = torch.tensor(list(h.buffer_ptrs), dtype=torch.int64, device=device)
+    return buf, ptrs, h

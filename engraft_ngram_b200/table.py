@@ -219,19 +219,28 @@ def _as_i32(x, device) -> torch.Tensor:
 
 
 def synthetic_resident(n_rows: int, fmt: int, dim: int, seed: int, device, sigma: float = 1e-3,
-                       f32_sigma: float = 0.0085) -> torch.Tensor:
+                       f32_sigma: float = 0.0085, out: torch.Tensor | None = None) -> torch.Tensor:
     """Seeded synthetic table generated directly in the resident layout on the
     device (the full-size tables do not pass through host memory).  IQ4 rows:
     uniform random nibbles and sub-scales, fp16 block scales |N(0, sigma)|;
-    F32 rows ~N(0, f32_sigma^2)."""
+    F32 rows ~N(0, f32_sigma^2).  out: a uint8 buffer of at least
+    n_rows * stride bytes to fill (e.g. a shard in symmetric memory)."""
     lib = L.load()
     stride = int(lib.engram_row_stride(fmt, dim))
     g = torch.Generator(device=device)
     g.manual_seed(seed)
+    if out is not None:
+        if out.numel() < n_rows * stride:
+            raise ValueError("synthetic_resident: out is too small")
+        out = out.reshape(-1)[: n_rows * stride].view(n_rows, stride)
     if fmt == L.FMT_F32:
         t = torch.randn(n_rows, dim, generator=g, device=device, dtype=torch.float32) * f32_sigma
+        if out is not None:
+            out.copy_(t.view(torch.uint8).reshape(n_rows, stride))
+            return out.reshape(-1)
         return t.view(torch.uint8).reshape(-1)
-    out = torch.empty(n_rows, stride, dtype=torch.uint8, device=device)
+    if out is None:
+        out = torch.empty(n_rows, stride, dtype=torch.uint8, device=device)
     chunk = 1 << 24
     for lo in range(0, n_rows, chunk):
         hi = min(n_rows, lo + chunk)

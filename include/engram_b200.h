@@ -189,6 +189,21 @@ ENGRAM_API int engram_forward_indirect(const engram_table* t, const engram_overl
                                        int64_t* hit_count, void* stream);
 
 /*
+ * engram_forward over a row-sharded table read in place: row g lives at local
+ * row g / world of rank (g % world)'s shard, and shard_rows (device array
+ * [world] of pointers valid in this process, e.g. each rank's shard in torch
+ * symmetric memory, mapped over NVLink) gives each shard's first row.  The
+ * kernels copy each row straight from its owner's memory (peer loads), so no
+ * exchange step runs before the forward.  t supplies the addressing constants
+ * of the whole table (n_rows = all rows); its rows pointer is not read.  No
+ * reference counterpart: the reference is single-process.
+ */
+ENGRAM_API int engram_forward_sharded(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                      const int32_t* seg_start, int64_t t0, int64_t n, const void* shard_rows,
+                                      int32_t world, int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                                      int64_t* hit_count, void* stream);
+
+/*
  * Row-sharded table (owner(g) = g mod world, local index g / world), step 1 of
  * the exchange: from the global ids [n] (n = positions * heads) and the overlay
  * slots (nullable; entries with slot >= 0 need no table row), builds

@@ -9,6 +9,8 @@ tolerance is 1e-5 of the row norm).
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
 import pytest
 import torch
@@ -372,6 +374,53 @@ def test_row_sharded_table_matches_resident_table(eb, world, fmt, dim, mode):
         got = out.view(torch.int32).cpu().numpy() if mode == O.MODE_CONCAT_F32 else out.view(torch.int16).cpu().numpy()
         want = ref.reshape(T, -1).view(np.int32) if mode == O.MODE_CONCAT_F32 else ref.view(np.int16)
         assert np.array_equal(got.reshape(want.shape), want), r
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("fmt,dim", [(O.FMT_IQ4_XS, 256), (O.FMT_IQ4_NL, 160), (O.FMT_F32, 128),
+                                     (O.FMT_IQ4_XS, 512), (O.FMT_IQ4_NL, 96)])
+@pytest.mark.parametrize("mode", [O.MODE_CONCAT_F32, O.MODE_PAIRSUM_ADD_BF16])
+def test_sharded_table_read_in_place_matches_resident_table(eb, world, fmt, dim, mode):
+    """engram_forward_sharded with W ranks' shards emulated as separate buffers
+    on one GPU (row g at row g / W of shard g % W): outputs, slots and the hit
+    count equal the forward over the whole resident table."""
+    from engraft_ngram_b200.shard import ShardedTable
+    rng = np.random.default_rng(31 * world + dim + mode)
+    n_rows = 20_003
+    spec = random_spec(fmt, dim, n_rows, 9 + world)
+    full = device_table(eb, spec)
+    shards = [full.rows.view(full.n_rows, full.row_stride)[r::world].contiguous().reshape(-1) for r in range(world)]
+    ptrs = torch.tensor([sh.data_ptr() for sh in shards], dtype=torch.int64, device=DEV)
+    T = 1100
+    toks = zipf_tokens(rng, T)
+    ss = torch.from_numpy(FX.seg_starts(np.sort(rng.integers(0, 4, size=T))))
+    ov_ids = np.unique(np.concatenate([np.unique(spec.ids(toks))[::4], rng.integers(0, n_rows, size=50)]))
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids.astype(np.int32)), DEV)
+    rows_var = torch.from_numpy((rng.standard_normal((len(ov_ids), dim)) * 0.01).astype(np.float32)).to(DEV)
+    res0 = O.bf16_bits((rng.standard_normal((T, 8 * dim)) * 0.5).astype(np.float32))
+    outs = []
+    for r in (None, world - 1):
+        if mode == O.MODE_CONCAT_F32:
+            out = torch.empty(T, 16, dim, device=DEV)
+        else:
+            out = torch.from_numpy(res0.view(np.int16).copy()).to(DEV).view(torch.bfloat16)
+        slots = torch.empty(T, 16, dtype=torch.int32, device=DEV)
+        hits = torch.zeros(1, dtype=torch.int64, device=DEV)
+        if r is None:
+            ov = omap.descriptor(rows_var)
+            toks_d, ss_d = torch.from_numpy(toks).to(DEV), ss.to(DEV)  # alive until the kernel has run
+            st = eb._lib.load().engram_forward(C.byref(full.ctable), C.byref(ov), toks_d.data_ptr(), ss_d.data_ptr(),
+                                               0, T, mode, out.data_ptr(), None, slots.data_ptr(), hits.data_ptr(),
+                                               eb._lib.stream_of(DEV))
+            eb._lib.check(st, "engram_forward")
+        else:
+            sh = ShardedTable(shards[r], fmt, dim, full.head_vocab_sizes, full.head_offsets, full.layer_multipliers,
+                              full.eos_token_id, world, r, full.n_rows, peer_ptrs=ptrs)
+            sh.forward(toks, ss, omap, rows_var, out, mode, slots_out=slots, hit_count=hits)
+        torch.cuda.synchronize()
+        outs.append((out.view(torch.int16).cpu().numpy(), slots.cpu().numpy(), int(hits.item())))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1]) and outs[0][2] == outs[1][2]
 
 
 def test_sharded_table_through_the_public_autograd_api(eb):

@@ -69,6 +69,14 @@ def parse():
     ap.add_argument("--shard-exchange", choices=["peer", "nccl"], default="peer",
                     help="--shard: rows read in place from their owners over NVLink (symmetric memory) or moved by "
                          "NCCL all-to-all of ids and rows")
+    ap.add_argument("--no-sharded-line", action="store_true",
+                    help="N>1: skip the second measurement with the table row-sharded")
+    ap.add_argument("--stage", choices=["push", "pull", "off"], default="pull",
+                    help="--shard, peer reads: copy the next step's rows of other ranks on a side stream while the "
+                         "current step runs (ShardedTable.prefetch), so the forward reads every row locally; push: "
+                         "the owners store them into the requesters' stages; pull: each rank loads its own")
+    ap.add_argument("--stage-blocks", type=int, default=0,
+                    help="grid cap of the staging copy (0: the whole GPU)")
     ap.add_argument("--shard", action="store_true",
                     help="row-sharded table: each rank holds rows g with g %% N == rank; rows move by NCCL all-to-all")
     return ap.parse_args()
@@ -122,6 +130,8 @@ class Workload:
         offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
         mult = synthetic_multipliers(seed)
         self.shard = None
+        self.stage = False
+        self.stage_blocks = int(cfg.get("stage_blocks", 0))
         if cfg.get("shard"):
             from engraft_ngram_b200.shard import ShardedTable, local_exchange, nccl_exchange, peer_shard_buffer
             n_local = (cfg["rows"] - rank + world - 1) // world
@@ -132,6 +142,9 @@ class Workload:
                 self.shard = ShardedTable(buf, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"],
                                           peer_ptrs=ptrs)
                 self.exchange = None
+                self.stage = cfg.get("stage", "push") != "off"
+                if cfg.get("stage", "push") == "push":
+                    self.shard.enable_push_staging(cfg["seqs"] * cfg["seq_len"], max_blocks=self.stage_blocks)
             else:
                 rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device)
                 self.shard = ShardedTable(rows, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"])
@@ -152,6 +165,10 @@ class Workload:
         gen.manual_seed(seed * 1000 + 17 + rank)
         self.tokens = census if rank == 0 else zipf_tokens(torch, self.T, gen, cdf)
         self.seg_start = (torch.arange(self.T, device=device, dtype=torch.int32) // cfg["seq_len"]) * cfg["seq_len"]
+        # staged sharded reads: step k+1's rows are copied while step k runs; the two steps' batches live in two
+        # buffers (same tokens here), so each copy is for a distinct batch
+        self.tok_bufs = [self.tokens, self.tokens.clone()] if self.stage else [self.tokens]
+        self.k = 0
         self.positions = None
         if self.decode:  # uniform histories; output rows are the sequences' last tokens
             census = torch.randint(0, VOCAB, (self.T,), generator=gen0, device=device, dtype=torch.int32)
@@ -227,11 +244,26 @@ class Workload:
         self.stream = torch.cuda.current_stream(device).cuda_stream
         self.ov_desc = self.omap.descriptor(self.rows_var) if self.R else L.EngramOverlay(None, 0, None, None, 0)
 
+    def join_stage(self):
+        """The current stream waits for the staging copy in flight (push: the
+        copy and the barrier that completes it on every rank)."""
+        import torch
+        cur = torch.cuda.current_stream(self.dev)
+        if self.shard.push is not None:
+            self.shard.push.join(cur)
+        elif self.shard._side is not None:
+            cur.wait_stream(self.shard._side)
+
     # one step through the C ABI (device-resident inputs)
     def forward(self, hit_count=None):
         import ctypes as C
         if self.shard is not None:
-            self.shard.forward(self.tokens, self.seg_start, self.omap, self.rows_var, self.out, self.mode,
+            tok = self.tok_bufs[self.k % len(self.tok_bufs)]
+            if self.stage:  # the next step's rows of other ranks, copied while this step runs
+                self.shard.prefetch(self.tok_bufs[(self.k + 1) % 2], self.seg_start, max_blocks=self.stage_blocks,
+                                    omap=self.omap)
+            self.k += 1
+            self.shard.forward(tok, self.seg_start, self.omap, self.rows_var, self.out, self.mode,
                                self.exchange, slots_out=self.slots if self.R else None, hit_count=hit_count)
             return
         if self.decode:
@@ -551,16 +583,27 @@ def run_scan(args, device):
     print(json.dumps(line), flush=True)
 
 
+def shard_text(cfg):
+    if not cfg.get("shard"):
+        return ""
+    if cfg.get("shard_exchange", "peer") != "peer":
+        return "+row-sharded table (id mod N, NCCL all-to-all of ids and rows)"
+    if cfg.get("stage", "push") == "push":
+        return ("+row-sharded table (id mod N; during the previous step each owner stores the rows it holds into "
+                "the other ranks' stage buffers over NVLink, on a side stream; the forward reads local HBM)")
+    if cfg.get("stage", "push") == "pull":
+        return ("+row-sharded table (id mod N; the rows of other ranks are loaded from their owners over NVLink on a "
+                "side stream during the previous step, the forward reads local HBM)")
+    return "+row-sharded table (id mod N; rows read from their owners over NVLink inside the forward)"
+
+
 def config_json(cfg, args):
     return {"workload": f"{args.config}: {cfg['seqs']}x{cfg['seq_len']} tokens/GPU, Zipf(1.1) over {VOCAB}, "
                         f"{cfg['rows']}-row x {cfg['dim']} {cfg['fmt']} table, R={cfg['R']} overlay rows, "
                         f"{cfg['mode']} emit, {'fwd+bwd+Adam' if cfg['bwd'] else 'fwd only'}",
             "table_rows": cfg["rows"], "dim": cfg["dim"], "format": cfg["fmt"], "positions_per_gpu": cfg["seqs"] * cfg["seq_len"],
             "overlay_rows": cfg["R"], "emit": cfg["mode"],
-            "parallelism": f"dp{args.gpus}" + (("+row-sharded table (id mod N; rows read from their owners over "
-                                                 "NVLink inside the forward)" if cfg.get("shard_exchange", "peer") == "peer"
-                                                 else "+row-sharded table (id mod N, NCCL all-to-all of ids and rows)")
-                                                if cfg.get("shard") else ""),
+            "parallelism": f"dp{args.gpus}" + shard_text(cfg),
             "optimizer_exchange": (None if args.gpus == 1 else
                                    ("one peer-memory kernel per rank (sum over ranks + Adam + stores to every rank)"
                                     if cfg.get("exchange", "peer") == "peer" else "NCCL reduce-scatter + all-gather")),
@@ -584,6 +627,8 @@ def main():
     cfg["shard"] = bool(args.shard)
     cfg["exchange"] = args.exchange
     cfg["shard_exchange"] = args.shard_exchange
+    cfg["stage"] = args.stage
+    cfg["stage_blocks"] = args.stage_blocks
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -605,50 +650,34 @@ def main():
     nbytes = wl.algorithmic_bytes()
     step_bytes = nbytes["fwd"] + nbytes["bwd"] + nbytes["adam"]
 
-    for _ in range(max(3, args.warmup)):
-        wl.step(ddist)
-    torch.cuda.synchronize()
     K = args.steps
-    f0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    f1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    b1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        if ddist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-        n_launch0 = lib.engram_launch_count()
-        e0.record()
-        for k in range(K):
-            f0[k].record()
-            wl.forward()
-            f1[k].record()
-            if cfg["bwd"] and wl.R:
-                wl.backward()
-                b1[k].record()
-                wl.optimizer(ddist)
-        e1.record()
-        torch.cuda.synchronize()
-        launches = lib.engram_launch_count() - n_launch0
-        if ddist is not None:
-            dist.barrier()
-    ms = e0.elapsed_time(e1) / K
-    fwd_ms = sum(a.elapsed_time(b) for a, b in zip(f0, f1)) / K
-    bwd_ms = sum(a.elapsed_time(b) for a, b in zip(f1, b1)) / K if cfg["bwd"] and wl.R else 0.0
-    t = torch.tensor([ms, fwd_ms], device=device, dtype=torch.float64)
-    if ddist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, fwd_ms = float(t[0]), float(t[1])
+        ms, fwd_ms, bwd_ms, launches = time_steps(wl, K, args.warmup, ddist)
     value = 16 * wl.n_out * world / (ms * 1e-3)
+    n_out, pairsum = wl.n_out, wl.mode == wl.L.MODE_PAIRSUM_ADD_BF16
 
     e2e = None
     if not args.no_e2e and not wl.decode:
         e2e = run_e2e(wl, args, device, ddist, world)
 
+    row_sharded = None
+    if world > 1 and not cfg["shard"] and args.config == "cfg5" and not args.no_sharded_line:
+        # the same step with the table row-sharded (id mod N), measured in the same run
+        del wl
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        cfg2 = dict(cfg, shard=True, shard_exchange="peer", stage="pull")
+        wl2 = Workload(cfg2, rank, world, args.seed, device)
+        ms2, fwd2, bwd2, _ = time_steps(wl2, K, args.warmup, ddist)
+        row_sharded = {"value": 16 * wl2.n_out * world / (ms2 * 1e-3), "unit": "rows/s", "ms_per_step": ms2,
+                       "phase_ms": {"forward": fwd2, "backward": bwd2, "optimizer_and_exchange": ms2 - fwd2 - bwd2},
+                       "parallelism": f"dp{world}" + shard_text(cfg2),
+                       "table_bytes_per_gpu": int(wl2.shard.n_local * wl2.shard.stride)}
+
     if rank == 0:
         peak, peak_kind = measured_peak_gbs()
         fwd_gbs = nbytes["fwd"] / (fwd_ms * 1e-3) / 1e9
-        traffic, tfile = profiled_traffic("k_forward_pairsum" if wl.mode == wl.L.MODE_PAIRSUM_ADD_BF16 else "k_forward_concat")
+        traffic, tfile = profiled_traffic("k_forward_pairsum" if pairsum else "k_forward_concat")
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -657,10 +686,10 @@ def main():
             "gbps": step_bytes * world / (ms * 1e-3) / 1e9,
             "algorithmic_bytes_per_step_per_gpu": step_bytes,
             "bytes_breakdown": nbytes,
-            "hit_fraction": nbytes["hits"] / (16 * wl.n_out),
+            "hit_fraction": nbytes["hits"] / (16 * n_out),
             "phase_ms": {"forward": fwd_ms, "backward": bwd_ms, "optimizer_and_exchange": ms - fwd_ms - bwd_ms},
             "us_per_step": ms * 1e3,
-            "roofline": {"kernel": "engram_forward (k_forward_pairsum_fixed<IQ4_XS,256>)" if wl.mode else "engram_forward (k_forward_concat)",
+            "roofline": {"kernel": "engram_forward (k_forward_pairsum_fixed<IQ4_XS,256>)" if pairsum else "engram_forward (k_forward_concat)",
                          "bound": "hbm", "achieved": fwd_gbs, "peak": peak, "unit": "GB/s", "frac": fwd_gbs / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s",
                          "traffic": traffic, "traffic_source": tfile, "algorithmic_bytes_per_launch": nbytes["fwd"],
@@ -669,6 +698,8 @@ def main():
             "clocks": clk.summary(),
             "e2e": e2e,
         }
+        if row_sharded is not None:
+            line["row_sharded"] = row_sharded
         if world == 1 and not args.no_cpu_baseline:
             try:
                 b = cpu_oracle_step_time(cfg, args.seed)
@@ -687,6 +718,50 @@ def main():
         dist.destroy_process_group()
 
 
+def time_steps(wl, K, warmup, ddist):
+    """max(3, warmup) untimed steps, then K steps between CUDA events on the
+    launching stream, bracketed by a barrier and a synchronize; the step time
+    and the forward time are maxima over ranks.  Returns (ms per step, forward
+    ms, backward ms, kernel launches in the timed region)."""
+    import torch
+    lib = wl.L.load()
+    bwd = wl.cfg["bwd"] and wl.R
+    for _ in range(max(3, warmup)):
+        wl.step(ddist)
+    torch.cuda.synchronize()
+    f0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    f1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    b1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ddist is not None:
+        ddist.barrier()
+    torch.cuda.synchronize()
+    n_launch0 = lib.engram_launch_count()
+    e0.record()
+    for k in range(K):
+        f0[k].record()
+        wl.forward()
+        f1[k].record()
+        if bwd:
+            wl.backward()
+            b1[k].record()
+            wl.optimizer(ddist)
+    if wl.stage:  # the copy for the step after the last is timed too
+        wl.join_stage()
+    e1.record()
+    torch.cuda.synchronize()
+    launches = lib.engram_launch_count() - n_launch0
+    if ddist is not None:
+        ddist.barrier()
+    ms = e0.elapsed_time(e1) / K
+    fwd_ms = sum(a.elapsed_time(b) for a, b in zip(f0, f1)) / K
+    bwd_ms = sum(a.elapsed_time(b) for a, b in zip(f1, b1)) / K if bwd else 0.0
+    t = torch.tensor([ms, fwd_ms, bwd_ms], device=wl.dev, dtype=torch.float64)
+    if ddist is not None:
+        ddist.all_reduce(t, op=ddist.ReduceOp.MAX)
+    return float(t[0]), float(t[1]), float(t[2]), int(launches)
+
+
 def run_e2e(wl, args, device, ddist, world):
     """Same step through the public Python API with host inputs: tokens and
     segment starts copied from pinned host memory each step, the hit count read
@@ -700,11 +775,20 @@ def run_e2e(wl, args, device, ddist, world):
     rows_var = wl.p0.clone().requires_grad_(True)
     opt = eb.OverlayAdam([rows_var], lr=wl.lr, reg_ref=wl.p0, reg_mu=wl.mu)
     hits = torch.zeros(1, dtype=torch.int64, device=device)
+    pending = []  # staged sharded reads: the next step's inputs, copied and prefetched one step ahead
 
     def one():
         residual = wl.out.detach()
-        tok = tok_h.to(device, non_blocking=True)
-        ss = ss_h.to(device, non_blocking=True)
+        if wl.stage:
+            if not pending:
+                pending.append((tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True)))
+            tok, ss = pending.pop()
+            nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
+            wl.table.prefetch(nxt[0], nxt[1], max_blocks=wl.stage_blocks, omap=wl.omap)
+            pending.append(nxt)
+        else:
+            tok = tok_h.to(device, non_blocking=True)
+            ss = ss_h.to(device, non_blocking=True)
         hits.zero_()
         opt.zero_grad()
         if wl.mode == wl.L.MODE_PAIRSUM_ADD_BF16:
@@ -729,6 +813,8 @@ def run_e2e(wl, args, device, ddist, world):
     e0.record()
     for _ in range(K):
         one()
+    if wl.stage:
+        wl.join_stage()
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / K

@@ -116,6 +116,18 @@ SIGNATURES = {
     "engram_forward_sharded": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
                                          C.c_int64, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_stage_bytes": (C.c_int64, [C.POINTER(EngramTable), C.c_int64]),
+    "engram_stage_sharded": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
+                                       C.c_int64, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
+                                       C.c_void_p]),
+    "engram_stage_plan_words": (C.c_int64, [C.c_int64, C.c_int32]),
+    "engram_stage_plan": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                    C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_stage_push": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
+                                    C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
+    "engram_forward_staged": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
+                                        C.c_int64, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
+                                        C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "engram_selftest_mod": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),
     "engram_launch_count": (C.c_int64, []),
 }

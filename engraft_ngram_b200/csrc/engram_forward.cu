@@ -36,10 +36,13 @@ struct PosMap {
     const uint8_t* const* shard = nullptr;
     uint32_t world = 1;
     int wshift = 0;
-    // Address of row r: T.rows + r * stride, or the row in its owner's shard.
-    __device__ __forceinline__ const uint8_t* row_ptr(const uint8_t* rows, int64_t stride, int32_t r) const {
-        if (shard == nullptr) return rows + (int64_t)r * stride;
-        uint32_t o, l;
+    // nullable (sharded reads only): rows of other ranks already copied into
+    // this GPU's memory, head h of output row i at stage + (i * nh + h) * stride
+    // (engram_stage_sharded); rows owned by `rank` are still read in place
+    const uint8_t* stage = nullptr;
+    uint32_t rank = 0;
+    // Owner rank o of global row r and its row l in that rank's shard.
+    __device__ __forceinline__ void owner_of(int32_t r, uint32_t& o, uint32_t& l) const {
         if (wshift >= 0) {
             o = (uint32_t)r & (world - 1u);
             l = (uint32_t)r >> wshift;
@@ -47,6 +50,15 @@ struct PosMap {
             l = (uint32_t)r / world;
             o = (uint32_t)r - l * world;
         }
+    }
+    // Address of row r serving head h of output row i: T.rows + r * stride, its
+    // staged copy, or the row in its owner's shard.
+    __device__ __forceinline__ const uint8_t* row_ptr(const uint8_t* rows, int64_t stride, int32_t r, int64_t i,
+                                                      int h, int nh) const {
+        if (shard == nullptr) return rows + (int64_t)r * stride;
+        uint32_t o, l;
+        owner_of(r, o, l);
+        if (stage != nullptr && o != rank) return stage + (i * nh + h) * stride;
         const uint8_t* base =
             reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(shard) + o));
         return base + (int64_t)l * stride;
@@ -99,6 +111,61 @@ __global__ void __launch_bounds__(256) k_hash(engram_table T, const int32_t* __r
         const int64_t i = k / nh;
         const int h = (int)(k - i * nh);
         ids_out[k] = hash_row(T, tokens, seg_start, pm.at(i), h);
+    }
+}
+
+// Copies every row of another rank that the sharded forward over the same
+// output rows reads into this GPU's memory: head h of output row i to
+// stage + (i * nh + h) * stride.  One warp per output row; each lane keeps up
+// to kStageLoads 16-byte pieces in flight.  Rows of this rank are skipped (the
+// forward reads them in place), so are the heads the overlay serves (the
+// forward reads their fp32 rows; OV.n_rows == 0: no overlay).
+constexpr int kStageLoads = 8;
+__global__ void __launch_bounds__(256) k_stage_sharded(engram_table T, engram_overlay OV,
+                                                       const int32_t* __restrict__ tokens,
+                                                       const int32_t* __restrict__ seg_start, PosMap pm, int64_t n,
+                                                       uint8_t* __restrict__ stage) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int nh = T.n_heads;
+    const int pieces = (int)(T.row_stride >> 4);
+    const int total = nh * pieces;
+    const unsigned long long* shard = reinterpret_cast<const unsigned long long*>(pm.shard);
+    for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; i < n; i += nw) {
+        int32_t gid = 0;
+        bool copy = false;  // another rank's row that the overlay does not replace
+        if (lane < nh) {
+            const int64_t t = pm.at(i);
+            gid = hash_ctx(T, load_ctx(T, tokens, seg_start, t), t, lane);
+            uint32_t o, l;
+            pm.owner_of(gid, o, l);
+            copy = o != pm.rank && overlay_slot(OV, gid) < 0;
+        }
+        const unsigned want = __ballot_sync(kFull, copy);
+        uint8_t* srow = stage + i * nh * T.row_stride;
+        for (int j0 = 0; j0 < total; j0 += 32 * kStageLoads) {
+            uint4 v[kStageLoads];
+            int dst[kStageLoads];  // byte offset in srow, -1: nothing to copy
+#pragma unroll
+            for (int u = 0; u < kStageLoads; u++) {
+                const int j = j0 + u * 32 + lane;
+                const int h = j / pieces;
+                const int p = j - h * pieces;
+                const int32_t g = __shfl_sync(kFull, gid, h < nh ? h : 0);
+                dst[u] = -1;
+                if (j < total && ((want >> h) & 1u)) {
+                    uint32_t o, l;
+                    pm.owner_of(g, o, l);
+                    const uint8_t* src = reinterpret_cast<const uint8_t*>(__ldg(shard + o)) +
+                                         (int64_t)l * T.row_stride + p * 16;
+                    v[u] = *reinterpret_cast<const uint4*>(src);
+                    dst[u] = h * (int)T.row_stride + p * 16;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kStageLoads; u++)
+                if (dst[u] >= 0) __stcg(reinterpret_cast<uint4*>(srow + dst[u]), v[u]);
+        }
     }
 }
 
@@ -242,10 +309,10 @@ __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engra
                 sl[u] = s;
                 if (c < cpp) {
                     if (FMT == ENGRAM_FMT_F32) {
-                        const float* src = s >= 0 ? ovr + (int64_t)s * dim : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, g));
+                        const float* src = s >= 0 ? ovr + (int64_t)s * dim : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, g, i, h, nh));
                         v[u] = __ldg(reinterpret_cast<const float4*>(src) + cc);
                     } else if (s < 0) {
-                        raw[u] = raw4<FMT>(pm.row_ptr(rows, T.row_stride, g), cc, dim);
+                        raw[u] = raw4<FMT>(pm.row_ptr(rows, T.row_stride, g, i, h, nh), cc, dim);
                     }
                 }
             }
@@ -343,9 +410,9 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                     const int32_t s1 = __shfl_sync(kFull, ph.slot, hpn + gs);
                     if (c < cpp) {
                         ld_f8(s0 >= 0 ? ovr + (int64_t)s0 * dim + 8 * cc
-                                      : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, ga)) + 8 * cc, fa[u]);
+                                      : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, ga, i, gs, nh)) + 8 * cc, fa[u]);
                         ld_f8(s1 >= 0 ? ovr + (int64_t)s1 * dim + 8 * cc
-                                      : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, gb)) + 8 * cc, fb[u]);
+                                      : reinterpret_cast<const float*>(pm.row_ptr(rows, T.row_stride, gb, i, hpn + gs, nh)) + 8 * cc, fb[u]);
                     }
                 }
 #pragma unroll
@@ -366,8 +433,8 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                     const int32_t gb = __shfl_sync(kFull, ph.row, hpn + gs);
                     const int32_t s1 = __shfl_sync(kFull, ph.slot, hpn + gs);
                     if (c < cpp) {
-                        if (s0 < 0) ra[u] = raw8<FMT>(pm.row_ptr(rows, T.row_stride, ga), cc, dim);
-                        if (s1 < 0) rb[u] = raw8<FMT>(pm.row_ptr(rows, T.row_stride, gb), cc, dim);
+                        if (s0 < 0) ra[u] = raw8<FMT>(pm.row_ptr(rows, T.row_stride, ga, i, gs, nh), cc, dim);
+                        if (s1 < 0) rb[u] = raw8<FMT>(pm.row_ptr(rows, T.row_stride, gb, i, hpn + gs, nh), cc, dim);
                     }
                 }
 #pragma unroll
@@ -482,7 +549,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
             const int p = j - h * pieces;
             const int32_t g = __shfl_sync(kFull, gid, h < nh ? h : 0);
             if (j < row_pieces)
-                cp_async16_f(bb + res_bytes + h * T.row_stride + p * 16, pm.row_ptr(rows, T.row_stride, g) + p * 16);
+                cp_async16_f(bb + res_bytes + h * T.row_stride + p * 16, pm.row_ptr(rows, T.row_stride, g, pos, h, nh) + p * 16);
         }
         cp_async_commit_f();
     };
@@ -684,7 +751,9 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     const uint8_t* rows = static_cast<const uint8_t*>(T.rows);
     const bool head_lane = lane < G::NH;
 
-    auto issue = [&](int64_t pos, int32_t gid, int b) {
+    // Copies position pos's residual and the table rows of its heads that the
+    // overlay does not serve (slot < 0; an overlay head reads its fp32 row instead).
+    auto issue = [&](int64_t pos, int32_t gid, int32_t slot, int b) {
         uint8_t* bb = wbuf + b * G::BUF;
         const uint4* src = reinterpret_cast<const uint4*>(out + pos * (G::HPN * DIM));
 #pragma unroll
@@ -695,9 +764,10 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
             const int h = j / G::PIECES;
             const int p = j - h * G::PIECES;
             const int32_t g = __shfl_sync(kFull, gid, h < G::NH ? h : 0);
-            if (j < G::NH * G::PIECES)
+            const int32_t sl = __shfl_sync(kFull, slot, h < G::NH ? h : 0);
+            if (j < G::NH * G::PIECES && sl < 0)
                 cp_async16_f(bb + G::RES + h * G::ROW + p * 16,
-                             (SHARD ? pm.row_ptr(rows, G::ROW, g) : rows + (int64_t)g * G::ROW) + p * 16);
+                             (SHARD ? pm.row_ptr(rows, G::ROW, g, pos, h, G::NH) : rows + (int64_t)g * G::ROW) + p * 16);
         }
         cp_async_commit_f();
     };
@@ -706,8 +776,8 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     int64_t i = first;
     TokCtx c0 = load_ctx(T, tokens, seg_start, pm.at(i));
     int32_t gid = head_lane ? hash_ctx(T, c0, pm.at(i), lane) : 0;
-    issue(i, head_lane ? pm.row(i, lane, G::NH, gid) : 0, 0);
     int32_t slot = head_lane ? probe_finish(OV, gid, probe_start(OV, gid)) : -1;
+    issue(i, head_lane ? pm.row(i, lane, G::NH, gid) : 0, slot, 0);
     int64_t i1 = i + nw;
     int32_t gid1 = 0;
     ProbeState pr1{0u, -1, -1};
@@ -728,8 +798,16 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     int b = 0;
     for (; i < n; i += nw) {
         const int64_t inext = i + nw;
-        if (inext < n) issue(inext, row1, b ^ 1);
+        // the next position's probe (its key loads were issued an iteration ago) decides which rows to copy
+        const int32_t slot1 = (inext < n && head_lane) ? probe_finish(OV, gid1, pr1) : -1;
+        if (inext < n) issue(inext, row1, slot1, b ^ 1);
         else cp_async_commit_f();
+        if (slot1 >= 0) {  // the next position's overlay row: pull it into L1 while this position computes
+            const char* orow_p = reinterpret_cast<const char*>(OV.rows + (int64_t)slot1 * DIM);
+#pragma unroll
+            for (int l = 0; l < DIM * 4 / 128; l++)
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(orow_p + 128 * l));
+        }
         if (head_lane) {
             if (ids_out) ids_out[i * G::NH + lane] = gid;
             if (slots_out) slots_out[i * G::NH + lane] = slot;
@@ -766,15 +844,9 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
             }
         }
         __syncwarp();  // buffer b is refilled next iteration
-        // advance the pipeline: k+1's probe resolves, k+2 is hashed and probed, k+3's tokens load
+        // advance the pipeline: k+2 is hashed and probed, k+3's tokens load
         gid = gid1;
-        slot = (inext < n && head_lane) ? probe_finish(OV, gid1, pr1) : -1;
-        if (slot >= 0) {  // next position's overlay row: pull it into L1 while this iteration's copies land
-            const char* orow_p = reinterpret_cast<const char*>(OV.rows + (int64_t)slot * DIM);
-#pragma unroll
-            for (int l = 0; l < DIM * 4 / 128; l++)
-                asm volatile("prefetch.global.L1 [%0];" ::"l"(orow_p + 128 * l));
-        }
+        slot = slot1;
         const int64_t i2 = inext + nw;
         if (i2 < n) {
             gid1 = head_lane ? hash_ctx(T, c2, pm.at(i2), lane) : 0;
@@ -969,15 +1041,67 @@ extern "C" int engram_forward_indirect(const engram_table* t, const engram_overl
                         hit_count, stream);
 }
 
+namespace {
+int sharded_map(PosMap& pm, const void* shard_rows, int32_t world, int32_t rank) {
+    if (!shard_rows || world < 1 || world > 1024 || rank < 0 || rank >= world) return ENGRAM_ERR_ARG;
+    pm.shard = static_cast<const uint8_t* const*>(shard_rows);
+    pm.world = (uint32_t)world;
+    pm.rank = (uint32_t)rank;
+    pm.wshift = (world & (world - 1)) == 0 ? __builtin_ctz((unsigned)world) : -1;
+    return ENGRAM_OK;
+}
+}  // namespace
+
+extern "C" int64_t engram_stage_bytes(const engram_table* t, int64_t n) {
+    if (!t || n < 0) return ENGRAM_ERR_ARG;
+    return n * t->n_heads * t->row_stride;
+}
+
+extern "C" int engram_stage_sharded(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                    const int32_t* seg_start, int64_t t0, int64_t n, const void* shard_rows,
+                                    int32_t world, int32_t rank, void* stage, int32_t max_blocks, void* stream) {
+    if (!t || t0 < 0 || n < 0 || max_blocks < 0) return ENGRAM_ERR_ARG;
+    PosMap pm{t0, nullptr, 0, nullptr};
+    const int st = sharded_map(pm, shard_rows, world, rank);
+    if (st != ENGRAM_OK) return st;
+    if (t->row_stride % 16 || t->n_heads < 1 || t->n_heads > 32) return ENGRAM_ERR_FORMAT;
+    if (n == 0 || world == 1) return ENGRAM_OK;  // one rank: every row is local
+    if (!tokens || !stage || !aligned16(stage)) return ENGRAM_ERR_ARG;
+    engram_overlay OV{nullptr, 0, nullptr, nullptr, 0};
+    if (ov && ov->n_rows > 0) {
+        OV = *ov;
+        if (!OV.map_keys || !OV.map_slots || (OV.capacity & (OV.capacity - 1)) != 0 || OV.capacity < 2 * OV.n_rows)
+            return ENGRAM_ERR_ARG;
+    }
+    const int64_t want = (n + 7) / 8;
+    const int64_t cap = max_blocks > 0 ? max_blocks : (int64_t)sm_count() * 8;
+    k_stage_sharded<<<(int)(want < cap ? want : cap), 256, 0, (cudaStream_t)stream>>>(*t, OV, tokens, seg_start, pm, n,
+                                                                                       static_cast<uint8_t*>(stage));
+    count_launches(1);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int engram_forward_staged(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                     const int32_t* seg_start, int64_t t0, int64_t n, const void* shard_rows,
+                                     int32_t world, int32_t rank, const void* stage, int32_t mode, void* out,
+                                     int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream) {
+    if (t0 < 0) return ENGRAM_ERR_ARG;
+    PosMap pm{t0, nullptr, 0, nullptr};
+    const int st = sharded_map(pm, shard_rows, world, rank);
+    if (st != ENGRAM_OK) return st;
+    if (world > 1 && n > 0 && (!stage || !aligned16(stage))) return ENGRAM_ERR_ARG;
+    pm.stage = world > 1 ? static_cast<const uint8_t*>(stage) : nullptr;
+    return forward_impl(t, ov, tokens, seg_start, pm, n, mode, out, ids_out, slots_out, hit_count, stream);
+}
+
 extern "C" int engram_forward_sharded(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
                                       const int32_t* seg_start, int64_t t0, int64_t n, const void* shard_rows,
                                       int32_t world, int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
                                       int64_t* hit_count, void* stream) {
-    if (!shard_rows || world < 1 || world > 1024) return ENGRAM_ERR_ARG;
+    if (t0 < 0) return ENGRAM_ERR_ARG;
     PosMap pm{t0, nullptr, 0, nullptr};
-    pm.shard = static_cast<const uint8_t* const*>(shard_rows);
-    pm.world = (uint32_t)world;
-    pm.wshift = (world & (world - 1)) == 0 ? __builtin_ctz((unsigned)world) : -1;
+    const int st = sharded_map(pm, shard_rows, world, 0);
+    if (st != ENGRAM_OK) return st;
     return forward_impl(t, ov, tokens, seg_start, pm, n, mode, out, ids_out, slots_out, hit_count, stream);
 }
 

@@ -3,7 +3,12 @@
 Each rank holds 1/W of the table.  Two ways to read it:
 - peer memory (peer_ptrs set): every rank's shard lives in torch symmetric
   memory, so the forward kernels copy each row straight from its owner over
-  NVLink (engram_forward_sharded); nothing runs before the forward;
+  NVLink (engram_forward_sharded); nothing runs before the forward.  The
+  shards never change (training updates the overlay only), so the rows of
+  other ranks that a forward will read can be copied ahead, on a side stream
+  while the previous step runs (prefetch -> engram_stage_sharded); the
+  forward over the same tokens then reads every row from local HBM
+  (engram_forward_staged);
 - an exchange (NCCL): a rank hashes its positions, skips the heads the overlay
   serves, sends the distinct remaining row ids to their owners (all-to-all-v),
   receives the quantised rows (a second all-to-all-v) into local HBM, and runs
@@ -16,6 +21,7 @@ The overlay itself is replicated and updated as in the data-parallel path
 from __future__ import annotations
 
 import ctypes as C
+from collections import OrderedDict
 
 import numpy as np
 import torch
@@ -49,6 +55,10 @@ class ShardedTable:
         self.exchange = exchange
         self.peer_ptrs = peer_ptrs
         self.is_sharded = True
+        self._staged = OrderedDict()  # prefetch key -> _Staged, waiting for its forward
+        self._free = []  # _Staged buffers whose forward has been issued
+        self._side = None  # the prefetch stream
+        self.push = None  # PushStage: owners copy rows into the requesters' stages (enable_push_staging)
         # addressing constants of the whole table; the rows pointer is replaced per step
         self.ngram_size, self.heads_per_ngram = int(ngram_size), int(heads_per_ngram)
         self.n_heads = (int(ngram_size) - 1) * int(heads_per_ngram)
@@ -112,6 +122,88 @@ class ShardedTable:
         rows = exchange(self, send_ids, send_counts)
         return rows, rix
 
+    @staticmethod
+    def _key(tokens: torch.Tensor, ss: torch.Tensor | None, t0: int, n: int):
+        return (tokens.data_ptr(), tokens._version, 0 if ss is None else ss.data_ptr(),
+                -1 if ss is None else ss._version, int(t0), int(n))
+
+    def enable_push_staging(self, n_tokens_max: int, group=None, max_blocks: int = 0) -> None:
+        """Make prefetch() push-based and collective: every rank's tokens go to
+        symmetric memory, and each owner copies the rows it holds into the
+        requesters' stage buffers with NVLink stores (engram_stage_push) instead
+        of each rank pulling its rows with NVLink loads.  Every rank of the
+        group then calls prefetch() and forward() in the same order, with the
+        same t0 and n and with or without seg_start alike; n_tokens_max bounds
+        the token arrays.  A collective: every rank calls it."""
+        if self.peer_ptrs is None:
+            raise RuntimeError("push staging needs the peer shards (peer_ptrs)")
+        self.push = PushStage(self, n_tokens_max, group, max_blocks)
+
+    def prefetch(self, tokens, seg_start=None, t0: int = 0, n: int | None = None, max_blocks: int = 0,
+                 stream: torch.cuda.Stream | None = None, omap: OverlayMap | None = None) -> None:
+        """Copy the rows of other ranks that forward(tokens, seg_start, ..., t0, n)
+        will read into this GPU's memory, on `stream` (default: the table's own
+        side stream, ordered after the work already queued on the current
+        stream).  The next forward() over the same int32 device tensors (same
+        storage, not modified since) waits for the copy and reads those rows
+        locally; any other forward reads in place as before.  omap: the overlay
+        map the forward will use; the rows of the heads it serves are not
+        copied, and a forward with another map reads in place.  Up to two
+        prefetches wait at a time; a third drops the oldest.  max_blocks caps the
+        copy's grid (0: every SM), leaving SMs to the work it overlaps."""
+        if self.peer_ptrs is None:
+            raise RuntimeError("prefetch needs the peer shards (peer_ptrs)")
+        dev = self.device
+        tokens = _as_i32(tokens, dev)
+        if n is None:
+            n = tokens.numel() - t0
+        ss = None if seg_start is None else _as_i32(seg_start, dev)
+        key = self._key(tokens, ss, t0, n)
+        if self.world == 1:
+            return
+        if self.push is not None:
+            self.push.prefetch(key, tokens, ss, t0, n)
+            return
+        if key in self._staged:
+            return
+        while len(self._staged) >= 2:
+            self._free.append(self._staged.popitem(last=False)[1])
+        need = max(int(L.load().engram_stage_bytes(C.byref(self.ctable), n)), 16)
+        L.check(min(need, 0), "engram_stage_bytes")
+        slot = next((f for f in self._free if f.buf.numel() >= need), None)
+        if slot is None:
+            if self._free:  # grow the smallest buffer
+                slot = min(self._free, key=lambda f: f.buf.numel())
+                slot.buf = torch.empty(need, dtype=torch.uint8, device=dev)
+            else:
+                slot = _Staged(torch.empty(need, dtype=torch.uint8, device=dev))
+        else:
+            self._free.remove(slot)
+        cur = torch.cuda.current_stream(dev)
+        if stream is None:
+            if self._side is None:
+                self._side = torch.cuda.Stream(dev)
+            stream = self._side
+        stream.wait_stream(cur)
+        if slot.consumed is not None:  # the previous forward over this buffer has read it
+            stream.wait_event(slot.consumed)
+        ov = None
+        if omap is not None and omap.R:
+            ov = L.EngramOverlay(None, omap.R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
+        st = L.load().engram_stage_sharded(C.byref(self.ctable), None if ov is None else C.byref(ov),
+                                           tokens.data_ptr(), L.ptr(ss), t0, n, self.peer_ptrs.data_ptr(), self.world,
+                                           self.rank, slot.buf.data_ptr(), int(max_blocks), stream.cuda_stream)
+        L.check(st, "engram_stage_sharded")
+        slot.omap = None if ov is None else omap.keys.data_ptr()
+        tokens.record_stream(stream)
+        if ss is not None:
+            ss.record_stream(stream)
+        slot.ready = torch.cuda.Event()
+        slot.ready.record(stream)
+        slot.consumed = None
+        slot.keep = (tokens, ss)
+        self._staged[key] = slot
+
     def forward(self, tokens, seg_start, omap: OverlayMap, rows_var, out: torch.Tensor, mode: int,
                 exchange=None, slots_out=None, hit_count=None, t0: int = 0, n: int | None = None):
         """With peer_ptrs: one fused forward reading rows from their owners.
@@ -126,6 +218,37 @@ class ShardedTable:
         stream = L.stream_of(dev)
         if self.peer_ptrs is not None and exchange is None:
             ov = omap.descriptor(rows_var)
+            key = self._key(tokens, ss, t0, n)
+            if self.push is not None and self.push.has(key):
+                b, buf, rix, ready = self.push.take(key)
+                cur = torch.cuda.current_stream(dev)
+                cur.wait_event(ready)
+                desc = L.EngramTable.from_buffer_copy(self.ctable)
+                desc.rows = buf.data_ptr()
+                desc.n_rows = max(1, n * self.n_heads)
+                st = lib.engram_forward_indirect(C.byref(desc), C.byref(ov), tokens.data_ptr(), L.ptr(ss), t0, n,
+                                                 rix.data_ptr(), mode, out.data_ptr(), None, L.ptr(slots_out),
+                                                 L.ptr(hit_count), stream)
+                L.check(st, "engram_forward_indirect")
+                self.push.consumed(b, cur)
+                return out
+            slot = self._staged.pop(key, None) if self._staged else None
+            if slot is not None and slot.omap is not None and (not omap.R or omap.keys.data_ptr() != slot.omap):
+                self._free.append(slot)  # staged without the rows of another overlay's heads: read in place
+                slot = None
+            if slot is not None:
+                cur = torch.cuda.current_stream(dev)
+                cur.wait_event(slot.ready)
+                st = lib.engram_forward_staged(C.byref(self.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(ss), t0,
+                                               n, self.peer_ptrs.data_ptr(), self.world, self.rank,
+                                               slot.buf.data_ptr(), mode, out.data_ptr(), None, L.ptr(slots_out),
+                                               L.ptr(hit_count), stream)
+                L.check(st, "engram_forward_staged")
+                slot.consumed = torch.cuda.Event()
+                slot.consumed.record(cur)
+                slot.keep = None
+                self._free.append(slot)
+                return out
             st = lib.engram_forward_sharded(C.byref(self.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(ss), t0, n,
                                             self.peer_ptrs.data_ptr(), self.world, mode, out.data_ptr(), None,
                                             L.ptr(slots_out), L.ptr(hit_count), stream)
@@ -151,6 +274,144 @@ class ShardedTable:
         L.check(st, "engram_forward_indirect")
         self._keep = (rows_buf, rix, ids)  # alive until the stream has consumed them
         return out
+
+
+class PushStage:
+    """Collective, push-based staging for a row-sharded table in peer memory.
+
+    Each rank's stage holds every row of its next forward, grouped by owner
+    (engram_stage_plan), so each owner writes a requester's rows as one
+    contiguous run of NVLink stores (engram_stage_push) and the forward reads
+    local HBM through a row index (engram_forward_indirect).  Buffers, two sets
+    (batch j uses set j % 2): in symmetric memory the tokens and segment
+    starts [n_tokens_max], the plan [world * (ceil(n_tokens_max / 32) + 1)]
+    and the stage [n_tokens_max * n_heads * row_stride bytes]; locally the row
+    index [n_tokens_max * n_heads].  On the table's side stream, prefetch(j):
+      copy this rank's tokens (and segment starts) into set b; plan the stage;
+      wait until this rank's forward over set b's previous batch is done;
+      barrier (4-byte NCCL all-reduce on a group of its own): every rank's
+        tokens and plan of batch j are in place, every rank's stage b is free,
+        and every owner's copy for batch j-1 has landed (batch j-1 is ready);
+      engram_stage_push: this rank's rows of every rank's batch j go into that
+        rank's stage b.
+    A forward over batch j waits for the next barrier after its push: the one
+    in prefetch(j+1), or one the forward issues itself if prefetch(j+1) has
+    not been called.  No kernel waits on another GPU."""
+
+    def __init__(self, table: "ShardedTable", n_tokens_max: int, group=None, max_blocks: int = 0):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        group = group if group is not None else dist.group.WORLD
+        if dist.get_world_size(group) != table.world or dist.get_rank(group) != table.rank:
+            raise ValueError("the group's ranks must be the table's ranks")
+        self.table = table
+        self.dist = dist
+        dev = table.device
+        lib = L.load()
+        self.n_max = int(n_tokens_max)
+        self.max_blocks = int(max_blocks)
+        stage_bytes = max(self.n_max * table.n_heads * table.stride, 16)
+        plan_words = max(int(lib.engram_stage_plan_words(self.n_max, table.world)), 1)
+        self.tok, self.seg, self.plan, self.stage, self.rix, self._handles, self.ptrs = [], [], [], [], [], [], []
+        for _ in range(2):
+            bufs = (symm.empty(max(self.n_max, 1), dtype=torch.int32, device=dev),
+                    symm.empty(max(self.n_max, 1), dtype=torch.int32, device=dev),
+                    symm.empty(plan_words, dtype=torch.int32, device=dev),
+                    symm.empty(stage_bytes, dtype=torch.uint8, device=dev))
+            hs = [symm.rendezvous(x, group) for x in bufs]
+            for lst, x in zip((self.tok, self.seg, self.plan, self.stage), bufs):
+                lst.append(x)
+            self._handles.append(hs)
+            # per set: token, segment, plan and stage pointers of every rank, valid in this process
+            self.ptrs.append(tuple(torch.tensor(list(h.buffer_ptrs), dtype=torch.int64, device=dev) for h in hs))
+            self.rix.append(torch.empty(max(self.n_max * table.n_heads, 1), dtype=torch.int32, device=dev))
+        # the barrier gets a communicator of its own, so it never queues behind the step's collectives
+        self.group = dist.new_group(ranks=list(range(table.world)))
+        self.side = torch.cuda.Stream(dev)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.j = 0  # batches prefetched so far
+        self.keys = {}  # key -> set index, pushed and not yet read
+        self.ready = [None, None]  # event after the barrier that completed set b's pushes
+        self.done = [None, None]  # event after the forward that read set b
+        self.unbarriered = None  # set whose push no barrier has followed yet
+
+    def _barrier(self) -> None:
+        with torch.cuda.stream(self.side):
+            self.dist.all_reduce(self.flag, group=self.group)
+        if self.unbarriered is not None:
+            ev = torch.cuda.Event()
+            ev.record(self.side)
+            self.ready[self.unbarriered] = ev
+            self.unbarriered = None
+
+    def prefetch(self, key, tokens: torch.Tensor, ss: torch.Tensor | None, t0: int, n: int) -> None:
+        t = self.table
+        if tokens.numel() > self.n_max or t0 + n > self.n_max:
+            raise ValueError(f"{tokens.numel()} tokens (t0 + n = {t0 + n}) exceed n_tokens_max {self.n_max}")
+        b = self.j % 2
+        self.j += 1
+        for k in [k for k, v in self.keys.items() if v == b]:  # a batch pushed two prefetches ago, never read
+            del self.keys[k]
+        lib = L.load()
+        cur = torch.cuda.current_stream(t.device)
+        self.side.wait_stream(cur)
+        with torch.cuda.stream(self.side):
+            self.tok[b][: tokens.numel()].copy_(tokens)
+            if ss is not None:
+                self.seg[b][: ss.numel()].copy_(ss)
+        tokens.record_stream(self.side)
+        if ss is not None:
+            ss.record_stream(self.side)
+        st = lib.engram_stage_plan(C.byref(t.ctable), self.tok[b].data_ptr(),
+                                   None if ss is None else self.seg[b].data_ptr(), t0, n, t.world,
+                                   self.plan[b].data_ptr(), self.rix[b].data_ptr(), self.side.cuda_stream)
+        L.check(st, "engram_stage_plan")
+        if self.done[b] is not None:
+            self.side.wait_event(self.done[b])
+        self._barrier()
+        tp, sp, pp, stp = self.ptrs[b]
+        st = lib.engram_stage_push(C.byref(t.ctable), tp.data_ptr(), None if ss is None else sp.data_ptr(),
+                                   pp.data_ptr(), t0, n, stp.data_ptr(), t.world, t.rank, self.max_blocks,
+                                   self.side.cuda_stream)
+        L.check(st, "engram_stage_push")
+        self.ready[b] = None
+        self.unbarriered = b
+        self.keys[key] = b
+
+    def has(self, key) -> bool:
+        return key in self.keys
+
+    def take(self, key):
+        """(set index, this rank's stage, its row index, the event after which
+        every owner's rows are in the stage)."""
+        b = self.keys.pop(key)
+        if self.ready[b] is None:  # no prefetch has followed this batch's push: close it now
+            self._barrier()
+        return b, self.stage[b], self.rix[b], self.ready[b]
+
+    def consumed(self, b: int, stream: torch.cuda.Stream) -> None:
+        """The forward reading set b is queued on `stream`: the next push into b waits for it."""
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.done[b] = ev
+
+    def join(self, stream: torch.cuda.Stream) -> None:
+        """`stream` waits for the staging in flight, the barrier that completes it included."""
+        if self.unbarriered is not None:
+            self._barrier()
+        stream.wait_stream(self.side)
+
+
+class _Staged:
+    """A prefetch buffer: rows of other ranks for one forward call."""
+    __slots__ = ("buf", "ready", "consumed", "keep", "omap")
+
+    def __init__(self, buf: torch.Tensor):
+        self.buf = buf
+        self.omap = None  # keys pointer of the overlay map whose heads were not copied
+        self.ready = None  # event: the copy has landed
+        self.consumed = None  # event: the forward that read it is done
+        self.keep = None  # inputs of the copy, alive until the forward is issued
 
 
 def nccl_exchange(group=None):

@@ -204,6 +204,61 @@ ENGRAM_API int engram_forward_sharded(const engram_table* t, const engram_overla
                                       int64_t* hit_count, void* stream);
 
 /*
+ * The sharded forward in two launches that can run apart: the rows of other
+ * ranks are copied ahead into this GPU's memory (the table shards never
+ * change, so the copy for the next batch can overlap the current step on a
+ * side stream), then the forward reads every row locally.
+ *
+ * engram_stage_bytes: bytes of `stage` for n output rows (n * n_heads *
+ * row_stride).
+ * engram_stage_sharded: for output rows [0, n) of positions t0.., head h of
+ * row i with owner g % world != rank is copied to stage + (i * n_heads + h) *
+ * row_stride (16-byte aligned); this rank's rows are not copied, nor are the
+ * heads the overlay ov serves (nullable; only its map is read, and it must be
+ * the map the forward uses).  max_blocks caps the grid (0: the whole GPU).
+ * world == 1 copies nothing.
+ * engram_forward_staged: engram_forward_sharded reading rank's own rows in
+ * place and every other row from `stage`, which must hold the copy made for
+ * the same tokens, seg_start, t0 and n (ordered before this call).  Outputs
+ * are bit-identical to engram_forward_sharded.  No reference counterpart.
+ */
+ENGRAM_API int64_t engram_stage_bytes(const engram_table* t, int64_t n);
+ENGRAM_API int engram_stage_sharded(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                    const int32_t* seg_start, int64_t t0, int64_t n, const void* shard_rows,
+                                    int32_t world, int32_t rank, void* stage, int32_t max_blocks, void* stream);
+/*
+ * Push staging, the collective form of the staged sharded read (world <= 16).
+ * Each rank's stage holds every row its forward reads, grouped by owner
+ * (block o = the rows rank o owns, in output-row-then-head order), so every
+ * owner writes each requester's block as contiguous NVLink stores; the forward
+ * is engram_forward_indirect with rows = the stage and row_index below.
+ *
+ * engram_stage_plan_words: int32 entries of a plan, world * (ceil(n/32) + 1).
+ * engram_stage_plan (requester, local): plan[o * (tiles + 1) + k] = stage row
+ *   of the first row of 32-row tile k served by owner o (entry `tiles` = end
+ *   of block o); row_index[i * n_heads + h] (n * n_heads int32) = stage row of
+ *   head h of output row i.  Every rank's stage then holds n * n_heads rows.
+ * engram_stage_push (owner, t->rows = its shard): for every rank r (itself
+ *   included) and every tile of r's batch (token_ptrs[r], seg_ptrs[r] or
+ *   none, plan_ptrs[r]: device arrays [world] of pointers valid here, e.g.
+ *   symmetric memory), the rows this rank owns go to stage_ptrs[r] from row
+ *   plan_r[rank][k] on.  The caller orders the ranks around it: every rank's
+ *   tokens and plan written and its previous forward over the stage done
+ *   before it, a barrier after it before any forward reads its stage.
+ * n * n_heads < 2^31.  No reference counterpart.
+ */
+ENGRAM_API int64_t engram_stage_plan_words(int64_t n, int32_t world);
+ENGRAM_API int engram_stage_plan(const engram_table* t, const int32_t* tokens, const int32_t* seg_start, int64_t t0,
+                                 int64_t n, int32_t world, int32_t* plan, int32_t* row_index, void* stream);
+ENGRAM_API int engram_stage_push(const engram_table* t, const void* token_ptrs, const void* seg_ptrs,
+                                 const void* plan_ptrs, int64_t t0, int64_t n, const void* stage_ptrs, int32_t world,
+                                 int32_t rank, int32_t max_blocks, void* stream);
+ENGRAM_API int engram_forward_staged(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                     const int32_t* seg_start, int64_t t0, int64_t n, const void* shard_rows,
+                                     int32_t world, int32_t rank, const void* stage, int32_t mode, void* out,
+                                     int32_t* ids_out, int32_t* slots_out, int64_t* hit_count, void* stream);
+
+/*
  * Row-sharded table (owner(g) = g mod world, local index g / world), step 1 of
  * the exchange: from the global ids [n] (n = positions * heads) and the overlay
  * slots (nullable; entries with slot >= 0 need no table row), builds

@@ -380,10 +380,14 @@ def test_row_sharded_table_matches_resident_table(eb, world, fmt, dim, mode):
 @pytest.mark.parametrize("fmt,dim", [(O.FMT_IQ4_XS, 256), (O.FMT_IQ4_NL, 160), (O.FMT_F32, 128),
                                      (O.FMT_IQ4_XS, 512), (O.FMT_IQ4_NL, 96)])
 @pytest.mark.parametrize("mode", [O.MODE_CONCAT_F32, O.MODE_PAIRSUM_ADD_BF16])
-def test_sharded_table_read_in_place_matches_resident_table(eb, world, fmt, dim, mode):
+@pytest.mark.parametrize("staged", [False, True])
+def test_sharded_table_read_in_place_matches_resident_table(eb, world, fmt, dim, mode, staged):
     """engram_forward_sharded with W ranks' shards emulated as separate buffers
     on one GPU (row g at row g / W of shard g % W): outputs, slots and the hit
-    count equal the forward over the whole resident table."""
+    count equal the forward over the whole resident table.  staged: the rows
+    of other ranks are first copied by ShardedTable.prefetch on its side
+    stream (engram_stage_sharded) and the forward reads them from there
+    (engram_forward_staged)."""
     from engraft_ngram_b200.shard import ShardedTable
     rng = np.random.default_rng(31 * world + dim + mode)
     n_rows = 20_003
@@ -416,11 +420,131 @@ def test_sharded_table_read_in_place_matches_resident_table(eb, world, fmt, dim,
         else:
             sh = ShardedTable(shards[r], fmt, dim, full.head_vocab_sizes, full.head_offsets, full.layer_multipliers,
                               full.eos_token_id, world, r, full.n_rows, peer_ptrs=ptrs)
-            sh.forward(toks, ss, omap, rows_var, out, mode, slots_out=slots, hit_count=hits)
+            if staged:
+                toks_d, ss_d = torch.from_numpy(toks).to(DEV), ss.to(DEV)
+                sh.prefetch(toks_d, ss_d, omap=omap)
+                assert len(sh._staged) == 1
+                sh.forward(toks_d, ss_d, omap, rows_var, out, mode, slots_out=slots, hit_count=hits)
+                assert not sh._staged and len(sh._free) == 1
+            else:
+                sh.forward(toks, ss, omap, rows_var, out, mode, slots_out=slots, hit_count=hits)
         torch.cuda.synchronize()
         outs.append((out.view(torch.int16).cpu().numpy(), slots.cpu().numpy(), int(hits.item())))
     assert np.array_equal(outs[0][0], outs[1][0])
     assert np.array_equal(outs[0][1], outs[1][1]) and outs[0][2] == outs[1][2]
+
+
+@pytest.mark.parametrize("world,rank", [(2, 1), (3, 0), (8, 5)])
+def test_stage_copies_exactly_the_rows_of_other_ranks(eb, world, rank):
+    """engram_stage_sharded over t0 > 0: head h of output row i holds the
+    resident bytes of its global row when another rank owns it and the overlay
+    does not serve it; the bytes of every other head are left as they were."""
+    rng = np.random.default_rng(5 * world + rank)
+    spec = random_spec(O.FMT_IQ4_XS, 256, 12_007, 40 + world)
+    full = device_table(eb, spec)
+    shards = [full.rows.view(full.n_rows, full.row_stride)[r::world].contiguous().reshape(-1) for r in range(world)]
+    ptrs = torch.tensor([sh.data_ptr() for sh in shards], dtype=torch.int64, device=DEV)
+    T, t0 = 700, 37
+    toks = zipf_tokens(rng, T)
+    ss_np = FX.seg_starts(np.sort(rng.integers(0, 3, size=T)))
+    toks_d, ss_d = torch.from_numpy(toks).to(DEV), torch.from_numpy(ss_np).to(DEV)
+    n = T - t0
+    lib = eb._lib.load()
+    nbytes = int(lib.engram_stage_bytes(C.byref(full.ctable), n))
+    assert nbytes == n * 16 * full.row_stride
+    stage = torch.full((nbytes,), 0xAB, dtype=torch.uint8, device=DEV)
+    ids = spec.ids(toks, ss_np)[t0:]
+    ov_ids = np.unique(ids.reshape(-1))[::5].astype(np.int32)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    ov = omap.descriptor(torch.zeros(len(ov_ids), 256, device=DEV))
+    st = lib.engram_stage_sharded(C.byref(full.ctable), C.byref(ov), toks_d.data_ptr(), ss_d.data_ptr(), t0, n,
+                                  ptrs.data_ptr(), world, rank, stage.data_ptr(), 7, eb._lib.stream_of(DEV))
+    eb._lib.check(st, "engram_stage_sharded")
+    torch.cuda.synchronize()
+    got = stage.cpu().numpy().reshape(n, 16, full.row_stride)
+    rows = full.rows.cpu().numpy().reshape(full.n_rows, full.row_stride)
+    remote = (ids % world != rank) & ~np.isin(ids, ov_ids)
+    assert remote.any() and (~remote).any() and np.isin(ids, ov_ids).any()
+    assert np.array_equal(got[remote], rows[ids[remote]])
+    assert (got[~remote] == 0xAB).all()
+
+
+@pytest.mark.parametrize("world", [2, 3, 8, 16])
+@pytest.mark.parametrize("fmt,dim", [(O.FMT_IQ4_XS, 256), (O.FMT_IQ4_NL, 96)])
+def test_push_stage_plan_and_copy(eb, world, fmt, dim):
+    """W emulated ranks on one GPU, each with its own batch: engram_stage_plan
+    lays out each requester's stage by owner (block o = rank o's rows in
+    output-row-then-head order), every owner's engram_stage_push fills its
+    block of every stage, and the forward over the stage through the row index
+    (engram_forward_indirect) equals the resident-table forward."""
+    from engraft_ngram_b200.shard import ShardedTable
+    rng = np.random.default_rng(17 * world + dim)
+    n_rows = 24_001
+    spec = random_spec(fmt, dim, n_rows, 70 + world)
+    full = device_table(eb, spec)
+    stride = full.row_stride
+    shards = [full.rows.view(n_rows, stride)[r::world].contiguous().reshape(-1) for r in range(world)]
+    sptrs = torch.tensor([sh.data_ptr() for sh in shards], dtype=torch.int64, device=DEV)
+    T, t0 = 900, 5
+    n = T - t0
+    toks = [zipf_tokens(rng, T) for _ in range(world)]
+    seg = [FX.seg_starts(np.sort(rng.integers(0, 3, size=T))) for _ in range(world)]
+    tok_d = [torch.from_numpy(x).to(DEV) for x in toks]
+    seg_d = [torch.from_numpy(x).to(DEV) for x in seg]
+    lib = eb._lib.load()
+    words = int(lib.engram_stage_plan_words(n, world))
+    assert words == world * ((n + 31) // 32 + 1)
+    plans = [torch.full((words,), -7, dtype=torch.int32, device=DEV) for _ in range(world)]
+    rix = [torch.full((n * 16,), -7, dtype=torch.int32, device=DEV) for _ in range(world)]
+    stages = [torch.full((n * 16 * stride,), 0xCD, dtype=torch.uint8, device=DEV) for _ in range(world)]
+    ptr = lambda xs: torch.tensor([x.data_ptr() for x in xs], dtype=torch.int64, device=DEV)
+    tp, gp, pp, stp = ptr(tok_d), ptr(seg_d), ptr(plans), ptr(stages)
+    tables = [ShardedTable(shards[r], fmt, dim, full.head_vocab_sizes, full.head_offsets, full.layer_multipliers,
+                           full.eos_token_id, world, r, n_rows, peer_ptrs=sptrs) for r in range(world)]
+    for r in range(world):
+        st = lib.engram_stage_plan(C.byref(tables[r].ctable), tok_d[r].data_ptr(), seg_d[r].data_ptr(), t0, n, world,
+                                   plans[r].data_ptr(), rix[r].data_ptr(), eb._lib.stream_of(DEV))
+        eb._lib.check(st, "engram_stage_plan")
+    for o in range(world):  # every owner pushes its rows into every rank's stage, its own included
+        st = lib.engram_stage_push(C.byref(tables[o].ctable), tp.data_ptr(), gp.data_ptr(), pp.data_ptr(), t0, n,
+                                   stp.data_ptr(), world, o, 3 if o % 2 else 0, eb._lib.stream_of(DEV))
+        eb._lib.check(st, "engram_stage_push")
+    torch.cuda.synchronize()
+    rows = full.rows.cpu().numpy().reshape(n_rows, stride)
+    ov_ids = np.unique(rng.integers(0, n_rows, size=400)).astype(np.int32)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    rows_var = torch.from_numpy((rng.standard_normal((len(ov_ids), dim)) * 0.01).astype(np.float32)).to(DEV)
+    tiles = (n + 31) // 32
+    for r in range(world):
+        ids = spec.ids(toks[r], seg_start=seg[r])[t0:].astype(np.int64)
+        owner = ids % world
+        # the plan: blocks by owner, each in (output row, head) order
+        order = np.lexsort((np.arange(n * 16), owner.reshape(-1)))
+        want_rix = np.empty(n * 16, dtype=np.int64)
+        want_rix[order] = np.arange(n * 16)
+        got_rix = rix[r].cpu().numpy()
+        assert np.array_equal(got_rix, want_rix)
+        plan = plans[r].cpu().numpy().reshape(world, tiles + 1)
+        counts = np.bincount(owner.reshape(-1), minlength=world)
+        assert np.array_equal(plan[:, tiles], np.cumsum(counts))
+        assert np.array_equal(plan[:, 0], np.cumsum(counts) - counts)
+        stage = stages[r].cpu().numpy().reshape(n * 16, stride)
+        assert np.array_equal(stage[got_rix], rows[ids.reshape(-1)])
+        want = torch.empty(n, 16, dim, device=DEV)
+        ov = omap.descriptor(rows_var)
+        st = lib.engram_forward(C.byref(full.ctable), C.byref(ov), tok_d[r].data_ptr(), seg_d[r].data_ptr(), t0, n,
+                                O.MODE_CONCAT_F32, want.data_ptr(), None, None, None, eb._lib.stream_of(DEV))
+        eb._lib.check(st, "engram_forward")
+        desc = eb._lib.EngramTable.from_buffer_copy(tables[r].ctable)
+        desc.rows = stages[r].data_ptr()
+        desc.n_rows = n * 16
+        out = torch.empty(n, 16, dim, device=DEV)
+        st = lib.engram_forward_indirect(C.byref(desc), C.byref(ov), tok_d[r].data_ptr(), seg_d[r].data_ptr(), t0, n,
+                                         rix[r].data_ptr(), O.MODE_CONCAT_F32, out.data_ptr(), None, None, None,
+                                         eb._lib.stream_of(DEV))
+        eb._lib.check(st, "engram_forward_indirect")
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int32), want.view(torch.int32)), r
 
 
 def test_sharded_table_through_the_public_autograd_api(eb):

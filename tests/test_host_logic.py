@@ -2,6 +2,7 @@
 validation, .pleo files, the install seam."""
 from __future__ import annotations
 
+import sys
 import types
 
 import numpy as np
@@ -107,3 +108,19 @@ def test_overlay_emb_refuses_cpu_tensors():
     ov = eb.OverlayEmb(object(), [1, 2, 3], torch.zeros(0, 160), {})
     with pytest.raises(RuntimeError):
         ov.build(3)
+
+
+def test_bench_command_line_and_config_text(monkeypatch):
+    """bench.py parses its flags and names the multi-GPU layout it ran
+    (replicated, staged row-sharded, in-place row-sharded, NCCL row-sharded)."""
+    import bench
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--gpus", "2", "--shard", "--stage-blocks", "32"])
+    args = bench.parse()
+    assert args.shard and args.stage == "pull" and args.stage_blocks == 32 and args.shard_exchange == "peer"
+    cfg = dict(bench.CONFIGS["cfg5"], shard=True, shard_exchange="peer", stage="push", exchange="peer")
+    text = bench.config_json(cfg, args)["parallelism"]
+    assert text.startswith("dp2+row-sharded") and "stores the rows" in text
+    assert "loaded from their owners" in bench.shard_text(dict(cfg, stage="pull"))
+    assert "inside the forward" in bench.shard_text(dict(cfg, stage="off"))
+    assert "NCCL all-to-all" in bench.shard_text(dict(cfg, shard_exchange="nccl"))
+    assert bench.shard_text(dict(cfg, shard=False)) == ""

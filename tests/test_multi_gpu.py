@@ -85,3 +85,101 @@ def test_peer_exchange_matches_nccl_collectives_on_two_ranks():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(out) == {0: True, 1: True}
+
+
+def _sharded_staging(rank: int, world: int, port: int, out) -> None:
+    """Each rank: its shard in symmetric memory; three batches run through the
+    prefetch-then-forward pipeline with push staging and with pull staging, and
+    once read in place; every output equals the forward over the whole
+    resident table."""
+    import ctypes as C
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        import engraft_ngram_b200 as eb
+        from engraft_ngram_b200 import _lib as L
+        from engraft_ngram_b200.shard import ShardedTable, peer_shard_buffer
+        from engraft_ngram_b200.table import synthetic_head_sizes, synthetic_multipliers, synthetic_resident
+        n_rows, fmt, dim, T, eos = 60_013, L.FMT_NAMES["iq4_xs"], 256, 1500, 151_935
+        mode = L.MODE_PAIRSUM_ADD_BF16
+        sizes = synthetic_head_sizes(n_rows)
+        offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
+        mult = synthetic_multipliers(4)
+        full = eb.DeviceTable(synthetic_resident(n_rows, fmt, dim, 11, dev), fmt, dim, sizes, offs, mult, eos,
+                              n_rows=n_rows)
+        stride = full.row_stride
+        buf, ptrs, _h = peer_shard_buffer(n_rows, fmt, dim, dev)
+        mine = full.rows.view(n_rows, stride)[rank::world].reshape(-1)
+        buf[: mine.numel()].copy_(mine)
+        torch.cuda.synchronize()
+        dist.barrier()
+        push = ShardedTable(buf, fmt, dim, sizes, offs, mult, eos, world, rank, n_rows, peer_ptrs=ptrs)
+        push.enable_push_staging(T)
+        pull = ShardedTable(buf, fmt, dim, sizes, offs, mult, eos, world, rank, n_rows, peer_ptrs=ptrs)
+        rng = np.random.default_rng(9)  # the overlay is the same on every rank
+        ov_ids = np.unique(rng.integers(0, n_rows, size=3000)).astype(np.int32)
+        omap = eb.OverlayMap(torch.from_numpy(ov_ids), dev)
+        rows_var = torch.from_numpy((rng.standard_normal((len(ov_ids), dim)) * 0.01).astype(np.float32)).to(dev)
+        ranks = np.arange(1, 151_937, dtype=np.float64)
+        cdf = np.cumsum(ranks ** -1.1)
+        cdf /= cdf[-1]
+        rr = np.random.default_rng(200 + rank)  # each rank its own batches
+        batches = []
+        for _ in range(3):
+            toks = np.searchsorted(cdf, rr.random(T)).astype(np.int32)
+            seg = np.sort(rr.integers(0, 3, size=T))
+            ss = np.concatenate([[0], np.flatnonzero(np.diff(seg)) + 1])
+            starts = np.repeat(ss, np.diff(np.concatenate([ss, [T]]))).astype(np.int32)
+            batches.append((torch.from_numpy(toks).to(dev), torch.from_numpy(starts).to(dev)))
+        res0 = (torch.from_numpy(rr.standard_normal((T, 8 * dim)).astype(np.float32)) * 0.5).to(dev).to(torch.bfloat16)
+
+        def resident(tok, ss):
+            out = res0.clone()
+            ov = omap.descriptor(rows_var)
+            st = L.load().engram_forward(C.byref(full.ctable), C.byref(ov), tok.data_ptr(), ss.data_ptr(), 0, T, mode,
+                                         out.data_ptr(), None, None, None, L.stream_of(dev))
+            L.check(st, "engram_forward")
+            return out
+
+        ok = True
+        for table in (push, pull):
+            table.prefetch(*batches[0], omap=omap)
+            for k in range(3):
+                if k + 1 < 3:
+                    table.prefetch(*batches[k + 1], omap=omap)
+                got = res0.clone()
+                table.forward(batches[k][0], batches[k][1], omap, rows_var, got, mode)
+                ok &= torch.equal(got.view(torch.int16), resident(*batches[k]).view(torch.int16))
+        got = res0.clone()
+        pull.forward(batches[1][0], batches[1][1], omap, rows_var, got, mode)  # not prefetched: read in place
+        ok &= torch.equal(got.view(torch.int16), resident(*batches[1]).view(torch.int16))
+        torch.cuda.synchronize()
+        dist.barrier()
+        out[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_row_sharded_staging_matches_resident_table_on_two_ranks():
+    """Two ranks, table row-sharded in symmetric memory: push-staged,
+    pull-staged and in-place sharded forwards equal the resident-table forward
+    bit for bit, over three pipelined batches."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_staging, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(out) == {0: True, 1: True}

@@ -764,14 +764,20 @@ def time_steps(wl, K, warmup, ddist):
 
 def run_e2e(wl, args, device, ddist, world):
     """Same step through the public Python API with host inputs: tokens and
-    segment starts copied from pinned host memory each step, the hit count read
-    back to the host each step."""
+    segment starts copied from pinned host memory each step, the hit count
+    copied back to pinned host memory each step.  The host reads a step's hit
+    count while the next step runs (it waits on the step's event one step
+    later, as a training loop that logs the previous step does), so the host's
+    launch work overlaps the GPU's; the last count is read after the timed
+    loop's final synchronize."""
     import torch
     eb = wl.eb
     K = max(1, min(args.steps, 200))
     tok_h = wl.tokens.cpu().pin_memory()
     ss_h = wl.seg_start.cpu().pin_memory()
-    hit_h = torch.zeros(1, dtype=torch.int64).pin_memory()
+    hit_h = [torch.zeros(1, dtype=torch.int64).pin_memory() for _ in range(2)]
+    done = [None, None]
+    counter = [0]
     rows_var = wl.p0.clone().requires_grad_(True)
     opt = eb.OverlayAdam([rows_var], lr=wl.lr, reg_ref=wl.p0, reg_mu=wl.mu)
     hits = torch.zeros(1, dtype=torch.int64, device=device)
@@ -800,9 +806,16 @@ def run_e2e(wl, args, device, ddist, world):
             if ddist is not None:
                 ddist.all_reduce(rows_var.grad)
             opt.step()
-        hit_h.copy_(hits, non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()
-        return int(hit_h.item())
+        b = counter[0] % 2
+        counter[0] += 1
+        hit_h[b].copy_(hits, non_blocking=True)
+        done[b] = torch.cuda.Event()
+        done[b].record(torch.cuda.current_stream(device))
+        prev = done[b ^ 1]
+        if prev is None:
+            return None
+        prev.synchronize()  # the previous step's result, read while this step runs
+        return int(hit_h[b ^ 1].item())
 
     for _ in range(3):
         one()
@@ -817,6 +830,9 @@ def run_e2e(wl, args, device, ddist, world):
         wl.join_stage()
     e1.record()
     torch.cuda.synchronize()
+    last = int(hit_h[(counter[0] - 1) % 2].item())
+    if last <= 0 and wl.R:
+        raise RuntimeError("e2e: the last step reported no overlay hits")
     ms = e0.elapsed_time(e1) / K
     t = torch.tensor([ms], device=device, dtype=torch.float64)
     if ddist is not None:

@@ -57,7 +57,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=DEFAULT_STEPS)
     ap.add_argument("--warmup", type=int, default=DEFAULT_WARMUP)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS) + ["scan"])
+    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS) + ["scan", "ple"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -583,6 +583,80 @@ def run_scan(args, device):
     print(json.dumps(line), flush=True)
 
 
+def run_ple(args, device):
+    """The PLE block after the gather (engraft/replica/layers.py:565-626) at the
+    reference's width (hc = 4, n_embd = 2560, 4 conv taps, dilation 3) over
+    2048 positions: the two fp32 projection GEMMs (cuBLAS) and the two block
+    kernels, each timed with CUDA events; positions/s for the whole block."""
+    import types
+    import torch
+    import engraft_ngram_b200 as eb
+    from engraft_ngram_b200 import _lib as L
+    hc, n, K, dil, T = 4, 2560, 4, 3, 2048
+    g = torch.Generator(device=device)
+    g.manual_seed(args.seed)
+    r = lambda *s: torch.randn(*s, generator=g, device=device) * 0.1  # noqa: E731
+    w = types.SimpleNamespace(w_key=r(hc * n, n), w_value=r(n, n), norm_key=1 + r(hc * n), norm_query=1 + r(hc * n),
+                              norm_conv=1 + r(hc * n), conv1d=r(hc * n, K))
+    emb, hidden, hist = r(T, n), r(T, hc, n), r((K - 1) * dil, hc, n)
+    hp = types.SimpleNamespace(hc_mult=hc, n_embd=n, f_norm_rms_eps=1e-6, ple_ngram_size=dil)
+    lib = L.load()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key, value = torch.empty(T, hc * n, device=device), torch.empty(T, n, device=device)
+    gate, normed, out = (torch.empty(T, hc, device=device), torch.empty(T, hc, n, device=device),
+                         torch.empty(T, hc, n, device=device))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    K_steps = max(1, min(args.steps, 50))
+    for _ in range(3):
+        eb.ple_forward(emb, hidden, w, hist, hp)
+    torch.cuda.synchronize()
+    t_gemm = t_gate = t_conv = 0.0
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    for _ in range(K_steps):  # the same launches as ple_forward, with events between them
+        ev[0].record()
+        torch.matmul(emb, w.w_key.t(), out=key)
+        torch.matmul(emb, w.w_value.t(), out=value)
+        ev[1].record()
+        L.check(lib.engram_ple_gate(key.data_ptr(), hc * n, value.data_ptr(), n, hidden.data_ptr(),
+                                    w.norm_key.data_ptr(), w.norm_query.data_ptr(), w.norm_conv.data_ptr(), T, hc, n,
+                                    1e-6, gate.data_ptr(), None, normed.data_ptr(), stream), "engram_ple_gate")
+        ev[2].record()
+        L.check(lib.engram_ple_conv(value.data_ptr(), n, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
+                                    hist.data_ptr(), hist.shape[0], w.conv1d.data_ptr(), K, dil, T, hc, n,
+                                    out.data_ptr(), stream), "engram_ple_conv")
+        ev[3].record()
+        torch.cuda.synchronize()
+        t_gemm += ev[0].elapsed_time(ev[1])
+        t_gate += ev[1].elapsed_time(ev[2])
+        t_conv += ev[2].elapsed_time(ev[3])
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    t_gemm, t_gate, t_conv = (x / K_steps for x in (t_gemm, t_gate, t_conv))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K_steps):
+        eb.ple_forward(emb, hidden, w, hist, hp)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K_steps
+    peak, peak_kind = measured_peak_gbs()
+    C = T * hc * n * 4
+    gate_bytes = 2 * C + T * n * 4 + C + 3 * hc * n * 4  # key, hidden, value, normed out, norm weights
+    conv_bytes = C + C + T * n * 4 + C + hc * n * K * 4  # normed, hidden, value, out, conv weights
+    flops = 2.0 * T * n * (hc * n + n)
+    line = {"metric": "PLE block positions/s (layers.ple_forward, hc=4, n_embd=2560, 2048 positions, fp32)",
+            "value": T / (ms * 1e-3), "unit": "positions/s", "ms_per_call": ms,
+            "phase_ms": {"projections_cublas_fp32": t_gemm, "engram_ple_gate": t_gate, "engram_ple_conv": t_conv},
+            "gemm_tflops": flops / (t_gemm * 1e-3) / 1e12,
+            "roofline": {"engram_ple_gate": {"bound": "hbm", "achieved": gate_bytes / (t_gate * 1e-3) / 1e9,
+                                             "peak": peak, "unit": "GB/s", "frac": gate_bytes / (t_gate * 1e-3) / 1e9 / peak},
+                         "engram_ple_conv": {"bound": "hbm", "achieved": conv_bytes / (t_conv * 1e-3) / 1e9,
+                                             "peak": peak, "unit": "GB/s", "frac": conv_bytes / (t_conv * 1e-3) / 1e9 / peak},
+                         "peak_source": peak_kind},
+            "config": {"workload": "ple: 2048 positions, hc=4, n_embd=2560, K=4, dilation 3, history 9 rows"}}
+    print(json.dumps(line), flush=True)
+
+
 def shard_text(cfg):
     if not cfg.get("shard"):
         return ""
@@ -615,9 +689,10 @@ START = time.perf_counter()
 
 def main():
     args = parse()
-    if args.config == "scan":
+    if args.config in ("scan", "ple"):
         import torch
-        run_scan(args, torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
+        run = run_scan if args.config == "scan" else run_ple
+        run(args, torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
         return
     cfg = dict(CONFIGS[args.config])
     if args.table_rows:
@@ -778,8 +853,18 @@ def run_e2e(wl, args, device, ddist, world):
     hit_h = [torch.zeros(1, dtype=torch.int64).pin_memory() for _ in range(2)]
     done = [None, None]
     counter = [0]
-    rows_var = wl.p0.clone().requires_grad_(True)
-    opt = eb.OverlayAdam([rows_var], lr=wl.lr, reg_ref=wl.p0, reg_mu=wl.mu)
+    if wl.peer is not None:  # data-parallel through autograd: row gradients go to their owners (PeerRows.attach)
+        from engraft_ngram_b200.dist import PeerAdam
+        wl.peer.rows_var.copy_(wl.p0)
+        rows_var = wl.peer.rows_var.requires_grad_(True)
+        wl.peer.attach(wl.omap)
+        opt = PeerAdam(wl.peer, lr=wl.lr, reg_ref=wl.p0, reg_mu=wl.mu)
+        api = "engraft_ngram_b200.engram_residual_add + autograd backward into PeerRows + PeerAdam.step"
+    else:
+        rows_var = wl.p0.clone().requires_grad_(True)
+        opt = eb.OverlayAdam([rows_var], lr=wl.lr, reg_ref=wl.p0, reg_mu=wl.mu)
+        api = ("engraft_ngram_b200.engram_residual_add + autograd backward + "
+               + ("NCCL all-reduce of the row gradients + " if ddist is not None else "") + "OverlayAdam.step")
     hits = torch.zeros(1, dtype=torch.int64, device=device)
     pending = []  # staged sharded reads: the next step's inputs, copied and prefetched one step ahead
 
@@ -803,7 +888,7 @@ def run_e2e(wl, args, device, ddist, world):
             out = eb.engram_embed(wl.table, tok, rows_var, wl.omap, ss, 0, wl.T, hits)
         if wl.cfg["bwd"] and wl.R:
             out.backward(wl.dout.reshape(out.shape))
-            if ddist is not None:
+            if ddist is not None and wl.peer is None:
                 ddist.all_reduce(rows_var.grad)
             opt.step()
         b = counter[0] % 2
@@ -839,8 +924,7 @@ def run_e2e(wl, args, device, ddist, world):
         ddist.all_reduce(t, op=ddist.ReduceOp.MAX)
     ms = float(t[0])
     return {"value": 16 * wl.T * world / (ms * 1e-3), "unit": "rows/s", "ms_per_step": ms, "steps": K,
-            "h2d_bytes_per_step": 8 * wl.T, "d2h_bytes_per_step": 8,
-            "api": "engraft_ngram_b200.engram_residual_add + autograd backward + OverlayAdam.step"}
+            "h2d_bytes_per_step": 8 * wl.T, "d2h_bytes_per_step": 8, "api": api}
 
 
 if __name__ == "__main__":

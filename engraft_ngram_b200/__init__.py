@@ -18,7 +18,9 @@ from ._lib import FMT_F32, FMT_IQ4_NL, FMT_IQ4_XS, MODE_CONCAT_F32, MODE_PAIRSUM
 from .optim import OverlayAdam, reg_scale
 from .overlay import (OverlayEmb, OverlayMap, engram_embed, engram_embed_at, engram_residual_add, row_gradients,
                       seg_starts_from_segment_ids)
-from .patch import install, install_rowsets, install_scan, uninstall, uninstall_rowsets, uninstall_scan
+from .patch import (install, install_ple, install_rowsets, install_scan, uninstall, uninstall_ple, uninstall_rowsets,
+                    uninstall_scan)
+from .ple import ple_forward
 from .pleo import read_pleo, read_pleo_device, write_pleo
 from .rowset import DeviceRowSet, build_all_read_row_set, build_rows_var, sum_overlays, write_merged_pleo
 from .scan import scan_hits
@@ -30,7 +32,7 @@ __all__ = [
     "uninstall_scan", "install_rowsets", "uninstall_rowsets", "DeviceRowSet", "build_all_read_row_set",
     "build_rows_var", "sum_overlays", "write_merged_pleo", "read_pleo",
     "write_pleo", "read_pleo_device", "FMT_F32", "FMT_IQ4_NL", "FMT_IQ4_XS", "MODE_CONCAT_F32",
-    "MODE_PAIRSUM_ADD_BF16", "load_library", "scan_hits",
+    "MODE_PAIRSUM_ADD_BF16", "load_library", "scan_hits", "ple_forward", "install_ple", "uninstall_ple",
 ]
 
 

@@ -128,6 +128,12 @@ SIGNATURES = {
     "engram_forward_staged": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
                                         C.c_int64, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                         C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_ple_gate": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                  C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_float, C.c_void_p,
+                                  C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_ple_conv": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                  C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_int32, C.c_int32,
+                                  C.c_void_p, C.c_void_p]),
     "engram_selftest_mod": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),
     "engram_launch_count": (C.c_int64, []),
 }

@@ -126,6 +126,10 @@ class PeerRows:
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
         self.R, self.dim = int(R), int(dim)
+        chk = torch.tensor([self.R, -self.R, self.dim, -self.dim], dtype=torch.int64, device=device)
+        dist.all_reduce(chk, op=dist.ReduceOp.MAX, group=self.group)
+        if int(chk[0]) != -int(chk[1]) or int(chk[2]) != -int(chk[3]):
+            raise ValueError(f"PeerRows: every rank needs the same R and dim (this rank: R={self.R}, dim={self.dim})")
         size_max = -(-self.R // self.world)
         self.recv = symm.empty(max(self.world * size_max, 1), self.dim, dtype=torch.float32, device=device)
         self.rows_var = symm.empty(max(self.R, 1), self.dim, dtype=torch.float32, device=device)
@@ -154,3 +158,43 @@ class PeerRows:
         adam_owner_step(self.recv, self.rows_ptrs, self.world, self.rank, self.R, self.dim, m, v, p0, step, lr,
                         beta1, beta2, eps, reg_scale)
         self.barrier()
+
+    def attach(self, omap) -> None:
+        """Route the autograd backward of engram_embed / engram_residual_add
+        through this exchange: when they are given self.rows_var and `omap`,
+        the row gradients go straight into the owners' receive buffers (as
+        backward()) and rows_var.grad is left unset; PeerAdam steps the rows."""
+        if omap.R != self.R:
+            raise ValueError(f"overlay map has {omap.R} rows, the exchange {self.R}")
+        omap.peer = self
+
+
+class PeerAdam:
+    """The data-parallel counterpart of OverlayAdam over a PeerRows exchange:
+    same hyper-parameters and regulariser (reg_ref = the starting rows of all
+    R rows, reg_mu), Adam moments kept for this rank's rows only; step() is
+    PeerRows.step (barrier, owner sum + Adam + stores into every rank,
+    barrier), a collective.  The row gradients come from the backward of a
+    forward over peer.rows_var with the map attached (PeerRows.attach)."""
+
+    def __init__(self, peer: PeerRows, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
+                 reg_ref: torch.Tensor | None = None, reg_mu: float = 0.0):
+        from .optim import reg_scale
+        if lr < 0 or eps < 0 or not (0 <= betas[0] < 1 and 0 <= betas[1] < 1):
+            raise ValueError(f"invalid Adam hyper-parameters lr={lr} betas={betas} eps={eps}")
+        self.peer, self.lr, self.betas, self.eps = peer, float(lr), tuple(betas), float(eps)
+        lo, hi = shard_bounds(peer.R, peer.world, peer.rank)
+        dev = peer.rows_var.device
+        self.m = torch.zeros(max(hi - lo, 1), peer.dim, device=dev)
+        self.v = torch.zeros(max(hi - lo, 1), peer.dim, device=dev)
+        self.reg_scale = reg_scale(reg_mu, reg_ref) if reg_ref is not None and reg_mu != 0.0 else 0.0
+        self.p0 = reg_ref[lo:hi].detach().contiguous() if self.reg_scale != 0.0 else None
+        self.t = 0
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        """Nothing to clear: every backward rewrites all of this rank's blocks."""
+
+    def step(self) -> None:
+        self.t += 1
+        self.peer.step(self.m, self.v, self.p0, self.t, self.lr, self.betas[0], self.betas[1], self.eps,
+                       self.reg_scale)

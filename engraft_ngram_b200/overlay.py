@@ -34,6 +34,7 @@ class OverlayMap:
         ids = _as_i32(ids, device).reshape(-1)
         self.R = int(ids.numel())
         self.ids = ids
+        self.peer = None  # a PeerRows exchange the autograd backward hands row gradients to (PeerRows.attach)
         self.capacity = 0 if self.R == 0 else max(2, 1 << int(np.ceil(np.log2(2 * self.R))))
         self.keys = torch.empty(max(self.capacity, 1), dtype=torch.int32, device=device)
         self.slots = torch.empty(max(self.capacity, 1), dtype=torch.int32, device=device)
@@ -121,6 +122,7 @@ class _ConcatFn(torch.autograd.Function):
         slots = torch.empty(n, nh, dtype=torch.int32, device=dev) if need_grad else None
         _emit(dtable, omap, rv, tokens, seg_start, t0, n, L.MODE_CONCAT_F32, out, slots, hit_count)
         ctx.meta = (nh, dtable.heads_per_ngram, dim, omap.R, n)
+        ctx.peer = _peer_of(omap, rows_var)
         ctx.save_for_backward(slots if slots is not None else torch.empty(0, dtype=torch.int32, device=dev))
         return out
 
@@ -131,6 +133,9 @@ class _ConcatFn(torch.autograd.Function):
         if not ctx.needs_input_grad[0] or R == 0 or slots.numel() == 0:
             return (None,) * 8
         grad = grad_out.contiguous().to(torch.float32)
+        if ctx.peer is not None:  # row gradients stored into their owners' receive buffers; no .grad
+            ctx.peer.backward(slots, grad, nh, hpn, L.MODE_CONCAT_F32)
+            return (None,) * 8
         grad_rows = row_gradients(slots, grad, nh, hpn, dim, R, L.MODE_CONCAT_F32)
         return (grad_rows,) + (None,) * 7
 
@@ -152,6 +157,7 @@ class _PairSumAddFn(torch.autograd.Function):
         _emit(dtable, omap, rv, tokens, seg_start, t0, n, L.MODE_PAIRSUM_ADD_BF16, residual, slots, hit_count)
         ctx.mark_dirty(residual)
         ctx.meta = (nh, hpn, dim, omap.R, n)
+        ctx.peer = _peer_of(omap, rows_var)
         ctx.save_for_backward(slots if slots is not None else torch.empty(0, dtype=torch.int32, device=dev))
         return residual
 
@@ -162,8 +168,20 @@ class _PairSumAddFn(torch.autograd.Function):
         grad_rows = None
         if ctx.needs_input_grad[1] and R > 0 and slots.numel():
             g = grad_res.contiguous().to(torch.bfloat16)
-            grad_rows = row_gradients(slots, g, nh, hpn, dim, R, L.MODE_PAIRSUM_ADD_BF16)
+            if ctx.peer is not None:  # row gradients stored into their owners' receive buffers; no .grad
+                ctx.peer.backward(slots, g, nh, hpn, L.MODE_PAIRSUM_ADD_BF16)
+            else:
+                grad_rows = row_gradients(slots, g, nh, hpn, dim, R, L.MODE_PAIRSUM_ADD_BF16)
         return (grad_res, grad_rows) + (None,) * 7
+
+
+def _peer_of(omap: OverlayMap, rows_var: torch.Tensor):
+    """The PeerRows attached to this overlay map (PeerRows.attach) when rows_var
+    is its rows_var: the backward then hands the row gradients to it."""
+    peer = getattr(omap, "peer", None)
+    if peer is None or rows_var.data_ptr() != peer.rows_var.data_ptr():
+        return None
+    return peer
 
 
 def row_gradients(slots: torch.Tensor, grad: torch.Tensor, n_heads: int, hpn: int, dim: int, R: int,

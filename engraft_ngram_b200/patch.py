@@ -46,6 +46,39 @@ def uninstall_scan(damage_module=None):
     return dmg
 
 
+_PLE_TARGETS = (("engraft.replica.layers", "ple_forward"), ("engraft.replica.model", "ple_forward"))
+
+
+def install_ple(modules: dict | None = None) -> None:
+    """Routes the reference's ple_forward (engraft/replica/layers.py:565-626, and
+    the name engraft.replica.model imported) to engraft_ngram_b200.ple_forward
+    for calls that need no gradient; calls that do (the descent's backward
+    through the block) keep the reference's function.  modules: name -> module
+    overrides, for tests."""
+    from . import ple
+    for mod_name, attr in _PLE_TARGETS:
+        mod = (modules or {}).get(mod_name) or importlib.import_module(mod_name)
+        saved = _saved.setdefault(id(mod), {})
+        if attr not in saved:
+            saved[attr] = getattr(mod, attr)
+        original = saved[attr]
+
+        def routed(emb, hidden, w, hist, hparams, *args, _orig=original, **kw):
+            if ple.needs_grad(emb, hidden, w, hist) or not emb.is_cuda:
+                return _orig(emb, hidden, w, hist, hparams, *args, **kw)
+            return ple.ple_forward(emb, hidden, w, hist, hparams, *args, **kw)
+
+        setattr(mod, attr, routed)
+
+
+def uninstall_ple(modules: dict | None = None) -> None:
+    for mod_name, attr in _PLE_TARGETS:
+        mod = (modules or {}).get(mod_name) or importlib.import_module(mod_name)
+        orig = _saved.get(id(mod), {}).pop(attr, None)
+        if orig is not None:
+            setattr(mod, attr, orig)
+
+
 _ROWSET_TARGETS = (
     ("engraft.replica.distill", "build_rows_var"),
     ("engraft.descend_corpus", "build_all_read_row_set"),

@@ -1,0 +1,104 @@
+"""The PLE block that consumes the gathered rows, on the GPU: the drop-in for
+`engraft.replica.layers.ple_forward` (engraft/replica/layers.py:565-626), same
+arguments and results.
+
+The key and value projections are two fp32 GEMMs (cuBLAS through torch.matmul,
+TF32 off, as the reference computes them in fp32); everything after them is two
+kernels of this library: engram_ple_gate (grouped RMS norms, the sign-sqrt
+sigmoid gate and the norm of the gated value, one block per position) and
+engram_ple_conv (the causal dilated depthwise conv over [history; positions],
+silu and the block's residual sum).  Results agree with the reference to fp32
+rounding (different reduction orders).
+
+Forward only: the block's backward is not built here, so a call that needs a
+gradient raises; `install_ple` routes those calls to the reference's own
+function and the rest here.
+"""
+from __future__ import annotations
+
+import contextlib
+
+import torch
+
+from . import _lib as L
+
+_GRAD_FIELDS = ("w_key", "w_value", "norm_key", "norm_query", "norm_conv", "conv1d")
+
+
+@contextlib.contextmanager
+def _fp32_matmul():
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        yield
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def needs_grad(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor) -> bool:
+    if not torch.is_grad_enabled():
+        return False
+    ts = [emb, hidden, hist] + [getattr(w, f) for f in _GRAD_FIELDS]
+    return any(isinstance(t, torch.Tensor) and t.requires_grad for t in ts)
+
+
+def _f32(x: torch.Tensor, name: str, shape) -> torch.Tensor:
+    if not x.is_cuda or x.dtype != torch.float32:
+        raise ValueError(f"{name}: needs a float32 CUDA tensor (got {x.dtype} on {x.device})")
+    if tuple(x.shape) != tuple(shape):
+        raise ValueError(f"{name}: shape {tuple(x.shape)}, expected {tuple(shape)}")
+    return x.contiguous()
+
+
+def ple_forward(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor, hparams,
+                diag: dict | None = None, detach_value: bool = False, detach_gate: bool = False):
+    """(hidden + gated + silu(conv), new history tail): see the reference's
+    docstring.  detach_value / detach_gate change only gradients, which this
+    forward-only block does not produce; diag receives the same five tensors."""
+    if needs_grad(emb, hidden, w, hist):
+        raise NotImplementedError("engraft_ngram_b200.ple_forward is forward-only; run the block's backward "
+                                  "with the reference's ple_forward (install_ple routes such calls there)")
+    hc, n = int(hparams.hc_mult), int(hparams.n_embd)
+    eps, dil = float(hparams.f_norm_rms_eps), int(hparams.ple_ngram_size)
+    T = emb.shape[0]
+    K = int(w.conv1d.shape[1])
+    emb = _f32(emb, "emb", (T, n))
+    hidden = _f32(hidden, "hidden", (T, hc, n))
+    w_key = _f32(w.w_key, "w_key", (hc * n, n))
+    w_value = _f32(w.w_value, "w_value", (n, n))
+    nk = _f32(w.norm_key.reshape(-1), "norm_key", (hc * n,))
+    nq = _f32(w.norm_query.reshape(-1), "norm_query", (hc * n,))
+    nc = _f32(w.norm_conv.reshape(-1), "norm_conv", (hc * n,))
+    cw = _f32(w.conv1d, "conv1d", (hc * n, K))
+    H = hist.shape[0]
+    hist = _f32(hist, "hist", (H, hc, n)) if H else hist
+    dev = emb.device
+    lib = L.load()
+    stream = L.stream_of(dev)
+    key = torch.empty(T, hc * n, device=dev)
+    value = torch.empty(T, n, device=dev)
+    with _fp32_matmul():
+        torch.matmul(emb, w_key.t(), out=key)
+        torch.matmul(emb, w_value.t(), out=value)
+    gate = torch.empty(T, hc, device=dev)
+    s = torch.empty(T, hc, device=dev) if diag is not None else None
+    normed = torch.empty(T, hc, n, device=dev)
+    st = lib.engram_ple_gate(key.data_ptr(), hc * n, value.data_ptr(), n, hidden.data_ptr(), nk.data_ptr(),
+                             nq.data_ptr(), nc.data_ptr(), T, hc, n, eps, gate.data_ptr(), L.ptr(s),
+                             normed.data_ptr(), stream)
+    L.check(st, "engram_ple_gate")
+    out = torch.empty(T, hc, n, device=dev)
+    st = lib.engram_ple_conv(value.data_ptr(), n, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
+                             hist.data_ptr() if H else None, H, cw.data_ptr(), K, dil, T, hc, n, out.data_ptr(),
+                             stream)
+    L.check(st, "engram_ple_conv")
+    hist_len = (K - 1) * dil
+    hist_full = torch.cat([hist.to(normed.dtype), normed], dim=0) if H else normed
+    new_hist = hist_full[-hist_len:] if hist_len > 0 else hist_full[:0]
+    if diag is not None:
+        diag["s"] = s
+        diag["gate"] = gate
+        diag["value_norm"] = value.norm(dim=-1)
+        diag["gated_norm"] = (value.unsqueeze(1) * gate.unsqueeze(-1)).norm(dim=-1)
+        diag["hidden_norm"] = hidden.norm(dim=-1)
+    return out, new_hist

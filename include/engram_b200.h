@@ -481,6 +481,31 @@ ENGRAM_API int64_t engram_launch_count(void);
 /* Library version (major*10000 + minor*100 + patch). */
 ENGRAM_API int engram_version(void);
 
+/*
+ * The PLE block that consumes the gathered rows (engraft/replica/layers.py:
+ * 565-626, ple_forward), after its two projections key = emb @ w_key.T
+ * [T, hc*n] and value = emb @ w_value.T [T, n] (plain GEMMs, run by the
+ * caller).  fp32 throughout; hc <= 8, n % 4 == 0; row strides in floats,
+ * multiples of 4; arrays 16-byte aligned.
+ * engram_ple_gate: per position t and stream j,
+ *   s = <rmsnorm(key_j) * norm_key_j, rmsnorm(hidden_j) * norm_query_j> / sqrt(n),
+ *   gate[t, j] = sigmoid(sign(s) * sqrt(max(|s|, 1e-6))), s_out (nullable) = s,
+ *   normed[t, j, :] = rmsnorm(value * gate) * norm_conv_j,
+ *   with rmsnorm(x) = x * rsqrt(mean(x^2) + eps) (layers.py:23-42).
+ * engram_ple_conv: out[t, j, c] = hidden + value[t, c] * gate[t, j] +
+ *   silu(sum_k conv_w[j*n + c, k] * x[t - (K-1-k)*dilation]), x = normed rows,
+ *   or hist rows [hist_len, hc, n] before position 0, or 0 before the history
+ *   (causal_depthwise_conv, layers.py:257-293).
+ */
+ENGRAM_API int engram_ple_gate(const float* key, int64_t key_stride, const float* value, int64_t value_stride,
+                               const float* hidden, const float* norm_key, const float* norm_query,
+                               const float* norm_conv, int64_t T, int32_t hc, int32_t n_embd, float eps,
+                               float* gate, float* s_out, float* normed, void* stream);
+ENGRAM_API int engram_ple_conv(const float* value, int64_t value_stride, const float* hidden, const float* gate,
+                               const float* normed, const float* hist, int64_t hist_len, const float* conv_w,
+                               int32_t K, int32_t dilation, int64_t T, int32_t hc, int32_t n_embd, float* out,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

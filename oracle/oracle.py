@@ -279,3 +279,41 @@ def sum_overlays(files, true_rows_of):
     for c in moved[moved >= 1].tolist():
         hist[str(c)] = hist.get(str(c), 0) + 1
     return union, merged, (int((moved >= 1).sum()), int((moved >= 2).sum()), hist)
+
+
+def ple_forward(emb, hidden, w_key, w_value, norm_key, norm_query, norm_conv, conv1d, hist, hc, n_embd, eps,
+                dilation):
+    """The PLE block restated in float32 numpy (engraft/replica/layers.py:565-626,
+    with rmsnorm layers.py:23-42 and causal_depthwise_conv layers.py:257-293):
+    key/value projections, grouped RMS norms, the sign-sqrt sigmoid gate, the
+    gated value's norm, the causal dilated depthwise conv over [history; T] and
+    silu; returns (hidden + gated + conv, the last (K-1)*dilation rows of
+    [history; normed])."""
+    T = emb.shape[0]
+
+    def rms(x, w):
+        ms = (x * x).mean(axis=-1, keepdims=True, dtype=np.float32)
+        return (x * (1.0 / np.sqrt(ms + np.float32(eps)))) * w.reshape(hc, n_embd)
+
+    key = (emb @ w_key.T).reshape(T, hc, n_embd)
+    s = (rms(key, norm_key) * rms(hidden, norm_query)).sum(axis=-1, dtype=np.float32) / np.float32(np.sqrt(n_embd))
+    mag = np.sqrt(np.maximum(np.abs(s), np.float32(1e-6)))
+    gate = (1.0 / (1.0 + np.exp(-(np.sign(s) * mag)))).astype(np.float32)
+    value = emb @ w_value.T
+    gated = value[:, None, :] * gate[:, :, None]
+    normed = rms(gated, norm_conv)
+    C = hc * n_embd
+    full = np.concatenate([hist.reshape(-1, C), normed.reshape(T, C)]).astype(np.float32)
+    H = hist.shape[0]
+    K = conv1d.shape[1]
+    acc = np.zeros((T, C), dtype=np.float32)
+    for k in range(K):
+        back = (K - 1 - k) * dilation
+        for t in range(T):
+            if H + t - back >= 0:
+                acc[t] += full[H + t - back] * conv1d[:, k]
+    conv = (acc / (1.0 + np.exp(-acc))).astype(np.float32).reshape(T, hc, n_embd)
+    out = (hidden + gated + conv).astype(np.float32)
+    hist_len = (K - 1) * dilation
+    new_hist = np.concatenate([hist, normed])[-hist_len:] if hist_len > 0 else normed[:0]
+    return out, new_hist.astype(np.float32)

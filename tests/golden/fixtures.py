@@ -177,3 +177,25 @@ def rowset_case_sets(all_read: np.ndarray) -> dict:
 
 
 ROWSET_EXCLUDE = {0: [1, 2], 3: [0], 5: [4, 5, 6]}
+
+
+# The PLE block (engraft/replica/layers.py:565-626) at reduced width: hc streams
+# of n_embd channels, conv of K taps with dilation 3 (the n-gram size).
+PLE_CASES = [  # (seed, T, history rows)
+    (1, 11, 0),   # start of a sequence: empty history
+    (2, 5, 9),    # a full history of (K-1)*dilation rows
+    (3, 1, 9),    # one decode step
+    (4, 4, 5),    # a history shorter than (K-1)*dilation
+]
+PLE_HC, PLE_N, PLE_K, PLE_DIL, PLE_EPS = 2, 256, 4, 3, 1e-6
+
+
+def ple_case(seed: int, T: int, n_hist: int, hc: int = PLE_HC, n: int = PLE_N, K: int = PLE_K) -> dict:
+    """Seeded inputs of one ple_forward call: emb [T, n], hidden [T, hc, n],
+    hist [n_hist, hc, n], and the block's weights (norm weights near 1, the
+    rest ~N(0, 0.1^2) as the reference's layer tests draw them)."""
+    rng = np.random.default_rng(1000 + seed)
+    f = lambda *s: (rng.standard_normal(s) * 0.1).astype(np.float32)  # noqa: E731
+    return dict(emb=f(T, n), hidden=f(T, hc, n), hist=f(n_hist, hc, n), w_key=f(hc * n, n), w_value=f(n, n),
+                norm_key=(1.0 + f(hc * n)).astype(np.float32), norm_query=(1.0 + f(hc * n)).astype(np.float32),
+                norm_conv=(1.0 + f(hc * n)).astype(np.float32), conv1d=f(hc * n, K))

@@ -293,6 +293,21 @@ def main(ref_root: str) -> None:
         out["merged_bytes_sha"] = np.array(hashlib.sha256(mp.read_bytes()).hexdigest())
         out["merged_n_frozen"] = np.int64(info["n_rows_frozen"])
 
+    # ---- 9. the PLE block that consumes the gathered rows (layers.py:565-626) --------
+    import engraft.replica.layers as RL
+
+    class _PleHP:
+        hc_mult, n_embd, f_norm_rms_eps, ple_ngram_size = FX.PLE_HC, FX.PLE_N, FX.PLE_EPS, FX.PLE_DIL
+
+    for seed, T, n_hist in FX.PLE_CASES:
+        c = FX.ple_case(seed, T, n_hist)
+        w = RL.PleWeights(**{k: torch.from_numpy(c[k]) for k in
+                             ("w_key", "w_value", "norm_key", "norm_query", "norm_conv", "conv1d")})
+        o, h = RL.ple_forward(torch.from_numpy(c["emb"]), torch.from_numpy(c["hidden"]), w,
+                              torch.from_numpy(c["hist"]), _PleHP)
+        out[f"ple{seed}_out"] = o.numpy()
+        out[f"ple{seed}_hist"] = h.numpy()
+
     meta = dict(reference_root=str(ref_root), torch=torch.__version__, numpy=np.__version__,
                 gguf=getattr(gguf, "__version__", "0.19.0"))
     out["meta"] = np.array(repr(meta))

@@ -1,0 +1,124 @@
+"""The PLE block (engraft/replica/layers.py:565-626) on the GPU against the
+reference's own outputs (golden vectors), the numpy oracle and, at the real
+width (hc = 4, n_embd = 2560), a plain torch fp32 statement of the same
+formula."""
+from __future__ import annotations
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import fixtures as FX
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+TOL = 2e-5  # fp32, relative to the largest magnitude: cuBLAS and the block reductions round in their own order
+
+
+def _weights(c):
+    return types.SimpleNamespace(**{k: torch.from_numpy(c[k]).to(DEV) for k in
+                                    ("w_key", "w_value", "norm_key", "norm_query", "norm_conv", "conv1d")})
+
+
+def _hp(hc, n, dil=FX.PLE_DIL, eps=FX.PLE_EPS):
+    return types.SimpleNamespace(hc_mult=hc, n_embd=n, f_norm_rms_eps=eps, ple_ngram_size=dil)
+
+
+def _close(got, want):
+    got = got.detach().cpu().numpy() if isinstance(got, torch.Tensor) else got
+    return np.abs(got - want).max() <= TOL * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("case", FX.PLE_CASES)
+def test_ple_block_matches_reference_golden(golden, case):
+    import engraft_ngram_b200 as eb
+    seed, T, n_hist = case
+    c = FX.ple_case(seed, T, n_hist)
+    d = {}
+    out, hist = eb.ple_forward(torch.from_numpy(c["emb"]).to(DEV), torch.from_numpy(c["hidden"]).to(DEV),
+                               _weights(c), torch.from_numpy(c["hist"]).to(DEV), _hp(FX.PLE_HC, FX.PLE_N), diag=d)
+    torch.cuda.synchronize()
+    ref_out, ref_hist = O.ple_forward(c["emb"], c["hidden"], c["w_key"], c["w_value"], c["norm_key"],
+                                      c["norm_query"], c["norm_conv"], c["conv1d"], c["hist"], FX.PLE_HC, FX.PLE_N,
+                                      FX.PLE_EPS, FX.PLE_DIL)
+    assert _close(out, ref_out) and _close(hist, ref_hist)
+    assert _close(out, golden[f"ple{seed}_out"]) and _close(hist, golden[f"ple{seed}_hist"])
+    assert set(d) == {"s", "gate", "value_norm", "gated_norm", "hidden_norm"} and d["gate"].shape == (T, FX.PLE_HC)
+
+
+def _torch_ple(emb, hidden, w, hist, hc, n, eps, dil):
+    """The reference formula in plain torch fp32 on the GPU (TF32 off)."""
+    T = emb.shape[0]
+
+    def rms(x, wt):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * wt.reshape(hc, n)
+
+    key = (emb @ w.w_key.T).reshape(T, hc, n)
+    s = (rms(key, w.norm_key) * rms(hidden, w.norm_query)).sum(-1) / n ** 0.5
+    gate = torch.sigmoid(torch.sign(s) * torch.sqrt(s.abs().clamp_min(1e-6)))
+    value = emb @ w.w_value.T
+    gated = value.unsqueeze(1) * gate.unsqueeze(-1)
+    normed = rms(gated, w.norm_conv)
+    K = w.conv1d.shape[1]
+    full = torch.cat([hist, normed]).reshape(-1, hc * n)
+    H = hist.shape[0]
+    acc = torch.zeros(T, hc * n, device=emb.device)
+    for k in range(K):
+        back = (K - 1 - k) * dil
+        for t in range(T):
+            if H + t - back >= 0:
+                acc[t] += full[H + t - back] * w.conv1d[:, k]
+    out = hidden + gated + torch.nn.functional.silu(acc).reshape(T, hc, n)
+    return out, torch.cat([hist, normed])[-(K - 1) * dil:]
+
+
+@pytest.mark.parametrize("T,n_hist", [(6, 9), (24, 0)])
+def test_ple_block_at_real_width(T, n_hist):
+    """hc = 4, n_embd = 2560, K = 4, dilation 3 (the reference's PLE layer)."""
+    import engraft_ngram_b200 as eb
+    hc, n, K = 4, 2560, 4
+    g = torch.Generator(device=DEV).manual_seed(T)
+    r = lambda *s: torch.randn(*s, generator=g, device=DEV) * 0.1  # noqa: E731
+    w = types.SimpleNamespace(w_key=r(hc * n, n), w_value=r(n, n), norm_key=1 + r(hc * n), norm_query=1 + r(hc * n),
+                              norm_conv=1 + r(hc * n), conv1d=r(hc * n, K))
+    emb, hidden, hist = r(T, n), r(T, hc, n), r(n_hist, hc, n)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        want_out, want_hist = _torch_ple(emb, hidden, w, hist, hc, n, 1e-6, 3)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    out, new_hist = eb.ple_forward(emb, hidden, w, hist, _hp(hc, n, 3, 1e-6))
+    torch.cuda.synchronize()
+    assert _close(out, want_out.cpu().numpy()) and _close(new_hist, want_hist.cpu().numpy())
+
+
+def test_ple_block_refuses_gradients_and_install_routes_them():
+    """A call that needs a gradient raises in the B200 block; install_ple sends
+    such calls to the original function and the others to the B200 block."""
+    import engraft_ngram_b200 as eb
+    c = FX.ple_case(1, 3, 0)
+    w = _weights(c)
+    emb = torch.from_numpy(c["emb"]).to(DEV).requires_grad_(True)
+    hidden = torch.from_numpy(c["hidden"]).to(DEV)
+    hist = torch.from_numpy(c["hist"]).to(DEV)
+    with pytest.raises(NotImplementedError):
+        eb.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N))
+    calls = []
+    fake = types.ModuleType("fake_layers")
+    fake.ple_forward = lambda *a, **k: calls.append("orig") or ("orig", None)
+    fake_model = types.ModuleType("fake_model")
+    fake_model.ple_forward = fake.ple_forward
+    mods = {"engraft.replica.layers": fake, "engraft.replica.model": fake_model}
+    eb.install_ple(mods)
+    try:
+        assert fake.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N)) == ("orig", None)
+        with torch.no_grad():
+            out, _ = fake_model.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N))
+        assert isinstance(out, torch.Tensor) and calls == ["orig"]
+    finally:
+        eb.uninstall_ple(mods)
+    assert fake.ple_forward is not None and fake.ple_forward(None, None, None, None, None) == ("orig", None)

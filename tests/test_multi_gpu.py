@@ -183,3 +183,91 @@ def test_row_sharded_staging_matches_resident_table_on_two_ranks():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(out) == {0: True, 1: True}
+
+
+def _autograd_peer(rank: int, world: int, port: int, out) -> None:
+    """Each rank: three steps through the public autograd API on its own batch,
+    once with the row gradients routed into PeerRows (attach + PeerAdam) and
+    once with the NCCL all-reduce of rows_var.grad + OverlayAdam; the rows and
+    the hit counts agree bit for bit."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        import engraft_ngram_b200 as eb
+        from engraft_ngram_b200 import _lib as L
+        from engraft_ngram_b200.dist import PeerAdam, PeerRows
+        from engraft_ngram_b200.table import synthetic_head_sizes, synthetic_multipliers, synthetic_resident
+        n_rows, fmt, dim, T, eos = 70_001, L.FMT_NAMES["iq4_xs"], 256, 1200, 151_935
+        sizes = synthetic_head_sizes(n_rows)
+        offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
+        table = eb.DeviceTable(synthetic_resident(n_rows, fmt, dim, 21, dev), fmt, dim, sizes, offs,
+                               synthetic_multipliers(6), eos, n_rows=n_rows)
+        ranks = np.arange(1, 151_937, dtype=np.float64)
+        cdf = np.cumsum(ranks ** -1.1)
+        cdf /= cdf[-1]
+        rr = np.random.default_rng(300 + rank)
+        batches = [torch.from_numpy(np.searchsorted(cdf, rr.random(T)).astype(np.int32)).to(dev) for _ in range(3)]
+        g0 = np.random.default_rng(8)  # overlay ids, start rows and residual: the same on every rank
+        shared = torch.from_numpy(np.searchsorted(cdf, g0.random(T)).astype(np.int32)).to(dev)
+        ids = table.global_ids(shared).reshape(-1)
+        ov_ids = torch.unique(torch.cat([ids[::3], torch.from_numpy(g0.integers(0, n_rows, 500)).to(dev).int()]))
+        R = int(ov_ids.numel())
+        p0 = torch.from_numpy((g0.standard_normal((R, dim)) * 0.01).astype(np.float32)).to(dev)
+        res0 = torch.from_numpy((g0.standard_normal((T, 8 * dim)) * 0.5).astype(np.float32)).to(dev).to(torch.bfloat16)
+        dout = torch.from_numpy((rr.standard_normal((T, 8 * dim)) * 1e-3).astype(np.float32)).to(dev).to(torch.bfloat16)
+
+        def run(peer_mode: bool):
+            omap = eb.OverlayMap(ov_ids, dev)
+            hits = torch.zeros(3, dtype=torch.int64, device=dev)
+            if peer_mode:
+                peer = PeerRows(R, dim, dev)
+                peer.rows_var.copy_(p0)
+                rows_var = peer.rows_var.requires_grad_(True)
+                peer.attach(omap)
+                opt = PeerAdam(peer, lr=1e-3, reg_ref=p0, reg_mu=0.1)
+            else:
+                rows_var = p0.clone().requires_grad_(True)
+                opt = eb.OverlayAdam([rows_var], lr=1e-3, reg_ref=p0, reg_mu=0.1)
+            for k in range(3):
+                opt.zero_grad()
+                o = eb.engram_residual_add(res0.clone(), table, batches[k], rows_var, omap, None, 0, hits[k:k + 1])
+                o.backward(dout)
+                if not peer_mode:
+                    assert rows_var.grad is not None
+                    dist.all_reduce(rows_var.grad)
+                else:
+                    assert rows_var.grad is None
+                opt.step()
+            torch.cuda.synchronize()
+            return rows_var.detach().clone(), hits
+
+        a, ha = run(True)
+        b, hb = run(False)
+        out[rank] = bool(torch.equal(a.view(torch.int32), b.view(torch.int32)) and torch.equal(ha, hb))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_autograd_through_peer_rows_matches_allreduce_on_two_ranks():
+    """Two ranks, public autograd API: PeerRows.attach + PeerAdam equals the
+    NCCL all-reduce of the row gradients + OverlayAdam bit for bit."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_autograd_peer, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(out) == {0: True, 1: True}

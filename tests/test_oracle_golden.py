@@ -153,3 +153,22 @@ def test_oracle_sum_overlays_matches_reference_golden(golden):
     assert hashlib.sha256(merged.tobytes()).hexdigest() == str(golden["sumov_merged_sha"])
     man = ast.literal_eval(str(golden["sumov_manifest"]))
     assert (moved, shared, hist) == (man["n_rows_moved_any"], man["n_rows_shared"], man["facts_per_row_histogram"])
+
+
+PLE_TOL = 2e-6  # fp32: numpy's and torch's reductions and matmuls round in different orders
+
+
+@pytest.mark.parametrize("case", FX.PLE_CASES)
+def test_ple_block_oracle_matches_reference(golden, case):
+    """The numpy restatement of ple_forward against the reference's own torch
+    function on the same seeded inputs (empty, full, single-step and short
+    histories): output and new history within PLE_TOL relative to the largest
+    magnitude."""
+    seed, T, n_hist = case
+    c = FX.ple_case(seed, T, n_hist)
+    out, hist = O.ple_forward(c["emb"], c["hidden"], c["w_key"], c["w_value"], c["norm_key"], c["norm_query"],
+                              c["norm_conv"], c["conv1d"], c["hist"], FX.PLE_HC, FX.PLE_N, FX.PLE_EPS, FX.PLE_DIL)
+    ref_out, ref_hist = golden[f"ple{seed}_out"], golden[f"ple{seed}_hist"]
+    assert out.shape == ref_out.shape and hist.shape == ref_hist.shape
+    assert np.abs(out - ref_out).max() <= PLE_TOL * max(1.0, np.abs(ref_out).max())
+    assert np.abs(hist - ref_hist).max() <= PLE_TOL * max(1.0, np.abs(ref_hist).max())

@@ -69,6 +69,9 @@ def parse():
     ap.add_argument("--shard-exchange", choices=["peer", "nccl"], default="peer",
                     help="--shard: rows read in place from their owners over NVLink (symmetric memory) or moved by "
                          "NCCL all-to-all of ids and rows")
+    ap.add_argument("--e2e-exchange", choices=["nccl", "peer"], default="nccl",
+                    help="N>1 e2e through autograd: NCCL all-reduce of rows_var.grad + OverlayAdam, or the row "
+                         "gradients stored into their owners (PeerRows.attach) + PeerAdam")
     ap.add_argument("--no-sharded-line", action="store_true",
                     help="N>1: skip the second measurement with the table row-sharded")
     ap.add_argument("--stage", choices=["push", "pull", "off"], default="pull",
@@ -193,6 +196,13 @@ class Workload:
             self.ov_ids = torch.zeros(0, dtype=torch.int32, device=device)
         self.R = int(self.ov_ids.numel())
         self.omap = eb.OverlayMap(self.ov_ids, device)
+        self.remote_rows = 0  # row-sharded: rows per step this rank copies from other ranks (overlay heads skip)
+        if self.shard is not None and world > 1:
+            ids = self.shard.global_ids(self.tokens, self.seg_start).reshape(-1)
+            remote = (ids % world) != rank
+            if self.R:
+                remote &= ~torch.isin(ids, self.ov_ids)
+            self.remote_rows = int(remote.sum())
         if self.shard is not None:  # true rows live on their owners; start from seeded values instead
             gp = torch.Generator(device=device)
             gp.manual_seed(seed * 1000 + 5)
@@ -748,6 +758,13 @@ def main():
                        "phase_ms": {"forward": fwd2, "backward": bwd2, "optimizer_and_exchange": ms2 - fwd2 - bwd2},
                        "parallelism": f"dp{world}" + shard_text(cfg2),
                        "table_bytes_per_gpu": int(wl2.shard.n_local * wl2.shard.stride)}
+        # what crossed NVLink for the table: the other ranks' rows this rank read (max over ranks)
+        rr = torch.tensor([wl2.remote_rows], dtype=torch.int64, device=device)
+        dist.all_reduce(rr, op=dist.ReduceOp.MAX)
+        nv_bytes = int(rr[0]) * wl2.shard.stride
+        row_sharded["nvlink"] = {"remote_rows_per_step": int(rr[0]), "bytes_per_step": nv_bytes,
+                                 "achieved_gbps": nv_bytes / (ms2 * 1e-3) / 1e9, "peer_copy_gbps": 770.0,
+                                 "frac_of_peer_copy": nv_bytes / (ms2 * 1e-3) / 1e9 / 770.0}
 
     if rank == 0:
         peak, peak_kind = measured_peak_gbs()
@@ -853,7 +870,7 @@ def run_e2e(wl, args, device, ddist, world):
     hit_h = [torch.zeros(1, dtype=torch.int64).pin_memory() for _ in range(2)]
     done = [None, None]
     counter = [0]
-    if wl.peer is not None:  # data-parallel through autograd: row gradients go to their owners (PeerRows.attach)
+    if wl.peer is not None and args.e2e_exchange == "peer":  # autograd backward into the owners (PeerRows.attach)
         from engraft_ngram_b200.dist import PeerAdam
         wl.peer.rows_var.copy_(wl.p0)
         rows_var = wl.peer.rows_var.requires_grad_(True)
@@ -888,7 +905,7 @@ def run_e2e(wl, args, device, ddist, world):
             out = eb.engram_embed(wl.table, tok, rows_var, wl.omap, ss, 0, wl.T, hits)
         if wl.cfg["bwd"] and wl.R:
             out.backward(wl.dout.reshape(out.shape))
-            if ddist is not None and wl.peer is None:
+            if ddist is not None and rows_var.grad is not None:
                 ddist.all_reduce(rows_var.grad)
             opt.step()
         b = counter[0] % 2

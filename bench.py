@@ -612,7 +612,9 @@ def run_ple(args, device):
     hp = types.SimpleNamespace(hc_mult=hc, n_embd=n, f_norm_rms_eps=1e-6, ple_ngram_size=dil)
     lib = L.load()
     stream = torch.cuda.current_stream(device).cuda_stream
-    key, value = torch.empty(T, hc * n, device=device), torch.empty(T, n, device=device)
+    from engraft_ngram_b200 import ple as P
+    kv = torch.empty(T, hc * n + n, device=device)
+    value = kv[:, hc * n:]
     gate, normed, out = (torch.empty(T, hc, device=device), torch.empty(T, hc, n, device=device),
                          torch.empty(T, hc, n, device=device))
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -620,19 +622,24 @@ def run_ple(args, device):
     for _ in range(3):
         eb.ple_forward(emb, hidden, w, hist, hp)
     torch.cuda.synchronize()
+    stride = hc * n + n
+    t_fp32 = 0.0
+    for _ in range(K_steps):  # the plain fp32 projection, for comparison
+        ev[0].record()
+        P.project(emb, w, kv, "fp32")
+        ev[1].record()
+        torch.cuda.synchronize()
+        t_fp32 += ev[0].elapsed_time(ev[1])
     t_gemm = t_gate = t_conv = 0.0
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
     for _ in range(K_steps):  # the same launches as ple_forward, with events between them
         ev[0].record()
-        torch.matmul(emb, w.w_key.t(), out=key)
-        torch.matmul(emb, w.w_value.t(), out=value)
+        P.project(emb, w, kv)
         ev[1].record()
-        L.check(lib.engram_ple_gate(key.data_ptr(), hc * n, value.data_ptr(), n, hidden.data_ptr(),
+        L.check(lib.engram_ple_gate(kv.data_ptr(), stride, value.data_ptr(), stride, hidden.data_ptr(),
                                     w.norm_key.data_ptr(), w.norm_query.data_ptr(), w.norm_conv.data_ptr(), T, hc, n,
                                     1e-6, gate.data_ptr(), None, normed.data_ptr(), stream), "engram_ple_gate")
         ev[2].record()
-        L.check(lib.engram_ple_conv(value.data_ptr(), n, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
+        L.check(lib.engram_ple_conv(value.data_ptr(), stride, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
                                     hist.data_ptr(), hist.shape[0], w.conv1d.data_ptr(), K, dil, T, hc, n,
                                     out.data_ptr(), stream), "engram_ple_conv")
         ev[3].record()
@@ -640,8 +647,7 @@ def run_ple(args, device):
         t_gemm += ev[0].elapsed_time(ev[1])
         t_gate += ev[1].elapsed_time(ev[2])
         t_conv += ev[2].elapsed_time(ev[3])
-    torch.backends.cuda.matmul.allow_tf32 = prev
-    t_gemm, t_gate, t_conv = (x / K_steps for x in (t_gemm, t_gate, t_conv))
+    t_gemm, t_gate, t_conv, t_fp32 = (x / K_steps for x in (t_gemm, t_gate, t_conv, t_fp32))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(K_steps):
@@ -656,8 +662,9 @@ def run_ple(args, device):
     flops = 2.0 * T * n * (hc * n + n)
     line = {"metric": "PLE block positions/s (layers.ple_forward, hc=4, n_embd=2560, 2048 positions, fp32)",
             "value": T / (ms * 1e-3), "unit": "positions/s", "ms_per_call": ms,
-            "phase_ms": {"projections_cublas_fp32": t_gemm, "engram_ple_gate": t_gate, "engram_ple_conv": t_conv},
+            "phase_ms": {f"projections_{P.PROJECTION}": t_gemm, "engram_ple_gate": t_gate, "engram_ple_conv": t_conv},
             "gemm_tflops": flops / (t_gemm * 1e-3) / 1e12,
+            "projections_fp32_sgemm": {"ms": t_fp32, "tflops": flops / (t_fp32 * 1e-3) / 1e12},
             "roofline": {"engram_ple_gate": {"bound": "hbm", "achieved": gate_bytes / (t_gate * 1e-3) / 1e9,
                                              "peak": peak, "unit": "GB/s", "frac": gate_bytes / (t_gate * 1e-3) / 1e9 / peak},
                          "engram_ple_conv": {"bound": "hbm", "achieved": conv_bytes / (t_conv * 1e-3) / 1e9,

@@ -24,18 +24,6 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kPleMaxHc = 8;
 constexpr int kGateThreads = 256;
 
-__device__ __forceinline__ float block_sum(float v, float* red, int tid) {
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(kFull, v, d);
-    __syncthreads();  // red is reused between calls
-    if ((tid & 31) == 0) red[tid >> 5] = v;
-    __syncthreads();
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < kGateThreads / 32; w++) s += red[w];
-    return s;
-}
-
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restrict__ key, int64_t key_stride,
@@ -46,47 +34,64 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
                                                            const float* __restrict__ norm_conv, int64_t T, int hc,
                                                            int n, float eps, float* __restrict__ gate_out,
                                                            float* __restrict__ s_out, float* __restrict__ normed) {
-    __shared__ float red[kGateThreads / 32];
+    // per stream j: sum key^2, sum hidden^2, sum (key*nk)(hidden*nq); then sum value^2
+    constexpr int kSums = 3 * kPleMaxHc + 1;
+    __shared__ float part[kGateThreads / 32][kSums];
     __shared__ float coef[2 * kPleMaxHc];  // per stream: gate, rsqrt of the gated mean square
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n4 = n >> 2;
     for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
         const float4* k4 = reinterpret_cast<const float4*>(key + t * key_stride);
         const float4* v4 = reinterpret_cast<const float4*>(value + t * value_stride);
         const float4* h4 = reinterpret_cast<const float4*>(hidden + t * (int64_t)hc * n);
-        float ssv = 0.f;
+        float acc[kSums];
+#pragma unroll
+        for (int q = 0; q < kSums; q++) acc[q] = 0.f;
         for (int c = tid; c < n4; c += kGateThreads) {
             const float4 v = __ldg(v4 + c);
-            ssv += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            acc[3 * kPleMaxHc] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+            for (int j = 0; j < kPleMaxHc; j++) {
+                if (j < hc) {
+                    const float4 k = __ldg(k4 + j * n4 + c), h = __ldg(h4 + j * n4 + c);
+                    const float4 a = __ldg(reinterpret_cast<const float4*>(norm_key + (int64_t)j * n) + c);
+                    const float4 b = __ldg(reinterpret_cast<const float4*>(norm_query + (int64_t)j * n) + c);
+                    acc[3 * j] += k.x * k.x + k.y * k.y + k.z * k.z + k.w * k.w;
+                    acc[3 * j + 1] += h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
+                    acc[3 * j + 2] += (k.x * a.x) * (h.x * b.x) + (k.y * a.y) * (h.y * b.y) +
+                                      (k.z * a.z) * (h.z * b.z) + (k.w * a.w) * (h.w * b.w);
+                }
+            }
         }
-        ssv = block_sum(ssv, red, tid);
-        for (int j = 0; j < hc; j++) {
-            float ssk = 0.f, ssq = 0.f, dot = 0.f;
-            const float4* nk4 = reinterpret_cast<const float4*>(norm_key + (int64_t)j * n);
-            const float4* nq4 = reinterpret_cast<const float4*>(norm_query + (int64_t)j * n);
-            for (int c = tid; c < n4; c += kGateThreads) {
-                const float4 k = __ldg(k4 + j * n4 + c), h = __ldg(h4 + j * n4 + c);
-                const float4 a = __ldg(nk4 + c), b = __ldg(nq4 + c);
-                ssk += k.x * k.x + k.y * k.y + k.z * k.z + k.w * k.w;
-                ssq += h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
-                dot += (k.x * a.x) * (h.x * b.x) + (k.y * a.y) * (h.y * b.y) + (k.z * a.z) * (h.z * b.z) +
-                       (k.w * a.w) * (h.w * b.w);
+        // one block reduction for all the sums: shuffles within warps, then thread q adds the warps' q-th sum
+#pragma unroll
+        for (int q = 0; q < kSums; q++) {
+            float x = acc[q];
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) x += __shfl_xor_sync(kFull, x, d);
+            if (lane == 0) part[warp][q] = x;
+        }
+        __syncthreads();
+        if (tid < hc) {
+            const int j = tid;
+            float ssk = 0.f, ssq = 0.f, dot = 0.f, ssv = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGateThreads / 32; w++) {
+                ssk += part[w][3 * j];
+                ssq += part[w][3 * j + 1];
+                dot += part[w][3 * j + 2];
+                ssv += part[w][3 * kPleMaxHc];
             }
-            ssk = block_sum(ssk, red, tid);
-            ssq = block_sum(ssq, red, tid);
-            dot = block_sum(dot, red, tid);
-            if (tid == 0) {
-                const float rk = 1.0f / sqrtf(ssk / (float)n + eps);
-                const float rq = 1.0f / sqrtf(ssq / (float)n + eps);
-                const float s = dot * rk * rq / sqrtf((float)n);
-                const float mag = sqrtf(fmaxf(fabsf(s), 1e-6f));
-                const float sg = s > 0.f ? 1.f : (s < 0.f ? -1.f : 0.f);
-                const float g = sigmoidf_(sg * mag);
-                gate_out[t * hc + j] = g;
-                if (s_out) s_out[t * hc + j] = s;
-                coef[2 * j] = g;
-                coef[2 * j + 1] = 1.0f / sqrtf(g * g * (ssv / (float)n) + eps);
-            }
+            const float rk = 1.0f / sqrtf(ssk / (float)n + eps);
+            const float rq = 1.0f / sqrtf(ssq / (float)n + eps);
+            const float s = dot * rk * rq / sqrtf((float)n);
+            const float mag = sqrtf(fmaxf(fabsf(s), 1e-6f));
+            const float sg = s > 0.f ? 1.f : (s < 0.f ? -1.f : 0.f);
+            const float g = sigmoidf_(sg * mag);
+            gate_out[t * hc + j] = g;
+            if (s_out) s_out[t * hc + j] = s;
+            coef[2 * j] = g;
+            coef[2 * j + 1] = 1.0f / sqrtf(g * g * (ssv / (float)n) + eps);
         }
         __syncthreads();
         for (int j = 0; j < hc; j++) {
@@ -98,7 +103,7 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
                 o4[c] = make_float4(v.x * g * r * w.x, v.y * g * r * w.y, v.z * g * r * w.z, v.w * g * r * w.w);
             }
         }
-        __syncthreads();  // coef is rewritten by the next position
+        __syncthreads();  // part and coef are rewritten by the next position
     }
 }
 
@@ -117,6 +122,11 @@ __global__ void __launch_bounds__(256) k_ple_conv(const float* __restrict__ valu
         const int j = (int)(c / n);
         const int64_t cv = c - (int64_t)j * n;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float4 w4[4];  // K == 4: the 4 taps of channel c + q in one 16-byte load
+        if (K == 4) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) w4[q] = __ldg(reinterpret_cast<const float4*>(conv_w + (c + q) * 4));
+        }
         for (int k = 0; k < K; k++) {
             const int64_t src = t - (int64_t)(K - 1 - k) * dilation;
             const float* row;
@@ -126,7 +136,12 @@ __global__ void __launch_bounds__(256) k_ple_conv(const float* __restrict__ valu
             const float4 x = __ldg(reinterpret_cast<const float4*>(row + c));
             const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-            for (int q = 0; q < 4; q++) acc[q] = __fadd_rn(acc[q], __fmul_rn(xs[q], __ldg(conv_w + (c + q) * K + k)));
+            for (int q = 0; q < 4; q++) {
+                float wk;
+                if (K == 4) wk = k == 0 ? w4[q].x : (k == 1 ? w4[q].y : (k == 2 ? w4[q].z : w4[q].w));
+                else wk = __ldg(conv_w + (c + q) * K + k);
+                acc[q] = __fadd_rn(acc[q], __fmul_rn(xs[q], wk));
+            }
         }
         const float g = __ldg(gate + t * hc + j);
         const float4 v = __ldg(reinterpret_cast<const float4*>(value + t * value_stride + cv));
@@ -174,7 +189,8 @@ extern "C" int engram_ple_conv(const float* value, int64_t value_stride, const f
     if (value_stride < n_embd || (value_stride & 3)) return ENGRAM_ERR_ARG;
     if (T == 0) return ENGRAM_OK;
     if (!value || !hidden || !gate || !normed || !conv_w || !out || (hist_len > 0 && !hist)) return ENGRAM_ERR_ARG;
-    if (!aligned16(value) || !aligned16(hidden) || !aligned16(normed) || !aligned16(out) || (hist && !aligned16(hist)))
+    if (!aligned16(value) || !aligned16(hidden) || !aligned16(normed) || !aligned16(out) || (hist && !aligned16(hist)) ||
+        (K == 4 && !aligned16(conv_w)))
         return ENGRAM_ERR_ARG;
     const int64_t total = T * ((int64_t)hc * n_embd / 4);
     const int64_t want = (total + 255) / 256, cap = (int64_t)sm_count() * 8;

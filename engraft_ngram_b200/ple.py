@@ -2,13 +2,19 @@
 `engraft.replica.layers.ple_forward` (engraft/replica/layers.py:565-626), same
 arguments and results.
 
-The key and value projections are two fp32 GEMMs (cuBLAS through torch.matmul,
-TF32 off, as the reference computes them in fp32); everything after them is two
-kernels of this library: engram_ple_gate (grouped RMS norms, the sign-sqrt
-sigmoid gate and the norm of the gated value, one block per position) and
-engram_ple_conv (the causal dilated depthwise conv over [history; positions],
-silu and the block's residual sum).  Results agree with the reference to fp32
-rounding (different reduction orders).
+The key and value projections are one GEMM against [w_key; w_value] (cuBLAS
+through torch.matmul).  PROJECTION selects its arithmetic:
+  "3xtf32" (default): each fp32 operand split into a TF32 head and the fp32
+    remainder, x = hi + lo, and A B = hi_A hi_B + hi_A lo_B + lo_A hi_B on the
+    tensor cores (the split-precision method of NVIDIA's CUTLASS "3xTF32"),
+    with fp32 accumulation: fp32-level accuracy at tensor-core speed;
+  "fp32": plain fp32 SGEMM (TF32 off), the reference's own arithmetic.
+Everything after the projections is two kernels of this library:
+engram_ple_gate (grouped RMS norms, the sign-sqrt sigmoid gate and the norm of
+the gated value, one block per position) and engram_ple_conv (the causal
+dilated depthwise conv over [history; positions], silu and the block's residual
+sum).  Results agree with the reference to fp32 rounding (different reduction
+orders).
 
 Forward only: the block's backward is not built here, so a call that needs a
 gradient raises; `install_ple` routes those calls to the reference's own
@@ -23,16 +29,58 @@ import torch
 from . import _lib as L
 
 _GRAD_FIELDS = ("w_key", "w_value", "norm_key", "norm_query", "norm_conv", "conv1d")
+PROJECTION = "3xtf32"  # or "fp32"
 
 
 @contextlib.contextmanager
-def _fp32_matmul():
+def _matmul_tf32(on: bool):
     prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = on
     try:
         yield
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def split_tf32(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """x = hi + lo exactly: hi keeps the 10 explicit mantissa bits TF32 holds
+    (the low 13 bits cleared), lo = x - hi is the fp32 remainder."""
+    hi = (x.contiguous().view(torch.int32) & -8192).view(torch.float32)
+    return hi, x - hi
+
+
+def _weights_kv(w, mode: str):
+    """[w_key; w_value] and, for 3xtf32, its split, cached on `w` until a weight changes."""
+    key = (mode, w.w_key.data_ptr(), w.w_key._version, w.w_value.data_ptr(), w.w_value._version)
+    cached = getattr(w, "_engram_b200_kv", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    kv = torch.cat([w.w_key, w.w_value], dim=0).contiguous()
+    parts = split_tf32(kv) if mode == "3xtf32" else (kv,)
+    try:
+        setattr(w, "_engram_b200_kv", (key, parts))
+    except AttributeError:  # a weights object without attributes of its own: no cache
+        pass
+    return parts
+
+
+def project(emb: torch.Tensor, w, out: torch.Tensor, mode: str | None = None) -> torch.Tensor:
+    """out [T, hc*n + n] = emb @ [w_key; w_value].T (key columns, then value)."""
+    mode = mode or PROJECTION
+    if mode == "fp32":
+        (kv,) = _weights_kv(w, "fp32")
+        with _matmul_tf32(False):
+            torch.matmul(emb, kv.t(), out=out)
+        return out
+    if mode != "3xtf32":
+        raise ValueError(f"projection mode {mode!r}")
+    b_hi, b_lo = _weights_kv(w, "3xtf32")
+    a_hi, a_lo = split_tf32(emb)
+    with _matmul_tf32(True):
+        torch.matmul(a_lo, b_hi.t(), out=out)  # the small terms first
+        out.addmm_(a_hi, b_lo.t())
+        out.addmm_(a_hi, b_hi.t())
+    return out
 
 
 def needs_grad(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor) -> bool:
@@ -64,8 +112,8 @@ def ple_forward(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor, 
     K = int(w.conv1d.shape[1])
     emb = _f32(emb, "emb", (T, n))
     hidden = _f32(hidden, "hidden", (T, hc, n))
-    w_key = _f32(w.w_key, "w_key", (hc * n, n))
-    w_value = _f32(w.w_value, "w_value", (n, n))
+    _f32(w.w_key, "w_key", (hc * n, n))
+    _f32(w.w_value, "w_value", (n, n))
     nk = _f32(w.norm_key.reshape(-1), "norm_key", (hc * n,))
     nq = _f32(w.norm_query.reshape(-1), "norm_query", (hc * n,))
     nc = _f32(w.norm_conv.reshape(-1), "norm_conv", (hc * n,))
@@ -75,20 +123,18 @@ def ple_forward(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor, 
     dev = emb.device
     lib = L.load()
     stream = L.stream_of(dev)
-    key = torch.empty(T, hc * n, device=dev)
-    value = torch.empty(T, n, device=dev)
-    with _fp32_matmul():
-        torch.matmul(emb, w_key.t(), out=key)
-        torch.matmul(emb, w_value.t(), out=value)
+    kv = project(emb, w, torch.empty(T, hc * n + n, device=dev))
+    stride = hc * n + n
+    value = kv[:, hc * n:]
     gate = torch.empty(T, hc, device=dev)
     s = torch.empty(T, hc, device=dev) if diag is not None else None
     normed = torch.empty(T, hc, n, device=dev)
-    st = lib.engram_ple_gate(key.data_ptr(), hc * n, value.data_ptr(), n, hidden.data_ptr(), nk.data_ptr(),
+    st = lib.engram_ple_gate(kv.data_ptr(), stride, value.data_ptr(), stride, hidden.data_ptr(), nk.data_ptr(),
                              nq.data_ptr(), nc.data_ptr(), T, hc, n, eps, gate.data_ptr(), L.ptr(s),
                              normed.data_ptr(), stream)
     L.check(st, "engram_ple_gate")
     out = torch.empty(T, hc, n, device=dev)
-    st = lib.engram_ple_conv(value.data_ptr(), n, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
+    st = lib.engram_ple_conv(value.data_ptr(), stride, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
                              hist.data_ptr() if H else None, H, cw.data_ptr(), K, dil, T, hc, n, out.data_ptr(),
                              stream)
     L.check(st, "engram_ple_conv")

@@ -32,8 +32,15 @@ def _close(got, want):
     return np.abs(got - want).max() <= TOL * max(1.0, np.abs(want).max())
 
 
+@pytest.fixture(params=["3xtf32", "fp32"])
+def projection(request, monkeypatch):
+    from engraft_ngram_b200 import ple
+    monkeypatch.setattr(ple, "PROJECTION", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("case", FX.PLE_CASES)
-def test_ple_block_matches_reference_golden(golden, case):
+def test_ple_block_matches_reference_golden(golden, case, projection):
     import engraft_ngram_b200 as eb
     seed, T, n_hist = case
     c = FX.ple_case(seed, T, n_hist)
@@ -76,7 +83,7 @@ def _torch_ple(emb, hidden, w, hist, hc, n, eps, dil):
 
 
 @pytest.mark.parametrize("T,n_hist", [(6, 9), (24, 0)])
-def test_ple_block_at_real_width(T, n_hist):
+def test_ple_block_at_real_width(T, n_hist, projection):
     """hc = 4, n_embd = 2560, K = 4, dilation 3 (the reference's PLE layer)."""
     import engraft_ngram_b200 as eb
     hc, n, K = 4, 2560, 4

@@ -124,3 +124,16 @@ def test_bench_command_line_and_config_text(monkeypatch):
     assert "inside the forward" in bench.shard_text(dict(cfg, stage="off"))
     assert "NCCL all-to-all" in bench.shard_text(dict(cfg, shard_exchange="nccl"))
     assert bench.shard_text(dict(cfg, shard=False)) == ""
+
+
+def test_tf32_split_is_exact():
+    """split_tf32: hi keeps 10 explicit mantissa bits (low 13 bits zero) and
+    hi + lo reproduces x exactly, for normal, tiny, huge and signed values."""
+    from engraft_ngram_b200.ple import split_tf32
+    g = torch.Generator().manual_seed(0)
+    x = torch.cat([torch.randn(1000, generator=g), torch.randn(100, generator=g) * 1e-30,
+                   torch.randn(100, generator=g) * 1e30, torch.tensor([0.0, -0.0, 1.0, -3.5])])
+    hi, lo = split_tf32(x)
+    assert torch.equal((hi.view(torch.int32) & 8191), torch.zeros_like(x, dtype=torch.int32))
+    assert torch.equal(hi + lo, x)
+    assert (lo.abs() <= x.abs() * 2.0 ** -10).all()

@@ -107,26 +107,26 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
     }
 }
 
+// Grid: x over 4-channel groups of one position, y over positions (strided),
+// so a thread keeps its channels' conv taps in registers across positions.
 __global__ void __launch_bounds__(256) k_ple_conv(const float* __restrict__ value, int64_t value_stride,
                                                   const float* __restrict__ hidden, const float* __restrict__ gate,
                                                   const float* __restrict__ normed, const float* __restrict__ hist,
                                                   int64_t hist_len, const float* __restrict__ conv_w, int K,
                                                   int dilation, int64_t T, int hc, int n, float* __restrict__ out) {
-    const int64_t C = (int64_t)hc * n, C4 = C >> 2;
-    const int64_t total = T * C4;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t t = e / C4;
-        const int64_t c4 = e - t * C4;
-        const int64_t c = c4 * 4;
-        const int j = (int)(c / n);
-        const int64_t cv = c - (int64_t)j * n;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        float4 w4[4];  // K == 4: the 4 taps of channel c + q in one 16-byte load
-        if (K == 4) {
+    const int C = hc * n, C4 = C >> 2;
+    const int c4 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c4 >= C4) return;
+    const int c = c4 * 4;
+    const int j = c4 / (n >> 2);
+    const int cv = c - j * n;
+    float4 w4[4];  // K == 4: the 4 taps of channel c + q in one 16-byte load
+    if (K == 4) {
 #pragma unroll
-            for (int q = 0; q < 4; q++) w4[q] = __ldg(reinterpret_cast<const float4*>(conv_w + (c + q) * 4));
-        }
+        for (int q = 0; q < 4; q++) w4[q] = __ldg(reinterpret_cast<const float4*>(conv_w + (int64_t)(c + q) * 4));
+    }
+    for (int64_t t = blockIdx.y; t < T; t += gridDim.y) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int k = 0; k < K; k++) {
             const int64_t src = t - (int64_t)(K - 1 - k) * dilation;
             const float* row;
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(256) k_ple_conv(const float* __restrict__ valu
             for (int q = 0; q < 4; q++) {
                 float wk;
                 if (K == 4) wk = k == 0 ? w4[q].x : (k == 1 ? w4[q].y : (k == 2 ? w4[q].z : w4[q].w));
-                else wk = __ldg(conv_w + (c + q) * K + k);
+                else wk = __ldg(conv_w + (int64_t)(c + q) * K + k);
                 acc[q] = __fadd_rn(acc[q], __fmul_rn(xs[q], wk));
             }
         }
@@ -192,9 +192,12 @@ extern "C" int engram_ple_conv(const float* value, int64_t value_stride, const f
     if (!aligned16(value) || !aligned16(hidden) || !aligned16(normed) || !aligned16(out) || (hist && !aligned16(hist)) ||
         (K == 4 && !aligned16(conv_w)))
         return ENGRAM_ERR_ARG;
-    const int64_t total = T * ((int64_t)hc * n_embd / 4);
-    const int64_t want = (total + 255) / 256, cap = (int64_t)sm_count() * 8;
-    k_ple_conv<<<(int)(want < cap ? want : cap), 256, 0, (cudaStream_t)stream>>>(
+    if ((int64_t)hc * n_embd >= ((int64_t)1 << 30)) return ENGRAM_ERR_RANGE;
+    const int C4 = hc * n_embd / 4;
+    const int gx = (C4 + 255) / 256;
+    const int64_t want_y = ((int64_t)sm_count() * 8 + gx - 1) / gx;
+    const int64_t gy = T < want_y ? T : (want_y < 65535 ? want_y : 65535);
+    k_ple_conv<<<dim3(gx, (unsigned)(gy > 0 ? gy : 1)), 256, 0, (cudaStream_t)stream>>>(
         value, value_stride, hidden, gate, normed, hist, hist_len, conv_w, K, dilation, T, hc, n_embd, out);
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;

@@ -109,51 +109,89 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
 
 // Grid: x over 4-channel groups of one position, y over positions (strided),
 // so a thread keeps its channels' conv taps in registers across positions.
+// KT = 4: the reference's 4 taps, unrolled, two positions per iteration (t and
+// t + gridDim.y) so that their loads are in flight together; KT = 0: any K.
+template <int KT>
 __global__ void __launch_bounds__(256) k_ple_conv(const float* __restrict__ value, int64_t value_stride,
                                                   const float* __restrict__ hidden, const float* __restrict__ gate,
                                                   const float* __restrict__ normed, const float* __restrict__ hist,
                                                   int64_t hist_len, const float* __restrict__ conv_w, int K,
                                                   int dilation, int64_t T, int hc, int n, float* __restrict__ out) {
+    constexpr int P = KT > 0 ? 2 : 1;
+    constexpr int KR = KT > 0 ? KT : 1;  // taps held in registers
     const int C = hc * n, C4 = C >> 2;
     const int c4 = blockIdx.x * blockDim.x + threadIdx.x;
     if (c4 >= C4) return;
     const int c = c4 * 4;
     const int j = c4 / (n >> 2);
     const int cv = c - j * n;
-    float4 w4[4];  // K == 4: the 4 taps of channel c + q in one 16-byte load
-    if (K == 4) {
-#pragma unroll
-        for (int q = 0; q < 4; q++) w4[q] = __ldg(reinterpret_cast<const float4*>(conv_w + (int64_t)(c + q) * 4));
-    }
-    for (int64_t t = blockIdx.y; t < T; t += gridDim.y) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k = 0; k < K; k++) {
-            const int64_t src = t - (int64_t)(K - 1 - k) * dilation;
-            const float* row;
-            if (src >= 0) row = normed + src * C;
-            else if (hist_len + src >= 0) row = hist + (hist_len + src) * C;
-            else continue;
-            const float4 x = __ldg(reinterpret_cast<const float4*>(row + c));
-            const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                float wk;
-                if (K == 4) wk = k == 0 ? w4[q].x : (k == 1 ? w4[q].y : (k == 2 ? w4[q].z : w4[q].w));
-                else wk = __ldg(conv_w + (int64_t)(c + q) * K + k);
-                acc[q] = __fadd_rn(acc[q], __fmul_rn(xs[q], wk));
-            }
-        }
-        const float g = __ldg(gate + t * hc + j);
-        const float4 v = __ldg(reinterpret_cast<const float4*>(value + t * value_stride + cv));
-        const float4 h = __ldg(reinterpret_cast<const float4*>(hidden + t * C + c));
-        const float vs[4] = {v.x, v.y, v.z, v.w}, hs[4] = {h.x, h.y, h.z, h.w};
-        float o[4];
+    float w[4][KR];
+    if (KT > 0) {
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-            const float silu = acc[q] * sigmoidf_(acc[q]);
-            o[q] = __fadd_rn(__fadd_rn(hs[q], __fmul_rn(vs[q], g)), silu);
+            const float4 wq = __ldg(reinterpret_cast<const float4*>(conv_w + (int64_t)(c + q) * 4));
+            w[q][0] = wq.x;
+            if (KR > 1) w[q][KR > 1 ? 1 : 0] = wq.y;
+            if (KR > 2) w[q][KR > 2 ? 2 : 0] = wq.z;
+            if (KR > 3) w[q][KR > 3 ? 3 : 0] = wq.w;
         }
-        reinterpret_cast<float4*>(out + t * C)[c4] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+    auto tap_row = [&](int64_t t, int k) -> const float* {
+        const int64_t src = t - (int64_t)(K - 1 - k) * dilation;
+        return src >= 0 ? normed + src * C : (hist_len + src >= 0 ? hist + (hist_len + src) * C : nullptr);
+    };
+    for (int64_t tb = blockIdx.y; tb < T; tb += P * (int64_t)gridDim.y) {
+        float4 x[P][KR], v[P], h[P];
+        float g[P];
+#pragma unroll
+        for (int p = 0; p < P; p++) {
+            const int64_t t = tb + p * (int64_t)gridDim.y;
+            if (t < T) {
+                if (KT > 0) {
+#pragma unroll
+                    for (int k = 0; k < KR; k++) {
+                        const float* row = tap_row(t, k);
+                        x[p][k] = row ? __ldg(reinterpret_cast<const float4*>(row + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+                g[p] = __ldg(gate + t * hc + j);
+                v[p] = __ldg(reinterpret_cast<const float4*>(value + t * value_stride + cv));
+                h[p] = __ldg(reinterpret_cast<const float4*>(hidden + t * C + c));
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < P; p++) {
+            const int64_t t = tb + p * (int64_t)gridDim.y;
+            if (t >= T) break;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            if (KT > 0) {
+#pragma unroll
+                for (int k = 0; k < KR; k++) {
+                    if (tap_row(t, k) == nullptr) continue;  // before the history: no term, as in the reference
+                    const float xs[4] = {x[p][k].x, x[p][k].y, x[p][k].z, x[p][k].w};
+#pragma unroll
+                    for (int q = 0; q < 4; q++) acc[q] = __fadd_rn(acc[q], __fmul_rn(xs[q], w[q][k]));
+                }
+            } else {
+                for (int k = 0; k < K; k++) {
+                    const float* row = tap_row(t, k);
+                    if (row == nullptr) continue;
+                    const float4 xv = __ldg(reinterpret_cast<const float4*>(row + c));
+                    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        acc[q] = __fadd_rn(acc[q], __fmul_rn(xs[q], __ldg(conv_w + (int64_t)(c + q) * K + k)));
+                }
+            }
+            const float vs[4] = {v[p].x, v[p].y, v[p].z, v[p].w}, hs[4] = {h[p].x, h[p].y, h[p].z, h[p].w};
+            float o[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float silu = acc[q] * sigmoidf_(acc[q]);
+                o[q] = __fadd_rn(__fadd_rn(hs[q], __fmul_rn(vs[q], g[p])), silu);
+            }
+            reinterpret_cast<float4*>(out + t * C)[c4] = make_float4(o[0], o[1], o[2], o[3]);
+        }
     }
 }
 
@@ -197,8 +235,13 @@ extern "C" int engram_ple_conv(const float* value, int64_t value_stride, const f
     const int gx = (C4 + 255) / 256;
     const int64_t want_y = ((int64_t)sm_count() * 8 + gx - 1) / gx;
     const int64_t gy = T < want_y ? T : (want_y < 65535 ? want_y : 65535);
-    k_ple_conv<<<dim3(gx, (unsigned)(gy > 0 ? gy : 1)), 256, 0, (cudaStream_t)stream>>>(
-        value, value_stride, hidden, gate, normed, hist, hist_len, conv_w, K, dilation, T, hc, n_embd, out);
+    const dim3 grid(gx, (unsigned)(gy > 0 ? gy : 1));
+    if (K == 4)
+        k_ple_conv<4><<<grid, 256, 0, (cudaStream_t)stream>>>(value, value_stride, hidden, gate, normed, hist,
+                                                              hist_len, conv_w, K, dilation, T, hc, n_embd, out);
+    else
+        k_ple_conv<0><<<grid, 256, 0, (cudaStream_t)stream>>>(value, value_stride, hidden, gate, normed, hist,
+                                                              hist_len, conv_w, K, dilation, T, hc, n_embd, out);
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }

@@ -69,7 +69,7 @@ def parse():
     ap.add_argument("--shard-exchange", choices=["peer", "nccl"], default="peer",
                     help="--shard: rows read in place from their owners over NVLink (symmetric memory) or moved by "
                          "NCCL all-to-all of ids and rows")
-    ap.add_argument("--e2e-exchange", choices=["nccl", "peer"], default="nccl",
+    ap.add_argument("--e2e-exchange", choices=["nccl", "peer"], default="peer",
                     help="N>1 e2e through autograd: NCCL all-reduce of rows_var.grad + OverlayAdam, or the row "
                          "gradients stored into their owners (PeerRows.attach) + PeerAdam")
     ap.add_argument("--no-sharded-line", action="store_true",

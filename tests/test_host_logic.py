@@ -117,6 +117,7 @@ def test_bench_command_line_and_config_text(monkeypatch):
     monkeypatch.setattr(sys, "argv", ["bench.py", "--gpus", "2", "--shard", "--stage-blocks", "32"])
     args = bench.parse()
     assert args.shard and args.stage == "pull" and args.stage_blocks == 32 and args.shard_exchange == "peer"
+    assert args.e2e_exchange == "peer"
     cfg = dict(bench.CONFIGS["cfg5"], shard=True, shard_exchange="peer", stage="push", exchange="peer")
     text = bench.config_json(cfg, args)["parallelism"]
     assert text.startswith("dp2+row-sharded") and "stores the rows" in text

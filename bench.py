@@ -331,7 +331,12 @@ class Workload:
                 self.optimizer(dist)
 
     def algorithmic_bytes(self):
-        """Bytes the math must move once per step (formulas in DESIGN.md)."""
+        """Bytes the math must move once per step: the forward's token reads, the
+        table rows of the non-overlay heads, the distinct overlay rows touched
+        and the residual read + write (or the CONCAT output); the backward's dOut
+        rows of the (position, group) pairs with a hit (of the hit heads in
+        CONCAT mode) and the row-gradient writes; Adam's 8 floats per element of
+        this rank's overlay rows."""
         import torch
         T, nh, hpn, dim = self.n_out, self.nh, self.hpn, self.dim
         raw_row = {self.L.FMT_F32: dim * 4, self.L.FMT_IQ4_NL: dim // 32 * 18, self.L.FMT_IQ4_XS: dim // 256 * 136}[self.fmt]

@@ -695,10 +695,12 @@ struct XsGeom {
 
 // Values [8q, 8q+8) of one row as four float pairs (v[k] = values 8q+2k, 8q+2k+1).
 template <int FMT, int DIM>
-__device__ __forceinline__ void xs_row(const uint8_t* row, const float* ov_row, int q, const float* kv, float2* v) {
-    if (ov_row != nullptr) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(ov_row + 8 * q));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(ov_row + 8 * q) + 1);
+// ov: the overlay serves this head, and ovv holds its values [8q, 8q+8) (loaded ahead by the caller).
+__device__ __forceinline__ void xs_row(const uint8_t* row, bool ov, const float4* ovv, int q, const float* kv,
+                                       float2* v) {
+    if (ov) {
+        const float4 a = ovv[0];
+        const float4 b = ovv[1];
         v[0] = make_float2(a.x, a.y);
         v[1] = make_float2(a.z, a.w);
         v[2] = make_float2(b.x, b.y);
@@ -817,19 +819,52 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         __syncwarp();
         const uint8_t* bb = wbuf + b * G::BUF;
         __nv_bfloat16* orow = out + i * (G::HPN * DIM);
-#pragma unroll
-        for (int g = 0; g < G::HPN; g++) {
+        // The overlay rows of group g + 1's two heads load while group g computes: their L2 latency
+        // overlaps a group's dequantisation instead of stalling it.
+        float4 nva[G::NQ][2], nvb[G::NQ][2];
+        bool nha = false, nhb = false;
+        auto ov_fetch = [&](int g, float4 (&va)[G::NQ][2], float4 (&vb)[G::NQ][2], bool& ha, bool& hb) {
             const int32_t sa = __shfl_sync(kFull, slot, g);
             const int32_t sb = __shfl_sync(kFull, slot, G::HPN + g);
-            const float* oa = sa >= 0 ? OV.rows + (int64_t)sa * DIM : nullptr;
-            const float* ob = sb >= 0 ? OV.rows + (int64_t)sb * DIM : nullptr;
+            ha = sa >= 0;
+            hb = sb >= 0;
+#pragma unroll
+            for (int jq = 0; jq < G::NQ; jq++) {
+                const int q = lane + 32 * jq;
+                if (q < DIM / 8) {
+                    if (ha) {
+                        const float4* p = reinterpret_cast<const float4*>(OV.rows + (int64_t)sa * DIM + 8 * q);
+                        va[jq][0] = __ldg(p);
+                        va[jq][1] = __ldg(p + 1);
+                    }
+                    if (hb) {
+                        const float4* p = reinterpret_cast<const float4*>(OV.rows + (int64_t)sb * DIM + 8 * q);
+                        vb[jq][0] = __ldg(p);
+                        vb[jq][1] = __ldg(p + 1);
+                    }
+                }
+            }
+        };
+        ov_fetch(0, nva, nvb, nha, nhb);
+#pragma unroll
+        for (int g = 0; g < G::HPN; g++) {
+            float4 cva[G::NQ][2], cvb[G::NQ][2];
+#pragma unroll
+            for (int jq = 0; jq < G::NQ; jq++) {
+                cva[jq][0] = nva[jq][0];
+                cva[jq][1] = nva[jq][1];
+                cvb[jq][0] = nvb[jq][0];
+                cvb[jq][1] = nvb[jq][1];
+            }
+            const bool ha = nha, hb = nhb;
+            if (g + 1 < G::HPN) ov_fetch(g + 1, nva, nvb, nha, nhb);
 #pragma unroll
             for (int jq = 0; jq < G::NQ; jq++) {
                 const int q = lane + 32 * jq;
                 if (q < DIM / 8) {
                     float2 va[4], vb[4];
-                    xs_row<FMT, DIM>(bb + G::RES + g * G::ROW, oa, q, kv, va);
-                    xs_row<FMT, DIM>(bb + G::RES + (G::HPN + g) * G::ROW, ob, q, kv, vb);
+                    xs_row<FMT, DIM>(bb + G::RES + g * G::ROW, ha, cva[jq], q, kv, va);
+                    xs_row<FMT, DIM>(bb + G::RES + (G::HPN + g) * G::ROW, hb, cvb[jq], q, kv, vb);
                     const int v0 = g * DIM + 8 * q;
                     const uint4 r = *reinterpret_cast<const uint4*>(bb + 2 * v0);
                     const uint32_t w[4] = {r.x, r.y, r.z, r.w};

@@ -819,10 +819,11 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         __syncwarp();
         const uint8_t* bb = wbuf + b * G::BUF;
         __nv_bfloat16* orow = out + i * (G::HPN * DIM);
-        // The overlay rows of group g + 1's two heads load while group g computes: their L2 latency
-        // overlaps a group's dequantisation instead of stalling it.
-        float4 nva[G::NQ][2], nvb[G::NQ][2];
-        bool nha = false, nhb = false;
+        // The overlay rows of group g + 2's two heads load while group g computes: their L2 latency
+        // overlaps two groups' dequantisation instead of stalling one.  A ring of 3 register slots.
+        constexpr int kAhead = 2, kRing = kAhead + 1;
+        float4 ova[kRing][G::NQ][2], ovb[kRing][G::NQ][2];
+        bool oha[kRing], ohb[kRing];
         auto ov_fetch = [&](int g, float4 (&va)[G::NQ][2], float4 (&vb)[G::NQ][2], bool& ha, bool& hb) {
             const int32_t sa = __shfl_sync(kFull, slot, g);
             const int32_t sb = __shfl_sync(kFull, slot, G::HPN + g);
@@ -845,26 +846,23 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
                 }
             }
         };
-        ov_fetch(0, nva, nvb, nha, nhb);
+#pragma unroll
+        for (int g = 0; g < kAhead && g < G::HPN; g++) ov_fetch(g, ova[g], ovb[g], oha[g], ohb[g]);
 #pragma unroll
         for (int g = 0; g < G::HPN; g++) {
-            float4 cva[G::NQ][2], cvb[G::NQ][2];
-#pragma unroll
-            for (int jq = 0; jq < G::NQ; jq++) {
-                cva[jq][0] = nva[jq][0];
-                cva[jq][1] = nva[jq][1];
-                cvb[jq][0] = nvb[jq][0];
-                cvb[jq][1] = nvb[jq][1];
+            const int r = g % kRing;
+            if (g + kAhead < G::HPN) {
+                const int rn = (g + kAhead) % kRing;
+                ov_fetch(g + kAhead, ova[rn], ovb[rn], oha[rn], ohb[rn]);
             }
-            const bool ha = nha, hb = nhb;
-            if (g + 1 < G::HPN) ov_fetch(g + 1, nva, nvb, nha, nhb);
+            const bool ha = oha[r], hb = ohb[r];
 #pragma unroll
             for (int jq = 0; jq < G::NQ; jq++) {
                 const int q = lane + 32 * jq;
                 if (q < DIM / 8) {
                     float2 va[4], vb[4];
-                    xs_row<FMT, DIM>(bb + G::RES + g * G::ROW, ha, cva[jq], q, kv, va);
-                    xs_row<FMT, DIM>(bb + G::RES + (G::HPN + g) * G::ROW, hb, cvb[jq], q, kv, vb);
+                    xs_row<FMT, DIM>(bb + G::RES + g * G::ROW, ha, ova[r][jq], q, kv, va);
+                    xs_row<FMT, DIM>(bb + G::RES + (G::HPN + g) * G::ROW, hb, ovb[r][jq], q, kv, vb);
                     const int v0 = g * DIM + 8 * q;
                     const uint4 r = *reinterpret_cast<const uint4*>(bb + 2 * v0);
                     const uint32_t w[4] = {r.x, r.y, r.z, r.w};

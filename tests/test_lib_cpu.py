@@ -120,3 +120,48 @@ def test_division_magic_equals_python_mod(lib):
         o = np.empty_like(x)
         assert lib.engram_selftest_mod(x.ctypes.data, len(x), d, o.ctypes.data) == 0
         assert np.array_equal(o, x % np.uint64(d)), d
+
+
+def test_sharded_staged_and_ple_entry_points_reject_bad_arguments(lib):
+    """The row-sharded, staging and PLE entry points refuse bad arguments with
+    the documented codes before any launch (these calls never reach the GPU)."""
+    st, t = _init(lib)
+    assert st == 0
+    ov = L.EngramOverlay(None, 0, None, None, 0)
+    tok, seg, ptrs = 0x1000, 0x2000, 0x3000
+    # engram_forward_sharded / engram_forward_staged
+    assert lib.engram_forward_sharded(C.byref(t), C.byref(ov), tok, seg, -1, 5, ptrs, 2, 0, 0x4000, None, None,
+                                      None, None) == L.ERR_ARG
+    assert lib.engram_forward_sharded(C.byref(t), C.byref(ov), tok, seg, 0, 5, None, 2, 0, 0x4000, None, None,
+                                      None, None) == L.ERR_ARG
+    assert lib.engram_forward_staged(C.byref(t), C.byref(ov), tok, seg, 0, 5, ptrs, 2, 2, 0x5000, 0, 0x4000, None,
+                                     None, None, None) == L.ERR_ARG  # rank outside the world
+    assert lib.engram_forward_staged(C.byref(t), C.byref(ov), tok, seg, 0, 5, ptrs, 2, 0, None, 0, 0x4000, None,
+                                     None, None, None) == L.ERR_ARG  # no stage with another rank's rows to read
+    # pull staging
+    assert lib.engram_stage_bytes(C.byref(t), 10) == 10 * 16 * 512
+    assert lib.engram_stage_bytes(C.byref(t), -1) == L.ERR_ARG
+    assert lib.engram_stage_sharded(C.byref(t), None, tok, seg, 0, 10, ptrs, 2, 0, 0x5008, 0, None) == L.ERR_ARG
+    assert lib.engram_stage_sharded(C.byref(t), None, tok, seg, 0, 10, ptrs, 2, 0, 0x5000, -1, None) == L.ERR_ARG
+    assert lib.engram_stage_sharded(C.byref(t), None, tok, seg, 0, 10, ptrs, 0, 0, 0x5000, 0, None) == L.ERR_ARG
+    assert lib.engram_stage_sharded(C.byref(t), None, tok, seg, 0, 10, ptrs, 1, 0, 0x5000, 0, None) == 0  # one rank
+    # push staging
+    assert lib.engram_stage_plan_words(100, 2) == 2 * (4 + 1)
+    assert lib.engram_stage_plan_words(-1, 2) == L.ERR_ARG
+    assert lib.engram_stage_plan(C.byref(t), tok, seg, 0, 10, 17, 0x6000, 0x7000, None) == L.ERR_RANGE
+    assert lib.engram_stage_plan(C.byref(t), None, seg, 0, 10, 2, 0x6000, 0x7000, None) == L.ERR_ARG
+    assert lib.engram_stage_push(C.byref(t), ptrs, None, ptrs, 0, 10, ptrs, 2, 2, 0, None) == L.ERR_ARG
+    assert lib.engram_stage_push(C.byref(t), ptrs, None, ptrs, 0, 10, ptrs, 17, 0, 0, None) == L.ERR_RANGE
+    # the PLE block
+    args = [0x1000, 2560 * 5, 0x2000, 2560 * 5, 0x3000, 0x4000, 0x5000, 0x6000]
+    assert lib.engram_ple_gate(*args, 4, 9, 2560, 1e-6, 0x7000, None, 0x8000, None) == L.ERR_ARG  # hc > 8
+    assert lib.engram_ple_gate(*args, 4, 4, 2562, 1e-6, 0x7000, None, 0x8000, None) == L.ERR_ARG  # n % 4
+    bad = list(args)
+    bad[0] = 0x1004
+    assert lib.engram_ple_gate(*bad, 4, 4, 2560, 1e-6, 0x7000, None, 0x8000, None) == L.ERR_ARG  # misaligned key
+    conv = [0x1000, 2560, 0x2000, 0x3000, 0x4000]
+    assert lib.engram_ple_conv(*conv, None, 9, 0x5000, 4, 3, 4, 4, 2560, 0x6000, None) == L.ERR_ARG  # no history
+    assert lib.engram_ple_conv(*conv, None, 0, 0x5000, 0, 3, 4, 4, 2560, 0x6000, None) == L.ERR_ARG  # K = 0
+    assert lib.engram_ple_conv(*conv, None, 0, 0x5004, 4, 3, 4, 4, 2560, 0x6000, None) == L.ERR_ARG  # taps misaligned
+    assert lib.engram_ple_conv(0x1000, 1 << 27, 0x2000, 0x3000, 0x4000, None, 0, 0x5000, 4, 3, 4, 8, 1 << 27,
+                               0x6000, None) == L.ERR_RANGE  # hc * n too large for the kernel's indexing

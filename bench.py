@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the parity check of the timed kernels against the CPU oracle (N=1)")
     ap.add_argument("--table-rows", type=int, default=None, help="override (profiling a small case)")
     ap.add_argument("--seqs", type=int, default=None, help="override sequences per GPU")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
@@ -360,6 +362,111 @@ class Workload:
         return dict(fwd=fwd, bwd=bwd, adam=adam, hits=H, touched=touched)
 
 
+# ------------------------------------------------------------ parity check
+def parity_check(wl, n_sample=4096, seed=1234):
+    """Checks the timed kernels on the full-size workload against the CPU
+    oracle, outside the timed region, with the same C-ABI calls as the timed
+    step (the oracle is the checker here, never the thing measured):
+    - engram_hash ids and the timed forward's overlay slots, every (position,
+      head) of the batch, against the oracle's hash (engraft/table.py:111-144)
+      and row_map membership: bit-exact;
+    - the bf16 residual of n_sample seeded positions after the timed forward,
+      against the oracle's forward (IQ4_XS dequant engraft/replica/dequant.py:
+      150-189, pair sums into the residual) run on those positions' rows, copied
+      back from the resident table (every position reads heads whose global ids
+      lie above 2^28, i.e. resident byte offsets above 2^32): bit-exact;
+    - every overlay row gradient of the timed backward over the whole batch,
+      against the oracle's in-order sums: bit-exact;
+    - every row of one Adam step (engram_adam_step, with the descent's
+      regulariser) from those gradients: bit-exact, and within 1e-5 of the
+      row norm as the north star states.
+    Returns the `parity` object of the bench line."""
+    import ctypes as C
+    import torch
+    from oracle import oracle as O
+    L, dev = wl.L, wl.dev
+    lib = L.load()
+    T, nh, hpn, dim, R = wl.T, wl.nh, wl.hpn, wl.dim, wl.R
+    if wl.shard is not None or wl.decode or wl.fmt != L.FMT_IQ4_XS or wl.mode != L.MODE_PAIRSUM_ADD_BF16:
+        return {"checked": False, "why": "the check covers the resident IQ4_XS pair-sum step"}
+    t_begin = time.perf_counter()
+    tab = wl.table
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+    sample = torch.sort(torch.randperm(T, generator=gen)[:n_sample]).values
+    sample_dev = sample.to(dev)
+    res_before = wl.out[sample_dev].view(torch.int16).cpu().numpy().view(np.uint16)
+    ids_gpu = tab.global_ids(wl.tokens, wl.seg_start).cpu().numpy()
+    hits = torch.zeros(1, dtype=torch.int64, device=dev)
+    wl.forward(hits)  # the timed call: fused forward into the residual, slots out
+    torch.cuda.synchronize()
+    slots_gpu = wl.slots.cpu().numpy()
+    res_after = wl.out[sample_dev].view(torch.int16).cpu().numpy().view(np.uint16)
+    grad_gpu = torch.empty(R, dim, dtype=torch.float32, device=dev)
+    st = lib.engram_backward(wl.slots.data_ptr(), T, nh, hpn, wl.mode, wl.dout.data_ptr(), dim, R,
+                             grad_gpu.data_ptr(), wl.ws.data_ptr(), wl.ws_bytes, wl.stream)
+    L.check(st, "engram_backward")
+    p_gpu = wl.rows_var.detach().clone()
+    m_gpu, v_gpu = torch.zeros_like(p_gpu), torch.zeros_like(p_gpu)
+    st = lib.engram_adam_step(p_gpu.data_ptr(), grad_gpu.data_ptr(), m_gpu.data_ptr(), v_gpu.data_ptr(),
+                              wl.p0.data_ptr(), p_gpu.numel(), 1, wl.lr, 0.9, 0.999, 1e-8, wl.reg_scale, wl.stream)
+    L.check(st, "engram_adam_step")
+    torch.cuda.synchronize()
+
+    # the oracle on the host
+    toks = wl.tokens.cpu().numpy()
+    ss = wl.seg_start.cpu().numpy()
+    ids_ref = O.hash_ids(toks, tab.ngram_size, tab.heads_per_ngram, tab.layer_multipliers, tab.head_vocab_sizes,
+                         tab.head_offsets, tab.eos_token_id, seg_start=ss)
+    ov_ids = wl.ov_ids.cpu().numpy()
+    k = np.searchsorted(ov_ids, ids_ref)
+    k_c = np.minimum(k, R - 1)
+    slots_ref = np.where((k < R) & (ov_ids[k_c] == ids_ref), k_c, -1).astype(np.int32)
+    # the sampled positions' rows, copied back from the resident table, as the reference's raw 136-byte rows
+    s_ids = ids_ref[sample.numpy()]
+    uniq, local = np.unique(s_ids, return_inverse=True)
+    local = local.reshape(s_ids.shape).astype(np.int32)
+    stride = tab.row_stride
+    resident = tab.rows.view(tab.n_rows, stride)[torch.from_numpy(uniq.astype(np.int64)).to(dev)].cpu().numpy()
+    raw = np.concatenate([resident[:, 128:136], resident[:, 0:128]], axis=1)  # [d|scales_h|scales_l][qs]
+    pack_ok = bool(np.array_equal(O.pack(O.FMT_IQ4_XS, dim, raw), resident))
+    pos_in = np.searchsorted(uniq, ov_ids)
+    pos_c = np.minimum(pos_in, len(uniq) - 1)
+    ov_local = np.where(uniq[pos_c] == ov_ids, pos_c, len(uniq) + np.arange(R)).astype(np.int32)
+    rows_host = wl.rows_var.detach().cpu().numpy()
+    out_ref, _ = O.forward(O.FMT_IQ4_XS, dim, raw, local, hpn, rows_host, ov_local, O.MODE_PAIRSUM_ADD_BF16,
+                           residual=res_before)
+    dout_host = wl.dout.view(torch.int16).cpu().numpy().view(np.uint16)
+    g_ref = O.backward(slots_ref, hpn, dout_host, dim, R, O.MODE_PAIRSUM_ADD_BF16)
+    p_ref, m_ref, v_ref = rows_host.copy(), np.zeros_like(rows_host), np.zeros_like(rows_host)
+    O.adam_(p_ref, g_ref, m_ref, v_ref, 1, wl.lr, p0=wl.p0.cpu().numpy(), reg_scale=np.float32(wl.reg_scale))
+
+    def diff(a, b):
+        return int(np.count_nonzero(np.asarray(a).view(np.uint32 if np.asarray(a).itemsize == 4 else np.uint16)
+                                    != np.asarray(b).view(np.uint32 if np.asarray(b).itemsize == 4 else np.uint16)))
+
+    p_got = p_gpu.cpu().numpy()
+    norm = np.linalg.norm(p_ref, axis=1, keepdims=True)
+    rel = float((np.abs(p_got - p_ref) / np.maximum(norm, 1e-30)).max()) if R else 0.0
+    read = slots_ref[sample.numpy()] < 0  # heads whose table row the forward dequantised
+    big = s_ids >= (1 << 28)
+    mism = {"ids": diff(ids_gpu, ids_ref), "slots": diff(slots_gpu, slots_ref),
+            "residual": diff(res_after, out_ref), "row_gradients": diff(grad_gpu.cpu().numpy(), g_ref),
+            "adam_rows": diff(p_got, p_ref), "adam_m": diff(m_gpu.cpu().numpy(), m_ref),
+            "adam_v": diff(v_gpu.cpu().numpy(), v_ref), "resident_layout": 0 if pack_ok else 1}
+    return {
+        "checked": {"ids": int(ids_ref.size), "slots": int(slots_ref.size), "residual_values": int(out_ref.size),
+                    "residual_positions": int(n_sample), "row_gradient_values": int(g_ref.size),
+                    "adam_values": int(p_ref.size),
+                    "table_rows_dequantised": int(read.sum()),
+                    "table_rows_above_2^28": int((read & big).sum()),
+                    "max_resident_byte_offset": int(int(s_ids[read].max()) * stride) if read.any() else 0},
+        "mismatches": mism, "all_bit_exact": not any(mism.values()),
+        "adam_max_abs_err_rel_row_norm": rel, "tolerance_rel_row_norm": 1e-5, "within_tolerance": rel <= 1e-5,
+        "oracle": "oracle/engram_oracle.c (C restatement of the reference path), host threads", "seconds":
+            round(time.perf_counter() - t_begin, 2)}
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -507,16 +614,13 @@ def run_reference(args, cfg, rank):
     per_step_budget = max(0.02, 150.0 / max(1, args.steps + args.warmup))
     frac = min(1.0, per_step_budget / max(base["t_step"], 1e-9))
     T_s = base["T_s"]
-    pos_frac = frac * T_full / T_s  # fraction of the oracle's sample batch to run per step
+    # each step runs the whole sample batch (T_s positions: the unit the oracle call takes) and scales its
+    # time by T_full / T_s; the Adam sample is the fraction `frac` of the overlay rows, scaled by R / rows
+    scale_fb = T_full / T_s
     times = []
     for k in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        if pos_frac >= 1.0:
-            base["fwd_bwd"]()
-            scale_fb = T_full / T_s
-        else:
-            base["fwd_bwd"]()  # the sample batch is the smallest unit the oracle call takes
-            scale_fb = T_full / T_s
+        base["fwd_bwd"]()
         t_fb = time.perf_counter() - t0
         t1 = time.perf_counter()
         nrows = max(1, int(base["R"] * min(1.0, frac)))
@@ -535,8 +639,9 @@ def run_reference(args, cfg, rank):
         "config": config_json(cfg, args),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": base["threads"], "kind": "port",
                          "sample": f"oracle (C restatement, OpenMP {base['threads']} threads of {cores}) on "
-                                   f"{base['T_s']} positions x 16 rows per step (extrapolated to {T_full}), Adam over "
-                                   f"the sampled overlay rows (scaled to R={cfg['R']}); table slice {base['n_rows']} rows"},
+                                   f"{base['T_s']} positions x 16 rows per step, time x{scale_fb:.0f} (extrapolated "
+                                   f"to {T_full} positions), Adam over {max(1, int(base['R'] * frac))} of the overlay "
+                                   f"rows, time scaled to R={cfg['R']}; table slice {base['n_rows']} rows"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -746,6 +851,9 @@ def main():
     ddist = dist if world > 1 else None
     nbytes = wl.algorithmic_bytes()
     step_bytes = nbytes["fwd"] + nbytes["bwd"] + nbytes["adam"]
+    parity = None
+    if world == 1 and not args.no_check:
+        parity = parity_check(wl)
 
     K = args.steps
     with ClockSampler(local) as clk:
@@ -802,6 +910,8 @@ def main():
             "clocks": clk.summary(),
             "e2e": e2e,
         }
+        if parity is not None:
+            line["parity"] = parity
         if row_sharded is not None:
             line["row_sharded"] = row_sharded
         if world == 1 and not args.no_cpu_baseline:

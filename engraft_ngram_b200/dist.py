@@ -14,8 +14,25 @@ single-process step, W>1 sums the per-rank gradients in rank order.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
+
+
+def symmetric_memory():
+    """torch's symmetric-memory module, with NVLink multicast turned off.
+
+    The kernels of this package read and write peer buffers with plain loads,
+    cp.async and plain stores only; none issues a multicast operation.  With
+    TORCH_SYMM_MEM_DISABLE_MULTICAST=1 torch maps each buffer into the other
+    ranks' processes without binding it to an NVLink multicast object, so a
+    rank that ends while it holds such a buffer leaves no multicast object
+    behind for the other GPUs.  The switch is set before every allocation
+    this package makes, so it holds whichever allocation comes first."""
+    os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
+    import torch.distributed._symmetric_memory as symm
+    return symm
 
 
 def shard_bounds(R: int, world: int, rank: int) -> tuple[int, int]:
@@ -119,7 +136,7 @@ class PeerRows:
     another GPU."""
 
     def __init__(self, R: int, dim: int, device, group=None):
-        import torch.distributed._symmetric_memory as symm
+        symm = symmetric_memory()
         if dim % 4:
             raise ValueError("PeerRows needs dim % 4 == 0 (16-byte row pieces)")
         self.group = group if group is not None else dist.group.WORLD

@@ -300,7 +300,8 @@ class PushStage:
 
     def __init__(self, table: "ShardedTable", n_tokens_max: int, group=None, max_blocks: int = 0):
         import torch.distributed as dist
-        import torch.distributed._symmetric_memory as symm
+        from .dist import symmetric_memory
+        symm = symmetric_memory()
         group = group if group is not None else dist.group.WORLD
         if dist.get_world_size(group) != table.world or dist.get_rank(group) != table.rank:
             raise ValueError("the group's ranks must be the table's ranks")
@@ -456,7 +457,8 @@ def peer_shard_buffer(n_rows: int, fmt: int, dim: int, device, group=None):
     every rank's buffer address in this process (for ShardedTable's
     peer_ptrs).  A collective: every rank of the group calls it."""
     import torch.distributed as dist
-    import torch.distributed._symmetric_memory as symm
+    from .dist import symmetric_memory
+    symm = symmetric_memory()
     group = group if group is not None else dist.group.WORLD
     world = dist.get_world_size(group)
     stride = int(L.load().engram_row_stride(fmt, dim))

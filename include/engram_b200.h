@@ -2,7 +2,8 @@
  * engram_b200.h -- C ABI of the B200 (sm_100a) Engram/PLE table path.
  *
  * The reference (fulvian/engraft-ngram) is Python; the FFI it would bind for
- * this path is ctypes (INTEGRATION.md shows the stub).  Every entry point:
+ * this path is ctypes (engraft_ngram_b200/_lib.py is that binding).  Every
+ * entry point:
  *   - takes plain pointers and sizes (device pointers unless noted "host");
  *   - is enqueued on the caller's CUDA stream (`stream`, a cudaStream_t; NULL =
  *     the legacy default stream), makes no host synchronisation and allocates
@@ -342,7 +343,10 @@ ENGRAM_API int engram_backward(const int32_t* slots, int64_t n, int32_t n_heads,
  * ENGRAM_ERR_WORKSPACE and launch nothing (about n*n_heads <= 500,000 entries
  * with R <= 500,000 rows fits).  The first call on a device looks up the
  * array's device address with that device current, so make that first call
- * before any stream capture.  All calls share the array: two calls whose
+ * before any stream capture.  The address is kept for the life of the
+ * process: cudaDeviceReset on that device ends the context holding the array,
+ * and this entry point must not be called on that device afterwards.  All
+ * calls share the array: two calls whose
  * kernels overlap on the GPU (different streams, or different host threads on
  * one device) race and corrupt each other's results, so serialise them.
  * Nothing in the array needs to start at zero: each call writes every scratch

@@ -19,13 +19,39 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+# Every rank runs with NVLS off in NCCL and with torch's symmetric memory mapped
+# without an NVLink multicast object; no kernel here waits on another GPU, and
+# the process group's short timeout ends a rank whose peer stops answering.
+RANK_ENV = dict(MASTER_ADDR="127.0.0.1", NCCL_NVLS_ENABLE="0", TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
+PG_TIMEOUT_S = 60
+
+
+def _run_ranks(target, world: int = 2) -> dict:
+    """Runs target(rank, world, port, out) in `world` spawned processes and
+    returns out.  A rank is never killed: each one ends by itself, at the
+    latest when a collective of its process group times out."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, out), daemon=True) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=20 * PG_TIMEOUT_S)
+    alive = [p.pid for p in procs if p.is_alive()]
+    assert not alive, f"ranks still running after {20 * PG_TIMEOUT_S} s: {alive}"
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return dict(out)
+
+
 def _peer_vs_nccl(rank: int, world: int, port: int, out) -> None:
     import torch.distributed as dist
     from datetime import timedelta
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(RANK_ENV, MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=PG_TIMEOUT_S), device_id=dev)
     try:
         import engraft_ngram_b200 as eb
         from engraft_ngram_b200 import _lib as L
@@ -71,20 +97,7 @@ def test_peer_exchange_matches_nccl_collectives_on_two_ranks():
     """Two ranks: backward into the owners' buffers + the owner step equal the
     dense backward + NCCL reduce-scatter + Adam + all-gather bit for bit (a
     two-term sum does not depend on order)."""
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    out = ctx.Manager().dict()
-    port = _free_port()
-    procs = [ctx.Process(target=_peer_vs_nccl, args=(r, 2, port, out)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    assert dict(out) == {0: True, 1: True}
+    assert _run_ranks(_peer_vs_nccl) == {0: True, 1: True}
 
 
 def _sharded_staging(rank: int, world: int, port: int, out) -> None:
@@ -95,10 +108,10 @@ def _sharded_staging(rank: int, world: int, port: int, out) -> None:
     import ctypes as C
     import torch.distributed as dist
     from datetime import timedelta
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(RANK_ENV, MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=PG_TIMEOUT_S), device_id=dev)
     try:
         import engraft_ngram_b200 as eb
         from engraft_ngram_b200 import _lib as L
@@ -169,20 +182,7 @@ def test_row_sharded_staging_matches_resident_table_on_two_ranks():
     """Two ranks, table row-sharded in symmetric memory: push-staged,
     pull-staged and in-place sharded forwards equal the resident-table forward
     bit for bit, over three pipelined batches."""
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    out = ctx.Manager().dict()
-    port = _free_port()
-    procs = [ctx.Process(target=_sharded_staging, args=(r, 2, port, out)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    assert dict(out) == {0: True, 1: True}
+    assert _run_ranks(_sharded_staging) == {0: True, 1: True}
 
 
 def _autograd_peer(rank: int, world: int, port: int, out) -> None:
@@ -192,10 +192,10 @@ def _autograd_peer(rank: int, world: int, port: int, out) -> None:
     the hit counts agree bit for bit."""
     import torch.distributed as dist
     from datetime import timedelta
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(RANK_ENV, MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=PG_TIMEOUT_S), device_id=dev)
     try:
         import engraft_ngram_b200 as eb
         from engraft_ngram_b200 import _lib as L
@@ -257,17 +257,4 @@ def _autograd_peer(rank: int, world: int, port: int, out) -> None:
 def test_autograd_through_peer_rows_matches_allreduce_on_two_ranks():
     """Two ranks, public autograd API: PeerRows.attach + PeerAdam equals the
     NCCL all-reduce of the row gradients + OverlayAdam bit for bit."""
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    out = ctx.Manager().dict()
-    port = _free_port()
-    procs = [ctx.Process(target=_autograd_peer, args=(r, 2, port, out)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    assert dict(out) == {0: True, 1: True}
+    assert _run_ranks(_autograd_peer) == {0: True, 1: True}

@@ -76,7 +76,11 @@ def parse():
                          "gradients stored into their owners (PeerRows.attach) + PeerAdam")
     ap.add_argument("--no-sharded-line", action="store_true",
                     help="N>1: skip the second measurement with the table row-sharded")
-    ap.add_argument("--stage", choices=["push", "pull", "off"], default="pull",
+    ap.add_argument("--layout", choices=["sharded", "replicated"], default="sharded",
+                    help="N>1, config 5: the table row-sharded across the ranks (owner = id mod N; each rank's "
+                         "distinct remote rows planned two batches ahead and exchanged by NCCL all-to-all on a side "
+                         "stream), or replicated on every rank; the other layout is measured beside it")
+    ap.add_argument("--stage", choices=["exchange", "push", "pull", "off"], default="exchange",
                     help="--shard, peer reads: copy the next step's rows of other ranks on a side stream while the "
                          "current step runs (ShardedTable.prefetch), so the forward reads every row locally; push: "
                          "the owners store them into the requesters' stages; pull: each rank loads its own")
@@ -140,15 +144,23 @@ class Workload:
         if cfg.get("shard"):
             from engraft_ngram_b200.shard import ShardedTable, local_exchange, nccl_exchange, peer_shard_buffer
             n_local = (cfg["rows"] - rank + world - 1) // world
-            if cfg.get("shard_exchange", "peer") == "peer" and world > 1:
+            if cfg.get("stage") == "exchange":
+                # this rank's shard in plain local memory; the rows of other ranks arrive deduplicated through
+                # NCCL all-to-alls planned two batches ahead (ShardedTable.enable_exchange_staging)
+                rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device)
+                self.shard = ShardedTable(rows, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"])
+                self.shard.enable_exchange_staging(cfg["seqs"] * cfg["seq_len"])
+                self.exchange = None
+                self.stage = "exchange"
+            elif cfg.get("shard_exchange", "peer") == "peer" and world > 1:
                 # every rank's shard in symmetric memory: the forward reads rows in place over NVLink
                 buf, ptrs, self._shard_handle = peer_shard_buffer(cfg["rows"], fmt, self.dim, device)
                 rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device, out=buf)
                 self.shard = ShardedTable(buf, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"],
                                           peer_ptrs=ptrs)
                 self.exchange = None
-                self.stage = cfg.get("stage", "push") != "off"
-                if cfg.get("stage", "push") == "push":
+                self.stage = cfg.get("stage", "push") if cfg.get("stage", "push") in ("push", "pull") else False
+                if self.stage == "push":
                     self.shard.enable_push_staging(cfg["seqs"] * cfg["seq_len"], max_blocks=self.stage_blocks)
             else:
                 rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device)
@@ -172,7 +184,9 @@ class Workload:
         self.seg_start = (torch.arange(self.T, device=device, dtype=torch.int32) // cfg["seq_len"]) * cfg["seq_len"]
         # staged sharded reads: step k+1's rows are copied while step k runs; the two steps' batches live in two
         # buffers (same tokens here), so each copy is for a distinct batch
-        self.tok_bufs = [self.tokens, self.tokens.clone()] if self.stage else [self.tokens]
+        # (the exchange is planned two batches ahead, so three batches are in flight: three buffers)
+        self.depth = 2 if self.stage == "exchange" else 1
+        self.tok_bufs = ([self.tokens] + [self.tokens.clone() for _ in range(self.depth)]) if self.stage else [self.tokens]
         self.k = 0
         self.positions = None
         if self.decode:  # uniform histories; output rows are the sequences' last tokens
@@ -198,13 +212,15 @@ class Workload:
             self.ov_ids = torch.zeros(0, dtype=torch.int32, device=device)
         self.R = int(self.ov_ids.numel())
         self.omap = eb.OverlayMap(self.ov_ids, device)
-        self.remote_rows = 0  # row-sharded: rows per step this rank copies from other ranks (overlay heads skip)
+        self.remote_rows = 0  # row-sharded: (position, head) pairs per step served by other ranks (overlay heads skip)
+        self.remote_distinct = 0  # ... and the distinct rows among them (what the exchange moves)
         if self.shard is not None and world > 1:
             ids = self.shard.global_ids(self.tokens, self.seg_start).reshape(-1)
             remote = (ids % world) != rank
             if self.R:
                 remote &= ~torch.isin(ids, self.ov_ids)
             self.remote_rows = int(remote.sum())
+            self.remote_distinct = int(torch.unique(ids[remote]).numel())
         if self.shard is not None:  # true rows live on their owners; start from seeded values instead
             gp = torch.Generator(device=device)
             gp.manual_seed(seed * 1000 + 5)
@@ -261,7 +277,9 @@ class Workload:
         copy and the barrier that completes it on every rank)."""
         import torch
         cur = torch.cuda.current_stream(self.dev)
-        if self.shard.push is not None:
+        if self.shard.xstage is not None:
+            cur.wait_stream(self.shard.xstage.side)
+        elif self.shard.push is not None:
             self.shard.push.join(cur)
         elif self.shard._side is not None:
             cur.wait_stream(self.shard._side)
@@ -270,10 +288,11 @@ class Workload:
     def forward(self, hit_count=None):
         import ctypes as C
         if self.shard is not None:
-            tok = self.tok_bufs[self.k % len(self.tok_bufs)]
-            if self.stage:  # the next step's rows of other ranks, copied while this step runs
-                self.shard.prefetch(self.tok_bufs[(self.k + 1) % 2], self.seg_start, max_blocks=self.stage_blocks,
-                                    omap=self.omap)
+            nb = len(self.tok_bufs)
+            tok = self.tok_bufs[self.k % nb]
+            if self.stage:  # a later step's rows of other ranks, staged while this step runs
+                self.shard.prefetch(self.tok_bufs[(self.k + self.depth) % nb], self.seg_start,
+                                    max_blocks=self.stage_blocks, omap=self.omap)
             self.k += 1
             self.shard.forward(tok, self.seg_start, self.omap, self.rows_var, self.out, self.mode,
                                self.exchange, slots_out=self.slots if self.R else None, hit_count=hit_count)
@@ -787,6 +806,9 @@ def run_ple(args, device):
 def shard_text(cfg):
     if not cfg.get("shard"):
         return ""
+    if cfg.get("stage") == "exchange":
+        return ("+row-sharded table (id mod N; each rank's distinct rows of other ranks planned two batches ahead "
+                "and exchanged by NCCL all-to-all on a side stream; local rows read in place)")
     if cfg.get("shard_exchange", "peer") != "peer":
         return "+row-sharded table (id mod N, NCCL all-to-all of ids and rows)"
     if cfg.get("stage", "push") == "push":
@@ -826,7 +848,9 @@ def main():
         cfg["rows"] = args.table_rows
     if args.seqs:
         cfg["seqs"] = args.seqs
-    cfg["shard"] = bool(args.shard)
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    # config 5 at N > 1: the north star's layout (the table row-sharded, id mod N) is the headline by default
+    cfg["shard"] = bool(args.shard) or (args.config == "cfg5" and world_env > 1 and args.layout == "sharded")
     cfg["exchange"] = args.exchange
     cfg["shard_exchange"] = args.shard_exchange
     cfg["stage"] = args.stage
@@ -865,26 +889,30 @@ def main():
     if not args.no_e2e and not wl.decode:
         e2e = run_e2e(wl, args, device, ddist, world)
 
-    row_sharded = None
-    if world > 1 and not cfg["shard"] and args.config == "cfg5" and not args.no_sharded_line:
-        # the same step with the table row-sharded (id mod N), measured in the same run
-        del wl
+    layout = None
+    if world > 1 and args.config == "cfg5":
+        layout = {"headline": "row_sharded" if cfg["shard"] else "replicated"}
+        if cfg["shard"]:
+            layout["row_sharded"] = sharded_stats(wl, ms, fwd_ms, bwd_ms, ddist, world, device)
+    if world > 1 and args.config == "cfg5" and not args.no_sharded_line:
+        # the other layout, measured in the same run on the same batches; the two forwards are compared bit
+        # for bit on this rank's batch (the overlay rows of the replicated run, the same residual)
         torch.cuda.synchronize()
-        torch.cuda.empty_cache()
-        cfg2 = dict(cfg, shard=True, shard_exchange="peer", stage="pull")
+        cfg2 = dict(cfg, shard=not cfg["shard"], stage="exchange")
         wl2 = Workload(cfg2, rank, world, args.seed, device)
+        sh, rep = (wl, wl2) if cfg["shard"] else (wl2, wl)
+        layout["sharded_vs_resident_forward"] = compare_layouts(sh, rep, ddist, device)
+        if not cfg["shard"]:
+            del wl
         ms2, fwd2, bwd2, _ = time_steps(wl2, K, args.warmup, ddist)
-        row_sharded = {"value": 16 * wl2.n_out * world / (ms2 * 1e-3), "unit": "rows/s", "ms_per_step": ms2,
-                       "phase_ms": {"forward": fwd2, "backward": bwd2, "optimizer_and_exchange": ms2 - fwd2 - bwd2},
-                       "parallelism": f"dp{world}" + shard_text(cfg2),
-                       "table_bytes_per_gpu": int(wl2.shard.n_local * wl2.shard.stride)}
-        # what crossed NVLink for the table: the other ranks' rows this rank read (max over ranks)
-        rr = torch.tensor([wl2.remote_rows], dtype=torch.int64, device=device)
-        dist.all_reduce(rr, op=dist.ReduceOp.MAX)
-        nv_bytes = int(rr[0]) * wl2.shard.stride
-        row_sharded["nvlink"] = {"remote_rows_per_step": int(rr[0]), "bytes_per_step": nv_bytes,
-                                 "achieved_gbps": nv_bytes / (ms2 * 1e-3) / 1e9, "peer_copy_gbps": 770.0,
-                                 "frac_of_peer_copy": nv_bytes / (ms2 * 1e-3) / 1e9 / 770.0}
+        side = {"value": 16 * wl2.n_out * world / (ms2 * 1e-3), "unit": "rows/s", "ms_per_step": ms2,
+                "phase_ms": {"forward": fwd2, "backward": bwd2, "optimizer_and_exchange": ms2 - fwd2 - bwd2},
+                "parallelism": f"dp{world}" + shard_text(cfg2)}
+        if cfg2["shard"]:
+            side.update(sharded_stats(wl2, ms2, fwd2, bwd2, ddist, world, device))
+            layout["row_sharded"] = side
+        else:
+            layout["replicated"] = side
 
     if rank == 0:
         peak, peak_kind = measured_peak_gbs()
@@ -912,8 +940,8 @@ def main():
         }
         if parity is not None:
             line["parity"] = parity
-        if row_sharded is not None:
-            line["row_sharded"] = row_sharded
+        if layout is not None:
+            line["layouts"] = layout
         if world == 1 and not args.no_cpu_baseline:
             try:
                 b = cpu_oracle_step_time(cfg, args.seed)
@@ -930,6 +958,50 @@ def main():
     if ddist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def sharded_stats(wl, ms, fwd_ms, bwd_ms, ddist, world, device):
+    """What the row-sharded table moves per step (max over ranks): the (position,
+    head) pairs served by other ranks, the distinct rows among them (the rows
+    the exchange carries) and their bytes over NVLink."""
+    import torch
+    rr = torch.tensor([wl.remote_rows, wl.remote_distinct], dtype=torch.int64, device=device)
+    ddist.all_reduce(rr, op=ddist.ReduceOp.MAX)
+    nv_bytes = int(rr[1]) * wl.shard.stride
+    return {"table_bytes_per_gpu": int(wl.shard.n_local * wl.shard.stride),
+            "nvlink": {"remote_pairs_per_step": int(rr[0]), "distinct_remote_rows_per_step": int(rr[1]),
+                       "dedup_factor": int(rr[0]) / max(int(rr[1]), 1), "bytes_per_step": nv_bytes,
+                       "achieved_gbps": nv_bytes / (ms * 1e-3) / 1e9, "peer_copy_gbps": 770.0,
+                       "frac_of_peer_copy": nv_bytes / (ms * 1e-3) / 1e9 / 770.0}}
+
+
+def compare_layouts(sh, rep, ddist, device):
+    """The row-sharded forward (this rank's shard + the deduplicated exchange)
+    against the forward over the replicated resident table, on this rank's
+    batch, with the replicated run's overlay rows and the same residual:
+    bf16 bits and slots compared on the device (mismatches summed over ranks)."""
+    import ctypes as C
+    import torch
+    L = rep.L
+    res0 = rep.out.clone()
+    a, b = res0.clone(), res0.clone()
+    sa = torch.empty_like(rep.slots)
+    sb = torch.empty_like(rep.slots)
+    ha = torch.zeros(1, dtype=torch.int64, device=device)
+    hb = torch.zeros(1, dtype=torch.int64, device=device)
+    tok = rep.tokens.clone()
+    sh.shard.forward(tok, rep.seg_start, rep.omap, rep.rows_var, a, rep.mode, slots_out=sa, hit_count=ha)
+    ov = rep.omap.descriptor(rep.rows_var)
+    st = L.load().engram_forward(C.byref(rep.table.ctable), C.byref(ov), tok.data_ptr(), rep.seg_start.data_ptr(), 0,
+                                 rep.T, rep.mode, b.data_ptr(), None, sb.data_ptr(), hb.data_ptr(), rep.stream)
+    L.check(st, "engram_forward")
+    mism = torch.stack([(a.view(torch.int16) != b.view(torch.int16)).sum(), (sa != sb).sum(), (ha != hb).sum()])
+    checked = torch.tensor([a.numel(), sa.numel()], dtype=torch.int64, device=device)
+    ddist.all_reduce(mism)
+    ddist.all_reduce(checked)
+    del res0
+    return {"residual_values": int(checked[0]), "slots": int(checked[1]), "mismatches": int(mism.sum()),
+            "bit_exact": int(mism.sum()) == 0}
 
 
 def time_steps(wl, K, warmup, ddist):
@@ -1009,10 +1081,10 @@ def run_e2e(wl, args, device, ddist, world):
 
     def one():
         residual = wl.out.detach()
-        if wl.stage:
-            if not pending:
+        if wl.stage:  # this step's inputs were copied and prefetched wl.depth steps ago
+            while len(pending) < wl.depth:
                 pending.append((tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True)))
-            tok, ss = pending.pop()
+            tok, ss = pending.pop(0)
             nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
             wl.table.prefetch(nxt[0], nxt[1], max_blocks=wl.stage_blocks, omap=wl.omap)
             pending.append(nxt)

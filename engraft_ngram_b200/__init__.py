@@ -16,8 +16,8 @@ from __future__ import annotations
 from . import _lib
 from ._lib import FMT_F32, FMT_IQ4_NL, FMT_IQ4_XS, MODE_CONCAT_F32, MODE_PAIRSUM_ADD_BF16
 from .optim import OverlayAdam, reg_scale
-from .overlay import (OverlayEmb, OverlayMap, engram_embed, engram_embed_at, engram_residual_add, row_gradients,
-                      seg_starts_from_segment_ids)
+from .overlay import (OverlayEmb, OverlayMap, engram_embed, engram_embed_at, engram_residual_add, forget_overlay_map,
+                      row_gradients, seg_starts_from_segment_ids)
 from .patch import (install, install_ple, install_rowsets, install_scan, uninstall, uninstall_ple, uninstall_rowsets,
                     uninstall_scan)
 from .ple import ple_forward
@@ -33,6 +33,7 @@ __all__ = [
     "build_rows_var", "sum_overlays", "write_merged_pleo", "read_pleo",
     "write_pleo", "read_pleo_device", "FMT_F32", "FMT_IQ4_NL", "FMT_IQ4_XS", "MODE_CONCAT_F32",
     "MODE_PAIRSUM_ADD_BF16", "load_library", "scan_hits", "ple_forward", "install_ple", "uninstall_ple",
+    "forget_overlay_map",
 ]
 
 

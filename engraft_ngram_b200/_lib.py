@@ -81,6 +81,13 @@ SIGNATURES = {
                                           C.c_void_p, C.c_void_p, C.c_void_p]),
     "engram_shard_requests": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p,
                                         C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_shard_plan": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
+                                    C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_int64,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "engram_forward_exchanged": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
+                                           C.c_int64, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
+                                           C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_void_p]),
     "engram_shard_gather": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p,
                                       C.c_void_p]),
     "engram_gather_rows": (C.c_int, [C.POINTER(EngramTable), C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),

@@ -41,6 +41,12 @@ struct PosMap {
     // (engram_stage_sharded); rows owned by `rank` are still read in place
     const uint8_t* stage = nullptr;
     uint32_t rank = 0;
+    // nullable (exchanged reads): this rank's own shard, read in place; the
+    // rows of other ranks sit in `stage`, the row of head h of output row i at
+    // stage + srix[i * nh + h] * stride (engram_shard_plan's row_index)
+    const uint8_t* local = nullptr;
+    const int32_t* srix = nullptr;
+    __device__ __host__ __forceinline__ bool sharded() const { return shard != nullptr || local != nullptr; }
     // Owner rank o of global row r and its row l in that rank's shard.
     __device__ __forceinline__ void owner_of(int32_t r, uint32_t& o, uint32_t& l) const {
         if (wshift >= 0) {
@@ -55,10 +61,18 @@ struct PosMap {
     // staged copy, or the row in its owner's shard.
     __device__ __forceinline__ const uint8_t* row_ptr(const uint8_t* rows, int64_t stride, int32_t r, int64_t i,
                                                       int h, int nh) const {
-        if (shard == nullptr) return rows + (int64_t)r * stride;
+        if (!sharded()) return rows + (int64_t)r * stride;
         uint32_t o, l;
         owner_of(r, o, l);
-        if (stage != nullptr && o != rank) return stage + (i * nh + h) * stride;
+        if (o != rank) {
+            if (srix != nullptr) {  // an entry the plan did not request reads row 0 (never used)
+                const int32_t k = __ldg(srix + i * nh + h);
+                return stage + (int64_t)(k < 0 ? 0 : k) * stride;
+            }
+            if (stage != nullptr) return stage + (i * nh + h) * stride;
+        } else if (local != nullptr) {
+            return local + (int64_t)l * stride;
+        }
         const uint8_t* base =
             reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(shard) + o));
         return base + (int64_t)l * stride;
@@ -926,7 +940,7 @@ template <int FMT, int DIM>
 void launch_pairsum_fixed(const engram_table& T, const engram_overlay& OV, const int32_t* tokens,
                           const int32_t* seg_start, PosMap pm, int64_t n, __nv_bfloat16* out, int32_t* ids_out,
                           int32_t* slots_out, unsigned long long* hit_count, cudaStream_t s) {
-    if (pm.shard) launch_pairsum_fixed_k<FMT, DIM, true>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out,
+    if (pm.sharded()) launch_pairsum_fixed_k<FMT, DIM, true>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out,
                                                          hit_count, s);
     else launch_pairsum_fixed_k<FMT, DIM, false>(T, OV, tokens, seg_start, pm, n, out, ids_out, slots_out,
                                                  hit_count, s);
@@ -1162,4 +1176,25 @@ extern "C" int engram_gather_rows(const engram_table* t, const int32_t* ids, int
     }
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int engram_forward_exchanged(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                        const int32_t* seg_start, int64_t t0, int64_t n, const void* local_rows,
+                                        int32_t world, int32_t rank, const void* recv_rows, const int32_t* row_index,
+                                        int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                                        int64_t* hit_count, void* stream) {
+    if (!t || t0 < 0 || world < 1 || world > 1024 || rank < 0 || rank >= world) return ENGRAM_ERR_ARG;
+    if (n > 0 && (!local_rows || !aligned16(local_rows))) return ENGRAM_ERR_ARG;
+    if (n > 0 && world > 1 && (!recv_rows || !row_index || !aligned16(recv_rows))) return ENGRAM_ERR_ARG;
+    if (t->row_stride % 16) return ENGRAM_ERR_FORMAT;
+    PosMap pm{t0, nullptr, 0, nullptr};
+    pm.world = (uint32_t)world;
+    pm.rank = (uint32_t)rank;
+    pm.wshift = (world & (world - 1)) == 0 ? __builtin_ctz((unsigned)world) : -1;
+    pm.local = static_cast<const uint8_t*>(local_rows);
+    if (world > 1) {
+        pm.stage = static_cast<const uint8_t*>(recv_rows);
+        pm.srix = row_index;
+    }
+    return forward_impl(t, ov, tokens, seg_start, pm, n, mode, out, ids_out, slots_out, hit_count, stream);
 }

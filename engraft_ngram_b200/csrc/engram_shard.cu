@@ -38,6 +38,7 @@ __global__ void k_set_insert(const int32_t* __restrict__ ids, const int32_t* __r
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += stride) {
         if (slots && slots[k] >= 0) continue;
         const int32_t g = ids[k];
+        if (g < 0) continue;  // an entry the plan does not request
         uint32_t pos = set_home(g, capacity);
         for (int64_t probe = 0; probe < capacity; probe++) {
             // a plain read first: repeated ids (Zipf-hot rows) then need no atomic
@@ -131,6 +132,49 @@ __global__ void k_row_index(const int32_t* __restrict__ ids, const int32_t* __re
     }
 }
 
+// The rows a rank reads from other ranks (engram_shard_plan): for each
+// (position, head) of positions t0..t0+n-1, the global id when another rank
+// owns it and the overlay does not serve it, else -1.  One thread per pair.
+__global__ void k_plan_ids(engram_table T, engram_overlay OV, const int32_t* __restrict__ tokens,
+                           const int32_t* __restrict__ seg_start, int64_t t0, int64_t n, int world, int rank,
+                           int32_t* __restrict__ out) {
+    const int nh = T.n_heads;
+    const int64_t total = n * nh;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = k / nh;
+        const int h = (int)(k - i * nh);
+        const int32_t g = hash_row(T, tokens, seg_start, t0 + i, h);
+        const bool remote = (int)((uint32_t)g % (uint32_t)world) != rank;
+        out[k] = (remote && overlay_slot(OV, g) < 0) ? g : -1;
+    }
+}
+
+// row_index[k] = the position of ids[k] in send_ids (its row in the reply), or
+// -1 for an entry not requested (ids[k] < 0); ids and row_index may be the same
+// array (each thread reads its entry before writing it).
+__global__ void k_row_index_inplace(const int32_t* ids, int64_t n, const int32_t* __restrict__ keys,
+                                    const int32_t* __restrict__ vals, int64_t capacity, int32_t* row_index) {
+    const uint32_t mask = (uint32_t)capacity - 1u;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n; k += stride) {
+        const int32_t g = ids[k];
+        int32_t r = -1;
+        if (g >= 0) {
+            uint32_t pos = set_home(g, capacity);
+            for (int64_t probe = 0; probe < capacity; probe++) {
+                const int32_t key = keys[pos];
+                if (key == g) {
+                    r = vals[pos];
+                    break;
+                }
+                if (key == -1) break;
+                pos = (pos + 1u) & mask;
+            }
+        }
+        row_index[k] = r;
+    }
+}
+
 // out[k] = shard row (ids[k] / world); one thread per 16-byte word.
 __global__ void k_shard_gather(const uint8_t* __restrict__ shard, int64_t stride, int64_t n_local,
                                const int32_t* __restrict__ ids, int64_t n, int world, uint8_t* __restrict__ out) {
@@ -179,5 +223,37 @@ extern "C" int engram_shard_gather(const void* shard_rows, int64_t stride, int64
     k_shard_gather<<<grid(n * (stride >> 4)), 256, 0, (cudaStream_t)stream>>>(
         static_cast<const uint8_t*>(shard_rows), stride, n_local, ids, n, world, static_cast<uint8_t*>(out));
     count_launches(1);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int engram_shard_plan(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                 const int32_t* seg_start, int64_t t0, int64_t n, int32_t world, int32_t rank,
+                                 int32_t* set_keys, int32_t* set_vals, int64_t capacity, int32_t* send_ids,
+                                 int64_t* counts, int32_t* row_index, void* stream) {
+    if (!t || t0 < 0 || n < 0 || world < 1 || world > kMaxWorld || rank < 0 || rank >= world) return ENGRAM_ERR_ARG;
+    if (!set_keys || !set_vals || !send_ids || !counts || !row_index) return ENGRAM_ERR_ARG;
+    if (n > 0 && !tokens) return ENGRAM_ERR_ARG;
+    const int64_t entries = n * t->n_heads;
+    if ((capacity & (capacity - 1)) != 0 || capacity < 2 * entries || capacity < 2 || capacity > (1LL << 31))
+        return ENGRAM_ERR_RANGE;
+    engram_overlay OV{nullptr, 0, nullptr, nullptr, 0};
+    if (ov && ov->n_rows > 0) {
+        OV = *ov;
+        if (!OV.map_keys || !OV.map_slots || (OV.capacity & (OV.capacity - 1)) != 0 || OV.capacity < 2 * OV.n_rows)
+            return ENGRAM_ERR_ARG;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(counts);
+    k_set_clear<<<grid(capacity), 256, 0, s>>>(set_keys, capacity, counts, world);
+    int launched = 1;
+    if (entries > 0) {
+        k_plan_ids<<<grid(entries), 256, 0, s>>>(*t, OV, tokens, seg_start, t0, n, world, rank, row_index);
+        k_set_insert<<<grid(entries), 256, 0, s>>>(row_index, nullptr, entries, set_keys, capacity);
+        k_owner_count<<<grid(capacity), 256, 0, s>>>(set_keys, capacity, world, cnt);
+        k_owner_scatter<<<grid(capacity), 256, 0, s>>>(set_keys, set_vals, capacity, world, cnt, cnt + world, send_ids);
+        k_row_index_inplace<<<grid(entries), 256, 0, s>>>(row_index, entries, set_keys, set_vals, capacity, row_index);
+        launched += 5;
+    }
+    count_launches(launched);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }

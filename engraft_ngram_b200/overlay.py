@@ -96,8 +96,9 @@ def _emit(dtable, omap: OverlayMap, rv: torch.Tensor, tokens, seg_start, t0: int
     """One forward launch into `out`: engram_forward on a resident table, or the
     row exchange plus engram_forward_indirect on a row-sharded table."""
     if getattr(dtable, "is_sharded", False):
-        if dtable.exchange is None and dtable.peer_ptrs is None:
-            raise RuntimeError("this ShardedTable has neither peer shards nor a row exchange (set .exchange)")
+        if dtable.exchange is None and dtable.peer_ptrs is None and dtable.xstage is None:
+            raise RuntimeError("this ShardedTable has no way to reach other ranks' rows: set .exchange, give it "
+                               "peer shards or enable exchange staging")
         dtable.forward(tokens, seg_start, omap, rv, out, mode, dtable.exchange, slots_out=slots,
                        hit_count=hit_count, t0=t0, n=n)
         return
@@ -275,21 +276,36 @@ def engram_residual_add(residual: torch.Tensor, dtable: DeviceTable, tokens, row
 _MAP_CACHE: dict = {}
 
 
-def _overlay_map_for(row_map: dict, device) -> OverlayMap:
-    """One device map per (row_map, device); the descent builds row_map once
-    per run (engraft/descend_corpus.py:776).  The entry keeps a reference to
-    the dict and a snapshot of its items, so a mutated or recycled dict is
-    never served a stale map."""
+def _overlay_map_for(row_map, device) -> OverlayMap:
+    """The device map of a reference row_map ({global_id: index}).
+
+    The descent builds row_map once per run and passes the same dict to every
+    step (engraft/descend_corpus.py:776), so one map is built per (dict,
+    device) and found again by the dict's identity and size in O(1): no
+    per-build pass over its R items.  A dict changed in place without a change
+    of size is not detected; after such a change call forget_overlay_map(row_map)
+    (or pass a new dict).  An OverlayMap passed as row_map is used as it is."""
+    if isinstance(row_map, OverlayMap):
+        return row_map
     key = (id(row_map), str(device))
-    snap = tuple(row_map.items())
     hit = _MAP_CACHE.get(key)
-    if hit is not None and hit[0] is row_map and hit[1] == snap:
+    if hit is not None and hit[0] is row_map and hit[1] == len(row_map):
         return hit[2]
     omap = OverlayMap.from_row_map(row_map, device)
     if len(_MAP_CACHE) > 16:
         _MAP_CACHE.pop(next(iter(_MAP_CACHE)))
-    _MAP_CACHE[key] = (row_map, snap, omap)
+    _MAP_CACHE[key] = (row_map, len(row_map), omap)  # holds the dict, so its id is not recycled
     return omap
+
+
+def forget_overlay_map(row_map=None) -> None:
+    """Drops the cached device map of row_map (all cached maps when None), so
+    the next build rebuilds it: needed after a dict is changed in place."""
+    if row_map is None:
+        _MAP_CACHE.clear()
+        return
+    for key in [k for k, v in _MAP_CACHE.items() if v[0] is row_map]:
+        del _MAP_CACHE[key]
 
 
 @dataclasses.dataclass
@@ -300,7 +316,8 @@ class OverlayEmb:
     rows_var's device with rows_var's dtype (float32), shape
     [n_positions-start, n_heads*dim], differentiable in rows_var.  `table` is
     the reference's table object (made resident once per device) or a
-    DeviceTable.  `overlay_cache` is accepted for signature compatibility: the
+    DeviceTable.  `row_map` is the reference's dict (its device map is built
+    once per dict; see forget_overlay_map) or an OverlayMap.  `overlay_cache` is accepted for signature compatibility: the
     fused gather needs no per-fragment cache.  `n_id_hits` / `n_key_hits`
     count the (position, head) pairs served by the overlay, as in the
     reference."""
@@ -332,10 +349,19 @@ class OverlayEmb:
         if not (0 <= start <= n_positions <= len(self.tokens)):
             raise ValueError(f"build: need 0 <= start <= n_positions <= len(tokens), got {start}, {n_positions}")
         omap = _overlay_map_for(self.row_map, dev)
-        toks = torch.as_tensor(np.asarray(self.tokens[:n_positions], dtype=np.int64))
+        if omap.R != self.rows_var.shape[0]:
+            raise ValueError(f"rows_var has {self.rows_var.shape[0]} rows, row_map {omap.R}")
+        toks = self.tokens[:n_positions]
+        if isinstance(toks, torch.Tensor):
+            toks = toks.to(torch.int64)
+        else:
+            toks = torch.from_numpy(np.asarray(toks, dtype=np.int64))
         if toks.numel() and (int(toks.max()) > 2**31 - 1 or int(toks.min()) < -2**31):
             raise ValueError("token id does not fit int32")
-        toks = toks.to(torch.int32).pin_memory().to(dev, non_blocking=True)
+        toks = toks.to(torch.int32)
+        if toks.device.type == "cpu":
+            toks = toks.pin_memory()
+        toks = toks.to(dev, non_blocking=True)
         ss = None
         if self._seg_start is not None:
             if len(self._seg_start) < n_positions:

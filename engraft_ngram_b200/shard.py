@@ -59,6 +59,7 @@ class ShardedTable:
         self._free = []  # _Staged buffers whose forward has been issued
         self._side = None  # the prefetch stream
         self.push = None  # PushStage: owners copy rows into the requesters' stages (enable_push_staging)
+        self.xstage = None  # ExchangeStage: deduplicated rows exchanged ahead of the forward (enable_exchange_staging)
         # addressing constants of the whole table; the rows pointer is replaced per step
         self.ngram_size, self.heads_per_ngram = int(ngram_size), int(heads_per_ngram)
         self.n_heads = (int(ngram_size) - 1) * int(heads_per_ngram)
@@ -139,6 +140,15 @@ class ShardedTable:
             raise RuntimeError("push staging needs the peer shards (peer_ptrs)")
         self.push = PushStage(self, n_tokens_max, group, max_blocks)
 
+    def enable_exchange_staging(self, n_tokens_max: int, exchange=None) -> None:
+        """Make prefetch() plan and exchange the rows of other ranks ahead of the
+        forward, deduplicated, through `exchange` (default NcclRowExchange():
+        NCCL all-to-alls on a process group of their own; LocalRowExchange for
+        emulated ranks).  Prefetching two batches ahead of the forward keeps
+        both the host and the forward from waiting on the exchange (see
+        ExchangeStage).  With NcclRowExchange a collective: every rank calls it."""
+        self.xstage = ExchangeStage(self, n_tokens_max, exchange if exchange is not None else NcclRowExchange())
+
     def prefetch(self, tokens, seg_start=None, t0: int = 0, n: int | None = None, max_blocks: int = 0,
                  stream: torch.cuda.Stream | None = None, omap: OverlayMap | None = None) -> None:
         """Copy the rows of other ranks that forward(tokens, seg_start, ..., t0, n)
@@ -151,14 +161,17 @@ class ShardedTable:
         copied, and a forward with another map reads in place.  Up to two
         prefetches wait at a time; a third drops the oldest.  max_blocks caps the
         copy's grid (0: every SM), leaving SMs to the work it overlaps."""
-        if self.peer_ptrs is None:
-            raise RuntimeError("prefetch needs the peer shards (peer_ptrs)")
         dev = self.device
         tokens = _as_i32(tokens, dev)
         if n is None:
             n = tokens.numel() - t0
         ss = None if seg_start is None else _as_i32(seg_start, dev)
         key = self._key(tokens, ss, t0, n)
+        if self.xstage is not None:
+            self.xstage.prefetch(key, tokens, ss, t0, n, omap)
+            return
+        if self.peer_ptrs is None:
+            raise RuntimeError("prefetch needs the peer shards (peer_ptrs) or exchange staging")
         if self.world == 1:
             return
         if self.push is not None:
@@ -216,6 +229,21 @@ class ShardedTable:
             n = tokens.numel() - t0
         ss = None if seg_start is None else _as_i32(seg_start, dev)
         stream = L.stream_of(dev)
+        if self.xstage is not None:
+            key = self._key(tokens, ss, t0, n)
+            if not self.xstage.has(key):  # not prefetched: plan and exchange now (the host waits for the plan)
+                self.xstage.prefetch(key, tokens, ss, t0, n, omap)
+            b, recv, rix, ready = self.xstage.take(key, omap)
+            cur = torch.cuda.current_stream(dev)
+            cur.wait_event(ready)
+            ov = omap.descriptor(rows_var)
+            st = lib.engram_forward_exchanged(C.byref(self.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(ss), t0, n,
+                                              self.shard.data_ptr(), self.world, self.rank, recv.data_ptr(),
+                                              rix.data_ptr(), mode, out.data_ptr(), None, L.ptr(slots_out),
+                                              L.ptr(hit_count), stream)
+            L.check(st, "engram_forward_exchanged")
+            self.xstage.consumed(b, cur)
+            return out
         if self.peer_ptrs is not None and exchange is None:
             ov = omap.descriptor(rows_var)
             key = self._key(tokens, ss, t0, n)
@@ -401,6 +429,192 @@ class PushStage:
         if self.unbarriered is not None:
             self._barrier()
         stream.wait_stream(self.side)
+
+
+class ExchangeStage:
+    """Row-sharded reads through a deduplicated row exchange, pipelined so that
+    neither the host nor the forward waits for it (ShardedTable.enable_exchange_staging).
+
+    prefetch(batch X), on the table's side stream:
+      1. engram_shard_plan: the distinct ids of X's (position, head) pairs that
+         another rank owns and the overlay does not serve, grouped by owner,
+         the per-owner counts, and each pair's row in the reply (row_index); a
+         Zipf-hot remote row is requested once per batch;
+      2. exchange.gather_counts: every rank's counts (a collective), copied to
+         pinned host memory behind an event;
+      3. the exchange of every batch planned before X and not yet exchanged:
+         the host reads that batch's counts (planned a step earlier when the
+         caller prefetches two batches ahead, so the event has long completed),
+         and exchange.rows sends the ids to their owners and brings their rows
+         back (collectives) into a receive buffer of the batch's own.
+    forward(X) exchanges X first if that has not happened (the host then waits
+    for X's counts), makes the current stream wait for X's rows and runs
+    engram_forward_exchanged: rows this rank owns read in place, the others
+    from the receive buffer.  Every rank calls prefetch and forward in the same
+    order with the same t0 and n (the collectives follow that order).  Up to
+    two batches wait at a time (three buffer sets: read, exchanged, planned); a
+    third prefetch drops the oldest."""
+
+    SETS = 3
+
+    def __init__(self, table: "ShardedTable", n_tokens_max: int, exchange):
+        self.table, self.exchange = table, exchange
+        dev = table.device
+        self.n_max = int(n_tokens_max)
+        entries = max(self.n_max * table.n_heads, 1)
+        self.cap = max(2, 1 << int(np.ceil(np.log2(2 * entries))))
+        self.set_keys = torch.empty(self.cap, dtype=torch.int32, device=dev)
+        self.set_vals = torch.empty(self.cap, dtype=torch.int32, device=dev)
+        W = table.world
+        self.send_ids = [torch.empty(entries, dtype=torch.int32, device=dev) for _ in range(self.SETS)]
+        self.rix = [torch.empty(entries, dtype=torch.int32, device=dev) for _ in range(self.SETS)]
+        self.counts = [torch.zeros(2 * W, dtype=torch.int64, device=dev) for _ in range(self.SETS)]
+        self.counts_host = [torch.zeros(W, W, dtype=torch.int64).pin_memory() for _ in range(self.SETS)]
+        self.ev_counts = [None] * self.SETS
+        self.ev_ready = [None] * self.SETS
+        self.ev_consumed = [None] * self.SETS
+        self.recv = [None] * self.SETS
+        self.state = [None] * self.SETS  # None | "planned" | "exchanged"
+        self.key = [None] * self.SETS
+        self.omap_keys = [None] * self.SETS
+        self.seq = [0] * self.SETS
+        self.n_seq = 0
+        self.side = torch.cuda.Stream(dev)
+        self._empty = torch.zeros(16, dtype=torch.uint8, device=dev)
+        self.last = None  # (distinct remote rows, remote (position, head) pairs) of the last exchanged batch
+
+    def has(self, key) -> bool:
+        return key in self.key
+
+    def prefetch(self, key, tokens: torch.Tensor, ss: torch.Tensor | None, t0: int, n: int, omap) -> None:
+        t = self.table
+        if key in self.key:
+            return
+        if n > self.n_max:
+            raise ValueError(f"{n} positions exceed n_tokens_max {self.n_max}")
+        free = [b for b in range(self.SETS) if self.state[b] is None]
+        if not free:  # drop the oldest waiting batch (every rank drops the same one)
+            b = min(range(self.SETS), key=lambda k: self.seq[k])
+            self.state[b] = self.key[b] = None
+            free = [b]
+        b = free[0]
+        lib = L.load()
+        cur = torch.cuda.current_stream(t.device)
+        self.side.wait_stream(cur)
+        if self.ev_consumed[b] is not None:
+            self.side.wait_event(self.ev_consumed[b])
+        self.recv[b] = None
+        ov = None
+        if omap is not None and omap.R:
+            ov = L.EngramOverlay(None, omap.R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
+        st = lib.engram_shard_plan(C.byref(t.ctable), None if ov is None else C.byref(ov), tokens.data_ptr(),
+                                   L.ptr(ss), t0, n, t.world, t.rank, self.set_keys.data_ptr(),
+                                   self.set_vals.data_ptr(), self.cap, self.send_ids[b].data_ptr(),
+                                   self.counts[b].data_ptr(), self.rix[b].data_ptr(), self.side.cuda_stream)
+        L.check(st, "engram_shard_plan")
+        tokens.record_stream(self.side)
+        if ss is not None:
+            ss.record_stream(self.side)
+        with torch.cuda.stream(self.side):
+            allc = self.exchange.gather_counts(t, self.counts[b][: t.world])
+            self.counts_host[b].copy_(allc.reshape(t.world, t.world), non_blocking=True)
+        self.ev_counts[b] = torch.cuda.Event()
+        self.ev_counts[b].record(self.side)
+        self.state[b], self.key[b] = "planned", key
+        self.omap_keys[b] = None if ov is None else omap.keys.data_ptr()
+        self.n_seq += 1
+        self.seq[b] = self.n_seq
+        for o in sorted((k for k in range(self.SETS) if self.state[k] == "planned" and k != b),
+                        key=lambda k: self.seq[k]):
+            self._exchange(o)
+
+    def _exchange(self, b: int) -> None:
+        t = self.table
+        self.ev_counts[b].synchronize()
+        m = self.counts_host[b]
+        send = [int(x) for x in m[t.rank].tolist()]
+        recv = [int(x) for x in m[:, t.rank].tolist()]
+        total = sum(send)
+        with torch.cuda.stream(self.side):
+            rows = self.exchange.rows(t, self.send_ids[b][:total], send, recv)
+        self.recv[b] = rows if rows.numel() else self._empty
+        self.ev_ready[b] = torch.cuda.Event()
+        self.ev_ready[b].record(self.side)
+        self.state[b] = "exchanged"
+        self.last = (total, None)
+
+    def take(self, key, omap):
+        """(receive buffer, row_index, ready event) of the prefetched batch `key`."""
+        b = self.key.index(key)
+        want = None if omap is None or not omap.R else omap.keys.data_ptr()
+        if want != self.omap_keys[b]:
+            raise ValueError("the batch was prefetched with another overlay map; prefetch it again with this one")
+        if self.state[b] == "planned":
+            self._exchange(b)
+        self.key[b] = None
+        return b, self.recv[b], self.rix[b], self.ev_ready[b]
+
+    def consumed(self, b: int, stream: torch.cuda.Stream) -> None:
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.ev_consumed[b] = ev
+        self.state[b] = None
+
+
+class NcclRowExchange:
+    """The collectives of ExchangeStage over torch.distributed, on a process
+    group of their own (NCCL between GPUs, gloo on CPU for tests) so they run
+    beside the step's other collectives instead of queueing behind them.
+    A collective to construct: every rank of `group` calls it."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        base = group if group is not None else dist.group.WORLD
+        self.group = dist.new_group(ranks=dist.get_process_group_ranks(base))
+
+    def gather_counts(self, table, counts: torch.Tensor) -> torch.Tensor:
+        """[W*W] int64: entry r*W + o = the rows rank r requests from owner o."""
+        W = table.world
+        out = torch.empty(W * W, dtype=torch.int64, device=counts.device)
+        self.dist.all_gather_into_tensor(out, counts.contiguous(), group=self.group)
+        return out
+
+    def rows(self, table, send_ids: torch.Tensor, send_counts, recv_counts) -> torch.Tensor:
+        """The rows of send_ids (grouped by owner, send_counts per owner) from
+        their owners, in send order: ids out (all-to-all), each owner gathers
+        the rows asked of it (ShardedTable.serve), rows back (all-to-all)."""
+        dev = send_ids.device
+        recv_ids = torch.empty(max(sum(recv_counts), 1), dtype=torch.int32, device=dev)[: sum(recv_counts)]
+        self.dist.all_to_all_single(recv_ids, send_ids, recv_counts, send_counts, group=self.group)
+        served = table.serve(recv_ids)
+        stride = table.stride
+        rows = torch.empty(max(sum(send_counts), 1) * stride, dtype=torch.uint8, device=dev)[: sum(send_counts) * stride]
+        self.dist.all_to_all_single(rows, served, [c * stride for c in send_counts],
+                                    [c * stride for c in recv_counts], group=self.group)
+        return rows
+
+
+class LocalRowExchange:
+    """ExchangeStage's exchange among shards held by one process (emulated
+    ranks, for tests): every owner serves from its own ShardedTable."""
+
+    def __init__(self, shards):
+        self.shards = shards
+
+    def gather_counts(self, table, counts: torch.Tensor) -> torch.Tensor:
+        W = table.world
+        out = torch.zeros(W, W, dtype=torch.int64, device=counts.device)
+        out[table.rank] = counts
+        return out.reshape(-1)
+
+    def rows(self, table, send_ids: torch.Tensor, send_counts, recv_counts) -> torch.Tensor:
+        parts, off = [], 0
+        for owner, c in enumerate(send_counts):
+            if c:
+                parts.append(self.shards[owner].serve(send_ids[off:off + c]))
+            off += c
+        return torch.cat(parts) if parts else torch.empty(0, dtype=torch.uint8, device=send_ids.device)
 
 
 class _Staged:

@@ -277,6 +277,44 @@ ENGRAM_API int engram_shard_requests(const int32_t* ids, const int32_t* slots, i
                                      int64_t* counts, int32_t* row_index, void* stream);
 
 /*
+ * Row-sharded table, the deduplicated exchange plan of one batch: for the
+ * (position, head) pairs of positions t0..t0+n-1 of `tokens` (hashed with t's
+ * addressing constants, as engram_hash) whose row another rank owns and the
+ * overlay ov (nullable; only its map is read) does not serve, builds
+ *   send_ids  (device int32 [<= n * n_heads]): the distinct such ids, grouped by
+ *             owner (no entry for `rank` itself);
+ *   counts    (device int64 [2*world]): counts[o] = ids for owner o; the rest is
+ *             scratch;
+ *   row_index (device int32 [n * n_heads]): the position of the pair's id in
+ *             send_ids (= its row in the reply), -1 for pairs served locally or
+ *             by the overlay.
+ * set_keys/set_vals: device int32 [capacity] scratch, capacity a power of two
+ * >= 2 * n * n_heads.  A Zipf-hot remote row is requested once per batch, not
+ * once per occurrence.  No reference counterpart: the reference is
+ * single-process.
+ */
+ENGRAM_API int engram_shard_plan(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                 const int32_t* seg_start, int64_t t0, int64_t n, int32_t world, int32_t rank,
+                                 int32_t* set_keys, int32_t* set_vals, int64_t capacity, int32_t* send_ids,
+                                 int64_t* counts, int32_t* row_index, void* stream);
+
+/*
+ * engram_forward over a row-sharded table after the exchange of a plan: rows
+ * this rank owns are read in place from local_rows (its shard: row g at local
+ * row g / world), every other row from recv_rows (the rows of the plan's
+ * send_ids, in send order, row_stride bytes each) at the row given by the
+ * plan's row_index for the same tokens, seg_start, t0 and n.  t supplies the
+ * addressing constants of the whole table; its rows pointer is not read.
+ * Outputs are bit-identical to engram_forward on the whole resident table.
+ * No reference counterpart.
+ */
+ENGRAM_API int engram_forward_exchanged(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                        const int32_t* seg_start, int64_t t0, int64_t n, const void* local_rows,
+                                        int32_t world, int32_t rank, const void* recv_rows, const int32_t* row_index,
+                                        int32_t mode, void* out, int32_t* ids_out, int32_t* slots_out,
+                                        int64_t* hit_count, void* stream);
+
+/*
  * Owner side: out[k] = the resident row of global id ids[k] from this rank's
  * shard (local index ids[k] / world; stride bytes per row, 16-byte multiple).
  * Ids outside the shard give zero rows.

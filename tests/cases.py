@@ -69,3 +69,21 @@ def overlay_case(golden, prefix: str, table: TableSpec) -> OverlayCase:
     n = n_prefix - start
     grad = FX.overlay_grad(int(g["seed"]), (n, table.n_heads * table.dim))
     return OverlayCase(table, tokens, seg_start, start, n, row_ids, rows_init, grad, g)
+
+
+def shard_plan_ref(ids, ov_ids, world: int, rank: int):
+    """The contract of engram_shard_plan restated in numpy (a test reference):
+    the pairs of `ids` (global row ids [n, n_heads]) whose owner id % world is
+    another rank and which the overlay (ov_ids) does not serve are requested;
+    send_ids holds each such id once, grouped by owner (ascending inside a group
+    here; the kernel leaves that order open), counts[o] the ids for owner o and
+    row_index each pair's position in send_ids (-1 when not requested)."""
+    flat = np.asarray(ids, dtype=np.int64).reshape(-1)
+    remote = (flat % world != rank) & ~np.isin(flat, np.asarray(ov_ids, dtype=np.int64))
+    uniq = np.unique(flat[remote])
+    send = uniq[np.argsort(uniq % world, kind="stable")]
+    counts = np.bincount(send % world, minlength=world).astype(np.int64)
+    order = np.argsort(send, kind="stable")
+    rix = np.full(flat.shape, -1, dtype=np.int32)
+    rix[remote] = order[np.searchsorted(send[order], flat[remote])]
+    return send.astype(np.int32), counts, rix

@@ -70,3 +70,86 @@ def test_shard_bounds_cover_all_rows():
             assert all(spans[i][1] == spans[i + 1][0] for i in range(W - 1))
     with pytest.raises(ValueError):
         shard_bounds(10, 2, 2)
+
+
+def _row_exchange_worker(rank, world, port, out_q):
+    """One rank of the row-sharded exchange on CPU: its batch's plan (the
+    numpy restatement of engram_shard_plan), every rank's counts gathered
+    (NcclRowExchange.gather_counts), ids out and rows back
+    (NcclRowExchange.rows, all-to-alls), each owner serving only rows it owns."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from cases import shard_plan_ref
+        from engraft_ngram_b200.shard import NcclRowExchange
+        from oracle import oracle as O
+        n_rows, stride, T = 50_021, 144, 3000
+        rng = np.random.default_rng(7)  # the table, its addressing and the overlay: the same on every rank
+        full = rng.integers(0, 256, size=(n_rows, stride), dtype=np.uint8)
+        sizes = [n_rows // 16 - 3 * (15 - h) for h in range(16)]
+        sizes[-1] += n_rows - sum(sizes)
+        offs = np.concatenate([[0], np.cumsum(sizes)[:-1]])
+        mult = [int(x) | 1 for x in rng.integers(1, 2**63, size=3, dtype=np.uint64)]
+        ranks = np.arange(1, 151_937, dtype=np.float64)
+        cdf = np.cumsum(ranks ** -1.1)
+        cdf /= cdf[-1]
+        toks = np.searchsorted(cdf, np.random.default_rng(100 + rank).random(T)).astype(np.int32)
+        ids = O.hash_ids(toks, 3, 8, mult, sizes, offs, 151_935)
+        ov_ids = np.unique(O.hash_ids(np.searchsorted(cdf, rng.random(T)).astype(np.int32), 3, 8, mult, sizes, offs,
+                                      151_935)[::5].reshape(-1))
+        send, counts, rix = shard_plan_ref(ids, ov_ids, world, rank)
+
+        class Shard:  # the owner side of the exchange: serves only the rows this rank holds
+            def __init__(self):
+                self.world, self.rank, self.stride, self.served = world, rank, stride, 0
+
+            def serve(self, recv_ids):
+                g = recv_ids.numpy().astype(np.int64)
+                assert (g % world == rank).all(), "an owner was asked for a row it does not hold"
+                self.served += len(g)
+                return torch.from_numpy(full[g].reshape(-1).copy())
+
+        table = Shard()
+        ex = NcclRowExchange()
+        allc = ex.gather_counts(table, torch.from_numpy(counts)).reshape(world, world).numpy()
+        ok = bool((allc[rank] == counts).all()) and allc[rank, rank] == 0
+        sc = [int(x) for x in allc[rank]]
+        rc = [int(x) for x in allc[:, rank]]
+        rows = ex.rows(table, torch.from_numpy(send), sc, rc).numpy().reshape(-1, stride)
+        ok &= rows.shape[0] == len(send) and bool((rows == full[send.astype(np.int64)]).all())
+        ok &= table.served == sum(rc)
+        # every (position, head) finds its row: the overlay, its own shard, or the reply at row_index
+        flat = ids.reshape(-1).astype(np.int64)
+        req = rix >= 0
+        ok &= bool((rows[rix[req]] == full[flat[req]]).all())
+        rest = flat[~req]
+        ok &= bool(((rest % world == rank) | np.isin(rest, ov_ids)).all())
+        remote_pairs = int(((flat % world != rank) & ~np.isin(flat, ov_ids)).sum())
+        out_q.put((rank, ok, len(send), remote_pairs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_row_sharded_exchange_protocol_on_cpu_ranks(world):
+    """world gloo ranks on CPU: owner = id mod world, each rank's distinct remote
+    rows grouped by owner, the gathered counts matrix, the id and row
+    all-to-alls with split sizes from that matrix, and the row index of every
+    (position, head) agree with the single-process resident table; a Zipf
+    batch requests fewer distinct rows than remote pairs."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_row_exchange_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, ok, distinct, pairs = q.get(timeout=240)
+        res[rank] = (ok, distinct, pairs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(v[0] for v in res.values()), res
+    assert all(0 < v[1] < v[2] for v in res.values()), res

@@ -434,6 +434,120 @@ def test_sharded_table_read_in_place_matches_resident_table(eb, world, fmt, dim,
     assert np.array_equal(outs[0][1], outs[1][1]) and outs[0][2] == outs[1][2]
 
 
+@pytest.mark.parametrize("world,rank", [(2, 1), (3, 2), (8, 5)])
+def test_shard_plan_matches_its_contract(eb, world, rank):
+    """engram_shard_plan over t0 > 0 with segments: the counts per owner, the
+    distinct ids of each owner's group and every pair's row_index equal the
+    numpy restatement of the contract (cases.shard_plan_ref); the order inside
+    an owner's group is free, so groups compare as sets and row_index through
+    send_ids."""
+    from cases import shard_plan_ref
+    rng = np.random.default_rng(11 * world + rank)
+    n_rows = 40_009
+    spec = random_spec(O.FMT_IQ4_XS, 256, n_rows, 3 + world)
+    full = device_table(eb, spec)
+    T, t0 = 2500, 300
+    toks = zipf_tokens(rng, T)
+    ss = FX.seg_starts(np.sort(rng.integers(0, 6, size=T)))
+    ids = spec.ids(toks, seg_start=ss, t0=t0)
+    ov_ids = np.unique(np.concatenate([np.unique(ids)[::3], rng.integers(0, n_rows, size=80)])).astype(np.int32)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    n = T - t0
+    entries = n * 16
+    cap = 1 << int(np.ceil(np.log2(2 * entries)))
+    keys = torch.empty(cap, dtype=torch.int32, device=DEV)
+    vals = torch.empty(cap, dtype=torch.int32, device=DEV)
+    send = torch.full((entries,), -7, dtype=torch.int32, device=DEV)
+    counts = torch.empty(2 * world, dtype=torch.int64, device=DEV)
+    rix = torch.empty(entries, dtype=torch.int32, device=DEV)
+    ov = eb._lib.EngramOverlay(None, omap.R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
+    toks_d, ss_d = torch.from_numpy(toks).to(DEV), torch.from_numpy(ss).to(DEV)
+    st = eb._lib.load().engram_shard_plan(C.byref(full.ctable), C.byref(ov), toks_d.data_ptr(), ss_d.data_ptr(), t0,
+                                          n, world, rank, keys.data_ptr(), vals.data_ptr(), cap, send.data_ptr(),
+                                          counts.data_ptr(), rix.data_ptr(), eb._lib.stream_of(DEV))
+    eb._lib.check(st, "engram_shard_plan")
+    torch.cuda.synchronize()
+    want_send, want_counts, want_rix = shard_plan_ref(ids, ov_ids, world, rank)
+    got_counts = counts[:world].cpu().numpy()
+    assert np.array_equal(got_counts, want_counts) and got_counts[rank] == 0
+    total = int(got_counts.sum())
+    got_send = send[:total].cpu().numpy()
+    off = np.concatenate([[0], np.cumsum(got_counts)])
+    for o in range(world):  # each owner's group holds exactly its ids
+        grp = got_send[off[o]:off[o + 1]]
+        assert np.array_equal(np.sort(grp), np.sort(want_send[want_send % world == o])), o
+    got_rix = rix.cpu().numpy()
+    assert np.array_equal(got_rix < 0, want_rix < 0)
+    flat = ids.reshape(-1)
+    assert np.array_equal(got_send[got_rix[got_rix >= 0]], flat[got_rix >= 0])
+    assert total < int((want_rix >= 0).sum())  # a Zipf batch repeats remote rows
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("fmt,dim,mode", [(O.FMT_IQ4_XS, 256, O.MODE_PAIRSUM_ADD_BF16),
+                                          (O.FMT_IQ4_NL, 160, O.MODE_CONCAT_F32),
+                                          (O.FMT_IQ4_XS, 512, O.MODE_PAIRSUM_ADD_BF16)])
+def test_exchange_staged_forward_matches_resident_table(eb, world, fmt, dim, mode):
+    """W ranks emulated on one GPU, each with exchange staging over a local
+    exchange: four batches pipelined with the prefetch two batches ahead (plan,
+    counts, deduplicated exchange, then engram_forward_exchanged) give outputs,
+    slots and hit counts bit-identical to the forward over the whole resident
+    table; a batch forwarded without a prefetch is planned on the spot."""
+    from engraft_ngram_b200.shard import LocalRowExchange, ShardedTable
+    rng = np.random.default_rng(41 * world + dim + mode)
+    n_rows = 25_013
+    spec = random_spec(fmt, dim, n_rows, 13 + world)
+    full = device_table(eb, spec)
+    shards = [ShardedTable.from_full(full, world, r) for r in range(world)]
+    ex = LocalRowExchange(shards)
+    T = 1300
+    batches = []
+    for _ in range(4):
+        toks = zipf_tokens(rng, T)
+        ss = FX.seg_starts(np.sort(rng.integers(0, 4, size=T)))
+        batches.append((torch.from_numpy(toks).to(DEV), torch.from_numpy(ss).to(DEV)))
+    read = np.unique(np.concatenate([spec.ids(b[0].cpu().numpy()) for b in batches]))
+    ov_ids = np.unique(np.concatenate([read[::5], rng.integers(0, n_rows, size=60)])).astype(np.int32)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    rows_var = torch.from_numpy((rng.standard_normal((len(ov_ids), dim)) * 0.01).astype(np.float32)).to(DEV)
+    res0 = O.bf16_bits((rng.standard_normal((T, 8 * dim)) * 0.5).astype(np.float32))
+
+    def run(forward):
+        out = (torch.empty(T, 16, dim, device=DEV) if mode == O.MODE_CONCAT_F32
+               else torch.from_numpy(res0.view(np.int16).copy()).to(DEV).view(torch.bfloat16))
+        slots = torch.empty(T, 16, dtype=torch.int32, device=DEV)
+        hits = torch.zeros(1, dtype=torch.int64, device=DEV)
+        forward(out, slots, hits)
+        torch.cuda.synchronize()
+        return out.view(torch.int16).cpu().numpy(), slots.cpu().numpy(), int(hits.item())
+
+    def resident(b):
+        def f(out, slots, hits):
+            ov = omap.descriptor(rows_var)
+            st = eb._lib.load().engram_forward(C.byref(full.ctable), C.byref(ov), b[0].data_ptr(), b[1].data_ptr(),
+                                               0, T, mode, out.data_ptr(), None, slots.data_ptr(), hits.data_ptr(),
+                                               eb._lib.stream_of(DEV))
+            eb._lib.check(st, "engram_forward")
+        return f
+
+    want = [run(resident(b)) for b in batches]
+    for r in range(world):
+        sh = shards[r]
+        sh.enable_exchange_staging(T, ex)
+        sh.prefetch(*batches[0], omap=omap)
+        sh.prefetch(*batches[1], omap=omap)
+        for k in range(3):
+            if k + 2 < 3:
+                sh.prefetch(*batches[k + 2], omap=omap)
+            got = run(lambda out, slots, hits: sh.forward(batches[k][0], batches[k][1], omap, rows_var, out, mode,
+                                                          slots_out=slots, hit_count=hits))
+            assert np.array_equal(got[0], want[k][0]) and np.array_equal(got[1], want[k][1]), (r, k)
+            assert got[2] == want[k][2]
+        got = run(lambda out, slots, hits: sh.forward(batches[3][0], batches[3][1], omap, rows_var, out, mode,
+                                                      slots_out=slots, hit_count=hits))
+        assert np.array_equal(got[0], want[3][0]) and got[2] == want[3][2], r
+
+
 @pytest.mark.parametrize("world,rank", [(2, 1), (3, 0), (8, 5)])
 def test_stage_copies_exactly_the_rows_of_other_ranks(eb, world, rank):
     """engram_stage_sharded over t0 > 0: head h of output row i holds the

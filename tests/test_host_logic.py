@@ -112,12 +112,14 @@ def test_overlay_emb_refuses_cpu_tensors():
 
 def test_bench_command_line_and_config_text(monkeypatch):
     """bench.py parses its flags and names the multi-GPU layout it ran
-    (replicated, staged row-sharded, in-place row-sharded, NCCL row-sharded)."""
+    (replicated, row-sharded with the deduplicated exchange (the default),
+    staged row-sharded, in-place row-sharded, NCCL row-sharded)."""
     import bench
     monkeypatch.setattr(sys, "argv", ["bench.py", "--gpus", "2", "--shard", "--stage-blocks", "32"])
     args = bench.parse()
-    assert args.shard and args.stage == "pull" and args.stage_blocks == 32 and args.shard_exchange == "peer"
-    assert args.e2e_exchange == "peer"
+    assert args.shard and args.stage == "exchange" and args.stage_blocks == 32 and args.shard_exchange == "peer"
+    assert args.e2e_exchange == "peer" and args.layout == "sharded"
+    assert "planned two batches ahead" in bench.shard_text(dict(bench.CONFIGS["cfg5"], shard=True, stage="exchange"))
     cfg = dict(bench.CONFIGS["cfg5"], shard=True, shard_exchange="peer", stage="push", exchange="peer")
     text = bench.config_json(cfg, args)["parallelism"]
     assert text.startswith("dp2+row-sharded") and "stores the rows" in text
@@ -138,3 +140,30 @@ def test_tf32_split_is_exact():
     assert torch.equal((hi.view(torch.int32) & 8191), torch.zeros_like(x, dtype=torch.int32))
     assert torch.equal(hi + lo, x)
     assert (lo.abs() <= x.abs() * 2.0 ** -10).all()
+
+
+def test_overlay_map_cache_is_found_by_identity_and_size(monkeypatch):
+    """OverlayEmb.build finds the device map of the same row_map dict without a
+    pass over its items; a size change or forget_overlay_map rebuilds it."""
+    from engraft_ngram_b200 import overlay as ov
+    built = []
+
+    class FakeMap:
+        def __init__(self, rm):
+            self.R = len(rm)
+
+    monkeypatch.setattr(ov.OverlayMap, "from_row_map", classmethod(lambda cls, rm, dev: built.append(1) or FakeMap(rm)))
+    ov.forget_overlay_map()
+    rm = {10: 0, 20: 1}
+    a = ov._overlay_map_for(rm, "cuda:0")
+    assert ov._overlay_map_for(rm, "cuda:0") is a and len(built) == 1
+    rm[30] = 2  # size changed: rebuilt
+    b = ov._overlay_map_for(rm, "cuda:0")
+    assert b is not a and b.R == 3 and len(built) == 2
+    ov.forget_overlay_map(rm)
+    assert ov._overlay_map_for(rm, "cuda:0") is not b and len(built) == 3
+    assert ov._overlay_map_for(rm, "cuda:1") is not None and len(built) == 4  # one map per device
+    pre = FakeMap({1: 0})
+    pre.__class__ = type("M", (ov.OverlayMap,), {})  # an OverlayMap passed as row_map is used as it is
+    assert ov._overlay_map_for(pre, "cuda:0") is pre
+    ov.forget_overlay_map()

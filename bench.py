@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-latency", action="store_true",
+                    help="N=1, config 5: skip the latency configurations (1, 2, 4 and the config-3 step)")
     ap.add_argument("--no-check", action="store_true",
                     help="skip the parity check of the timed kernels against the CPU oracle (N=1)")
     ap.add_argument("--table-rows", type=int, default=None, help="override (profiling a small case)")
@@ -666,6 +668,221 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_latency(wl, args, device):
+    """The latency configurations of BASELINE on one GPU, measured after the
+    headline step (CUDA events on the launching stream, inputs resident):
+    - cfg2: 1 x 2048 Zipf tokens, forward only, pair sums into a bf16 [2048,
+      2048] residual, on the resident 320M-row IQ4_XS table (no overlay);
+    - cfg1: 1 x 2048 uniform tokens, forward only, CONCAT fp32 [2048, 16, 128],
+      on a 2^20 x 128 fp32 table (no overlay);
+    - cfg4: 256 sequences x 1 new token (3 uniform history tokens each), CONCAT,
+      on the cfg1 table with 40,000 overlay rows (engram_forward_at);
+    - cfg3: the training step on the cfg1 table (2048 Zipf tokens, 40,000
+      overlay rows, CONCAT): forward, row gradients, Adam with the regulariser.
+    Each runs over 64 distinct batches (inputs and outputs larger than L2):
+    once as 64 separate launches ("stream"), once as the 64 calls captured in
+    one CUDA graph and replayed ("graph"); us per call, rows/s and algorithmic
+    GB/s of the graph replay."""
+    import ctypes as C
+    import torch
+    import engraft_ngram_b200 as eb
+    from engraft_ngram_b200 import _lib as L
+    from engraft_ngram_b200.table import synthetic_head_sizes, synthetic_multipliers, synthetic_resident
+    lib = L.load()
+    B = 64
+    out = {}
+    cdf = zipf_cdf(torch, device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(args.seed * 1000 + 31)
+
+    def measure(calls, rows_per_call, bytes_per_call):
+        """calls: list of B zero-argument launches on the current stream."""
+        stream = torch.cuda.current_stream(device)
+        for c in calls[:3]:
+            c()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for c in calls:
+            c()
+        e1.record()
+        torch.cuda.synchronize()
+        t_stream = e0.elapsed_time(e1) / len(calls)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for c in calls[:2]:
+                c()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for c in calls:
+                c()
+        g.replay()
+        torch.cuda.synchronize()
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t_graph = e0.elapsed_time(e1) / (reps * len(calls))
+        del g
+        return {"us_per_call_stream": t_stream * 1e3, "us_per_call_graph": t_graph * 1e3,
+                "rows_per_s_graph": rows_per_call / (t_graph * 1e-3),
+                "gbps_graph": bytes_per_call / (t_graph * 1e-3) / 1e9, "algorithmic_bytes_per_call": bytes_per_call}
+
+    ov0 = L.EngramOverlay(None, 0, None, None, 0)
+    T = 2048
+    # cfg2 on the headline table
+    if wl.shard is None and wl.fmt == L.FMT_IQ4_XS and wl.dim == 256:
+        toks = [zipf_tokens(torch, T, gen, cdf) for _ in range(B)]
+        res = (torch.randn(B, T, 8 * 256, generator=gen, device=device) * 0.5).to(torch.bfloat16)
+        ct = wl.table.ctable
+
+        def f2(k):
+            return lambda: L.check(lib.engram_forward(C.byref(ct), C.byref(ov0), toks[k].data_ptr(), None, 0, T,
+                                                      L.MODE_PAIRSUM_ADD_BF16, res[k].data_ptr(), None, None, None,
+                                                      torch.cuda.current_stream(device).cuda_stream), "engram_forward")
+        out["cfg2"] = measure([f2(k) for k in range(B)], 16 * T, T * (4 + 16 * 136 + 2 * 2 * 8 * 256))
+        out["cfg2"]["workload"] = "1x2048 Zipf tokens, 320M-row x 256 IQ4_XS table, pair sums into bf16 [2048, 2048]"
+        del res, toks
+    # the cfg1 table
+    n1, dim = 1 << 20, 128
+    sizes = synthetic_head_sizes(n1)
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
+    t1 = eb.DeviceTable(synthetic_resident(n1, L.FMT_F32, dim, args.seed + 1, device), L.FMT_F32, dim, sizes, offs,
+                        synthetic_multipliers(args.seed), EOS, n_rows=n1)
+    ct1 = t1.ctable
+    utoks = [torch.randint(0, VOCAB, (T,), generator=gen, device=device, dtype=torch.int32) for _ in range(B)]
+    emb = torch.empty(B, T, 16, dim, device=device)
+
+    def f1(k):
+        return lambda: L.check(lib.engram_forward(C.byref(ct1), C.byref(ov0), utoks[k].data_ptr(), None, 0, T,
+                                                  L.MODE_CONCAT_F32, emb[k].data_ptr(), None, None, None,
+                                                  torch.cuda.current_stream(device).cuda_stream), "engram_forward")
+    out["cfg1"] = measure([f1(k) for k in range(B)], 16 * T, T * (4 + 2 * 16 * dim * 4))
+    out["cfg1"]["workload"] = "1x2048 uniform tokens, 2^20 x 128 fp32 table, CONCAT fp32 [2048, 16, 128]"
+    del emb, utoks
+    # overlay of the cfg1 table: the 40,000 rows a Zipf census batch reads most
+    R = 40_000
+    census = zipf_tokens(torch, T * 16, gen, cdf)
+    ids = t1.global_ids(census).reshape(-1).to(torch.int64)
+    uniq, cnt = torch.unique(ids, return_counts=True)
+    top = uniq[torch.argsort(cnt, descending=True, stable=True)[:R]]
+    if top.numel() < R:
+        extra = torch.randint(0, n1, (4 * R,), generator=gen, device=device)
+        top = torch.cat([top, torch.unique(extra[~torch.isin(extra, uniq)])[: R - top.numel()]])
+    ov_ids = torch.sort(top).values.to(torch.int32)
+    omap = eb.OverlayMap(ov_ids, device)
+    p0 = t1.gather_rows(ov_ids)
+    rows_var = p0.clone()
+    ovd = omap.descriptor(rows_var)
+    # cfg4: decode-style
+    S, H = 256, 4
+    dtoks = [torch.randint(0, VOCAB, (S * H,), generator=gen, device=device, dtype=torch.int32) for _ in range(B)]
+    seg = (torch.arange(S * H, device=device, dtype=torch.int32) // H) * H
+    pos = torch.arange(S, device=device, dtype=torch.int64) * H + H - 1
+    demb = torch.empty(B, S, 16, dim, device=device)
+
+    def f4(k):
+        return lambda: L.check(lib.engram_forward_at(C.byref(ct1), C.byref(ovd), dtoks[k].data_ptr(), S * H,
+                                                     seg.data_ptr(), pos.data_ptr(), S, L.MODE_CONCAT_F32,
+                                                     demb[k].data_ptr(), None, None, None,
+                                                     torch.cuda.current_stream(device).cuda_stream), "engram_forward_at")
+    out["cfg4"] = measure([f4(k) for k in range(B)], 16 * S, S * (3 * 4 + 2 * 16 * dim * 4))
+    out["cfg4"]["workload"] = "256 sequences x 1 new token (3 uniform history tokens), cfg1 table, 40,000 overlay rows"
+    del demb, dtoks
+    # cfg3: the training step on the cfg1 table
+    ztoks = [zipf_tokens(torch, T, gen, cdf) for _ in range(B)]
+    cemb = torch.empty(T, 16, dim, device=device)
+    slots = torch.empty(T, 16, dtype=torch.int32, device=device)
+    dout = torch.randn(B, T, 16, dim, generator=gen, device=device) * 1e-3
+    grad = torch.empty(R, dim, device=device)
+    m, v = torch.zeros(R, dim, device=device), torch.zeros(R, dim, device=device)
+    wsb = int(lib.engram_backward_workspace_bytes(T, 16, R))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=device)
+    from engraft_ngram_b200.optim import reg_scale
+    rs = reg_scale(0.1, p0)
+
+    def f3(k):
+        def step():
+            s = torch.cuda.current_stream(device).cuda_stream
+            L.check(lib.engram_forward(C.byref(ct1), C.byref(ovd), ztoks[k].data_ptr(), None, 0, T, L.MODE_CONCAT_F32,
+                                       cemb.data_ptr(), None, slots.data_ptr(), None, s), "engram_forward")
+            L.check(lib.engram_backward(slots.data_ptr(), T, 16, 8, L.MODE_CONCAT_F32, dout[k].data_ptr(), dim, R,
+                                        grad.data_ptr(), ws.data_ptr(), wsb, s), "engram_backward")
+            L.check(lib.engram_adam_step(rows_var.data_ptr(), grad.data_ptr(), m.data_ptr(), v.data_ptr(),
+                                         p0.data_ptr(), rows_var.numel(), 1, 1e-3, 0.9, 0.999, 1e-8, rs, s),
+                    "engram_adam_step")
+        return step
+    step_bytes = T * (4 + 2 * 16 * dim * 4 + 16 * dim * 4) + 9 * R * dim * 4
+    out["cfg3"] = measure([f3(k) for k in range(B)], 16 * T, step_bytes)
+    out["cfg3"]["workload"] = ("training step: 2048 Zipf tokens, cfg1 table, 40,000 overlay rows, forward + row "
+                               "gradients + Adam (the Adam step count is held at 1 in the replayed graph)")
+    del dout, cemb
+    out["cfg3_dropin"] = run_dropin(t1, ov_ids, p0, ztoks, device, args)
+    # the reference's own format: 160-wide IQ4_NL rows
+    n_nl = 1 << 20
+    t_nl = eb.DeviceTable(synthetic_resident(n_nl, L.FMT_IQ4_NL, 160, args.seed + 2, device), L.FMT_IQ4_NL, 160,
+                          sizes, offs, synthetic_multipliers(args.seed), EOS, n_rows=n_nl)
+    out["cfg3_dropin_iq4nl160"] = run_dropin(t_nl, ov_ids, t_nl.gather_rows(ov_ids), ztoks, device, args)
+    return out
+
+
+def run_dropin(table, ov_ids, p0, toks, device, args, K=40):
+    """The reference's own call path through the drop-in: each step builds
+    OverlayEmb(table, tokens as a Python list, rows_var, row_map as a dict)
+    .build(2048) (engraft/replica/seq.py:1430-1432), backpropagates a gradient
+    and steps OverlayAdam with the descent's regulariser
+    (engraft/descend_corpus.py:921-947).  Reports the wall time per step
+    (synchronised at the end of K steps), the host (Python) time per step and
+    the device time (CUDA events around the K steps)."""
+    import torch
+    import engraft_ngram_b200 as eb
+    T = 2048
+    R = int(ov_ids.numel())
+    row_map = {int(g): k for k, g in enumerate(ov_ids.cpu().tolist())}
+    tok_lists = [t.cpu().tolist() for t in toks[:8]]
+    rows_var = p0.clone().requires_grad_(True)
+    opt = eb.OverlayAdam([rows_var], lr=1e-3, reg_ref=p0, reg_mu=0.1)
+    g = torch.Generator(device=device)
+    g.manual_seed(args.seed * 1000 + 77)
+    douts = [torch.randn(T, 16 * table.dim, generator=g, device=device) * 1e-3 for _ in range(4)]
+    hits = []
+
+    def step(k):
+        opt.zero_grad()
+        ov = eb.OverlayEmb(table, tok_lists[k % len(tok_lists)], rows_var, row_map)
+        emb = ov.build(T)
+        emb.backward(douts[k % len(douts)])
+        opt.step()
+        return ov
+
+    for k in range(3):
+        step(k)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host = 0.0
+    t0 = time.perf_counter()
+    e0.record()
+    last = None
+    for k in range(K):
+        h0 = time.perf_counter()
+        last = step(k)
+        host += time.perf_counter() - h0
+    e1.record()
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) / K
+    dev_ms = e0.elapsed_time(e1) / K
+    hits = last.n_id_hits
+    return {"us_per_step_wall": wall * 1e6, "host_us_per_step": host / K * 1e6, "device_us_per_step": dev_ms * 1e3,
+            "host_fraction": (host / K) / wall, "rows_per_s": 16 * T / wall, "n_id_hits_last": int(hits),
+            "api": "OverlayEmb(table, tokens list, rows_var, row_map dict).build(2048) + backward + OverlayAdam.step",
+            "workload": f"2048 Zipf tokens, {table.n_rows}-row x {table.dim} table (fmt {table.fmt}), R={R}"}
+
+
 def run_scan(args, device):
     """Throughput of the bulk hash + overlay hit scan (engraft/damage.py:168-224) on
     a device-resident Zipf corpus: positions/s (16 rows each)."""
@@ -888,6 +1105,9 @@ def main():
     e2e = None
     if not args.no_e2e and not wl.decode:
         e2e = run_e2e(wl, args, device, ddist, world)
+    latency = None
+    if world == 1 and args.config == "cfg5" and not args.no_latency:
+        latency = run_latency(wl, args, device)
 
     layout = None
     if world > 1 and args.config == "cfg5":
@@ -940,6 +1160,8 @@ def main():
         }
         if parity is not None:
             line["parity"] = parity
+        if latency is not None:
+            line["latency"] = latency
         if layout is not None:
             line["layouts"] = layout
         if world == 1 and not args.no_cpu_baseline:
@@ -976,13 +1198,18 @@ def sharded_stats(wl, ms, fwd_ms, bwd_ms, ddist, world, device):
 
 
 def compare_layouts(sh, rep, ddist, device):
-    """The row-sharded forward (this rank's shard + the deduplicated exchange)
-    against the forward over the replicated resident table, on this rank's
-    batch, with the replicated run's overlay rows and the same residual:
-    bf16 bits and slots compared on the device (mismatches summed over ranks)."""
+    """The row-sharded forward (a shard of the replicated run's table, this
+    rank's rows, with the same exchange staging as the timed run) against the
+    forward over the whole resident table, on this rank's batch, with the
+    replicated run's overlay rows and the same residual: bf16 bits, slots and
+    hit counts compared on the device (mismatches summed over ranks)."""
     import ctypes as C
     import torch
+    from engraft_ngram_b200.shard import ShardedTable
     L = rep.L
+    world, rank = rep.world, rep.rank
+    shard = ShardedTable.from_full(rep.table, world, rank)
+    shard.enable_exchange_staging(rep.T)
     res0 = rep.out.clone()
     a, b = res0.clone(), res0.clone()
     sa = torch.empty_like(rep.slots)
@@ -990,7 +1217,7 @@ def compare_layouts(sh, rep, ddist, device):
     ha = torch.zeros(1, dtype=torch.int64, device=device)
     hb = torch.zeros(1, dtype=torch.int64, device=device)
     tok = rep.tokens.clone()
-    sh.shard.forward(tok, rep.seg_start, rep.omap, rep.rows_var, a, rep.mode, slots_out=sa, hit_count=ha)
+    shard.forward(tok, rep.seg_start, rep.omap, rep.rows_var, a, rep.mode, slots_out=sa, hit_count=ha)
     ov = rep.omap.descriptor(rep.rows_var)
     st = L.load().engram_forward(C.byref(rep.table.ctable), C.byref(ov), tok.data_ptr(), rep.seg_start.data_ptr(), 0,
                                  rep.T, rep.mode, b.data_ptr(), None, sb.data_ptr(), hb.data_ptr(), rep.stream)
@@ -999,7 +1226,8 @@ def compare_layouts(sh, rep, ddist, device):
     checked = torch.tensor([a.numel(), sa.numel()], dtype=torch.int64, device=device)
     ddist.all_reduce(mism)
     ddist.all_reduce(checked)
-    del res0
+    torch.cuda.synchronize()
+    del res0, shard
     return {"residual_values": int(checked[0]), "slots": int(checked[1]), "mismatches": int(mism.sum()),
             "bit_exact": int(mism.sum()) == 0}
 

@@ -189,6 +189,47 @@ __global__ void k_shard_gather(const uint8_t* __restrict__ shard, int64_t stride
     }
 }
 
+// Owner side of the peer exchange (engram_shard_serve): the rows every other
+// rank requested from this rank, gathered from the local shard into send_rows,
+// requester by requester.  Requester r's ids for this owner are the slice
+// [sum_{o < rank} M[r][o], + M[r][rank]) of its send_ids (read over NVLink
+// through id_ptrs[r]); they land at send_rows rows [sum_{r' < r} M[r'][rank], +
+// M[r][rank]).  One thread per 16-byte word; rows at or past max_rows are not
+// written (the requester refuses such a batch on the host).
+__global__ void k_shard_serve(const uint8_t* __restrict__ shard, int64_t stride, int64_t n_local, int world, int rank,
+                              const unsigned long long* __restrict__ id_ptrs, const int64_t* __restrict__ M,
+                              uint8_t* __restrict__ send_rows, int64_t max_rows) {
+    __shared__ long long base[kMaxWorld + 1];  // first send row of each requester
+    __shared__ long long idoff[kMaxWorld];     // offset of this owner's slice in the requester's send_ids
+    if (threadIdx.x == 0) {
+        long long acc = 0;
+        for (int r = 0; r < world; r++) {
+            base[r] = acc;
+            acc += (r == rank) ? 0 : M[(int64_t)r * world + rank];
+            long long off = 0;
+            for (int o = 0; o < rank; o++) off += M[(int64_t)r * world + o];
+            idoff[r] = off;
+        }
+        base[world] = acc;
+    }
+    __syncthreads();
+    const int64_t total = base[world] < max_rows ? base[world] : max_rows;
+    const int64_t words = stride >> 4;
+    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total * words;
+         w += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t f = w / words, p = w - f * words;
+        int r = 0;
+        while (r + 1 < world && base[r + 1] <= f) r++;  // requester of send row f
+        const int32_t* ids = reinterpret_cast<const int32_t*>(id_ptrs[r]);
+        const int32_t g = ids[idoff[r] + (f - base[r])];
+        const int64_t local = (int64_t)g / world;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (g >= 0 && (int)(g % world) == rank && local < n_local)
+            v = __ldg(reinterpret_cast<const uint4*>(shard + local * stride) + p);
+        reinterpret_cast<uint4*>(send_rows + f * stride)[p] = v;
+    }
+}
+
 int grid(int64_t work) {
     const int64_t want = (work + 255) / 256, cap = (int64_t)sm_count() * 8;
     return (int)(want < 1 ? 1 : (want < cap ? want : cap));
@@ -255,5 +296,22 @@ extern "C" int engram_shard_plan(const engram_table* t, const engram_overlay* ov
         launched += 5;
     }
     count_launches(launched);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int engram_shard_serve(const void* shard_rows, int64_t stride, int64_t n_local, int32_t world, int32_t rank,
+                                  const void* id_ptrs, const int64_t* counts_all, void* send_rows, int64_t max_rows,
+                                  void* stream) {
+    if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || stride <= 0 || (stride & 15) || n_local < 0 ||
+        max_rows < 0)
+        return ENGRAM_ERR_ARG;
+    if (world == 1 || max_rows == 0) return ENGRAM_OK;
+    if (!shard_rows || !id_ptrs || !counts_all || !send_rows || !aligned16(shard_rows) || !aligned16(send_rows))
+        return ENGRAM_ERR_ARG;
+    const int64_t cap = (int64_t)sm_count() * 4;
+    k_shard_serve<<<(int)cap, 256, 0, (cudaStream_t)stream>>>(
+        static_cast<const uint8_t*>(shard_rows), stride, n_local, world, rank,
+        static_cast<const unsigned long long*>(id_ptrs), counts_all, static_cast<uint8_t*>(send_rows), max_rows);
+    count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }

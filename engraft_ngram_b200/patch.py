@@ -51,10 +51,11 @@ _PLE_TARGETS = (("engraft.replica.layers", "ple_forward"), ("engraft.replica.mod
 
 def install_ple(modules: dict | None = None) -> None:
     """Routes the reference's ple_forward (engraft/replica/layers.py:565-626, and
-    the name engraft.replica.model imported) to engraft_ngram_b200.ple_forward
-    for calls that need no gradient; calls that do (the descent's backward
-    through the block) keep the reference's function.  modules: name -> module
-    overrides, for tests."""
+    the name engraft.replica.model imported) to engraft_ngram_b200.ple_forward,
+    with or without gradients of emb, hidden and hist (the descent's backward
+    through the block); calls that need gradients of the block's own weights,
+    or whose tensors are not on a CUDA device, keep the reference's function.
+    modules: name -> module overrides, for tests."""
     from . import ple
     for mod_name, attr in _PLE_TARGETS:
         mod = (modules or {}).get(mod_name) or importlib.import_module(mod_name)
@@ -64,7 +65,7 @@ def install_ple(modules: dict | None = None) -> None:
         original = saved[attr]
 
         def routed(emb, hidden, w, hist, hparams, *args, _orig=original, **kw):
-            if ple.needs_grad(emb, hidden, w, hist) or not emb.is_cuda:
+            if ple.weights_need_grad(w) or not emb.is_cuda:
                 return _orig(emb, hidden, w, hist, hparams, *args, **kw)
             return ple.ple_forward(emb, hidden, w, hist, hparams, *args, **kw)
 

@@ -16,9 +16,14 @@ dilated depthwise conv over [history; positions], silu and the block's residual
 sum).  Results agree with the reference to fp32 rounding (different reduction
 orders).
 
-Forward only: the block's backward is not built here, so a call that needs a
-gradient raises; `install_ple` routes those calls to the reference's own
-function and the rest here.
+Backward: calls that need gradients of emb, hidden or hist (what the descent's
+loss.backward() differentiates, engraft/replica/seq.py:1457-1462) run through
+an autograd function whose backward is engram_ple_conv_backward (silu' and the
+transposed conv), engram_ple_gate_backward (the norms, the gate and the gated
+product in closed form) and one GEMM back through both projections, d_emb =
+[d_key, d_value] @ [w_key; w_value], in the forward's arithmetic.  Gradients of
+the block's weights (frozen in the descent) are not built: such a call raises,
+and `install_ple` routes it to the reference's own function.
 """
 from __future__ import annotations
 
@@ -90,6 +95,105 @@ def needs_grad(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor) -
     return any(isinstance(t, torch.Tensor) and t.requires_grad for t in ts)
 
 
+def weights_need_grad(w) -> bool:
+    """The block's weights need gradients (not built here)."""
+    return torch.is_grad_enabled() and any(isinstance(getattr(w, f), torch.Tensor) and getattr(w, f).requires_grad
+                                           for f in _GRAD_FIELDS)
+
+
+def project_back(dkv: torch.Tensor, w, out: torch.Tensor, mode: str | None = None) -> torch.Tensor:
+    """out [T, n] = dkv [T, hc*n + n] @ [w_key; w_value]: the gradient of emb
+    through both projections, in the same arithmetic as project()."""
+    mode = mode or PROJECTION
+    if mode == "fp32":
+        (kv,) = _weights_kv(w, "fp32")
+        with _matmul_tf32(False):
+            torch.matmul(dkv, kv, out=out)
+        return out
+    if mode != "3xtf32":
+        raise ValueError(f"projection mode {mode!r}")
+    b_hi, b_lo = _weights_kv(w, "3xtf32")
+    a_hi, a_lo = split_tf32(dkv)
+    with _matmul_tf32(True):
+        torch.matmul(a_lo, b_hi, out=out)
+        out.addmm_(a_hi, b_lo)
+        out.addmm_(a_hi, b_hi)
+    return out
+
+
+def _block_forward(emb, hidden, w, hist, nk, nq, nc, cw, hc, n, K, eps, dil, want_s):
+    """kv [T, hc*n + n], gate, s, normed and out of the block (the kernels)."""
+    T = emb.shape[0]
+    H = hist.shape[0]
+    dev = emb.device
+    lib = L.load()
+    stream = L.stream_of(dev)
+    kv = project(emb, w, torch.empty(T, hc * n + n, device=dev))
+    stride = hc * n + n
+    value = kv[:, hc * n:]
+    gate = torch.empty(T, hc, device=dev)
+    s = torch.empty(T, hc, device=dev) if want_s else None
+    normed = torch.empty(T, hc, n, device=dev)
+    st = lib.engram_ple_gate(kv.data_ptr(), stride, value.data_ptr(), stride, hidden.data_ptr(), nk.data_ptr(),
+                             nq.data_ptr(), nc.data_ptr(), T, hc, n, eps, gate.data_ptr(), L.ptr(s),
+                             normed.data_ptr(), stream)
+    L.check(st, "engram_ple_gate")
+    out = torch.empty(T, hc, n, device=dev)
+    st = lib.engram_ple_conv(value.data_ptr(), stride, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
+                             hist.data_ptr() if H else None, H, cw.data_ptr(), K, dil, T, hc, n, out.data_ptr(),
+                             stream)
+    L.check(st, "engram_ple_conv")
+    return kv, gate, s, normed, out
+
+
+class _PleBlockFn(torch.autograd.Function):
+    """The block with gradients of emb, hidden and hist (weights frozen)."""
+
+    @staticmethod
+    def forward(ctx, emb, hidden, hist, w, nk, nq, nc, cw, meta):
+        hc, n, K, eps, dil, detach_value, detach_gate = meta
+        kv, gate, s, normed, out = _block_forward(emb, hidden, w, hist, nk, nq, nc, cw, hc, n, K, eps, dil, True)
+        hist_len = (K - 1) * dil
+        full = torch.cat([hist, normed], dim=0) if hist.shape[0] else normed
+        new_hist = full[-hist_len:].clone() if hist_len > 0 else full[:0].clone()
+        ctx.save_for_backward(hidden, hist, kv, gate, s, normed, nk, nq, nc, cw)
+        ctx.w, ctx.meta = w, meta
+        ctx.tail_len = new_hist.shape[0]
+        ctx.mark_non_differentiable(gate, s)
+        return out, new_hist, gate, s
+
+    @staticmethod
+    def backward(ctx, dout, dtail, _dgate, _ds):
+        hidden, hist, kv, gate, s, normed, nk, nq, nc, cw = ctx.saved_tensors
+        hc, n, K, eps, dil, detach_value, detach_gate = ctx.meta
+        T, H = hidden.shape[0], hist.shape[0]
+        dev = hidden.device
+        lib = L.load()
+        stream = L.stream_of(dev)
+        dout = torch.zeros_like(hidden) if dout is None else dout.contiguous()
+        dtail = None if dtail is None or ctx.tail_len == 0 else dtail.contiguous()
+        dconv = torch.empty(T, hc, n, device=dev)
+        dnormed = torch.empty(T, hc, n, device=dev)
+        dhist = torch.empty(H, hc, n, device=dev) if (H and ctx.needs_input_grad[2]) else None
+        st = lib.engram_ple_conv_backward(normed.data_ptr(), hist.data_ptr() if H else None, H, cw.data_ptr(), K, dil,
+                                          T, hc, n, dout.data_ptr(), L.ptr(dtail), ctx.tail_len if dtail is not None
+                                          else 0, dconv.data_ptr(), dnormed.data_ptr(), L.ptr(dhist), stream)
+        L.check(st, "engram_ple_conv_backward")
+        stride = hc * n + n
+        dkv = torch.empty(T, stride, device=dev)
+        dhidden = torch.empty(T, hc, n, device=dev)
+        st = lib.engram_ple_gate_backward(kv.data_ptr(), stride, kv[:, hc * n:].data_ptr(), stride, hidden.data_ptr(),
+                                          nk.data_ptr(), nq.data_ptr(), nc.data_ptr(), gate.data_ptr(), s.data_ptr(),
+                                          dout.data_ptr(), dnormed.data_ptr(), T, hc, n, eps, int(detach_value),
+                                          int(detach_gate), dkv.data_ptr(), stride, dkv[:, hc * n:].data_ptr(), stride,
+                                          dhidden.data_ptr(), stream)
+        L.check(st, "engram_ple_gate_backward")
+        demb = None
+        if ctx.needs_input_grad[0]:
+            demb = project_back(dkv, ctx.w, torch.empty(T, n, device=dev))
+        return (demb, dhidden if ctx.needs_input_grad[1] else None, dhist, None, None, None, None, None, None)
+
+
 def _f32(x: torch.Tensor, name: str, shape) -> torch.Tensor:
     if not x.is_cuda or x.dtype != torch.float32:
         raise ValueError(f"{name}: needs a float32 CUDA tensor (got {x.dtype} on {x.device})")
@@ -101,11 +205,11 @@ def _f32(x: torch.Tensor, name: str, shape) -> torch.Tensor:
 def ple_forward(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor, hparams,
                 diag: dict | None = None, detach_value: bool = False, detach_gate: bool = False):
     """(hidden + gated + silu(conv), new history tail): see the reference's
-    docstring.  detach_value / detach_gate change only gradients, which this
-    forward-only block does not produce; diag receives the same five tensors."""
-    if needs_grad(emb, hidden, w, hist):
-        raise NotImplementedError("engraft_ngram_b200.ple_forward is forward-only; run the block's backward "
-                                  "with the reference's ple_forward (install_ple routes such calls there)")
+    docstring.  Differentiable in emb, hidden and hist (detach_value /
+    detach_gate as in the reference); diag receives the same five tensors."""
+    if weights_need_grad(w):
+        raise NotImplementedError("engraft_ngram_b200.ple_forward does not build gradients of the block's weights; "
+                                  "install_ple routes such calls to the reference's ple_forward")
     hc, n = int(hparams.hc_mult), int(hparams.n_embd)
     eps, dil = float(hparams.f_norm_rms_eps), int(hparams.ple_ngram_size)
     T = emb.shape[0]
@@ -114,37 +218,30 @@ def ple_forward(emb: torch.Tensor, hidden: torch.Tensor, w, hist: torch.Tensor, 
     hidden = _f32(hidden, "hidden", (T, hc, n))
     _f32(w.w_key, "w_key", (hc * n, n))
     _f32(w.w_value, "w_value", (n, n))
-    nk = _f32(w.norm_key.reshape(-1), "norm_key", (hc * n,))
-    nq = _f32(w.norm_query.reshape(-1), "norm_query", (hc * n,))
-    nc = _f32(w.norm_conv.reshape(-1), "norm_conv", (hc * n,))
-    cw = _f32(w.conv1d, "conv1d", (hc * n, K))
+    nk = _f32(w.norm_key.detach().reshape(-1), "norm_key", (hc * n,))
+    nq = _f32(w.norm_query.detach().reshape(-1), "norm_query", (hc * n,))
+    nc = _f32(w.norm_conv.detach().reshape(-1), "norm_conv", (hc * n,))
+    cw = _f32(w.conv1d.detach(), "conv1d", (hc * n, K))
     H = hist.shape[0]
-    hist = _f32(hist, "hist", (H, hc, n)) if H else hist
-    dev = emb.device
-    lib = L.load()
-    stream = L.stream_of(dev)
-    kv = project(emb, w, torch.empty(T, hc * n + n, device=dev))
-    stride = hc * n + n
-    value = kv[:, hc * n:]
-    gate = torch.empty(T, hc, device=dev)
-    s = torch.empty(T, hc, device=dev) if diag is not None else None
-    normed = torch.empty(T, hc, n, device=dev)
-    st = lib.engram_ple_gate(kv.data_ptr(), stride, value.data_ptr(), stride, hidden.data_ptr(), nk.data_ptr(),
-                             nq.data_ptr(), nc.data_ptr(), T, hc, n, eps, gate.data_ptr(), L.ptr(s),
-                             normed.data_ptr(), stream)
-    L.check(st, "engram_ple_gate")
-    out = torch.empty(T, hc, n, device=dev)
-    st = lib.engram_ple_conv(value.data_ptr(), stride, hidden.data_ptr(), gate.data_ptr(), normed.data_ptr(),
-                             hist.data_ptr() if H else None, H, cw.data_ptr(), K, dil, T, hc, n, out.data_ptr(),
-                             stream)
-    L.check(st, "engram_ple_conv")
-    hist_len = (K - 1) * dil
-    hist_full = torch.cat([hist.to(normed.dtype), normed], dim=0) if H else normed
-    new_hist = hist_full[-hist_len:] if hist_len > 0 else hist_full[:0]
+    hist = _f32(hist, "hist", (H, hc, n)) if H else hist.reshape(0, hc, n)
+    if needs_grad(emb, hidden, w, hist):
+        out, new_hist, gate, s = _PleBlockFn.apply(emb, hidden, hist, w, nk, nq, nc, cw,
+                                                   (hc, n, K, eps, dil, bool(detach_value), bool(detach_gate)))
+        value = None
+    else:
+        kv, gate, s, normed, out = _block_forward(emb, hidden, w, hist, nk, nq, nc, cw, hc, n, K, eps, dil,
+                                                  diag is not None)
+        value = kv[:, hc * n:]
+        hist_len = (K - 1) * dil
+        hist_full = torch.cat([hist.to(normed.dtype), normed], dim=0) if H else normed
+        new_hist = hist_full[-hist_len:] if hist_len > 0 else hist_full[:0]
     if diag is not None:
-        diag["s"] = s
-        diag["gate"] = gate
-        diag["value_norm"] = value.norm(dim=-1)
-        diag["gated_norm"] = (value.unsqueeze(1) * gate.unsqueeze(-1)).norm(dim=-1)
-        diag["hidden_norm"] = hidden.norm(dim=-1)
+        with torch.no_grad():
+            if value is None:  # the differentiable call keeps no value: project again for the diagnostics
+                value = project(emb.detach(), w, torch.empty(T, hc * n + n, device=emb.device))[:, hc * n:]
+            diag["s"] = s.detach().clone()
+            diag["gate"] = gate.detach().clone()
+            diag["value_norm"] = value.norm(dim=-1)
+            diag["gated_norm"] = (value.unsqueeze(1) * gate.detach().unsqueeze(-1)).norm(dim=-1)
+            diag["hidden_norm"] = hidden.detach().norm(dim=-1)
     return out, new_hist

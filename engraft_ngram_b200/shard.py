@@ -142,12 +142,18 @@ class ShardedTable:
 
     def enable_exchange_staging(self, n_tokens_max: int, exchange=None) -> None:
         """Make prefetch() plan and exchange the rows of other ranks ahead of the
-        forward, deduplicated, through `exchange` (default NcclRowExchange():
-        NCCL all-to-alls on a process group of their own; LocalRowExchange for
-        emulated ranks).  Prefetching two batches ahead of the forward keeps
+        forward, deduplicated, through `exchange`: "peer" (the default,
+        PeerRowExchange: owners gather into symmetric memory, requesters copy
+        with the copy engines), "nccl" (NcclRowExchange: NCCL all-to-alls on a
+        process group of their own) or an exchange object (LocalRowExchange
+        for emulated ranks).  Prefetching two batches ahead of the forward keeps
         both the host and the forward from waiting on the exchange (see
         ExchangeStage).  With NcclRowExchange a collective: every rank calls it."""
-        self.xstage = ExchangeStage(self, n_tokens_max, exchange if exchange is not None else NcclRowExchange())
+        if exchange is None or exchange == "peer":
+            exchange = PeerRowExchange(self, n_tokens_max)
+        elif exchange == "nccl":
+            exchange = NcclRowExchange()
+        self.xstage = ExchangeStage(self, n_tokens_max, exchange)
 
     def prefetch(self, tokens, seg_start=None, t0: int = 0, n: int | None = None, max_blocks: int = 0,
                  stream: torch.cuda.Stream | None = None, omap: OverlayMap | None = None) -> None:
@@ -466,7 +472,9 @@ class ExchangeStage:
         self.set_keys = torch.empty(self.cap, dtype=torch.int32, device=dev)
         self.set_vals = torch.empty(self.cap, dtype=torch.int32, device=dev)
         W = table.world
-        self.send_ids = [torch.empty(entries, dtype=torch.int32, device=dev) for _ in range(self.SETS)]
+        alloc = getattr(exchange, "alloc_ids", None)
+        self.send_ids = [alloc(b, entries) if alloc is not None else torch.empty(entries, dtype=torch.int32, device=dev)
+                         for b in range(self.SETS)]
         self.rix = [torch.empty(entries, dtype=torch.int32, device=dev) for _ in range(self.SETS)]
         self.counts = [torch.zeros(2 * W, dtype=torch.int64, device=dev) for _ in range(self.SETS)]
         self.counts_host = [torch.zeros(W, W, dtype=torch.int64).pin_memory() for _ in range(self.SETS)]
@@ -479,7 +487,9 @@ class ExchangeStage:
         self.omap_keys = [None] * self.SETS
         self.seq = [0] * self.SETS
         self.n_seq = 0
-        self.side = torch.cuda.Stream(dev)
+        # the plan and the owners' gathers run between the step's kernels: a high-priority side stream gets
+        # the SMs as soon as the current kernel's blocks retire
+        self.side = torch.cuda.Stream(dev, priority=-1)
         self._empty = torch.zeros(16, dtype=torch.uint8, device=dev)
         self.last = None  # (distinct remote rows, remote (position, head) pairs) of the last exchanged batch
 
@@ -517,6 +527,9 @@ class ExchangeStage:
             ss.record_stream(self.side)
         with torch.cuda.stream(self.side):
             allc = self.exchange.gather_counts(t, self.counts[b][: t.world])
+            serve = getattr(self.exchange, "serve", None)
+            if serve is not None:  # owners gather what the others asked of them now (no host sizes needed)
+                serve(t, b, allc)
             self.counts_host[b].copy_(allc.reshape(t.world, t.world), non_blocking=True)
         self.ev_counts[b] = torch.cuda.Event()
         self.ev_counts[b].record(self.side)
@@ -536,7 +549,11 @@ class ExchangeStage:
         recv = [int(x) for x in m[:, t.rank].tolist()]
         total = sum(send)
         with torch.cuda.stream(self.side):
-            rows = self.exchange.rows(t, self.send_ids[b][:total], send, recv)
+            fetch = getattr(self.exchange, "fetch", None)
+            if fetch is not None:
+                rows = fetch(t, b, m)
+            else:
+                rows = self.exchange.rows(t, self.send_ids[b][:total], send, recv)
         self.recv[b] = rows if rows.numel() else self._empty
         self.ev_ready[b] = torch.cuda.Event()
         self.ev_ready[b].record(self.side)
@@ -552,6 +569,7 @@ class ExchangeStage:
         if self.state[b] == "planned":
             self._exchange(b)
         self.key[b] = None
+        self.recv[b].record_stream(torch.cuda.current_stream(self.table.device))  # read by the forward there
         return b, self.recv[b], self.rix[b], self.ev_ready[b]
 
     def consumed(self, b: int, stream: torch.cuda.Stream) -> None:
@@ -593,6 +611,81 @@ class NcclRowExchange:
         self.dist.all_to_all_single(rows, served, [c * stride for c in send_counts],
                                     [c * stride for c in recv_counts], group=self.group)
         return rows
+
+
+class PeerRowExchange:
+    """ExchangeStage's exchange over peer memory with copy-engine transfers.
+
+    Each rank's send_ids (three sets) and a send buffer per set live in torch
+    symmetric memory (no multicast object).  Per batch: the counts all-gather
+    (NCCL, on a group of its own) also orders every rank's plan before the
+    owners read it; serve() has each owner gather, in one kernel
+    (engram_shard_serve), the rows every other rank asked of it into its send
+    buffer, reading the requests through the peers' send_ids, then a barrier
+    (a 4-byte all-reduce); fetch() has the requester copy its block from each
+    owner's send buffer with one cudaMemcpyAsync per owner (torch copy_ from a
+    peer view): copy engines over NVLink, no SMs.  The block sizes come from
+    the counts matrix read on the host one step late (ExchangeStage).  A
+    collective to construct: every rank of `group` calls it."""
+
+    def __init__(self, table: "ShardedTable", n_tokens_max: int, group=None, sets: int = 3):
+        import torch.distributed as dist
+        from .dist import symmetric_memory
+        symm = symmetric_memory()
+        self.dist = dist
+        base = group if group is not None else dist.group.WORLD
+        self.group = dist.new_group(ranks=dist.get_process_group_ranks(base))
+        W, dev = table.world, table.device
+        entries = max(int(n_tokens_max) * table.n_heads, 1)
+        self.max_rows = max((W - 1) * entries, 1)  # rows one owner may serve per batch
+        self.stride = table.stride
+        self.ids, self.id_ptrs, self.rows, self.row_handles, self._keep = [], [], [], [], []
+        for _ in range(sets):
+            ids = symm.empty(entries, dtype=torch.int32, device=dev)
+            hi = symm.rendezvous(ids, self.group)
+            rows = symm.empty(self.max_rows * self.stride, dtype=torch.uint8, device=dev)
+            hr = symm.rendezvous(rows, self.group)
+            self.ids.append(ids)
+            self.id_ptrs.append(torch.tensor(list(hi.buffer_ptrs), dtype=torch.int64, device=dev))
+            self.rows.append(rows)
+            self.row_handles.append(hr)
+            self._keep.append(hi)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def alloc_ids(self, b: int, entries: int) -> torch.Tensor:
+        return self.ids[b][:entries]
+
+    def gather_counts(self, table, counts: torch.Tensor) -> torch.Tensor:
+        W = table.world
+        out = torch.empty(W * W, dtype=torch.int64, device=counts.device)
+        self.dist.all_gather_into_tensor(out, counts.contiguous(), group=self.group)
+        return out
+
+    def serve(self, table, b: int, counts_all: torch.Tensor) -> None:
+        st = L.load().engram_shard_serve(table.shard.data_ptr(), table.stride, table.n_local, table.world, table.rank,
+                                         self.id_ptrs[b].data_ptr(), counts_all.data_ptr(), self.rows[b].data_ptr(),
+                                         self.max_rows, L.stream_of(table.device))
+        L.check(st, "engram_shard_serve")
+        self.dist.all_reduce(self.flag, group=self.group)  # every owner's rows are in place
+
+    def fetch(self, table, b: int, m: torch.Tensor) -> torch.Tensor:
+        """This rank's rows of batch set b, in send order (owner after owner)."""
+        W, me, stride = table.world, table.rank, self.stride
+        mm = m.tolist()
+        total = sum(mm[me])
+        out = torch.empty(max(total, 1) * stride, dtype=torch.uint8, device=table.device)
+        off = 0
+        for o in range(W):
+            cnt = mm[me][o]
+            if o == me or cnt == 0:
+                continue
+            base = sum(mm[r][o] for r in range(me) if r != o)  # this rank's first row in owner o's send buffer
+            if base + cnt > self.max_rows:
+                raise RuntimeError(f"owner {o} holds {base + cnt} rows for this batch, its send buffer {self.max_rows}")
+            src = self.row_handles[b].get_buffer(o, (self.max_rows * stride,), torch.uint8)
+            out[off * stride:(off + cnt) * stride].copy_(src[base * stride:(base + cnt) * stride], non_blocking=True)
+            off += cnt
+        return out[: total * stride]
 
 
 class LocalRowExchange:

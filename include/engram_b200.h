@@ -315,6 +315,24 @@ ENGRAM_API int engram_forward_exchanged(const engram_table* t, const engram_over
                                         int64_t* hit_count, void* stream);
 
 /*
+ * Owner side of the peer-memory exchange of engram_shard_plan's requests:
+ * counts_all (device int64 [world * world], entry r*world + o = M[r][o], the
+ * rows rank r requests from owner o: every rank's plan counts, gathered) and
+ * id_ptrs (device array [world] of pointers valid here, e.g. symmetric memory:
+ * each rank's send_ids) say what every other rank r wants from this rank:
+ * its ids at [sum_{o < rank} M[r][o], + M[r][rank]) of r's send_ids.  Their
+ * rows, read from this rank's shard (row g at local row g / world), go to
+ * send_rows, requester after requester: r's at rows [sum_{r' < r, r' != rank}
+ * M[r'][rank], + M[r][rank]), row_stride bytes each, so requester r can copy
+ * its block as one transfer.  Rows at or past max_rows are not written.  The
+ * caller orders it after every rank's plan and before any rank's copy.  No
+ * reference counterpart.
+ */
+ENGRAM_API int engram_shard_serve(const void* shard_rows, int64_t stride, int64_t n_local, int32_t world, int32_t rank,
+                                  const void* id_ptrs, const int64_t* counts_all, void* send_rows, int64_t max_rows,
+                                  void* stream);
+
+/*
  * Owner side: out[k] = the resident row of global id ids[k] from this rank's
  * shard (local index ids[k] / world; stride bytes per row, 16-byte multiple).
  * Ids outside the shard give zero rows.
@@ -547,6 +565,38 @@ ENGRAM_API int engram_ple_conv(const float* value, int64_t value_stride, const f
                                const float* normed, const float* hist, int64_t hist_len, const float* conv_w,
                                int32_t K, int32_t dilation, int64_t T, int32_t hc, int32_t n_embd, float* out,
                                void* stream);
+
+/*
+ * Backward of the PLE block after its projections (the autograd of
+ * engraft/replica/layers.py:565-626 that the descent's loss.backward() runs,
+ * engraft/replica/seq.py:1457-1462), fp32.
+ * engram_ple_gate_backward, per position t and stream j, from the forward's
+ *   inputs (key = emb @ w_key.T before its norm, value, hidden, the three norm
+ *   weights), its gate and s (engram_ple_gate's gate and s_out), the gradient
+ *   of out (dout [T, hc, n]) and of normed (dnormed [T, hc, n], from
+ *   engram_ple_conv_backward): dkey [T, hc*n] (row stride dkey_stride, the
+ *   gradient of key), dvalue [T, n] (row stride dvalue_stride) and dhidden
+ *   [T, hc, n] (the direct term of out plus the query norm's).  detach_value /
+ *   detach_gate: the reference's flags (the value, or the gate, gets no
+ *   gradient through gated = value * gate).  The projections' own backward,
+ *   d_emb = dkey @ w_key + dvalue @ w_value, is a GEMM the caller runs.
+ * engram_ple_conv_backward: dconv (device scratch [T, hc*n]) = dout * silu'(conv)
+ *   with conv recomputed from normed and hist; then the transposed conv:
+ *   dnormed [T, hc, n] and dhist [hist_len, hc, n] (nullable: not wanted),
+ *   adding dtail [tail_len, hc, n] (nullable), the gradient of the new history
+ *   tail (the last tail_len rows of [hist; normed]).
+ * Agrees with torch's autograd of the reference to fp32 rounding.
+ */
+ENGRAM_API int engram_ple_gate_backward(const float* key, int64_t key_stride, const float* value, int64_t value_stride,
+                                        const float* hidden, const float* norm_key, const float* norm_query,
+                                        const float* norm_conv, const float* gate, const float* s, const float* dout,
+                                        const float* dnormed, int64_t T, int32_t hc, int32_t n_embd, float eps,
+                                        int32_t detach_value, int32_t detach_gate, float* dkey, int64_t dkey_stride,
+                                        float* dvalue, int64_t dvalue_stride, float* dhidden, void* stream);
+ENGRAM_API int engram_ple_conv_backward(const float* normed, const float* hist, int64_t hist_len, const float* conv_w,
+                                        int32_t K, int32_t dilation, int64_t T, int32_t hc, int32_t n_embd,
+                                        const float* dout, const float* dtail, int64_t tail_len, float* dconv,
+                                        float* dnormed, float* dhist, void* stream);
 
 #ifdef __cplusplus
 }

@@ -87,3 +87,38 @@ def shard_plan_ref(ids, ov_ids, world: int, rank: int):
     rix = np.full(flat.shape, -1, dtype=np.int32)
     rix[remote] = order[np.searchsorted(send[order], flat[remote])]
     return send.astype(np.int32), counts, rix
+
+
+def ple_block_torch(emb, hidden, w, hist, hc: int, n: int, eps: float, dil: int, detach_value: bool = False,
+                    detach_gate: bool = False):
+    """The PLE block's formula (engraft/replica/layers.py:565-626) restated in
+    plain torch, differentiable, in the dtype of its inputs (the tests run it in
+    float64 as the reference for the CUDA backward).  Returns (out, new_hist)."""
+    import torch
+    T = emb.shape[0]
+
+    def rms(x, wt):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * wt.reshape(hc, n)
+
+    key = (emb @ w["w_key"].T).reshape(T, hc, n)
+    s = (rms(key, w["norm_key"]) * rms(hidden, w["norm_query"])).sum(-1) / n ** 0.5
+    gate = torch.sigmoid(torch.sign(s) * torch.sqrt(s.abs().clamp(min=1e-6)))
+    value = emb @ w["w_value"].T
+    g = gate.detach() if detach_gate else gate
+    v = value.detach() if detach_value else value
+    gated = v.unsqueeze(1) * g.unsqueeze(-1)
+    normed = rms(gated, w["norm_conv"])
+    K = w["conv1d"].shape[1]
+    H = hist.shape[0]
+    full = torch.cat([hist, normed]).reshape(H + T, hc * n)
+    pad = torch.cat([torch.zeros((K - 1) * dil, hc * n, dtype=full.dtype, device=full.device), full])
+    acc = torch.zeros(T, hc * n, dtype=full.dtype, device=full.device)
+    for k in range(K):
+        back = (K - 1 - k) * dil
+        # out t reads full row H + t - back, i.e. pad row (K-1)*dil + H + t - back; rows of pad before the
+        # history are zeros, which is the reference's "no term before the history"
+        lo = (K - 1) * dil + H - back
+        acc = acc + pad[lo:lo + T] * w["conv1d"][:, k]
+    out = hidden + gated + torch.nn.functional.silu(acc).reshape(T, hc, n)
+    tail = (K - 1) * dil
+    return out, torch.cat([hist, normed])[-tail:] if tail > 0 else normed[:0]

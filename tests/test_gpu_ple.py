@@ -103,17 +103,82 @@ def test_ple_block_at_real_width(T, n_hist, projection):
     assert _close(out, want_out.cpu().numpy()) and _close(new_hist, want_hist.cpu().numpy())
 
 
-def test_ple_block_refuses_gradients_and_install_routes_them():
-    """A call that needs a gradient raises in the B200 block; install_ple sends
-    such calls to the original function and the others to the B200 block."""
+def _ple_grads(eb, c, hc, n, dout, dtail, dv=False, dg=False, w=None):
+    emb, hidden, hist = (torch.as_tensor(c[k]).to(DEV).requires_grad_(True) for k in ("emb", "hidden", "hist"))
+    w = w if w is not None else _weights(c)
+    out, new_hist = eb.ple_forward(emb, hidden, w, hist, _hp(hc, n), detach_value=dv, detach_gate=dg)
+    loss = (out * torch.as_tensor(dout).to(DEV)).sum() + (new_hist * torch.as_tensor(dtail).to(DEV)).sum()
+    loss.backward()
+    torch.cuda.synchronize()
+    return {"demb": emb.grad, "dhidden": hidden.grad, "dhist": hist.grad}
+
+
+@pytest.mark.parametrize("case", FX.PLE_CASES)
+def test_ple_backward_matches_reference_golden(case, projection):
+    """Gradients of emb, hidden and hist through the B200 block (the CUDA
+    backward kernels and the projection GEMM back) equal the reference's own
+    autograd gradients (tests/golden/ple_backward_golden.npz) within the fp32
+    tolerance, with the detach_value / detach_gate variants on the first case."""
+    from pathlib import Path
+    import engraft_ngram_b200 as eb
+    from make_ple_backward_golden import VARIANTS, upstream
+    gold = np.load(Path(__file__).parent / "golden" / "ple_backward_golden.npz")
+    seed, T, n_hist = case
+    c = FX.ple_case(seed, T, n_hist)
+    first = case == FX.PLE_CASES[0]
+    for suffix, dv, dg in (VARIANTS if first else VARIANTS[:1]):
+        tail = min((FX.PLE_K - 1) * FX.PLE_DIL, n_hist + T)
+        dout, dtail = upstream(seed, T, tail)
+        got = _ple_grads(eb, c, FX.PLE_HC, FX.PLE_N, dout, dtail, dv, dg)
+        for name in ("demb", "dhidden", "dhist"):
+            want = gold[f"ple{seed}{suffix}_{name}"]
+            g = got[name]
+            if want.size == 0:
+                continue
+            assert g is not None and _close(g, want), (seed, suffix, name)
+
+
+@pytest.mark.parametrize("T,n_hist", [(24, 0), (6, 9)])
+def test_ple_backward_at_real_width(T, n_hist, projection):
+    """hc = 4, n_embd = 2560, K = 4, dilation 3: the CUDA backward against the
+    float64 torch restatement of the block differentiated by autograd."""
+    import engraft_ngram_b200 as eb
+    from cases import ple_block_torch
+    hc, n, K = 4, 2560, 4
+    g = torch.Generator(device=DEV).manual_seed(100 + T)
+    r = lambda *s: torch.randn(*s, generator=g, device=DEV) * 0.1  # noqa: E731
+    wd = dict(w_key=r(hc * n, n), w_value=r(n, n), norm_key=1 + r(hc * n), norm_query=1 + r(hc * n),
+              norm_conv=1 + r(hc * n), conv1d=r(hc * n, K))
+    c = dict(emb=r(T, n), hidden=r(T, hc, n), hist=r(n_hist, hc, n))
+    tail = min((K - 1) * 3, n_hist + T)
+    dout, dtail = torch.randn(T, hc, n, generator=g, device=DEV), torch.randn(tail, hc, n, generator=g, device=DEV)
+    got = _ple_grads(eb, c, hc, n, dout, dtail, w=types.SimpleNamespace(**wd))
+    emb, hidden, hist = (c[k].double().requires_grad_(True) for k in ("emb", "hidden", "hist"))
+    o, h = ple_block_torch(emb, hidden, {k: v.double() for k, v in wd.items()}, hist, hc, n, 1e-6, 3)
+    ((o * dout.double()).sum() + (h * dtail.double()).sum()).backward()
+    for name, t in (("demb", emb), ("dhidden", hidden), ("dhist", hist)):
+        if t.grad is None or t.numel() == 0:
+            continue
+        assert _close(got[name], t.grad.float().cpu().numpy()), name
+
+
+def test_ple_block_weight_gradients_route_to_the_reference():
+    """Gradients of emb, hidden and hist run on the B200 block; a call that
+    needs gradients of the block's weights raises there, and install_ple sends
+    exactly those calls to the original function."""
     import engraft_ngram_b200 as eb
     c = FX.ple_case(1, 3, 0)
     w = _weights(c)
     emb = torch.from_numpy(c["emb"]).to(DEV).requires_grad_(True)
     hidden = torch.from_numpy(c["hidden"]).to(DEV)
     hist = torch.from_numpy(c["hist"]).to(DEV)
+    out, _ = eb.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N))
+    out.sum().backward()
+    assert emb.grad is not None and torch.isfinite(emb.grad).all()
+    w_train = _weights(c)
+    w_train.conv1d.requires_grad_(True)
     with pytest.raises(NotImplementedError):
-        eb.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N))
+        eb.ple_forward(emb, hidden, w_train, hist, _hp(FX.PLE_HC, FX.PLE_N))
     calls = []
     fake = types.ModuleType("fake_layers")
     fake.ple_forward = lambda *a, **k: calls.append("orig") or ("orig", None)
@@ -122,10 +187,9 @@ def test_ple_block_refuses_gradients_and_install_routes_them():
     mods = {"engraft.replica.layers": fake, "engraft.replica.model": fake_model}
     eb.install_ple(mods)
     try:
-        assert fake.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N)) == ("orig", None)
-        with torch.no_grad():
-            out, _ = fake_model.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N))
-        assert isinstance(out, torch.Tensor) and calls == ["orig"]
+        assert fake.ple_forward(emb, hidden, w_train, hist, _hp(FX.PLE_HC, FX.PLE_N)) == ("orig", None)
+        out, _ = fake_model.ple_forward(emb, hidden, w, hist, _hp(FX.PLE_HC, FX.PLE_N))  # emb needs a gradient
+        assert isinstance(out, torch.Tensor) and out.requires_grad and calls == ["orig"]
     finally:
         eb.uninstall_ple(mods)
     assert fake.ple_forward is not None and fake.ple_forward(None, None, None, None, None) == ("orig", None)

@@ -258,3 +258,81 @@ def test_autograd_through_peer_rows_matches_allreduce_on_two_ranks():
     """Two ranks, public autograd API: PeerRows.attach + PeerAdam equals the
     NCCL all-reduce of the row gradients + OverlayAdam bit for bit."""
     assert _run_ranks(_autograd_peer) == {0: True, 1: True}
+
+
+def _exchange_staging(rank: int, world: int, port: int, out) -> None:
+    """Each rank: its shard in plain local memory and exchange staging (the
+    default peer exchange: owners gather into symmetric memory, requesters copy
+    with the copy engines); four batches with the prefetch two ahead, each
+    forward equal bit for bit to the resident-table forward of the same batch."""
+    import ctypes as C
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(RANK_ENV, MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=PG_TIMEOUT_S), device_id=dev)
+    try:
+        import engraft_ngram_b200 as eb
+        from engraft_ngram_b200 import _lib as L
+        from engraft_ngram_b200.shard import ShardedTable
+        from engraft_ngram_b200.table import synthetic_head_sizes, synthetic_multipliers, synthetic_resident
+        n_rows, fmt, dim, T, eos = 60_013, L.FMT_NAMES["iq4_xs"], 256, 1500, 151_935
+        mode = L.MODE_PAIRSUM_ADD_BF16
+        sizes = synthetic_head_sizes(n_rows)
+        offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
+        mult = synthetic_multipliers(4)
+        full = eb.DeviceTable(synthetic_resident(n_rows, fmt, dim, 11, dev), fmt, dim, sizes, offs, mult, eos,
+                              n_rows=n_rows)
+        ok = True
+        for exchange in ("peer", "nccl"):
+            sh = ShardedTable.from_full(full, world, rank)
+            sh.enable_exchange_staging(T, exchange)
+            rng = np.random.default_rng(9)  # the overlay is the same on every rank
+            ov_ids = np.unique(rng.integers(0, n_rows, size=3000)).astype(np.int32)
+            omap = eb.OverlayMap(torch.from_numpy(ov_ids), dev)
+            rows_var = torch.from_numpy((rng.standard_normal((len(ov_ids), dim)) * 0.01).astype(np.float32)).to(dev)
+            ranks = np.arange(1, 151_937, dtype=np.float64)
+            cdf = np.cumsum(ranks ** -1.1)
+            cdf /= cdf[-1]
+            rr = np.random.default_rng(400 + rank)  # each rank its own batches
+            batches = []
+            for _ in range(4):
+                toks = np.searchsorted(cdf, rr.random(T)).astype(np.int32)
+                seg = np.sort(rr.integers(0, 3, size=T))
+                ss = np.concatenate([[0], np.flatnonzero(np.diff(seg)) + 1])
+                starts = np.repeat(ss, np.diff(np.concatenate([ss, [T]]))).astype(np.int32)
+                batches.append((torch.from_numpy(toks).to(dev), torch.from_numpy(starts).to(dev)))
+            res0 = (torch.from_numpy(rr.standard_normal((T, 8 * dim)).astype(np.float32)) * 0.5).to(dev).to(
+                torch.bfloat16)
+
+            def resident(tok, ss):
+                o = res0.clone()
+                ov = omap.descriptor(rows_var)
+                st = L.load().engram_forward(C.byref(full.ctable), C.byref(ov), tok.data_ptr(), ss.data_ptr(), 0, T,
+                                             mode, o.data_ptr(), None, None, None, L.stream_of(dev))
+                L.check(st, "engram_forward")
+                return o
+
+            sh.prefetch(*batches[0], omap=omap)
+            sh.prefetch(*batches[1], omap=omap)
+            for k in range(4):
+                if k + 2 < 4:
+                    sh.prefetch(*batches[k + 2], omap=omap)
+                got = res0.clone()
+                sh.forward(batches[k][0], batches[k][1], omap, rows_var, got, mode)
+                ok &= torch.equal(got.view(torch.int16), resident(*batches[k]).view(torch.int16))
+            torch.cuda.synchronize()
+        dist.barrier()
+        out[rank] = bool(ok)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_exchange_staging_matches_resident_table_on_two_ranks():
+    """Two ranks, table row-sharded in local memory: the deduplicated exchange,
+    planned two batches ahead, over peer memory with copy-engine transfers and
+    over NCCL all-to-alls, feeds forwards bit-identical to the resident-table
+    forward."""
+    assert _run_ranks(_exchange_staging) == {0: True, 1: True}

@@ -172,3 +172,30 @@ def test_ple_block_oracle_matches_reference(golden, case):
     assert out.shape == ref_out.shape and hist.shape == ref_hist.shape
     assert np.abs(out - ref_out).max() <= PLE_TOL * max(1.0, np.abs(ref_out).max())
     assert np.abs(hist - ref_hist).max() <= PLE_TOL * max(1.0, np.abs(ref_hist).max())
+
+
+def test_ple_backward_restatement_matches_reference_golden():
+    """The float64 torch restatement of the PLE block (cases.ple_block_torch),
+    differentiated by autograd, gives the reference's own gradients of emb,
+    hidden and hist (tests/golden/ple_backward_golden.npz, made by running the
+    reference), with the detach_value / detach_gate variants."""
+    import torch
+    import fixtures as FX
+    from cases import ple_block_torch
+    from make_ple_backward_golden import VARIANTS, upstream
+    from pathlib import Path
+    gold = np.load(Path(__file__).parent / "golden" / "ple_backward_golden.npz")
+    for idx, (seed, T, n_hist) in enumerate(FX.PLE_CASES):
+        c = FX.ple_case(seed, T, n_hist)
+        w = {k: torch.from_numpy(c[k]).double() for k in
+             ("w_key", "w_value", "norm_key", "norm_query", "norm_conv", "conv1d")}
+        for suffix, dv, dg in (VARIANTS if idx == 0 else VARIANTS[:1]):
+            emb, hidden, hist = (torch.from_numpy(c[k]).double().requires_grad_(True) for k in ("emb", "hidden", "hist"))
+            o, h = ple_block_torch(emb, hidden, w, hist, FX.PLE_HC, FX.PLE_N, FX.PLE_EPS, FX.PLE_DIL, dv, dg)
+            dout, dtail = upstream(seed, T, h.shape[0])
+            ((o * torch.from_numpy(dout).double()).sum() + (h * torch.from_numpy(dtail).double()).sum()).backward()
+            for name, t in (("demb", emb), ("dhidden", hidden), ("dhist", hist)):
+                want = gold[f"ple{seed}{suffix}_{name}"]
+                got = t.grad.numpy() if t.grad is not None else np.zeros_like(want)
+                assert got.shape == want.shape
+                assert want.size == 0 or np.abs(got - want).max() <= 1e-5 * max(1.0, np.abs(want).max()), (seed, suffix, name)

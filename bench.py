@@ -80,8 +80,8 @@ def parse():
                     help="N>1: skip the second measurement with the table row-sharded")
     ap.add_argument("--layout", choices=["sharded", "replicated"], default="sharded",
                     help="N>1, config 5: the table row-sharded across the ranks (owner = id mod N; each rank's "
-                         "distinct remote rows planned two batches ahead and exchanged by NCCL all-to-all on a side "
-                         "stream), or replicated on every rank; the other layout is measured beside it")
+                         "remote rows routed three batches ahead, gathered by their owners and copied with the copy "
+                         "engines over NVLink), or replicated on every rank; the other layout is measured beside it")
     ap.add_argument("--stage", choices=["exchange", "push", "pull", "off"], default="exchange",
                     help="--shard, peer reads: copy the next step's rows of other ranks on a side stream while the "
                          "current step runs (ShardedTable.prefetch), so the forward reads every row locally; push: "
@@ -148,7 +148,8 @@ class Workload:
             n_local = (cfg["rows"] - rank + world - 1) // world
             if cfg.get("stage") == "exchange":
                 # this rank's shard in plain local memory; the rows of other ranks arrive deduplicated through
-                # NCCL all-to-alls planned two batches ahead (ShardedTable.enable_exchange_staging)
+                # owners' gathers and copy-engine transfers, staged three batches ahead
+                # (ShardedTable.enable_exchange_staging)
                 rows = synthetic_resident(n_local, fmt, self.dim, seed * 7919 + rank, device)
                 self.shard = ShardedTable(rows, fmt, self.dim, sizes, offs, mult, EOS, world, rank, cfg["rows"])
                 self.shard.enable_exchange_staging(cfg["seqs"] * cfg["seq_len"])
@@ -186,9 +187,11 @@ class Workload:
         self.seg_start = (torch.arange(self.T, device=device, dtype=torch.int32) // cfg["seq_len"]) * cfg["seq_len"]
         # staged sharded reads: step k+1's rows are copied while step k runs; the two steps' batches live in two
         # buffers (same tokens here), so each copy is for a distinct batch
-        # (the exchange is planned two batches ahead, so three batches are in flight: three buffers)
-        self.depth = 2 if self.stage == "exchange" else 1
+        # (the exchange is staged three batches ahead, so four batches are in flight: four buffers)
+        self.depth = 3 if self.stage == "exchange" else 1
         self.tok_bufs = ([self.tokens] + [self.tokens.clone() for _ in range(self.depth)]) if self.stage else [self.tokens]
+        self.tok_ready = torch.cuda.Event()  # the token buffers never change after this point
+        self.tok_ready.record(torch.cuda.current_stream(device))
         self.k = 0
         self.positions = None
         if self.decode:  # uniform histories; output rows are the sequences' last tokens
@@ -294,7 +297,7 @@ class Workload:
             tok = self.tok_bufs[self.k % nb]
             if self.stage:  # a later step's rows of other ranks, staged while this step runs
                 self.shard.prefetch(self.tok_bufs[(self.k + self.depth) % nb], self.seg_start,
-                                    max_blocks=self.stage_blocks, omap=self.omap)
+                                    max_blocks=self.stage_blocks, omap=self.omap, ready=self.tok_ready)
             self.k += 1
             self.shard.forward(tok, self.seg_start, self.omap, self.rows_var, self.out, self.mode,
                                self.exchange, slots_out=self.slots if self.R else None, hit_count=hit_count)
@@ -1024,8 +1027,8 @@ def shard_text(cfg):
     if not cfg.get("shard"):
         return ""
     if cfg.get("stage") == "exchange":
-        return ("+row-sharded table (id mod N; each rank's distinct rows of other ranks planned two batches ahead "
-                "and exchanged by NCCL all-to-all on a side stream; local rows read in place)")
+        return ("+row-sharded table (id mod N; the rows of other ranks routed three batches ahead, gathered by their owners "
+                "and copied with the copy engines over NVLink; local rows read in place)")
     if cfg.get("shard_exchange", "peer") != "peer":
         return "+row-sharded table (id mod N, NCCL all-to-all of ids and rows)"
     if cfg.get("stage", "push") == "push":
@@ -1189,8 +1192,26 @@ def sharded_stats(wl, ms, fwd_ms, bwd_ms, ddist, world, device):
     import torch
     rr = torch.tensor([wl.remote_rows, wl.remote_distinct], dtype=torch.int64, device=device)
     ddist.all_reduce(rr, op=ddist.ReduceOp.MAX)
-    nv_bytes = int(rr[1]) * wl.shard.stride
-    return {"table_bytes_per_gpu": int(wl.shard.n_local * wl.shard.stride),
+    nv_bytes = int(rr[0]) * wl.shard.stride  # the exchange moves one row per remote (position, head) pair
+    phases = None
+    xs = getattr(wl.shard, "xstage", None)
+    if xs is not None:  # a few more steps with the exchange's phases timed (after the timed region)
+        import torch
+        xs.timing = {}
+        for _ in range(5):
+            wl.step(ddist)
+        wl.join_stage()
+        torch.cuda.synchronize()
+        ph = xs.phase_ms()
+        xs.timing = None
+        keys = sorted(ph)
+        t = torch.tensor([ph[k] for k in keys], dtype=torch.float64, device=device)
+        ddist.all_reduce(t, op=ddist.ReduceOp.MAX)
+        phases = {k: float(v) for k, v in zip(keys, t.tolist())}
+        phases["note"] = ("ms per step, max over ranks: route and serve (the owner's gather) on the step's stream "
+                          "before the forward, fetch (copy-engine transfers) on the side stream, wait = the forward's "
+                          "stream blocked on its rows")
+    return {"table_bytes_per_gpu": int(wl.shard.n_local * wl.shard.stride), "exchange_phase_ms": phases,
             "nvlink": {"remote_pairs_per_step": int(rr[0]), "distinct_remote_rows_per_step": int(rr[1]),
                        "dedup_factor": int(rr[0]) / max(int(rr[1]), 1), "bytes_per_step": nv_bytes,
                        "achieved_gbps": nv_bytes / (ms * 1e-3) / 1e9, "peer_copy_gbps": 770.0,
@@ -1313,8 +1334,18 @@ def run_e2e(wl, args, device, ddist, world):
             while len(pending) < wl.depth:
                 pending.append((tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True)))
             tok, ss = pending.pop(0)
-            nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
-            wl.table.prefetch(nxt[0], nxt[1], max_blocks=wl.stage_blocks, omap=wl.omap)
+            xs = getattr(wl.table, "xstage", None)
+            if xs is not None:  # copied on the staging stream: the exchange waits for the copy, not for the step
+                with torch.cuda.stream(xs.side):
+                    nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
+                    ready = torch.cuda.Event()
+                    ready.record(xs.side)
+                for x in nxt:
+                    x.record_stream(torch.cuda.current_stream(device))
+                wl.table.prefetch(nxt[0], nxt[1], omap=wl.omap, ready=ready)
+            else:
+                nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
+                wl.table.prefetch(nxt[0], nxt[1], max_blocks=wl.stage_blocks, omap=wl.omap)
             pending.append(nxt)
         else:
             tok = tok_h.to(device, non_blocking=True)

@@ -88,6 +88,10 @@ SIGNATURES = {
                                            C.c_int64, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                            C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                            C.c_void_p]),
+    "engram_shard_route_scratch_words": (C.c_int64, [C.c_int64, C.c_int32, C.c_int32]),
+    "engram_shard_route": (C.c_int, [C.POINTER(EngramTable), C.POINTER(EngramOverlay), C.c_void_p, C.c_void_p,
+                                     C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_void_p]),
     "engram_shard_serve": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_int64, C.c_void_p]),
     "engram_shard_gather": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p,

@@ -14,6 +14,8 @@
 //      (engram_forward_indirect).
 // No kernel here reads another GPU's memory: remote rows arrive in local HBM
 // through NCCL before any kernel touches them.
+#include <climits>
+
 #include "engram_common.cuh"
 
 using namespace engram;
@@ -23,6 +25,35 @@ namespace {
 constexpr int kMaxWorld = 64;
 
 __device__ __forceinline__ uint32_t set_home(int32_t key, int64_t capacity) { return map_home(key, capacity); }
+
+// Exclusive scan of one value per thread over the block (blockDim a multiple of
+// 32, <= 1024); *total = the block's sum.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sums, uint32_t* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t s = lane < nwarps ? warp_sums[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += y;
+        }
+        if (lane < nwarps) warp_sums[lane] = s;
+    }
+    __syncthreads();
+    const uint32_t before = warp == 0 ? 0u : warp_sums[warp - 1];
+    *total = warp_sums[nwarps - 1];
+    const uint32_t res = before + x - v;
+    __syncthreads();
+    return res;
+}
 
 __global__ void k_set_clear(int32_t* keys, int64_t capacity, int64_t* counts, int world) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -189,16 +220,101 @@ __global__ void k_shard_gather(const uint8_t* __restrict__ shard, int64_t stride
     }
 }
 
+// engram_shard_route: the requests of a batch grouped by owner, one per
+// (position, head) served by another rank and not by the overlay, without
+// deduplication.  Tiles of kRouteTile entries: k_route_count hashes a tile,
+// writes each entry's id (or -1) and the tile's per-owner counts; k_route_scan
+// turns the counts into each tile's first slot per owner (owner-major); then
+// k_route_scatter places every requested id in its owner's group (the order
+// inside a group is free) and records its slot as the entry's row index.
+constexpr int kRouteThreads = 256, kRouteItems = 8, kRouteTile = kRouteThreads * kRouteItems;
+
+__global__ void __launch_bounds__(kRouteThreads) k_route_count(engram_table T, engram_overlay OV,
+                                                               const int32_t* __restrict__ tokens,
+                                                               const int32_t* __restrict__ seg_start, int64_t t0,
+                                                               int64_t n, int world, int rank,
+                                                               int32_t* __restrict__ ids, uint32_t* __restrict__ tile_cnt) {
+    __shared__ uint32_t cnt[kMaxWorld];
+    for (int o = threadIdx.x; o < world; o += blockDim.x) cnt[o] = 0;
+    __syncthreads();
+    const int nh = T.n_heads;
+    const int64_t total = n * nh;
+    const int64_t base = (int64_t)blockIdx.x * kRouteTile;
+#pragma unroll
+    for (int it = 0; it < kRouteItems; it++) {
+        const int64_t k = base + it * kRouteThreads + threadIdx.x;
+        if (k >= total) break;
+        const int64_t i = k / nh;
+        const int h = (int)(k - i * nh);
+        const int32_t g = hash_row(T, tokens, seg_start, t0 + i, h);
+        const int o = (int)((uint32_t)g % (uint32_t)world);
+        const bool req = o != rank && overlay_slot(OV, g) < 0;
+        ids[k] = req ? g : -1;
+        if (req) atomicAdd(cnt + o, 1u);
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < world; o += blockDim.x) tile_cnt[(int64_t)blockIdx.x * world + o] = cnt[o];
+}
+
+// One block: tile_cnt[b][o] -> the first slot of tile b's ids for owner o
+// (owners in ascending order, tiles in ascending order inside an owner);
+// counts[o] = requests for owner o.
+__global__ void __launch_bounds__(1024) k_route_scan(uint32_t* tile_cnt, int nblk, int world,
+                                                     unsigned long long* counts) {
+    __shared__ uint32_t warp_sums[32];
+    __shared__ unsigned long long carry;
+    if (threadIdx.x == 0) carry = 0ull;
+    __syncthreads();
+    for (int o = 0; o < world; o++) {
+        const unsigned long long owner_base = carry;
+        for (int b0 = 0; b0 < nblk; b0 += blockDim.x) {
+            const int b = b0 + threadIdx.x;
+            const uint32_t v = b < nblk ? tile_cnt[(int64_t)b * world + o] : 0u;
+            uint32_t tot;
+            const uint32_t ex = block_exclusive_scan(v, warp_sums, &tot);
+            if (b < nblk) tile_cnt[(int64_t)b * world + o] = (uint32_t)(carry + ex);
+            __syncthreads();
+            if (threadIdx.x == 0) carry += tot;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) counts[o] = carry - owner_base;
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) k_route_scatter(const int32_t* ids, int64_t total, int world,
+                                                                 const uint32_t* __restrict__ tile_first,
+                                                                 int32_t* __restrict__ send_ids, int32_t* row_index) {
+    __shared__ uint32_t cur[kMaxWorld];
+    for (int o = threadIdx.x; o < world; o += blockDim.x) cur[o] = tile_first[(int64_t)blockIdx.x * world + o];
+    __syncthreads();
+    const int64_t base = (int64_t)blockIdx.x * kRouteTile;
+#pragma unroll
+    for (int it = 0; it < kRouteItems; it++) {
+        const int64_t k = base + it * kRouteThreads + threadIdx.x;
+        if (k >= total) break;
+        const int32_t g = ids[k];
+        int32_t r = -1;
+        if (g >= 0) {
+            r = (int32_t)atomicAdd(cur + (int)((uint32_t)g % (uint32_t)world), 1u);
+            send_ids[r] = g;
+        }
+        row_index[k] = r;
+    }
+}
+
 // Owner side of the peer exchange (engram_shard_serve): the rows every other
 // rank requested from this rank, gathered from the local shard into send_rows,
 // requester by requester.  Requester r's ids for this owner are the slice
 // [sum_{o < rank} M[r][o], + M[r][rank]) of its send_ids (read over NVLink
 // through id_ptrs[r]); they land at send_rows rows [sum_{r' < r} M[r'][rank], +
-// M[r][rank]).  One thread per 16-byte word; rows at or past max_rows are not
-// written (the requester refuses such a batch on the host).
-__global__ void k_shard_serve(const uint8_t* __restrict__ shard, int64_t stride, int64_t n_local, int world, int rank,
-                              const unsigned long long* __restrict__ id_ptrs, const int64_t* __restrict__ M,
-                              uint8_t* __restrict__ send_rows, int64_t max_rows) {
+// M[r][rank]).  Rows at or past max_rows are not written (the requester refuses
+// such a batch on the host).
+__global__ void __launch_bounds__(256) k_shard_serve(const uint8_t* __restrict__ shard, int64_t stride,
+                                                     int64_t n_local, int world, int rank,
+                                                     const unsigned long long* __restrict__ id_ptrs,
+                                                     const int64_t* __restrict__ M, uint8_t* __restrict__ send_rows,
+                                                     int64_t max_rows) {
     __shared__ long long base[kMaxWorld + 1];  // first send row of each requester
     __shared__ long long idoff[kMaxWorld];     // offset of this owner's slice in the requester's send_ids
     if (threadIdx.x == 0) {
@@ -214,19 +330,43 @@ __global__ void k_shard_serve(const uint8_t* __restrict__ shard, int64_t stride,
     }
     __syncthreads();
     const int64_t total = base[world] < max_rows ? base[world] : max_rows;
-    const int64_t words = stride >> 4;
-    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total * words;
-         w += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t f = w / words, p = w - f * words;
-        int r = 0;
-        while (r + 1 < world && base[r + 1] <= f) r++;  // requester of send row f
-        const int32_t* ids = reinterpret_cast<const int32_t*>(id_ptrs[r]);
-        const int32_t g = ids[idoff[r] + (f - base[r])];
-        const int64_t local = (int64_t)g / world;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (g >= 0 && (int)(g % world) == rank && local < n_local)
-            v = __ldg(reinterpret_cast<const uint4*>(shard + local * stride) + p);
-        reinterpret_cast<uint4*>(send_rows + f * stride)[p] = v;
+    const int words = (int)(stride >> 4);
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    // a warp serves 32 send rows at a time: lane l reads the id of row g0 + l once (over NVLink), then the
+    // warp copies the 32 rows word by word, kServeLoads words per lane in flight
+    constexpr int kServeLoads = 8;
+    for (int64_t g0 = warp0 * 32; g0 < total; g0 += nwarps * 32) {
+        const int64_t f = g0 + lane;
+        int64_t src = -1;  // byte offset of the row in the shard, -1: none
+        if (f < total) {
+            int r = 0;
+            while (r + 1 < world && base[r + 1] <= f) r++;  // requester of send row f
+            const int32_t g = reinterpret_cast<const int32_t*>(id_ptrs[r])[idoff[r] + (f - base[r])];
+            const int64_t local = (int64_t)g / world;
+            if (g >= 0 && (int)(g % world) == rank && local < n_local) src = local * stride;
+        }
+        const int pairs = 32 * words;
+        for (int p0 = 0; p0 < pairs; p0 += 32 * kServeLoads) {
+            uint4 v[kServeLoads];
+            int64_t dst[kServeLoads];
+#pragma unroll
+            for (int u = 0; u < kServeLoads; u++) {
+                const int p = p0 + u * 32 + lane;
+                const int rr = p / words, w = p - rr * words;
+                const int64_t s_off = __shfl_sync(0xffffffffu, src, rr < 32 ? rr : 0);
+                dst[u] = -1;
+                if (p < pairs && g0 + rr < total) {
+                    v[u] = s_off >= 0 ? __ldg(reinterpret_cast<const uint4*>(shard + s_off) + w)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+                    dst[u] = (g0 + rr) * stride + 16 * w;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kServeLoads; u++)
+                if (dst[u] >= 0) __stcg(reinterpret_cast<uint4*>(send_rows + dst[u]), v[u]);
+        }
     }
 }
 
@@ -313,5 +453,40 @@ extern "C" int engram_shard_serve(const void* shard_rows, int64_t stride, int64_
         static_cast<const uint8_t*>(shard_rows), stride, n_local, world, rank,
         static_cast<const unsigned long long*>(id_ptrs), counts_all, static_cast<uint8_t*>(send_rows), max_rows);
     count_launches(1);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int64_t engram_shard_route_scratch_words(int64_t n, int32_t n_heads, int32_t world) {
+    if (n < 0 || n_heads < 1 || world < 1 || world > kMaxWorld) return ENGRAM_ERR_ARG;
+    const int64_t tiles = (n * n_heads + kRouteTile - 1) / kRouteTile;
+    return (tiles > 0 ? tiles : 1) * world;
+}
+
+extern "C" int engram_shard_route(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                  const int32_t* seg_start, int64_t t0, int64_t n, int32_t world, int32_t rank,
+                                  uint32_t* scratch, int64_t scratch_words, int32_t* send_ids, int64_t* counts,
+                                  int32_t* row_index, void* stream) {
+    if (!t || t0 < 0 || n < 0 || world < 1 || world > kMaxWorld || rank < 0 || rank >= world) return ENGRAM_ERR_ARG;
+    if (!scratch || !send_ids || !counts || !row_index || (n > 0 && !tokens)) return ENGRAM_ERR_ARG;
+    const int64_t entries = n * t->n_heads;
+    const int64_t tiles = (entries + kRouteTile - 1) / kRouteTile;
+    if (scratch_words < (tiles > 0 ? tiles : 1) * world) return ENGRAM_ERR_WORKSPACE;
+    if (tiles > INT_MAX) return ENGRAM_ERR_RANGE;
+    engram_overlay OV{nullptr, 0, nullptr, nullptr, 0};
+    if (ov && ov->n_rows > 0) {
+        OV = *ov;
+        if (!OV.map_keys || !OV.map_slots || (OV.capacity & (OV.capacity - 1)) != 0 || OV.capacity < 2 * OV.n_rows)
+            return ENGRAM_ERR_ARG;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(counts);
+    if (tiles == 0) {
+        cudaMemsetAsync(counts, 0, sizeof(int64_t) * world, s);
+        return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+    }
+    k_route_count<<<(int)tiles, kRouteThreads, 0, s>>>(*t, OV, tokens, seg_start, t0, n, world, rank, row_index, scratch);
+    k_route_scan<<<1, 1024, 0, s>>>(scratch, (int)tiles, world, cnt);
+    k_route_scatter<<<(int)tiles, kRouteThreads, 0, s>>>(row_index, entries, world, scratch, send_ids, row_index);
+    count_launches(3);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }

@@ -140,23 +140,27 @@ class ShardedTable:
             raise RuntimeError("push staging needs the peer shards (peer_ptrs)")
         self.push = PushStage(self, n_tokens_max, group, max_blocks)
 
-    def enable_exchange_staging(self, n_tokens_max: int, exchange=None) -> None:
+    def enable_exchange_staging(self, n_tokens_max: int, exchange=None, dedup: bool = False) -> None:
         """Make prefetch() plan and exchange the rows of other ranks ahead of the
         forward, deduplicated, through `exchange`: "peer" (the default,
         PeerRowExchange: owners gather into symmetric memory, requesters copy
         with the copy engines), "nccl" (NcclRowExchange: NCCL all-to-alls on a
         process group of their own) or an exchange object (LocalRowExchange
-        for emulated ranks).  Prefetching two batches ahead of the forward keeps
+        for emulated ranks).  dedup: request each distinct remote row once
+        per batch (engram_shard_plan, a device hash set) instead of once per
+        (position, head) (engram_shard_route, three cheap passes); worth it
+        where remote rows repeat inside a batch more than they do here.  Prefetching two batches ahead of the forward keeps
         both the host and the forward from waiting on the exchange (see
         ExchangeStage).  With NcclRowExchange a collective: every rank calls it."""
         if exchange is None or exchange == "peer":
             exchange = PeerRowExchange(self, n_tokens_max)
         elif exchange == "nccl":
             exchange = NcclRowExchange()
-        self.xstage = ExchangeStage(self, n_tokens_max, exchange)
+        self.xstage = ExchangeStage(self, n_tokens_max, exchange, dedup)
 
     def prefetch(self, tokens, seg_start=None, t0: int = 0, n: int | None = None, max_blocks: int = 0,
-                 stream: torch.cuda.Stream | None = None, omap: OverlayMap | None = None) -> None:
+                 stream: torch.cuda.Stream | None = None, omap: OverlayMap | None = None,
+                 ready: torch.cuda.Event | None = None) -> None:
         """Copy the rows of other ranks that forward(tokens, seg_start, ..., t0, n)
         will read into this GPU's memory, on `stream` (default: the table's own
         side stream, ordered after the work already queued on the current
@@ -166,7 +170,10 @@ class ShardedTable:
         map the forward will use; the rows of the heads it serves are not
         copied, and a forward with another map reads in place.  Up to two
         prefetches wait at a time; a third drops the oldest.  max_blocks caps the
-        copy's grid (0: every SM), leaving SMs to the work it overlaps."""
+        copy's grid (0: every SM), leaving SMs to the work it overlaps.
+        ready (exchange staging): an event after which tokens and seg_start
+        hold their values; the staging then waits for that event only, not for
+        all the work queued on the current stream, and overlaps it fully."""
         dev = self.device
         tokens = _as_i32(tokens, dev)
         if n is None:
@@ -174,7 +181,7 @@ class ShardedTable:
         ss = None if seg_start is None else _as_i32(seg_start, dev)
         key = self._key(tokens, ss, t0, n)
         if self.xstage is not None:
-            self.xstage.prefetch(key, tokens, ss, t0, n, omap)
+            self.xstage.prefetch(key, tokens, ss, t0, n, omap, ready)
             return
         if self.peer_ptrs is None:
             raise RuntimeError("prefetch needs the peer shards (peer_ptrs) or exchange staging")
@@ -241,7 +248,9 @@ class ShardedTable:
                 self.xstage.prefetch(key, tokens, ss, t0, n, omap)
             b, recv, rix, ready = self.xstage.take(key, omap)
             cur = torch.cuda.current_stream(dev)
+            t0 = self.xstage._mark(cur)
             cur.wait_event(ready)
+            self.xstage._span("wait", t0, cur)
             ov = omap.descriptor(rows_var)
             st = lib.engram_forward_exchanged(C.byref(self.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(ss), t0, n,
                                               self.shard.data_ptr(), self.world, self.rank, recv.data_ptr(),
@@ -438,39 +447,47 @@ class PushStage:
 
 
 class ExchangeStage:
-    """Row-sharded reads through a deduplicated row exchange, pipelined so that
-    neither the host nor the forward waits for it (ShardedTable.enable_exchange_staging).
+    """Row-sharded reads through a row exchange, pipelined so that neither the
+    host nor the forward waits for it (ShardedTable.enable_exchange_staging).
 
-    prefetch(batch X), on the table's side stream:
-      1. engram_shard_plan: the distinct ids of X's (position, head) pairs that
-         another rank owns and the overlay does not serve, grouped by owner,
-         the per-owner counts, and each pair's row in the reply (row_index); a
-         Zipf-hot remote row is requested once per batch;
-      2. exchange.gather_counts: every rank's counts (a collective), copied to
-         pinned host memory behind an event;
-      3. the exchange of every batch planned before X and not yet exchanged:
-         the host reads that batch's counts (planned a step earlier when the
-         caller prefetches two batches ahead, so the event has long completed),
-         and exchange.rows sends the ids to their owners and brings their rows
-         back (collectives) into a receive buffer of the batch's own.
-    forward(X) exchanges X first if that has not happened (the host then waits
-    for X's counts), makes the current stream wait for X's rows and runs
-    engram_forward_exchanged: rows this rank owns read in place, the others
-    from the receive buffer.  Every rank calls prefetch and forward in the same
-    order with the same t0 and n (the collectives follow that order).  Up to
-    two batches wait at a time (three buffer sets: read, exchanged, planned); a
-    third prefetch drops the oldest."""
+    A batch passes three stages, one per prefetch() call, so a caller that
+    prefetches three batches ahead of its forwards has, at step k: batch k+3
+    routed, batch k+2 served, batch k+1 fetched, batch k read by the forward.
+      route (current stream): engram_shard_route, the ids of the batch's
+        (position, head) pairs that another rank owns and the overlay does not
+        serve, grouped by owner, per-owner counts and each pair's row in the
+        reply (row_index) (engram_shard_plan instead with dedup: each distinct
+        row once); then, on the side stream, every rank's counts are
+        all-gathered (exchange.gather_counts, a collective) and copied to
+        pinned host memory;
+      serve (current stream): with a serving exchange (PeerRowExchange) the
+        owners gather the rows the others asked of them (engram_shard_serve);
+        then a barrier on the side stream (exchange.barrier);
+      fetch (side stream): the host reads the batch's counts (gathered two
+        steps earlier, so it does not wait) and the exchange brings the
+        owners' rows into a receive buffer of the batch's own (PeerRowExchange:
+        one copy-engine transfer per owner; NcclRowExchange / LocalRowExchange:
+        exchange.rows).
+    The two SM stages run on the caller's stream, between the step's kernels,
+    instead of queueing behind them on a side stream; the side stream carries
+    only copy-engine transfers and 4-byte collectives.  forward(X) runs the
+    stages X has not passed yet (the host then waits), makes the current
+    stream wait for X's rows and runs engram_forward_exchanged.  Every rank
+    calls prefetch and forward in the same order with the same t0 and n (the
+    collectives follow that order).  Four buffer sets: a fifth batch
+    prefetched before the oldest is read drops the oldest."""
 
-    SETS = 3
+    SETS = 4
 
-    def __init__(self, table: "ShardedTable", n_tokens_max: int, exchange):
+    def __init__(self, table: "ShardedTable", n_tokens_max: int, exchange, dedup: bool = False):
         self.table, self.exchange = table, exchange
+        self.dedup = bool(dedup)  # engram_shard_plan (distinct rows) or engram_shard_route (one row per pair)
         dev = table.device
         self.n_max = int(n_tokens_max)
         entries = max(self.n_max * table.n_heads, 1)
         self.cap = max(2, 1 << int(np.ceil(np.log2(2 * entries))))
         self.set_keys = torch.empty(self.cap, dtype=torch.int32, device=dev)
-        self.set_vals = torch.empty(self.cap, dtype=torch.int32, device=dev)
+        self.set_vals = torch.empty(self.cap if self.dedup else 1, dtype=torch.int32, device=dev)
         W = table.world
         alloc = getattr(exchange, "alloc_ids", None)
         self.send_ids = [alloc(b, entries) if alloc is not None else torch.empty(entries, dtype=torch.int32, device=dev)
@@ -478,104 +495,150 @@ class ExchangeStage:
         self.rix = [torch.empty(entries, dtype=torch.int32, device=dev) for _ in range(self.SETS)]
         self.counts = [torch.zeros(2 * W, dtype=torch.int64, device=dev) for _ in range(self.SETS)]
         self.counts_host = [torch.zeros(W, W, dtype=torch.int64).pin_memory() for _ in range(self.SETS)]
-        self.ev_counts = [None] * self.SETS
-        self.ev_ready = [None] * self.SETS
-        self.ev_consumed = [None] * self.SETS
+        self.allc = [None] * self.SETS        # every rank's counts, on the device
+        self.ev_counts = [None] * self.SETS   # side: counts gathered and copied to the host
+        self.ev_barrier = [None] * self.SETS  # side: every owner's gather of the batch is done
+        self.ev_ready = [None] * self.SETS    # side: the batch's rows are in its receive buffer
         self.recv = [None] * self.SETS
-        self.state = [None] * self.SETS  # None | "planned" | "exchanged"
+        self.state = [None] * self.SETS       # None | "routed" | "served" | "fetched"
         self.key = [None] * self.SETS
         self.omap_keys = [None] * self.SETS
         self.seq = [0] * self.SETS
         self.n_seq = 0
-        # the plan and the owners' gathers run between the step's kernels: a high-priority side stream gets
-        # the SMs as soon as the current kernel's blocks retire
-        self.side = torch.cuda.Stream(dev, priority=-1)
+        self.side = torch.cuda.Stream(dev)
         self._empty = torch.zeros(16, dtype=torch.uint8, device=dev)
-        self.last = None  # (distinct remote rows, remote (position, head) pairs) of the last exchanged batch
+        self.timing = None  # a dict of lists of (start, end) CUDA events per phase, when set (see phase_ms)
 
     def has(self, key) -> bool:
         return key in self.key
 
-    def prefetch(self, key, tokens: torch.Tensor, ss: torch.Tensor | None, t0: int, n: int, omap) -> None:
+    def _mark(self, stream):
+        if self.timing is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        return e
+
+    def _span(self, name, e0, stream):
+        if e0 is not None:
+            self.timing.setdefault(name, []).append((e0, self._mark(stream)))
+
+    def phase_ms(self) -> dict:
+        """Mean ms per batch of each timed phase (after a synchronize): route and
+        serve on the caller's stream, fetch on the side stream, wait = how long
+        the forward's stream waited for its rows."""
+        return {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in (self.timing or {}).items() if v}
+
+    def _oldest(self, state):
+        return sorted((k for k in range(self.SETS) if self.state[k] == state), key=lambda k: self.seq[k])
+
+    def prefetch(self, key, tokens: torch.Tensor, ss: torch.Tensor | None, t0: int, n: int, omap,
+                 ready: torch.cuda.Event | None = None) -> None:
         t = self.table
         if key in self.key:
             return
         if n > self.n_max:
             raise ValueError(f"{n} positions exceed n_tokens_max {self.n_max}")
+        cur = torch.cuda.current_stream(t.device)
+        for b in self._oldest("served"):  # the next forward waits for the oldest of them
+            self._fetch(b)
+        for b in self._oldest("routed"):
+            self._serve(b, cur)
         free = [b for b in range(self.SETS) if self.state[b] is None]
         if not free:  # drop the oldest waiting batch (every rank drops the same one)
             b = min(range(self.SETS), key=lambda k: self.seq[k])
             self.state[b] = self.key[b] = None
             free = [b]
         b = free[0]
+        if ready is not None:
+            cur.wait_event(ready)
+        t_route = self._mark(cur)
         lib = L.load()
-        cur = torch.cuda.current_stream(t.device)
-        self.side.wait_stream(cur)
-        if self.ev_consumed[b] is not None:
-            self.side.wait_event(self.ev_consumed[b])
-        self.recv[b] = None
         ov = None
         if omap is not None and omap.R:
             ov = L.EngramOverlay(None, omap.R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
-        st = lib.engram_shard_plan(C.byref(t.ctable), None if ov is None else C.byref(ov), tokens.data_ptr(),
-                                   L.ptr(ss), t0, n, t.world, t.rank, self.set_keys.data_ptr(),
-                                   self.set_vals.data_ptr(), self.cap, self.send_ids[b].data_ptr(),
-                                   self.counts[b].data_ptr(), self.rix[b].data_ptr(), self.side.cuda_stream)
-        L.check(st, "engram_shard_plan")
-        tokens.record_stream(self.side)
-        if ss is not None:
-            ss.record_stream(self.side)
+        if self.dedup:
+            st = lib.engram_shard_plan(C.byref(t.ctable), None if ov is None else C.byref(ov), tokens.data_ptr(),
+                                       L.ptr(ss), t0, n, t.world, t.rank, self.set_keys.data_ptr(),
+                                       self.set_vals.data_ptr(), self.cap, self.send_ids[b].data_ptr(),
+                                       self.counts[b].data_ptr(), self.rix[b].data_ptr(), cur.cuda_stream)
+            L.check(st, "engram_shard_plan")
+        else:
+            st = lib.engram_shard_route(C.byref(t.ctable), None if ov is None else C.byref(ov), tokens.data_ptr(),
+                                        L.ptr(ss), t0, n, t.world, t.rank, self.set_keys.data_ptr(), self.cap,
+                                        self.send_ids[b].data_ptr(), self.counts[b].data_ptr(), self.rix[b].data_ptr(),
+                                        cur.cuda_stream)
+            L.check(st, "engram_shard_route")
+        self._span("route", t_route, cur)
+        routed = torch.cuda.Event()
+        routed.record(cur)
+        self.side.wait_event(routed)
         with torch.cuda.stream(self.side):
             allc = self.exchange.gather_counts(t, self.counts[b][: t.world])
-            serve = getattr(self.exchange, "serve", None)
-            if serve is not None:  # owners gather what the others asked of them now (no host sizes needed)
-                serve(t, b, allc)
             self.counts_host[b].copy_(allc.reshape(t.world, t.world), non_blocking=True)
+        allc.record_stream(cur)
+        self.allc[b] = allc
         self.ev_counts[b] = torch.cuda.Event()
         self.ev_counts[b].record(self.side)
-        self.state[b], self.key[b] = "planned", key
+        self.recv[b] = None
+        self.state[b], self.key[b] = "routed", key
         self.omap_keys[b] = None if ov is None else omap.keys.data_ptr()
         self.n_seq += 1
         self.seq[b] = self.n_seq
-        for o in sorted((k for k in range(self.SETS) if self.state[k] == "planned" and k != b),
-                        key=lambda k: self.seq[k]):
-            self._exchange(o)
 
-    def _exchange(self, b: int) -> None:
+    def _serve(self, b: int, cur: torch.cuda.Stream) -> None:
+        serve = getattr(self.exchange, "serve", None)
+        if serve is not None:  # owners gather what the others asked of them, then a barrier
+            cur.wait_event(self.ev_counts[b])
+            t0 = self._mark(cur)
+            serve(self.table, b, self.allc[b])
+            self._span("serve", t0, cur)
+            served = torch.cuda.Event()
+            served.record(cur)
+            self.side.wait_event(served)
+            with torch.cuda.stream(self.side):
+                self.exchange.barrier()
+        self.ev_barrier[b] = torch.cuda.Event()
+        self.ev_barrier[b].record(self.side)
+        self.state[b] = "served"
+
+    def _fetch(self, b: int) -> None:
         t = self.table
         self.ev_counts[b].synchronize()
         m = self.counts_host[b]
-        send = [int(x) for x in m[t.rank].tolist()]
-        recv = [int(x) for x in m[:, t.rank].tolist()]
-        total = sum(send)
+        t0 = self._mark(self.side)
         with torch.cuda.stream(self.side):
             fetch = getattr(self.exchange, "fetch", None)
             if fetch is not None:
                 rows = fetch(t, b, m)
             else:
-                rows = self.exchange.rows(t, self.send_ids[b][:total], send, recv)
+                send = [int(x) for x in m[t.rank].tolist()]
+                recv = [int(x) for x in m[:, t.rank].tolist()]
+                rows = self.exchange.rows(t, self.send_ids[b][:sum(send)], send, recv)
+        self._span("fetch", t0, self.side)
         self.recv[b] = rows if rows.numel() else self._empty
         self.ev_ready[b] = torch.cuda.Event()
         self.ev_ready[b].record(self.side)
-        self.state[b] = "exchanged"
-        self.last = (total, None)
+        self.state[b] = "fetched"
 
     def take(self, key, omap):
-        """(receive buffer, row_index, ready event) of the prefetched batch `key`."""
+        """(set, receive buffer, row_index, ready event) of the prefetched batch `key`."""
         b = self.key.index(key)
         want = None if omap is None or not omap.R else omap.keys.data_ptr()
         if want != self.omap_keys[b]:
             raise ValueError("the batch was prefetched with another overlay map; prefetch it again with this one")
-        if self.state[b] == "planned":
-            self._exchange(b)
+        cur = torch.cuda.current_stream(self.table.device)
+        if self.state[b] == "routed":
+            self._serve(b, cur)
+        if self.state[b] == "served":
+            self._fetch(b)
         self.key[b] = None
-        self.recv[b].record_stream(torch.cuda.current_stream(self.table.device))  # read by the forward there
+        self.recv[b].record_stream(cur)  # read by the forward there
         return b, self.recv[b], self.rix[b], self.ev_ready[b]
 
     def consumed(self, b: int, stream: torch.cuda.Stream) -> None:
-        ev = torch.cuda.Event()
-        ev.record(stream)
-        self.ev_consumed[b] = ev
+        """The forward over set b is queued on `stream` (the set's next route
+        runs on the caller's stream after it)."""
         self.state[b] = None
 
 
@@ -628,7 +691,7 @@ class PeerRowExchange:
     the counts matrix read on the host one step late (ExchangeStage).  A
     collective to construct: every rank of `group` calls it."""
 
-    def __init__(self, table: "ShardedTable", n_tokens_max: int, group=None, sets: int = 3):
+    def __init__(self, table: "ShardedTable", n_tokens_max: int, group=None, sets: int = 4):
         import torch.distributed as dist
         from .dist import symmetric_memory
         symm = symmetric_memory()
@@ -651,9 +714,17 @@ class PeerRowExchange:
             self.row_handles.append(hr)
             self._keep.append(hi)
         self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._views = {}
 
     def alloc_ids(self, b: int, entries: int) -> torch.Tensor:
         return self.ids[b][:entries]
+
+    def _view(self, b: int, o: int) -> torch.Tensor:
+        """Owner o's send buffer of set b, mapped into this process (cached)."""
+        key = (b, o)
+        if key not in self._views:
+            self._views[key] = self.row_handles[b].get_buffer(o, (self.max_rows * self.stride,), torch.uint8)
+        return self._views[key]
 
     def gather_counts(self, table, counts: torch.Tensor) -> torch.Tensor:
         W = table.world
@@ -662,11 +733,15 @@ class PeerRowExchange:
         return out
 
     def serve(self, table, b: int, counts_all: torch.Tensor) -> None:
+        """This owner's gather for set b, on the current stream."""
         st = L.load().engram_shard_serve(table.shard.data_ptr(), table.stride, table.n_local, table.world, table.rank,
                                          self.id_ptrs[b].data_ptr(), counts_all.data_ptr(), self.rows[b].data_ptr(),
                                          self.max_rows, L.stream_of(table.device))
         L.check(st, "engram_shard_serve")
-        self.dist.all_reduce(self.flag, group=self.group)  # every owner's rows are in place
+
+    def barrier(self) -> None:
+        """A 4-byte all-reduce: once it completes, every owner's gather before it is done."""
+        self.dist.all_reduce(self.flag, group=self.group)
 
     def fetch(self, table, b: int, m: torch.Tensor) -> torch.Tensor:
         """This rank's rows of batch set b, in send order (owner after owner)."""
@@ -682,7 +757,7 @@ class PeerRowExchange:
             base = sum(mm[r][o] for r in range(me) if r != o)  # this rank's first row in owner o's send buffer
             if base + cnt > self.max_rows:
                 raise RuntimeError(f"owner {o} holds {base + cnt} rows for this batch, its send buffer {self.max_rows}")
-            src = self.row_handles[b].get_buffer(o, (self.max_rows * stride,), torch.uint8)
+            src = self._view(b, o)
             out[off * stride:(off + cnt) * stride].copy_(src[base * stride:(base + cnt) * stride], non_blocking=True)
             off += cnt
         return out[: total * stride]

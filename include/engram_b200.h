@@ -299,6 +299,22 @@ ENGRAM_API int engram_shard_plan(const engram_table* t, const engram_overlay* ov
                                  int64_t* counts, int32_t* row_index, void* stream);
 
 /*
+ * engram_shard_plan without the deduplication: every (position, head) pair of
+ * positions t0..t0+n-1 that another rank owns and the overlay ov (nullable)
+ * does not serve requests its row once, grouped by owner in send_ids (the order
+ * inside an owner's group is free); counts [2*world] and row_index [n *
+ * n_heads] as engram_shard_plan.  Three passes over the pairs and no hash set:
+ * cheaper than the plan where few remote rows repeat inside a batch.
+ * scratch: device uint32 [engram_shard_route_scratch_words(n, n_heads, world)].
+ * No reference counterpart.
+ */
+ENGRAM_API int64_t engram_shard_route_scratch_words(int64_t n, int32_t n_heads, int32_t world);
+ENGRAM_API int engram_shard_route(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                  const int32_t* seg_start, int64_t t0, int64_t n, int32_t world, int32_t rank,
+                                  uint32_t* scratch, int64_t scratch_words, int32_t* send_ids, int64_t* counts,
+                                  int32_t* row_index, void* stream);
+
+/*
  * engram_forward over a row-sharded table after the exchange of a plan: rows
  * this rank owns are read in place from local_rows (its shard: row g at local
  * row g / world), every other row from recv_rows (the rows of the plan's

@@ -434,6 +434,55 @@ def test_sharded_table_read_in_place_matches_resident_table(eb, world, fmt, dim,
     assert np.array_equal(outs[0][1], outs[1][1]) and outs[0][2] == outs[1][2]
 
 
+@pytest.mark.parametrize("world,rank", [(2, 0), (3, 1), (8, 7)])
+def test_shard_route_matches_its_contract(eb, world, rank):
+    """engram_shard_route over t0 > 0 with segments: one request per (position,
+    head) served by another rank and not by the overlay, grouped by owner with
+    the restated counts; every request slot is used by exactly one pair and
+    send_ids[row_index[k]] is pair k's id."""
+    rng = np.random.default_rng(13 * world + rank)
+    n_rows = 40_009
+    spec = random_spec(O.FMT_IQ4_XS, 256, n_rows, 5 + world)
+    full = device_table(eb, spec)
+    T, t0 = 2500, 211
+    toks = zipf_tokens(rng, T)
+    ss = FX.seg_starts(np.sort(rng.integers(0, 6, size=T)))
+    ids = spec.ids(toks, seg_start=ss, t0=t0).reshape(-1).astype(np.int64)
+    ov_ids = np.unique(np.concatenate([np.unique(ids)[::3], rng.integers(0, n_rows, size=80)])).astype(np.int32)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    n = T - t0
+    entries = n * 16
+    words = int(eb._lib.load().engram_shard_route_scratch_words(n, 16, world))
+    scratch = torch.empty(words, dtype=torch.int32, device=DEV)
+    send = torch.full((entries,), -7, dtype=torch.int32, device=DEV)
+    counts = torch.empty(2 * world, dtype=torch.int64, device=DEV)
+    rix = torch.empty(entries, dtype=torch.int32, device=DEV)
+    ov = eb._lib.EngramOverlay(None, omap.R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
+    toks_d, ss_d = torch.from_numpy(toks).to(DEV), torch.from_numpy(ss).to(DEV)
+    lib = eb._lib.load()
+    assert lib.engram_shard_route(C.byref(full.ctable), C.byref(ov), toks_d.data_ptr(), ss_d.data_ptr(), t0, n, world,
+                                  rank, scratch.data_ptr(), words - 1, send.data_ptr(), counts.data_ptr(),
+                                  rix.data_ptr(), eb._lib.stream_of(DEV)) == eb._lib.ERR_WORKSPACE
+    st = lib.engram_shard_route(C.byref(full.ctable), C.byref(ov), toks_d.data_ptr(), ss_d.data_ptr(), t0, n, world,
+                                rank, scratch.data_ptr(), words, send.data_ptr(), counts.data_ptr(), rix.data_ptr(),
+                                eb._lib.stream_of(DEV))
+    eb._lib.check(st, "engram_shard_route")
+    torch.cuda.synchronize()
+    req = (ids % world != rank) & ~np.isin(ids, ov_ids)
+    want_counts = np.bincount(ids[req] % world, minlength=world)
+    got_counts = counts[:world].cpu().numpy()
+    assert np.array_equal(got_counts, want_counts)
+    got_rix = rix.cpu().numpy()
+    assert np.array_equal(got_rix >= 0, req)
+    total = int(req.sum())
+    assert np.array_equal(np.sort(got_rix[req]), np.arange(total))  # each slot exactly once
+    got_send = send[:total].cpu().numpy()
+    assert np.array_equal(got_send[got_rix[req]], ids[req])
+    off = np.concatenate([[0], np.cumsum(got_counts)])
+    for o in range(world):
+        assert (got_send[off[o]:off[o + 1]] % world == o).all()
+
+
 @pytest.mark.parametrize("world,rank", [(2, 1), (3, 2), (8, 5)])
 def test_shard_plan_matches_its_contract(eb, world, rank):
     """engram_shard_plan over t0 > 0 with segments: the counts per owner, the
@@ -483,11 +532,12 @@ def test_shard_plan_matches_its_contract(eb, world, rank):
     assert total < int((want_rix >= 0).sum())  # a Zipf batch repeats remote rows
 
 
+@pytest.mark.parametrize("dedup", [False, True])
 @pytest.mark.parametrize("world", [2, 3, 8])
 @pytest.mark.parametrize("fmt,dim,mode", [(O.FMT_IQ4_XS, 256, O.MODE_PAIRSUM_ADD_BF16),
                                           (O.FMT_IQ4_NL, 160, O.MODE_CONCAT_F32),
                                           (O.FMT_IQ4_XS, 512, O.MODE_PAIRSUM_ADD_BF16)])
-def test_exchange_staged_forward_matches_resident_table(eb, world, fmt, dim, mode):
+def test_exchange_staged_forward_matches_resident_table(eb, world, fmt, dim, mode, dedup):
     """W ranks emulated on one GPU, each with exchange staging over a local
     exchange: four batches pipelined with the prefetch two batches ahead (plan,
     counts, deduplicated exchange, then engram_forward_exchanged) give outputs,
@@ -533,7 +583,7 @@ def test_exchange_staged_forward_matches_resident_table(eb, world, fmt, dim, mod
     want = [run(resident(b)) for b in batches]
     for r in range(world):
         sh = shards[r]
-        sh.enable_exchange_staging(T, ex)
+        sh.enable_exchange_staging(T, ex, dedup=dedup)
         sh.prefetch(*batches[0], omap=omap)
         sh.prefetch(*batches[1], omap=omap)
         for k in range(3):

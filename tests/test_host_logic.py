@@ -119,7 +119,7 @@ def test_bench_command_line_and_config_text(monkeypatch):
     args = bench.parse()
     assert args.shard and args.stage == "exchange" and args.stage_blocks == 32 and args.shard_exchange == "peer"
     assert args.e2e_exchange == "peer" and args.layout == "sharded"
-    assert "planned two batches ahead" in bench.shard_text(dict(bench.CONFIGS["cfg5"], shard=True, stage="exchange"))
+    assert "three batches ahead" in bench.shard_text(dict(bench.CONFIGS["cfg5"], shard=True, stage="exchange"))
     cfg = dict(bench.CONFIGS["cfg5"], shard=True, shard_exchange="peer", stage="push", exchange="peer")
     text = bench.config_json(cfg, args)["parallelism"]
     assert text.startswith("dp2+row-sharded") and "stores the rows" in text

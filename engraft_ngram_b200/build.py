@@ -14,7 +14,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libengram_b200.so"
 SOURCES = ["engram_table.cu", "engram_forward.cu", "engram_backward.cu", "engram_adam.cu", "engram_shard.cu", "engram_scan.cu",
-           "engram_rowset.cu", "engram_stage.cu", "engram_ple.cu"]
+           "engram_rowset.cu", "engram_stage.cu", "engram_ple.cu", "engram_gemm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -2,8 +2,11 @@
 `engraft.replica.layers.ple_forward` (engraft/replica/layers.py:565-626), same
 arguments and results.
 
-The key and value projections are one GEMM against [w_key; w_value] (cuBLAS
-through torch.matmul).  PROJECTION selects its arithmetic:
+The key and value projections are one GEMM against [w_key; w_value].
+PROJECTION selects its arithmetic and engine:
+  "tcgen05": this library's own tensor-core GEMM (engram_gemm_3xtf32: tcgen05
+    MMAs fed by TMA, the accumulator in tensor memory, the three 3xTF32
+    products issued from one load of each operand slice), fp32 accumulation;
   "3xtf32" (default): each fp32 operand split into a TF32 head and the fp32
     remainder, x = hi + lo, and A B = hi_A hi_B + hi_A lo_B + lo_A hi_B on the
     tensor cores (the split-precision method of NVIDIA's CUTLASS "3xTF32"),
@@ -28,13 +31,14 @@ and `install_ple` routes it to the reference's own function.
 from __future__ import annotations
 
 import contextlib
+import ctypes as C
 
 import torch
 
 from . import _lib as L
 
 _GRAD_FIELDS = ("w_key", "w_value", "norm_key", "norm_query", "norm_conv", "conv1d")
-PROJECTION = "3xtf32"  # or "fp32"
+PROJECTION = "3xtf32"  # or "fp32", "tcgen05"
 
 
 @contextlib.contextmanager
@@ -69,9 +73,53 @@ def _weights_kv(w, mode: str):
     return parts
 
 
+def gemm_tf32(terms, out: torch.Tensor, err: torch.Tensor | None = None) -> torch.Tensor:
+    """out [M, N] = sum of A @ B.T over the (A [M, K], B [N, K]) pairs in terms,
+    on the tensor cores (engram_gemm_tf32); fp32 contiguous CUDA tensors."""
+    M, K = terms[0][0].shape
+    N = terms[0][1].shape[0]
+    a = (C.c_void_p * len(terms))(*[x.data_ptr() for x, _ in terms])
+    b = (C.c_void_p * len(terms))(*[y.data_ptr() for _, y in terms])
+    st = L.load().engram_gemm_tf32(len(terms), a, b, M, N, K, K, K, out.data_ptr(), out.stride(0), L.ptr(err),
+                                   L.stream_of(out.device))
+    L.check(st, "engram_gemm_tf32")
+    return out
+
+
+def gemm_3xtf32(a_hi, a_lo, b_hi, b_lo, out: torch.Tensor, err: torch.Tensor | None = None) -> torch.Tensor:
+    """out [M, N] = (a_hi + a_lo) @ (b_hi + b_lo).T in 3xTF32 (the lo @ lo term
+    dropped), every K slice of the four operands loaded once (engram_gemm_3xtf32)."""
+    M, K = a_hi.shape
+    N = b_hi.shape[0]
+    st = L.load().engram_gemm_3xtf32(a_hi.data_ptr(), a_lo.data_ptr(), b_hi.data_ptr(), b_lo.data_ptr(), M, N, K,
+                                     a_hi.stride(0), b_hi.stride(0), out.data_ptr(), out.stride(0), L.ptr(err),
+                                     L.stream_of(out.device))
+    L.check(st, "engram_gemm_3xtf32")
+    return out
+
+
+def _weights_t(w):
+    """[w_key; w_value].T ([n, hc*n + n], K-major for the backward's GEMM) split
+    into TF32 head and remainder, cached on `w` until a weight changes."""
+    key = (w.w_key.data_ptr(), w.w_key._version, w.w_value.data_ptr(), w.w_value._version)
+    cached = getattr(w, "_engram_b200_kvt", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    parts = split_tf32(torch.cat([w.w_key, w.w_value], dim=0).t().contiguous())
+    try:
+        setattr(w, "_engram_b200_kvt", (key, parts))
+    except AttributeError:
+        pass
+    return parts
+
+
 def project(emb: torch.Tensor, w, out: torch.Tensor, mode: str | None = None) -> torch.Tensor:
     """out [T, hc*n + n] = emb @ [w_key; w_value].T (key columns, then value)."""
     mode = mode or PROJECTION
+    if mode == "tcgen05":
+        b_hi, b_lo = _weights_kv(w, "3xtf32")
+        a_hi, a_lo = split_tf32(emb)
+        return gemm_3xtf32(a_hi, a_lo, b_hi, b_lo, out)
     if mode == "fp32":
         (kv,) = _weights_kv(w, "fp32")
         with _matmul_tf32(False):
@@ -105,6 +153,10 @@ def project_back(dkv: torch.Tensor, w, out: torch.Tensor, mode: str | None = Non
     """out [T, n] = dkv [T, hc*n + n] @ [w_key; w_value]: the gradient of emb
     through both projections, in the same arithmetic as project()."""
     mode = mode or PROJECTION
+    if mode == "tcgen05":
+        b_hi, b_lo = _weights_t(w)
+        a_hi, a_lo = split_tf32(dkv)
+        return gemm_3xtf32(a_hi, a_lo, b_hi, b_lo, out)
     if mode == "fp32":
         (kv,) = _weights_kv(w, "fp32")
         with _matmul_tf32(False):

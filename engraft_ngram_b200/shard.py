@@ -248,9 +248,9 @@ class ShardedTable:
                 self.xstage.prefetch(key, tokens, ss, t0, n, omap)
             b, recv, rix, ready = self.xstage.take(key, omap)
             cur = torch.cuda.current_stream(dev)
-            t0 = self.xstage._mark(cur)
+            t_wait = self.xstage._mark(cur)
             cur.wait_event(ready)
-            self.xstage._span("wait", t0, cur)
+            self.xstage._span("wait", t_wait, cur)
             ov = omap.descriptor(rows_var)
             st = lib.engram_forward_exchanged(C.byref(self.ctable), C.byref(ov), tokens.data_ptr(), L.ptr(ss), t0, n,
                                               self.shard.data_ptr(), self.world, self.rank, recv.data_ptr(),

@@ -614,6 +614,33 @@ ENGRAM_API int engram_ple_conv_backward(const float* normed, const float* hist, 
                                         const float* dout, const float* dtail, int64_t tail_len, float* dconv,
                                         float* dnormed, float* dhist, void* stream);
 
+/*
+ * C[M, N] (row stride ldc floats) = sum over p < n_terms (1..3) of
+ * A_p[M, K] @ B_p[N, K]^T on the tensor cores (tcgen05.mma kind::tf32, operands
+ * loaded by TMA, fp32 accumulation in tensor memory): a and b are HOST arrays
+ * of n_terms device pointers to row-major fp32 matrices (row strides lda, ldb
+ * floats; K, lda, ldb multiples of 4; 16-byte aligned), each element read as
+ * TF32.  With the terms (A_lo, B_hi), (A_hi, B_lo), (A_hi, B_hi) of the split
+ * x = hi + lo (hi: x with its low 13 mantissa bits cleared) the result is the
+ * 3xTF32 product, fp32-level accurate: the PLE block's projections
+ * (engraft/replica/layers.py:587,593, key = emb @ w_key.T, value = emb @
+ * w_value.T) and their backward.  err (device int32, nullable) counts
+ * barrier waits that gave up (a bounded spin; 0 in any correct run).
+ */
+ENGRAM_API int engram_gemm_tf32(int32_t n_terms, const float* const* a, const float* const* b, int64_t M, int64_t N,
+                                int64_t K, int64_t lda, int64_t ldb, float* c, int64_t ldc, int32_t* err,
+                                void* stream);
+/*
+ * The same 3xTF32 product from the split operands in one pass: C = A_lo B_hi^T
+ * + A_hi B_lo^T + A_hi B_hi^T with A_hi, A_lo sharing row stride lda and B_hi,
+ * B_lo sharing ldb.  Each K slice of the four operands is loaded once and the
+ * three MMAs are issued from it (a third less operand traffic than
+ * engram_gemm_tf32 with three terms).  Same shape rules and err.
+ */
+ENGRAM_API int engram_gemm_3xtf32(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                                  int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, float* c, int64_t ldc,
+                                  int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

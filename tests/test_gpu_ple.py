@@ -32,7 +32,7 @@ def _close(got, want):
     return np.abs(got - want).max() <= TOL * max(1.0, np.abs(want).max())
 
 
-@pytest.fixture(params=["3xtf32", "fp32"])
+@pytest.fixture(params=["3xtf32", "fp32", "tcgen05"])
 def projection(request, monkeypatch):
     from engraft_ngram_b200 import ple
     monkeypatch.setattr(ple, "PROJECTION", request.param)
@@ -193,3 +193,59 @@ def test_ple_block_weight_gradients_route_to_the_reference():
     finally:
         eb.uninstall_ple(mods)
     assert fake.ple_forward is not None and fake.ple_forward(None, None, None, None, None) == ("orig", None)
+
+
+@pytest.mark.parametrize("M,N,K,terms", [(128, 256, 32, 1), (11, 300, 36, 1), (256, 768, 256, 3),
+                                         (2048, 2560, 1024, 3), (333, 513, 1000, 2)])
+def test_tcgen05_gemm_matches_float64(M, N, K, terms):
+    """engram_gemm_tf32 (tcgen05 MMAs, TMA-fed, TMEM accumulator): one TF32 term
+    within TF32 rounding of the float64 product; the 3xTF32 split within fp32
+    accumulation error; ragged M, N and K handled by the zero-filled tiles; no
+    barrier wait gave up."""
+    from engraft_ngram_b200.ple import gemm_tf32, split_tf32
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    A = torch.randn(M, K, generator=g, device=DEV)
+    B = torch.randn(N, K, generator=g, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = torch.full((M, N), float("nan"), device=DEV)
+    if terms == 1:
+        gemm_tf32([(A, B)], out, err)
+        tol = 4e-3
+    else:
+        a_hi, a_lo = split_tf32(A)
+        b_hi, b_lo = split_tf32(B)
+        gemm_tf32([(a_lo, b_hi), (a_hi, b_lo), (a_hi, b_hi)][-terms:], out, err)
+        tol = 2e-5 if terms == 3 else 3e-3
+    torch.cuda.synchronize()
+    want = A.double() @ B.double().T
+    assert int(err.item()) == 0
+    assert torch.isfinite(out).all()
+    rel = ((out.double() - want).abs().max() / want.abs().max()).item()
+    assert rel <= tol, rel
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 16), (11, 300, 36), (256, 768, 256), (2048, 2560, 1024),
+                                   (333, 513, 1000)])
+def test_fused_3xtf32_gemm_matches_float64_and_the_three_terms(M, N, K):
+    """engram_gemm_3xtf32 (one load of A_hi, A_lo, B_hi, B_lo per K slice, three
+    MMAs from it) is within fp32 accumulation error of the float64 product and
+    agrees with engram_gemm_tf32 over the same three terms to accumulation
+    order; ragged shapes zero-filled; no barrier wait gave up."""
+    from engraft_ngram_b200.ple import gemm_3xtf32, gemm_tf32, split_tf32
+    g = torch.Generator(device=DEV).manual_seed(3 * M + N + K)
+    A = torch.randn(M, K, generator=g, device=DEV)
+    B = torch.randn(N, K, generator=g, device=DEV)
+    a_hi, a_lo = split_tf32(A)
+    b_hi, b_lo = split_tf32(B)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    fused = torch.full((M, N), float("nan"), device=DEV)
+    gemm_3xtf32(a_hi, a_lo, b_hi, b_lo, fused, err)
+    terms = torch.full((M, N), float("nan"), device=DEV)
+    gemm_tf32([(a_lo, b_hi), (a_hi, b_lo), (a_hi, b_hi)], terms, err)
+    torch.cuda.synchronize()
+    want = A.double() @ B.double().T
+    scale = want.abs().max()
+    assert int(err.item()) == 0
+    assert torch.isfinite(fused).all()
+    assert ((fused.double() - want).abs().max() / scale).item() <= 2e-5
+    assert ((fused.double() - terms.double()).abs().max() / scale).item() <= 2e-5

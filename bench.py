@@ -9,9 +9,13 @@ policy makes every read row variable), bigram+trigram pair sums added into a
 bf16 residual stream [T, 2048].  One step = fused forward (hash -> overlay
 probe -> gather/dequant -> residual add) + deterministic row-gradient backward
 from a bf16 upstream gradient + the Adam step with the descent's regulariser.
-With N > 1 ranks every rank holds the table and its own batch; the overlay
-gradients are reduce-scattered over NCCL, each rank runs Adam on its 1/N of
-the overlay rows and the updated rows are all-gathered.
+With N > 1 ranks (weak scaling, each rank its own batch) the table is
+row-sharded by default (owner = id mod N): each step's rows of other ranks are
+routed three batches ahead, their ids stored straight into the owners' memory,
+gathered there and copied back by the copy engines over NVLink.  The overlay
+update crosses GPUs in peer memory: row gradients stored into their owners'
+buffers by the backward, one Adam kernel per owner that stores the new rows
+into every rank.  `--layout replicated` holds the whole table on every rank.
 
 `--impl reference` times the CPU restatement of the reference's algorithm (the
 oracle, all host threads) on a bounded sample of the same workload.
@@ -1027,8 +1031,9 @@ def shard_text(cfg):
     if not cfg.get("shard"):
         return ""
     if cfg.get("stage") == "exchange":
-        return ("+row-sharded table (id mod N; the rows of other ranks routed three batches ahead, gathered by their owners "
-                "and copied with the copy engines over NVLink; local rows read in place)")
+        return ("+row-sharded table (id mod N; the rows of other ranks routed three batches ahead with their ids "
+                "stored into the owners' memory, gathered by the owners and copied with the copy engines over "
+                "NVLink; local rows read in place)")
     if cfg.get("shard_exchange", "peer") != "peer":
         return "+row-sharded table (id mod N, NCCL all-to-all of ids and rows)"
     if cfg.get("stage", "push") == "push":
@@ -1208,9 +1213,10 @@ def sharded_stats(wl, ms, fwd_ms, bwd_ms, ddist, world, device):
         t = torch.tensor([ph[k] for k in keys], dtype=torch.float64, device=device)
         ddist.all_reduce(t, op=ddist.ReduceOp.MAX)
         phases = {k: float(v) for k, v in zip(keys, t.tolist())}
-        phases["note"] = ("ms per step, max over ranks: route and serve (the owner's gather) on the step's stream "
-                          "before the forward, fetch (copy-engine transfers) on the side stream, wait = the forward's "
-                          "stream blocked on its rows")
+        phases["note"] = ("ms per step, max over ranks: route (ids pushed to their owners), serve (the owner's "
+                          "local gather) and barrier (a 4-byte all-reduce) on the step's stream before the forward, "
+                          "fetch (copy-engine transfers) on the side stream, wait = the forward's stream blocked on "
+                          "its rows")
     return {"table_bytes_per_gpu": int(wl.shard.n_local * wl.shard.stride), "exchange_phase_ms": phases,
             "nvlink": {"remote_pairs_per_step": int(rr[0]), "distinct_remote_rows_per_step": int(rr[1]),
                        "dedup_factor": int(rr[0]) / max(int(rr[1]), 1), "bytes_per_step": nv_bytes,

@@ -303,47 +303,133 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_scatter(const int32_t* 
     }
 }
 
-// Owner side of the peer exchange (engram_shard_serve): the rows every other
-// rank requested from this rank, gathered from the local shard into send_rows,
-// requester by requester.  Requester r's ids for this owner are the slice
-// [sum_{o < rank} M[r][o], + M[r][rank]) of its send_ids (read over NVLink
-// through id_ptrs[r]); they land at send_rows rows [sum_{r' < r} M[r'][rank], +
-// M[r][rank]).  Rows at or past max_rows are not written (the requester refuses
-// such a batch on the host).
-__global__ void __launch_bounds__(256) k_shard_serve(const uint8_t* __restrict__ shard, int64_t stride,
-                                                     int64_t n_local, int world, int rank,
-                                                     const unsigned long long* __restrict__ id_ptrs,
-                                                     const int64_t* __restrict__ M, uint8_t* __restrict__ send_rows,
-                                                     int64_t max_rows) {
-    __shared__ long long base[kMaxWorld + 1];  // first send row of each requester
-    __shared__ long long idoff[kMaxWorld];     // offset of this owner's slice in the requester's send_ids
+// engram_shard_route_push: the requests of a batch written straight into their
+// owners' memory.  Requester `rank` owns region `rank` of every owner's request
+// buffer (region entries of int32 ids) and of its send buffer (region rows).
+// k_route_push hashes a tile of (position, head) pairs, counts each owner's
+// requests in shared memory, reserves the tile's slots with one atomic per
+// owner on the global counters, then stores every requested id into its
+// owner's region (a plain store over NVLink) and tags the pair with
+// owner * region + slot.  k_route_finish turns the tags into rows of the
+// receive buffer (owners' blocks in ascending owner order, so row = the
+// counts of lower owners + slot) and block 0 stores each count into its
+// owner's count array (entry `rank`).  The order inside an owner's block
+// depends on which tile reserved first; the forward reads every pair's own
+// row, so its output does not.
+constexpr int kPushThreads = 256, kPushItems = 8, kPushTile = kPushThreads * kPushItems;
+
+__global__ void __launch_bounds__(kPushThreads) k_route_push(engram_table T, engram_overlay OV,
+                                                             const int32_t* __restrict__ tokens,
+                                                             const int32_t* __restrict__ seg_start, int64_t t0,
+                                                             int64_t n, int world, int rank,
+                                                             const unsigned long long* __restrict__ id_ptrs,
+                                                             int64_t region, unsigned long long* __restrict__ cnt,
+                                                             int32_t* __restrict__ row_index) {
+    __shared__ uint32_t tile_cnt[kMaxWorld];
+    __shared__ unsigned long long first[kMaxWorld];
+    for (int o = threadIdx.x; o < world; o += blockDim.x) tile_cnt[o] = 0;
+    __syncthreads();
+    const int nh = T.n_heads;
+    const int64_t total = n * nh;
+    const int64_t base = (int64_t)blockIdx.x * kPushTile;
+    int32_t g[kPushItems];
+    uint32_t loc[kPushItems];
+#pragma unroll
+    for (int it = 0; it < kPushItems; it++) {
+        const int64_t k = base + it * kPushThreads + threadIdx.x;
+        g[it] = -1;
+        if (k < total) {
+            const int64_t i = k / nh;
+            const int h = (int)(k - i * nh);
+            const int32_t id = hash_row(T, tokens, seg_start, t0 + i, h);
+            const int o = (int)((uint32_t)id % (uint32_t)world);
+            if (o != rank && overlay_slot(OV, id) < 0) {
+                g[it] = id;
+                loc[it] = atomicAdd(tile_cnt + o, 1u);
+            }
+        }
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < world; o += blockDim.x)
+        first[o] = tile_cnt[o] ? atomicAdd(cnt + o, (unsigned long long)tile_cnt[o]) : 0ull;
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < kPushItems; it++) {
+        const int64_t k = base + it * kPushThreads + threadIdx.x;
+        if (k >= total) break;
+        int32_t tag = -1;
+        if (g[it] >= 0) {
+            const int o = (int)((uint32_t)g[it] % (uint32_t)world);
+            const int64_t slot = (int64_t)first[o] + loc[it];  // < region: a batch has at most region pairs
+            reinterpret_cast<int32_t*>(id_ptrs[o])[(int64_t)rank * region + slot] = g[it];
+            tag = (int32_t)(o * region + slot);
+        }
+        row_index[k] = tag;
+    }
+}
+
+__global__ void __launch_bounds__(256) k_route_finish(int64_t total, int world, int rank, int64_t region,
+                                                      const unsigned long long* __restrict__ cnt,
+                                                      const unsigned long long* __restrict__ count_ptrs,
+                                                      int32_t* __restrict__ row_index) {
+    __shared__ long long before[kMaxWorld];
+    if (threadIdx.x == 0) {
+        long long acc = 0;
+        for (int o = 0; o < world; o++) {
+            before[o] = acc;
+            acc += (long long)cnt[o];
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x < world && threadIdx.x != rank)
+        reinterpret_cast<long long*>(count_ptrs[threadIdx.x])[rank] = (long long)cnt[threadIdx.x];
+    __syncthreads();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += stride) {
+        const int32_t tag = row_index[k];
+        if (tag >= 0) {
+            const int o = (int)(tag / region);
+            row_index[k] = (int32_t)(before[o] + (tag - o * region));
+        }
+    }
+}
+
+// Owner side of the pushed exchange (engram_shard_serve_pushed): requester r's
+// ids for this owner are entries [0, counts[r]) of region r of req_ids (this
+// GPU's memory, written by r's route); the rows land in region r of send_rows,
+// in the same order.  A warp serves 32 send rows at a time: lane l looks up
+// row g0 + l once, then the warp copies the 32 rows word by word with
+// kServeLoads 16-byte loads per lane in flight.  Ids that are not this
+// owner's, or past its shard, give zero rows.
+__global__ void __launch_bounds__(256) k_serve_pushed(const uint8_t* __restrict__ shard, int64_t stride,
+                                                      int64_t n_local, int world, int rank,
+                                                      const int32_t* __restrict__ req_ids,
+                                                      const long long* __restrict__ req_counts, int64_t region,
+                                                      uint8_t* __restrict__ send_rows) {
+    __shared__ long long base[kMaxWorld + 1];  // first flattened row of each requester
     if (threadIdx.x == 0) {
         long long acc = 0;
         for (int r = 0; r < world; r++) {
             base[r] = acc;
-            acc += (r == rank) ? 0 : M[(int64_t)r * world + rank];
-            long long off = 0;
-            for (int o = 0; o < rank; o++) off += M[(int64_t)r * world + o];
-            idoff[r] = off;
+            long long c = r == rank ? 0 : req_counts[r];
+            acc += c < 0 ? 0 : (c > region ? region : c);
         }
         base[world] = acc;
     }
     __syncthreads();
-    const int64_t total = base[world] < max_rows ? base[world] : max_rows;
+    const int64_t total = base[world];
     const int words = (int)(stride >> 4);
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    // a warp serves 32 send rows at a time: lane l reads the id of row g0 + l once (over NVLink), then the
-    // warp copies the 32 rows word by word, kServeLoads words per lane in flight
     constexpr int kServeLoads = 8;
     for (int64_t g0 = warp0 * 32; g0 < total; g0 += nwarps * 32) {
         const int64_t f = g0 + lane;
-        int64_t src = -1;  // byte offset of the row in the shard, -1: none
+        int64_t src = -1, dst_row = -1;  // byte offset of the row in the shard (-1: zero row); its row in send_rows
         if (f < total) {
             int r = 0;
-            while (r + 1 < world && base[r + 1] <= f) r++;  // requester of send row f
-            const int32_t g = reinterpret_cast<const int32_t*>(id_ptrs[r])[idoff[r] + (f - base[r])];
+            while (r + 1 < world && base[r + 1] <= f) r++;
+            dst_row = (int64_t)r * region + (f - base[r]);
+            const int32_t g = req_ids[dst_row];
             const int64_t local = (int64_t)g / world;
             if (g >= 0 && (int)(g % world) == rank && local < n_local) src = local * stride;
         }
@@ -355,12 +441,14 @@ __global__ void __launch_bounds__(256) k_shard_serve(const uint8_t* __restrict__
             for (int u = 0; u < kServeLoads; u++) {
                 const int p = p0 + u * 32 + lane;
                 const int rr = p / words, w = p - rr * words;
-                const int64_t s_off = __shfl_sync(0xffffffffu, src, rr < 32 ? rr : 0);
+                const int src_lane = rr < 32 ? rr : 0;
+                const int64_t s_off = __shfl_sync(0xffffffffu, src, src_lane);
+                const int64_t d_row = __shfl_sync(0xffffffffu, dst_row, src_lane);
                 dst[u] = -1;
-                if (p < pairs && g0 + rr < total) {
+                if (p < pairs && d_row >= 0) {
                     v[u] = s_off >= 0 ? __ldg(reinterpret_cast<const uint4*>(shard + s_off) + w)
                                       : make_uint4(0u, 0u, 0u, 0u);
-                    dst[u] = (g0 + rr) * stride + 16 * w;
+                    dst[u] = d_row * stride + 16 * w;
                 }
             }
 #pragma unroll
@@ -439,23 +527,6 @@ extern "C" int engram_shard_plan(const engram_table* t, const engram_overlay* ov
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
 
-extern "C" int engram_shard_serve(const void* shard_rows, int64_t stride, int64_t n_local, int32_t world, int32_t rank,
-                                  const void* id_ptrs, const int64_t* counts_all, void* send_rows, int64_t max_rows,
-                                  void* stream) {
-    if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || stride <= 0 || (stride & 15) || n_local < 0 ||
-        max_rows < 0)
-        return ENGRAM_ERR_ARG;
-    if (world == 1 || max_rows == 0) return ENGRAM_OK;
-    if (!shard_rows || !id_ptrs || !counts_all || !send_rows || !aligned16(shard_rows) || !aligned16(send_rows))
-        return ENGRAM_ERR_ARG;
-    const int64_t cap = (int64_t)sm_count() * 4;
-    k_shard_serve<<<(int)cap, 256, 0, (cudaStream_t)stream>>>(
-        static_cast<const uint8_t*>(shard_rows), stride, n_local, world, rank,
-        static_cast<const unsigned long long*>(id_ptrs), counts_all, static_cast<uint8_t*>(send_rows), max_rows);
-    count_launches(1);
-    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
-}
-
 extern "C" int64_t engram_shard_route_scratch_words(int64_t n, int32_t n_heads, int32_t world) {
     if (n < 0 || n_heads < 1 || world < 1 || world > kMaxWorld) return ENGRAM_ERR_ARG;
     const int64_t tiles = (n * n_heads + kRouteTile - 1) / kRouteTile;
@@ -488,5 +559,58 @@ extern "C" int engram_shard_route(const engram_table* t, const engram_overlay* o
     k_route_scan<<<1, 1024, 0, s>>>(scratch, (int)tiles, world, cnt);
     k_route_scatter<<<(int)tiles, kRouteThreads, 0, s>>>(row_index, entries, world, scratch, send_ids, row_index);
     count_launches(3);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int engram_shard_route_push(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                       const int32_t* seg_start, int64_t t0, int64_t n, int32_t world, int32_t rank,
+                                       const void* id_ptrs, const void* count_ptrs, int64_t region, int64_t* counts,
+                                       int32_t* row_index, void* stream) {
+    if (!t || t0 < 0 || n < 0 || world < 1 || world > kMaxWorld || rank < 0 || rank >= world || region < 1)
+        return ENGRAM_ERR_ARG;
+    if (!id_ptrs || !count_ptrs || !counts || !row_index || (n > 0 && !tokens)) return ENGRAM_ERR_ARG;
+    const int64_t entries = n * t->n_heads;
+    if (entries > region) return ENGRAM_ERR_RANGE;
+    if ((int64_t)world * region > INT32_MAX) return ENGRAM_ERR_RANGE;
+    engram_overlay OV{nullptr, 0, nullptr, nullptr, 0};
+    if (ov && ov->n_rows > 0) {
+        OV = *ov;
+        if (!OV.map_keys || !OV.map_slots || (OV.capacity & (OV.capacity - 1)) != 0 || OV.capacity < 2 * OV.n_rows)
+            return ENGRAM_ERR_ARG;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(counts);
+    cudaMemsetAsync(counts, 0, sizeof(int64_t) * world, s);
+    const int64_t tiles = (entries + kPushTile - 1) / kPushTile;
+    if (tiles > INT_MAX) return ENGRAM_ERR_RANGE;
+    int launched = 0;
+    if (tiles > 0) {
+        k_route_push<<<(int)tiles, kPushThreads, 0, s>>>(*t, OV, tokens, seg_start, t0, n, world, rank,
+                                                         static_cast<const unsigned long long*>(id_ptrs), region, cnt,
+                                                         row_index);
+        launched++;
+    }
+    // publishes the counts (zero for an empty batch) even when there is nothing to route
+    k_route_finish<<<grid(entries > 0 ? entries : 1), 256, 0, s>>>(entries, world, rank, region, cnt,
+                                                                   static_cast<const unsigned long long*>(count_ptrs),
+                                                                   row_index);
+    count_launches(launched + 1);
+    return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+}
+
+extern "C" int engram_shard_serve_pushed(const void* shard_rows, int64_t stride, int64_t n_local, int32_t world,
+                                         int32_t rank, const int32_t* req_ids, const int64_t* req_counts,
+                                         int64_t region, void* send_rows, void* stream) {
+    if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || stride <= 0 || (stride & 15) || n_local < 0 ||
+        region < 1)
+        return ENGRAM_ERR_ARG;
+    if (world == 1) return ENGRAM_OK;
+    if (!shard_rows || !req_ids || !req_counts || !send_rows || !aligned16(shard_rows) || !aligned16(send_rows))
+        return ENGRAM_ERR_ARG;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    k_serve_pushed<<<(int)cap, 256, 0, (cudaStream_t)stream>>>(
+        static_cast<const uint8_t*>(shard_rows), stride, n_local, world, rank, req_ids,
+        reinterpret_cast<const long long*>(req_counts), region, static_cast<uint8_t*>(send_rows));
+    count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }

@@ -141,18 +141,21 @@ class ShardedTable:
         self.push = PushStage(self, n_tokens_max, group, max_blocks)
 
     def enable_exchange_staging(self, n_tokens_max: int, exchange=None, dedup: bool = False) -> None:
-        """Make prefetch() plan and exchange the rows of other ranks ahead of the
-        forward, deduplicated, through `exchange`: "peer" (the default,
-        PeerRowExchange: owners gather into symmetric memory, requesters copy
-        with the copy engines), "nccl" (NcclRowExchange: NCCL all-to-alls on a
-        process group of their own) or an exchange object (LocalRowExchange
-        for emulated ranks).  dedup: request each distinct remote row once
-        per batch (engram_shard_plan, a device hash set) instead of once per
-        (position, head) (engram_shard_route, three cheap passes); worth it
-        where remote rows repeat inside a batch more than they do here.  Prefetching two batches ahead of the forward keeps
-        both the host and the forward from waiting on the exchange (see
-        ExchangeStage).  With NcclRowExchange a collective: every rank calls it."""
-        if exchange is None or exchange == "peer":
+        """Make prefetch() route and exchange the rows of other ranks ahead of
+        the forward through `exchange`: "peer" (PeerRowExchange, the default:
+        requests pushed into the owners' memory, owners gather locally,
+        requesters copy with the copy engines), "nccl" (NcclRowExchange: NCCL
+        all-to-alls on a process group of their own) or an exchange object
+        (LocalPeerRowExchange or LocalRowExchange for emulated ranks).
+        dedup: request each distinct remote row once per batch
+        (engram_shard_plan, a device hash set) instead of once per (position,
+        head); it needs a counting exchange, so with exchange None it selects
+        "nccl".  Prefetching three batches ahead of the forward keeps both the
+        host and the forward from waiting on the exchange (ExchangeStage).  A
+        collective: every rank calls it."""
+        if exchange is None:
+            exchange = "nccl" if dedup else "peer"
+        if exchange == "peer":
             exchange = PeerRowExchange(self, n_tokens_max)
         elif exchange == "nccl":
             exchange = NcclRowExchange()
@@ -453,35 +456,48 @@ class ExchangeStage:
     A batch passes three stages, one per prefetch() call, so a caller that
     prefetches three batches ahead of its forwards has, at step k: batch k+3
     routed, batch k+2 served, batch k+1 fetched, batch k read by the forward.
-      route (current stream): engram_shard_route, the ids of the batch's
-        (position, head) pairs that another rank owns and the overlay does not
-        serve, grouped by owner, per-owner counts and each pair's row in the
-        reply (row_index) (engram_shard_plan instead with dedup: each distinct
-        row once); then, on the side stream, every rank's counts are
-        all-gathered (exchange.gather_counts, a collective) and copied to
-        pinned host memory;
-      serve (current stream): with a serving exchange (PeerRowExchange) the
-        owners gather the rows the others asked of them (engram_shard_serve);
-        then a barrier on the side stream (exchange.barrier);
-      fetch (side stream): the host reads the batch's counts (gathered two
-        steps earlier, so it does not wait) and the exchange brings the
-        owners' rows into a receive buffer of the batch's own (PeerRowExchange:
-        one copy-engine transfer per owner; NcclRowExchange / LocalRowExchange:
-        exchange.rows).
-    The two SM stages run on the caller's stream, between the step's kernels,
-    instead of queueing behind them on a side stream; the side stream carries
-    only copy-engine transfers and 4-byte collectives.  forward(X) runs the
-    stages X has not passed yet (the host then waits), makes the current
-    stream wait for X's rows and runs engram_forward_exchanged.  Every rank
-    calls prefetch and forward in the same order with the same t0 and n (the
-    collectives follow that order).  Four buffer sets: a fifth batch
-    prefetched before the oldest is read drops the oldest."""
+
+    With a pushing exchange (PeerRowExchange, LocalPeerRowExchange; the
+    default), one prefetch() call queues on the caller's stream:
+      serve: the owners' gather of the batch routed one call earlier
+        (engram_shard_serve_pushed, local reads and writes only);
+      route: engram_shard_route_push for the new batch, which stores each
+        remote (position, head) pair's id straight into its owner's request
+        buffer and its counts into the owner's count array, and a copy of this
+        rank's counts to pinned host memory;
+      barrier: a 4-byte all-reduce.  Once it completes, every rank's route of
+        this call is visible to its owners (served next call) and every
+        owner's gather of this call is done (fetched next call);
+    and on the side stream, after the barrier of the call that served it:
+      fetch: the batch's rows, one copy-engine transfer per owner from the
+        owner's send buffer (the host reads this rank's counts, copied two
+        calls earlier, so it does not wait).
+    No collective runs on the side stream: it carries only copy-engine
+    transfers, so nothing there competes with the forward for SMs.
+
+    With a counting exchange (NcclRowExchange, LocalRowExchange):
+      route (current stream): engram_shard_route (engram_shard_plan with
+        dedup: each distinct row once), the ids grouped by owner in a local
+        send_ids; then, on the side stream, every rank's counts are
+        all-gathered (exchange.gather_counts) and copied to the host;
+      serve: nothing;
+      fetch (side stream): exchange.rows moves ids out and rows back.
+
+    forward(X) runs the stages X has not passed yet (the host then waits),
+    makes the current stream wait for X's rows and runs
+    engram_forward_exchanged.  Every rank calls prefetch and forward in the
+    same order with the same t0 and n (the collectives and the buffer sets
+    follow that order).  Four buffer sets: a fifth batch prefetched before the
+    oldest is read drops the oldest."""
 
     SETS = 4
 
     def __init__(self, table: "ShardedTable", n_tokens_max: int, exchange, dedup: bool = False):
         self.table, self.exchange = table, exchange
         self.dedup = bool(dedup)  # engram_shard_plan (distinct rows) or engram_shard_route (one row per pair)
+        self.push = bool(getattr(exchange, "pushes", False))
+        if self.push and self.dedup:
+            raise ValueError("dedup needs a counting exchange (\"nccl\" or LocalRowExchange)")
         dev = table.device
         self.n_max = int(n_tokens_max)
         entries = max(self.n_max * table.n_heads, 1)
@@ -490,14 +506,17 @@ class ExchangeStage:
         self.set_vals = torch.empty(self.cap if self.dedup else 1, dtype=torch.int32, device=dev)
         W = table.world
         alloc = getattr(exchange, "alloc_ids", None)
-        self.send_ids = [alloc(b, entries) if alloc is not None else torch.empty(entries, dtype=torch.int32, device=dev)
-                         for b in range(self.SETS)]
+        if self.push:  # the route stores the ids in the owners' request buffers
+            self.send_ids = [None] * self.SETS
+        else:
+            self.send_ids = [alloc(b, entries) if alloc is not None
+                             else torch.empty(entries, dtype=torch.int32, device=dev) for b in range(self.SETS)]
         self.rix = [torch.empty(entries, dtype=torch.int32, device=dev) for _ in range(self.SETS)]
         self.counts = [torch.zeros(2 * W, dtype=torch.int64, device=dev) for _ in range(self.SETS)]
         self.counts_host = [torch.zeros(W, W, dtype=torch.int64).pin_memory() for _ in range(self.SETS)]
         self.allc = [None] * self.SETS        # every rank's counts, on the device
         self.ev_counts = [None] * self.SETS   # side: counts gathered and copied to the host
-        self.ev_barrier = [None] * self.SETS  # side: every owner's gather of the batch is done
+        self.ev_barrier = [None] * self.SETS  # every owner's gather of the batch is done
         self.ev_ready = [None] * self.SETS    # side: the batch's rows are in its receive buffer
         self.recv = [None] * self.SETS
         self.state = [None] * self.SETS       # None | "routed" | "served" | "fetched"
@@ -524,9 +543,9 @@ class ExchangeStage:
             self.timing.setdefault(name, []).append((e0, self._mark(stream)))
 
     def phase_ms(self) -> dict:
-        """Mean ms per batch of each timed phase (after a synchronize): route and
-        serve on the caller's stream, fetch on the side stream, wait = how long
-        the forward's stream waited for its rows."""
+        """Mean ms per batch of each timed phase (after a synchronize): route,
+        serve and barrier on the caller's stream, fetch on the side stream,
+        wait = how long the forward's stream waited for its rows."""
         return {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in (self.timing or {}).items() if v}
 
     def _oldest(self, state):
@@ -542,7 +561,8 @@ class ExchangeStage:
         cur = torch.cuda.current_stream(t.device)
         for b in self._oldest("served"):  # the next forward waits for the oldest of them
             self._fetch(b)
-        for b in self._oldest("routed"):
+        served = self._oldest("routed")
+        for b in served:
             self._serve(b, cur)
         free = [b for b in range(self.SETS) if self.state[b] is None]
         if not free:  # drop the oldest waiting batch (every rank drops the same one)
@@ -552,11 +572,30 @@ class ExchangeStage:
         b = free[0]
         if ready is not None:
             cur.wait_event(ready)
-        t_route = self._mark(cur)
-        lib = L.load()
         ov = None
         if omap is not None and omap.R:
             ov = L.EngramOverlay(None, omap.R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
+        if self.push:
+            if self.ev_ready[b] is not None:  # the set's last copies are done before its owners refill it
+                cur.wait_event(self.ev_ready[b])
+            t_route = self._mark(cur)
+            self.exchange.route(t, b, ov, tokens, ss, t0, n, self.counts[b], self.rix[b], cur)
+            self.counts_host[b][0].copy_(self.counts[b][: t.world], non_blocking=True)
+            self._span("route", t_route, cur)
+            self.ev_counts[b] = torch.cuda.Event()
+            self.ev_counts[b].record(cur)
+            self.allc[b] = None
+            t_bar = self._mark(cur)
+            self.exchange.barrier()
+            self._span("barrier", t_bar, cur)
+            done = torch.cuda.Event()
+            done.record(cur)
+            for s_ in served:
+                self.ev_barrier[s_] = done
+            self._routed(b, key, ov, omap)
+            return
+        t_route = self._mark(cur)
+        lib = L.load()
         if self.dedup:
             st = lib.engram_shard_plan(C.byref(t.ctable), None if ov is None else C.byref(ov), tokens.data_ptr(),
                                        L.ptr(ss), t0, n, t.world, t.rank, self.set_keys.data_ptr(),
@@ -580,6 +619,9 @@ class ExchangeStage:
         self.allc[b] = allc
         self.ev_counts[b] = torch.cuda.Event()
         self.ev_counts[b].record(self.side)
+        self._routed(b, key, ov, omap)
+
+    def _routed(self, b: int, key, ov, omap) -> None:
         self.recv[b] = None
         self.state[b], self.key[b] = "routed", key
         self.omap_keys[b] = None if ov is None else omap.keys.data_ptr()
@@ -587,30 +629,24 @@ class ExchangeStage:
         self.seq[b] = self.n_seq
 
     def _serve(self, b: int, cur: torch.cuda.Stream) -> None:
-        serve = getattr(self.exchange, "serve", None)
-        if serve is not None:  # owners gather what the others asked of them, then a barrier
-            cur.wait_event(self.ev_counts[b])
+        if self.push:  # this owner's gather; the barrier after it comes with the call's route (or take)
             t0 = self._mark(cur)
-            serve(self.table, b, self.allc[b])
+            self.exchange.serve(self.table, b)
             self._span("serve", t0, cur)
-            served = torch.cuda.Event()
-            served.record(cur)
-            self.side.wait_event(served)
-            with torch.cuda.stream(self.side):
-                self.exchange.barrier()
-        self.ev_barrier[b] = torch.cuda.Event()
-        self.ev_barrier[b].record(self.side)
+            self.ev_barrier[b] = None
+        else:
+            self.ev_barrier[b] = self.ev_counts[b]
         self.state[b] = "served"
 
     def _fetch(self, b: int) -> None:
         t = self.table
         self.ev_counts[b].synchronize()
         m = self.counts_host[b]
+        self.side.wait_event(self.ev_barrier[b])
         t0 = self._mark(self.side)
         with torch.cuda.stream(self.side):
-            fetch = getattr(self.exchange, "fetch", None)
-            if fetch is not None:
-                rows = fetch(t, b, m)
+            if self.push:
+                rows = self.exchange.fetch(t, b, [int(x) for x in m[0, : t.world].tolist()])
             else:
                 send = [int(x) for x in m[t.rank].tolist()]
                 recv = [int(x) for x in m[:, t.rank].tolist()]
@@ -628,8 +664,12 @@ class ExchangeStage:
         if want != self.omap_keys[b]:
             raise ValueError("the batch was prefetched with another overlay map; prefetch it again with this one")
         cur = torch.cuda.current_stream(self.table.device)
-        if self.state[b] == "routed":
+        if self.state[b] == "routed":  # its route's barrier came with the call that routed it
             self._serve(b, cur)
+            if self.push:
+                self.exchange.barrier()
+                self.ev_barrier[b] = torch.cuda.Event()
+                self.ev_barrier[b].record(cur)
         if self.state[b] == "served":
             self._fetch(b)
         self.key[b] = None
@@ -676,20 +716,79 @@ class NcclRowExchange:
         return rows
 
 
-class PeerRowExchange:
-    """ExchangeStage's exchange over peer memory with copy-engine transfers.
+class _PushExchange:
+    """The buffers and calls of a pushing exchange, per batch set b: this
+    owner's request buffer ids[b] (int32 [world, region]), count array
+    cnts[b] (int64 [world]) and send buffer rows[b] ([world, region] rows),
+    with device tables of every rank's request buffer and count array
+    (id_ptrs[b], cnt_ptrs[b]).  Subclasses say where the buffers live, how the
+    owners' send buffers are reached and what the barrier is."""
 
-    Each rank's send_ids (three sets) and a send buffer per set live in torch
-    symmetric memory (no multicast object).  Per batch: the counts all-gather
-    (NCCL, on a group of its own) also orders every rank's plan before the
-    owners read it; serve() has each owner gather, in one kernel
-    (engram_shard_serve), the rows every other rank asked of it into its send
-    buffer, reading the requests through the peers' send_ids, then a barrier
-    (a 4-byte all-reduce); fetch() has the requester copy its block from each
-    owner's send buffer with one cudaMemcpyAsync per owner (torch copy_ from a
-    peer view): copy engines over NVLink, no SMs.  The block sizes come from
-    the counts matrix read on the host one step late (ExchangeStage).  A
-    collective to construct: every rank of `group` calls it."""
+    pushes = True
+
+    def _setup(self, table: "ShardedTable", n_tokens_max: int, sets: int) -> None:
+        W = table.world
+        self.world, self.rank, self.stride, self.sets = W, table.rank, table.stride, sets
+        self.region = max(int(n_tokens_max) * table.n_heads, 1)  # a batch's pairs: the most one owner can get
+        if W * self.region > 2**31 - 1:
+            raise ValueError(f"{W} ranks x {self.region} pairs per batch exceed the int32 row tags")
+        self.ids, self.cnts, self.rows, self.id_ptrs, self.cnt_ptrs = [], [], [], [], []
+
+    def route(self, table, b: int, ov, tokens: torch.Tensor, ss, t0: int, n: int, counts: torch.Tensor,
+              row_index: torch.Tensor, stream: torch.cuda.Stream) -> None:
+        """engram_shard_route_push for set b on `stream`."""
+        st = L.load().engram_shard_route_push(C.byref(table.ctable), None if ov is None else C.byref(ov),
+                                              tokens.data_ptr(), L.ptr(ss), t0, n, self.world, self.rank,
+                                              self.id_ptrs[b].data_ptr(), self.cnt_ptrs[b].data_ptr(), self.region,
+                                              counts.data_ptr(), row_index.data_ptr(), stream.cuda_stream)
+        L.check(st, "engram_shard_route_push")
+
+    def serve(self, table, b: int) -> None:
+        """This owner's gather for set b, on the current stream."""
+        st = L.load().engram_shard_serve_pushed(table.shard.data_ptr(), table.stride, table.n_local, self.world,
+                                                self.rank, self.ids[b].data_ptr(), self.cnts[b].data_ptr(),
+                                                self.region, self.rows[b].data_ptr(), L.stream_of(table.device))
+        L.check(st, "engram_shard_serve_pushed")
+
+    def _send_rows(self, b: int, o: int) -> torch.Tensor:
+        raise NotImplementedError
+
+    def _before_fetch(self, b: int) -> None:
+        pass
+
+    def fetch(self, table, b: int, own) -> torch.Tensor:
+        """This rank's rows of set b (own[o] = the rows it asked of owner o), in
+        ascending owner order: one copy-engine transfer per owner from the
+        start of this rank's region of the owner's send buffer."""
+        W, me, stride, region = self.world, self.rank, self.stride, self.region
+        total = sum(own)
+        out = torch.empty(max(total, 1) * stride, dtype=torch.uint8, device=table.device)
+        self._before_fetch(b)
+        off = 0
+        for o in range(W):
+            cnt = own[o]
+            if o == me or cnt == 0:
+                continue
+            if cnt > region:
+                raise RuntimeError(f"{cnt} rows asked of owner {o}, its region holds {region}")
+            src = self._send_rows(b, o)[me * region * stride:(me * region + cnt) * stride]
+            out[off * stride:(off + cnt) * stride].copy_(src, non_blocking=True)
+            off += cnt
+        return out[: total * stride]
+
+
+class PeerRowExchange(_PushExchange):
+    """ExchangeStage's exchange between GPUs over peer memory: requests pushed
+    into the owners' memory by the route, owners gather locally, requesters
+    copy their rows with the copy engines.
+
+    Every buffer lives in torch symmetric memory (no multicast object), so
+    each rank's request buffers and count arrays are written by the others
+    (plain stores from engram_shard_route_push) and its send buffers are read
+    by the others' copy engines (torch copy_ from a peer view, one
+    cudaMemcpyAsync per owner: NVLink, no SMs).  The barrier is a 4-byte
+    all-reduce on a process group of the exchange's own.  A collective to
+    construct: every rank of `group` calls it."""
 
     def __init__(self, table: "ShardedTable", n_tokens_max: int, group=None, sets: int = 4):
         import torch.distributed as dist
@@ -698,69 +797,85 @@ class PeerRowExchange:
         self.dist = dist
         base = group if group is not None else dist.group.WORLD
         self.group = dist.new_group(ranks=dist.get_process_group_ranks(base))
-        W, dev = table.world, table.device
-        entries = max(int(n_tokens_max) * table.n_heads, 1)
-        self.max_rows = max((W - 1) * entries, 1)  # rows one owner may serve per batch
-        self.stride = table.stride
-        self.ids, self.id_ptrs, self.rows, self.row_handles, self._keep = [], [], [], [], []
+        self._setup(table, n_tokens_max, sets)
+        W, dev = self.world, table.device
+        self.row_handles, self._keep = [], []
         for _ in range(sets):
-            ids = symm.empty(entries, dtype=torch.int32, device=dev)
+            ids = symm.empty(W * self.region, dtype=torch.int32, device=dev)
             hi = symm.rendezvous(ids, self.group)
-            rows = symm.empty(self.max_rows * self.stride, dtype=torch.uint8, device=dev)
+            cnts = symm.empty(max(W, 2), dtype=torch.int64, device=dev)
+            hc = symm.rendezvous(cnts, self.group)
+            rows = symm.empty(W * self.region * self.stride, dtype=torch.uint8, device=dev)
             hr = symm.rendezvous(rows, self.group)
             self.ids.append(ids)
-            self.id_ptrs.append(torch.tensor(list(hi.buffer_ptrs), dtype=torch.int64, device=dev))
+            self.cnts.append(cnts)
             self.rows.append(rows)
+            self.id_ptrs.append(torch.tensor(list(hi.buffer_ptrs), dtype=torch.int64, device=dev))
+            self.cnt_ptrs.append(torch.tensor(list(hc.buffer_ptrs), dtype=torch.int64, device=dev))
             self.row_handles.append(hr)
-            self._keep.append(hi)
+            self._keep += [hi, hc]
         self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
         self._views = {}
 
-    def alloc_ids(self, b: int, entries: int) -> torch.Tensor:
-        return self.ids[b][:entries]
-
-    def _view(self, b: int, o: int) -> torch.Tensor:
+    def _send_rows(self, b: int, o: int) -> torch.Tensor:
         """Owner o's send buffer of set b, mapped into this process (cached)."""
         key = (b, o)
         if key not in self._views:
-            self._views[key] = self.row_handles[b].get_buffer(o, (self.max_rows * self.stride,), torch.uint8)
+            self._views[key] = self.row_handles[b].get_buffer(o, (self.rows[b].numel(),), torch.uint8)
         return self._views[key]
 
-    def gather_counts(self, table, counts: torch.Tensor) -> torch.Tensor:
-        W = table.world
-        out = torch.empty(W * W, dtype=torch.int64, device=counts.device)
-        self.dist.all_gather_into_tensor(out, counts.contiguous(), group=self.group)
-        return out
-
-    def serve(self, table, b: int, counts_all: torch.Tensor) -> None:
-        """This owner's gather for set b, on the current stream."""
-        st = L.load().engram_shard_serve(table.shard.data_ptr(), table.stride, table.n_local, table.world, table.rank,
-                                         self.id_ptrs[b].data_ptr(), counts_all.data_ptr(), self.rows[b].data_ptr(),
-                                         self.max_rows, L.stream_of(table.device))
-        L.check(st, "engram_shard_serve")
-
     def barrier(self) -> None:
-        """A 4-byte all-reduce: once it completes, every owner's gather before it is done."""
+        """A 4-byte all-reduce on the current stream: once it completes, the
+        work every rank queued before it is done."""
         self.dist.all_reduce(self.flag, group=self.group)
 
-    def fetch(self, table, b: int, m: torch.Tensor) -> torch.Tensor:
-        """This rank's rows of batch set b, in send order (owner after owner)."""
-        W, me, stride = table.world, table.rank, self.stride
-        mm = m.tolist()
-        total = sum(mm[me])
-        out = torch.empty(max(total, 1) * stride, dtype=torch.uint8, device=table.device)
-        off = 0
-        for o in range(W):
-            cnt = mm[me][o]
-            if o == me or cnt == 0:
-                continue
-            base = sum(mm[r][o] for r in range(me) if r != o)  # this rank's first row in owner o's send buffer
-            if base + cnt > self.max_rows:
-                raise RuntimeError(f"owner {o} holds {base + cnt} rows for this batch, its send buffer {self.max_rows}")
-            src = self._view(b, o)
-            out[off * stride:(off + cnt) * stride].copy_(src[base * stride:(base + cnt) * stride], non_blocking=True)
-            off += cnt
-        return out[: total * stride]
+
+class LocalPeerRowExchange(_PushExchange):
+    """The pushing exchange among W ranks emulated in one process on one GPU
+    (tests): one object per emulated rank, made by `LocalPeerRowExchange.
+    for_shards`, buffers in plain device memory.  The emulated ranks' calls
+    must interleave as real ranks' would: every rank's prefetch of a step
+    before any rank's next prefetch.  Each owner's gather records an event,
+    and a fetch waits for the gathers of every owner (the barrier's part)."""
+
+    def __init__(self, table: "ShardedTable", n_tokens_max: int, sets: int = 4):
+        self._setup(table, n_tokens_max, sets)
+        W, dev = self.world, table.device
+        for _ in range(sets):
+            self.ids.append(torch.empty(W * self.region, dtype=torch.int32, device=dev))
+            self.cnts.append(torch.zeros(max(W, 2), dtype=torch.int64, device=dev))
+            self.rows.append(torch.empty(W * self.region * self.stride, dtype=torch.uint8, device=dev))
+        self.served = [None] * sets
+        self.peers = None
+
+    @classmethod
+    def for_shards(cls, shards, n_tokens_max: int, sets: int = 4) -> list:
+        exs = [cls(sh, n_tokens_max, sets) for sh in shards]
+        for x in exs:
+            x.peers = exs
+            for b in range(sets):
+                x.id_ptrs.append(torch.tensor([p.ids[b].data_ptr() for p in exs], dtype=torch.int64,
+                                              device=shards[0].device))
+                x.cnt_ptrs.append(torch.tensor([p.cnts[b].data_ptr() for p in exs], dtype=torch.int64,
+                                               device=shards[0].device))
+        return exs
+
+    def serve(self, table, b: int) -> None:
+        super().serve(table, b)
+        self.served[b] = torch.cuda.Event()
+        self.served[b].record(torch.cuda.current_stream(table.device))
+
+    def barrier(self) -> None:
+        pass
+
+    def _before_fetch(self, b: int) -> None:
+        cur = torch.cuda.current_stream(self.rows[b].device)
+        for p in self.peers:
+            if p is not self and p.served[b] is not None:
+                cur.wait_event(p.served[b])
+
+    def _send_rows(self, b: int, o: int) -> torch.Tensor:
+        return self.peers[o].rows[b]
 
 
 class LocalRowExchange:

@@ -331,22 +331,40 @@ ENGRAM_API int engram_forward_exchanged(const engram_table* t, const engram_over
                                         int64_t* hit_count, void* stream);
 
 /*
- * Owner side of the peer-memory exchange of engram_shard_plan's requests:
- * counts_all (device int64 [world * world], entry r*world + o = M[r][o], the
- * rows rank r requests from owner o: every rank's plan counts, gathered) and
- * id_ptrs (device array [world] of pointers valid here, e.g. symmetric memory:
- * each rank's send_ids) say what every other rank r wants from this rank:
- * its ids at [sum_{o < rank} M[r][o], + M[r][rank]) of r's send_ids.  Their
- * rows, read from this rank's shard (row g at local row g / world), go to
- * send_rows, requester after requester: r's at rows [sum_{r' < r, r' != rank}
- * M[r'][rank], + M[r][rank]), row_stride bytes each, so requester r can copy
- * its block as one transfer.  Rows at or past max_rows are not written.  The
- * caller orders it after every rank's plan and before any rank's copy.  No
- * reference counterpart.
+ * The peer-memory exchange with pushed requests (the row-sharded step's
+ * default).  Every owner holds, per batch set, a request buffer int32
+ * [world][region], a count array int64 [world] and a send buffer of
+ * [world][region] rows, all mapped into every rank (e.g. torch symmetric
+ * memory); region >= n * n_heads, world * region <= 2^31 - 1.
+ *
+ * engram_shard_route_push (requester): every (position, head) pair of
+ * positions t0..t0+n-1 that another rank owns and the overlay ov (nullable)
+ * does not serve sends its id to its owner o: stored in region `rank` of o's
+ * request buffer (id_ptrs: device array [world] of pointers valid here, o's
+ * request buffer), and the total per owner in entry `rank` of o's count
+ * array (count_ptrs, likewise).  counts: device int64 [world], this rank's
+ * requests per owner (0 for itself).  row_index [n * n_heads]: the pair's row
+ * in the receive buffer, whose blocks follow in ascending owner order (block
+ * o = the rows asked of o, counts[o] of them), or -1 for a pair not
+ * requested.  The order inside a block is free.  A hashed pair, an owner
+ * computation and one store per request: no hash set, no collective.
+ *
+ * engram_shard_serve_pushed (owner): the rows requester r asked for (ids
+ * [0, req_counts[r]) of region r of req_ids, this owner's request buffer) are
+ * read from this rank's shard (row g at local row g / world) into region r of
+ * send_rows, in the same order, row_stride bytes each; requester r then copies
+ * req_counts[r] rows from the start of its region as one transfer.  Ids that
+ * are not this rank's give zero rows.  The caller orders every rank's route
+ * before any owner's serve, and every owner's serve before any requester's
+ * copy (a barrier).  No reference counterpart: the reference is single-process.
  */
-ENGRAM_API int engram_shard_serve(const void* shard_rows, int64_t stride, int64_t n_local, int32_t world, int32_t rank,
-                                  const void* id_ptrs, const int64_t* counts_all, void* send_rows, int64_t max_rows,
-                                  void* stream);
+ENGRAM_API int engram_shard_route_push(const engram_table* t, const engram_overlay* ov, const int32_t* tokens,
+                                       const int32_t* seg_start, int64_t t0, int64_t n, int32_t world, int32_t rank,
+                                       const void* id_ptrs, const void* count_ptrs, int64_t region, int64_t* counts,
+                                       int32_t* row_index, void* stream);
+ENGRAM_API int engram_shard_serve_pushed(const void* shard_rows, int64_t stride, int64_t n_local, int32_t world,
+                                         int32_t rank, const int32_t* req_ids, const int64_t* req_counts,
+                                         int64_t region, void* send_rows, void* stream);
 
 /*
  * Owner side: out[k] = the resident row of global id ids[k] from this rank's

@@ -598,6 +598,165 @@ def test_exchange_staged_forward_matches_resident_table(eb, world, fmt, dim, mod
         assert np.array_equal(got[0], want[3][0]) and got[2] == want[3][2], r
 
 
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_pushed_route_and_serve_match_their_contract(eb, world):
+    """W requesters emulated on one GPU, each with its own batch (t0 > 0,
+    segments, an overlay): engram_shard_route_push stores every remote,
+    non-overlay (position, head) id in region `requester` of its owner's
+    request buffer and the count in the owner's count array, leaves every
+    other entry alone, and gives each pair a distinct row in the receive
+    layout (owner blocks in ascending order) whose id is the pair's; then
+    engram_shard_serve_pushed on every owner writes exactly those rows of the
+    resident table into the requester's region of the send buffer."""
+    rng = np.random.default_rng(17 * world)
+    n_rows = 40_009
+    spec = random_spec(O.FMT_IQ4_XS, 256, n_rows, 7 + world)
+    full = device_table(eb, spec)
+    lib = eb._lib.load()
+    T, t0 = 1800, 133
+    n = T - t0
+    entries = n * 16
+    region = entries + 5
+    stride = full.row_stride
+    req_ids = [torch.full((world * region,), -7, dtype=torch.int32, device=DEV) for _ in range(world)]
+    req_cnt = [torch.full((world,), -1, dtype=torch.int64, device=DEV) for _ in range(world)]
+    id_ptrs = torch.tensor([x.data_ptr() for x in req_ids], dtype=torch.int64, device=DEV)
+    cnt_ptrs = torch.tensor([x.data_ptr() for x in req_cnt], dtype=torch.int64, device=DEV)
+    want_ids, got_counts, got_rix = [], [], []
+    ov_ids = np.unique(rng.integers(0, n_rows, size=400)).astype(np.int32)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    ov = eb._lib.EngramOverlay(None, omap.R, omap.keys.data_ptr(), omap.slots.data_ptr(), omap.capacity)
+    for r in range(world):
+        toks = zipf_tokens(rng, T)
+        ss = FX.seg_starts(np.sort(rng.integers(0, 5, size=T)))
+        ids = spec.ids(toks, seg_start=ss, t0=t0).reshape(-1).astype(np.int64)
+        want_ids.append(ids)
+        toks_d, ss_d = torch.from_numpy(toks).to(DEV), torch.from_numpy(ss).to(DEV)
+        counts = torch.full((world,), -3, dtype=torch.int64, device=DEV)
+        rix = torch.full((entries,), -9, dtype=torch.int32, device=DEV)
+        assert lib.engram_shard_route_push(C.byref(full.ctable), C.byref(ov), toks_d.data_ptr(), ss_d.data_ptr(),
+                                           t0, n, world, r, id_ptrs.data_ptr(), cnt_ptrs.data_ptr(), entries - 1,
+                                           counts.data_ptr(), rix.data_ptr(),
+                                           eb._lib.stream_of(DEV)) == eb._lib.ERR_RANGE
+        st = lib.engram_shard_route_push(C.byref(full.ctable), C.byref(ov), toks_d.data_ptr(), ss_d.data_ptr(), t0, n,
+                                         world, r, id_ptrs.data_ptr(), cnt_ptrs.data_ptr(), region, counts.data_ptr(),
+                                         rix.data_ptr(), eb._lib.stream_of(DEV))
+        eb._lib.check(st, "engram_shard_route_push")
+        got_counts.append(counts)
+        got_rix.append(rix)
+    torch.cuda.synchronize()
+    ids_h = [x.cpu().numpy().reshape(world, region) for x in req_ids]
+    cnt_h = [x.cpu().numpy() for x in req_cnt]
+    for r in range(world):
+        ids = want_ids[r]
+        req = (ids % world != r) & ~np.isin(ids, ov_ids)
+        want_counts = np.bincount(ids[req] % world, minlength=world)
+        counts = got_counts[r].cpu().numpy()
+        assert np.array_equal(counts, want_counts) and counts[r] == 0
+        base = np.concatenate([[0], np.cumsum(counts)])
+        rix = got_rix[r].cpu().numpy()
+        assert np.array_equal(rix >= 0, req)
+        assert np.array_equal(np.sort(rix[req]), np.arange(int(req.sum())))  # each receive row exactly once
+        owner = ids % world
+        for o in range(world):
+            if o == r:
+                assert (ids_h[o][r] == -7).all() and cnt_h[o][r] == -1  # nothing stored for itself
+                continue
+            c = int(counts[o])
+            assert cnt_h[o][r] == c
+            blk = ids_h[o][r]
+            assert (blk[c:] == -7).all()
+            sel = req & (owner == o)
+            assert np.array_equal(blk[rix[sel] - base[o]], ids[sel])  # the pair's row holds its id
+    # every owner serves its requesters' regions from its shard
+    rows = full.rows.cpu().numpy().reshape(full.n_rows, stride)
+    for o in range(world):
+        shard = full.rows.view(full.n_rows, stride)[o::world].contiguous()
+        send = torch.full((world * region * stride,), 0xCD, dtype=torch.uint8, device=DEV)
+        st = lib.engram_shard_serve_pushed(shard.data_ptr(), stride, shard.shape[0], world, o, req_ids[o].data_ptr(),
+                                           req_cnt[o].data_ptr(), region, send.data_ptr(), eb._lib.stream_of(DEV))
+        eb._lib.check(st, "engram_shard_serve_pushed")
+        torch.cuda.synchronize()
+        got = send.cpu().numpy().reshape(world, region, stride)
+        for r in range(world):
+            c = 0 if r == o else int(cnt_h[o][r])
+            assert np.array_equal(got[r, :c], rows[ids_h[o][r][:c].astype(np.int64)]), (o, r)
+            assert (got[r, c:] == 0xCD).all()
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("fmt,dim,mode", [(O.FMT_IQ4_XS, 256, O.MODE_PAIRSUM_ADD_BF16),
+                                          (O.FMT_IQ4_NL, 160, O.MODE_CONCAT_F32)])
+def test_pushed_exchange_staged_forward_matches_resident_table(eb, world, fmt, dim, mode):
+    """W ranks emulated on one GPU with the pushing exchange
+    (LocalPeerRowExchange), their calls interleaved as real ranks' are: six
+    batches per rank prefetched three ahead, the first five forwarded (the
+    fifth still waiting for its fetch, done on the spot); every forward's
+    output, slots and hit count are bit-identical to the forward over the whole
+    resident table.  (A batch forwarded before its owners served it needs the
+    other ranks inside the same call: the two-rank test covers it.)"""
+    from engraft_ngram_b200.shard import LocalPeerRowExchange, ShardedTable
+    rng = np.random.default_rng(43 * world + dim)
+    n_rows = 25_013
+    spec = random_spec(fmt, dim, n_rows, 17 + world)
+    full = device_table(eb, spec)
+    shards = [ShardedTable.from_full(full, world, r) for r in range(world)]
+    T, K, depth = 900, 6, 3
+    exs = LocalPeerRowExchange.for_shards(shards, T)
+    for sh, ex in zip(shards, exs):
+        sh.enable_exchange_staging(T, ex)
+    batches = []
+    for r in range(world):
+        bs = []
+        for _ in range(K):
+            toks = zipf_tokens(rng, T)
+            ss = FX.seg_starts(np.sort(rng.integers(0, 4, size=T)))
+            bs.append((torch.from_numpy(toks).to(DEV), torch.from_numpy(ss).to(DEV)))
+        batches.append(bs)
+    read = np.unique(np.concatenate([spec.ids(b[0].cpu().numpy()).reshape(-1) for bs in batches for b in bs]))
+    ov_ids = np.unique(np.concatenate([read[::5], rng.integers(0, n_rows, size=60)])).astype(np.int32)
+    omap = eb.OverlayMap(torch.from_numpy(ov_ids), DEV)
+    rows_var = torch.from_numpy((rng.standard_normal((len(ov_ids), dim)) * 0.01).astype(np.float32)).to(DEV)
+    res0 = O.bf16_bits((rng.standard_normal((T, 8 * dim)) * 0.5).astype(np.float32))
+
+    def fresh():
+        if mode == O.MODE_CONCAT_F32:
+            return torch.empty(T, 16, dim, device=DEV)
+        return torch.from_numpy(res0.view(np.int16).copy()).to(DEV).view(torch.bfloat16)
+
+    def resident(b):
+        out, slots = fresh(), torch.empty(T, 16, dtype=torch.int32, device=DEV)
+        hits = torch.zeros(1, dtype=torch.int64, device=DEV)
+        ov = omap.descriptor(rows_var)
+        st = eb._lib.load().engram_forward(C.byref(full.ctable), C.byref(ov), b[0].data_ptr(), b[1].data_ptr(), 0, T,
+                                           mode, out.data_ptr(), None, slots.data_ptr(), hits.data_ptr(),
+                                           eb._lib.stream_of(DEV))
+        eb._lib.check(st, "engram_forward")
+        return out, slots, hits
+
+    want = [[resident(b) for b in bs] for bs in batches]
+    got = [[None] * K for _ in range(world)]
+    for k in range(depth):
+        for r in range(world):
+            shards[r].prefetch(*batches[r][k], omap=omap)
+    for k in range(K - 1):
+        for r in range(world):  # every rank's prefetch of this step, then every rank's forward
+            if k + depth < K:
+                shards[r].prefetch(*batches[r][k + depth], omap=omap)
+        for r in range(world):
+            out, slots = fresh(), torch.empty(T, 16, dtype=torch.int32, device=DEV)
+            hits = torch.zeros(1, dtype=torch.int64, device=DEV)
+            shards[r].forward(batches[r][k][0], batches[r][k][1], omap, rows_var, out, mode, slots_out=slots,
+                              hit_count=hits)
+            got[r][k] = (out, slots, hits)
+    torch.cuda.synchronize()
+    for r in range(world):
+        for k in range(K - 1):
+            g, w = got[r][k], want[r][k]
+            assert torch.equal(g[0].view(torch.int16), w[0].view(torch.int16)), (r, k)
+            assert torch.equal(g[1], w[1]) and int(g[2].item()) == int(w[2].item()), (r, k)
+
+
 @pytest.mark.parametrize("world,rank", [(2, 1), (3, 0), (8, 5)])
 def test_stage_copies_exactly_the_rows_of_other_ranks(eb, world, rank):
     """engram_stage_sharded over t0 > 0: head h of output row i holds the

@@ -262,9 +262,11 @@ def test_autograd_through_peer_rows_matches_allreduce_on_two_ranks():
 
 def _exchange_staging(rank: int, world: int, port: int, out) -> None:
     """Each rank: its shard in plain local memory and exchange staging (the
-    default peer exchange: owners gather into symmetric memory, requesters copy
-    with the copy engines); four batches with the prefetch two ahead, each
-    forward equal bit for bit to the resident-table forward of the same batch."""
+    default peer exchange: requests pushed into the owners' symmetric memory,
+    owners gather locally, requesters copy with the copy engines; then the
+    NCCL all-to-all exchange); four batches, the last two forwarded with
+    stages still to run, each forward equal bit for bit to the resident-table
+    forward of the same batch."""
     import ctypes as C
     import torch.distributed as dist
     from datetime import timedelta
@@ -331,8 +333,8 @@ def _exchange_staging(rank: int, world: int, port: int, out) -> None:
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_exchange_staging_matches_resident_table_on_two_ranks():
-    """Two ranks, table row-sharded in local memory: the deduplicated exchange,
-    planned two batches ahead, over peer memory with copy-engine transfers and
-    over NCCL all-to-alls, feeds forwards bit-identical to the resident-table
-    forward."""
+    """Two ranks, table row-sharded in local memory: the exchange staged ahead
+    of the forward, over peer memory (pushed requests, copy-engine transfers)
+    and over NCCL all-to-alls, feeds forwards bit-identical to the
+    resident-table forward."""
     assert _run_ranks(_exchange_staging) == {0: True, 1: True}

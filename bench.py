@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=DEFAULT_STEPS)
     ap.add_argument("--warmup", type=int, default=DEFAULT_WARMUP)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS) + ["scan", "ple"])
+    ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS) + ["scan", "ple", "micro"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1027,6 +1027,201 @@ def run_ple(args, device):
     print(json.dumps(line), flush=True)
 
 
+def run_micro(args, device):
+    """The kernels off the config-5 step, each on a workload of its own at the
+    headline table's size, timed with CUDA events over K launches after three
+    warm-up launches: achieved GB/s = the bytes the call must move (stated per
+    kernel) / its mean time, against the measured copy peak.  One JSON line.
+    Also the command the per-kernel ncu summaries are captured from."""
+    import ctypes as C
+    import torch
+    import engraft_ngram_b200 as eb
+    from engraft_ngram_b200 import _lib as L
+    from engraft_ngram_b200.table import synthetic_head_sizes, synthetic_multipliers
+    lib = L.load()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    peak, peak_kind = measured_peak_gbs()
+    K = max(1, min(args.steps, 50))
+    g = torch.Generator(device=device)
+    g.manual_seed(args.seed)
+    cdf = zipf_cdf(torch, device)
+    sizes = synthetic_head_sizes(FULL_ROWS)
+    offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
+    mult = synthetic_multipliers(args.seed)
+    fmt, dim = L.FMT_IQ4_XS, 256
+    addr = eb.DeviceTable(torch.zeros(64, dtype=torch.uint8, device=device), fmt, dim, sizes, offs, mult, EOS,
+                          n_rows=FULL_ROWS, hash_only=True)
+    stride = addr.row_stride
+    out = {}
+
+    def timed(name, fn, nbytes, note):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / K
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": ms, "bytes": int(nbytes), "gbs": gbs, "frac": gbs / peak, "bytes_are": note}
+
+    # engram_hash: 16 M positions of a Zipf stream, 16 heads each
+    T = 1 << 24
+    toks = zipf_tokens(torch, T, g, cdf)
+    ids = torch.empty(T * 16, dtype=torch.int32, device=device)
+    timed("engram_hash (k_hash)", lambda: L.check(lib.engram_hash(C.byref(addr.ctable), toks.data_ptr(), None, 0, T,
+                                                                  ids.data_ptr(), stream), "engram_hash"),
+          T * (4 + 64), "4 B token in + 16 x 4 B ids out per position")
+    del ids
+    # row sets over the 320 M-row table: a 40 MB bitmap (it fits in L2, as in the descent's own use)
+    words = int(lib.engram_rowset_words(FULL_ROWS))
+    bm_a = torch.zeros(words, dtype=torch.int32, device=device)
+    bm_b = torch.zeros(words, dtype=torch.int32, device=device)
+    bm_c = torch.empty(words, dtype=torch.int32, device=device)
+    n_mark = 1 << 20
+    timed("engram_rowset_mark (k_mark_positions)",
+          lambda: L.check(lib.engram_rowset_mark(C.byref(addr.ctable), toks.data_ptr(), T, None, None, n_mark,
+                                                 bm_a.data_ptr(), stream), "engram_rowset_mark"),
+          n_mark * (4 + 16 * 4), "4 B token in + one 4 B bitmap word per head, per position")
+    some = torch.randint(0, FULL_ROWS, (1 << 22,), generator=g, device=device, dtype=torch.int32)
+    timed("engram_rowset_mark_ids (k_mark_ids)",
+          lambda: L.check(lib.engram_rowset_mark_ids(some.data_ptr(), some.numel(), FULL_ROWS, bm_b.data_ptr(),
+                                                     stream), "engram_rowset_mark_ids"),
+          some.numel() * 8, "4 B id in + one 4 B bitmap word per id")
+    timed("engram_rowset_combine (k_combine, union)",
+          lambda: L.check(lib.engram_rowset_combine(bm_a.data_ptr(), bm_b.data_ptr(), words, 0, bm_c.data_ptr(),
+                                                    stream), "engram_rowset_combine"),
+          3 * words * 4, "two bitmaps read, one written")
+    wsb = int(lib.engram_rowset_workspace_bytes(words))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=device)
+    cnt = torch.zeros(1, dtype=torch.int64, device=device)
+    lib.engram_rowset_extract(bm_c.data_ptr(), words, None, 0, cnt.data_ptr(), ws.data_ptr(), wsb, stream)
+    torch.cuda.synchronize()
+    members = int(cnt.item())
+    mem_ids = torch.empty(members, dtype=torch.int32, device=device)
+    timed("engram_rowset_extract (k_tile_*)",
+          lambda: L.check(lib.engram_rowset_extract(bm_c.data_ptr(), words, mem_ids.data_ptr(), members,
+                                                    cnt.data_ptr(), ws.data_ptr(), wsb, stream),
+                          "engram_rowset_extract"),
+          words * 4 + members * 4, "bitmap read + member ids written")
+    ix = torch.empty(some.numel(), dtype=torch.int32, device=device)
+    timed("engram_rowset_index (k_index)",
+          lambda: L.check(lib.engram_rowset_index(bm_c.data_ptr(), words, ws.data_ptr(), wsb, some.data_ptr(),
+                                                  some.numel(), ix.data_ptr(), stream), "engram_rowset_index"),
+          some.numel() * (4 + 4 + 4 + 4), "per id: id in, bitmap word, prefix word, index out")
+    del bm_a, bm_b, bm_c, ws, mem_ids, ix
+    # engram_overlay_accumulate: one .pleo file of 400 k rows x 160 into a 1 M-row union, distinct and repeated rows
+    n_ov, dim_ov, n_union = 400_000, 160, 1_000_000
+    acc = torch.zeros(n_union, dim_ov, device=device)
+    data = torch.randn(n_ov, dim_ov, generator=g, device=device)
+    base = torch.randn(n_ov, dim_ov, generator=g, device=device)
+    tgt = torch.randperm(n_union, generator=g, device=device)[:n_ov].to(torch.int32)
+    timed("engram_overlay_accumulate (k_overlay_accumulate, distinct rows)",
+          lambda: L.check(lib.engram_overlay_accumulate(acc.data_ptr(), tgt.data_ptr(), None, data.data_ptr(),
+                                                        base.data_ptr(), n_ov, dim_ov, stream),
+                          "engram_overlay_accumulate"),
+          n_ov * dim_ov * 4 * 4 + n_ov * 4, "data, base and the target row read, target written (fp32)")
+    tgt_rep = torch.randint(0, n_ov // 4, (n_ov,), generator=g, device=device, dtype=torch.int32)
+    order = torch.sort(tgt_rep.long(), stable=True).indices
+    timed("engram_overlay_accumulate (k_overlay_accumulate_runs, 4 rows per target)",
+          lambda: L.check(lib.engram_overlay_accumulate(acc.data_ptr(), tgt_rep.data_ptr(), order.data_ptr(),
+                                                        data.data_ptr(), base.data_ptr(), n_ov, dim_ov, stream),
+                          "engram_overlay_accumulate"),
+          n_ov * dim_ov * 4 * 2 + (n_ov // 4) * dim_ov * 4 * 2 + n_ov * 12,
+          "data and base read, each distinct target read and written once, index and order read")
+    del acc, data, base, tgt, tgt_rep, order
+    # the row-sharded exchange at W = 4 (emulated on this GPU): config 5's batch of 131,072 positions
+    W, me = 4, 1
+    n5 = 64 * 2048
+    region = n5 * 16
+    tok5 = toks[:n5].contiguous()
+    req_ids = [torch.empty(W * region, dtype=torch.int32, device=device) for _ in range(W)]
+    req_cnt = [torch.zeros(W, dtype=torch.int64, device=device) for _ in range(W)]
+    id_ptrs = torch.tensor([x.data_ptr() for x in req_ids], dtype=torch.int64, device=device)
+    cnt_ptrs = torch.tensor([x.data_ptr() for x in req_cnt], dtype=torch.int64, device=device)
+    counts = torch.zeros(W, dtype=torch.int64, device=device)
+    rix = torch.empty(region, dtype=torch.int32, device=device)
+    no_ov = L.EngramOverlay(None, 0, None, None, 0)
+    timed("engram_shard_route_push (k_route_push + k_route_finish)",
+          lambda: L.check(lib.engram_shard_route_push(C.byref(addr.ctable), C.byref(no_ov), tok5.data_ptr(), None, 0,
+                                                      n5, W, me, id_ptrs.data_ptr(), cnt_ptrs.data_ptr(), region,
+                                                      counts.data_ptr(), rix.data_ptr(), stream),
+                          "engram_shard_route_push"),
+          n5 * 4 + region * 4 * 2 + int(region * (W - 1) / W) * 4,
+          "tokens in, row_index written then rewritten, one 4 B id per remote pair")
+    n_local = (FULL_ROWS + W - 1) // W
+    # one buffer of a W=2 shard's rows (23 GB): a W=4 owner's shard below, every owner's shard of the W=2 stage;
+    # its contents do not change the timing
+    shard = torch.empty(((FULL_ROWS + 1) // 2) * stride, dtype=torch.uint8, device=device)
+    owner = (me + 1) % W
+    for r in range(W):  # every other requester's ids of this batch for `owner`
+        if r != owner:
+            L.check(lib.engram_shard_route_push(C.byref(addr.ctable), C.byref(no_ov), tok5.data_ptr(), None, 0, n5,
+                                                W, r, id_ptrs.data_ptr(), cnt_ptrs.data_ptr(), region,
+                                                counts.data_ptr(), rix.data_ptr(), stream), "engram_shard_route_push")
+    torch.cuda.synchronize()
+    served = int(req_cnt[owner].sum().item()) - int(req_cnt[owner][owner].item())
+    send = torch.empty(W * region * stride, dtype=torch.uint8, device=device)
+    timed("engram_shard_serve_pushed (k_serve_pushed)",
+          lambda: L.check(lib.engram_shard_serve_pushed(shard.data_ptr(), stride, n_local, W, owner,
+                                                        req_ids[owner].data_ptr(), req_cnt[owner].data_ptr(), region,
+                                                        send.data_ptr(), stream), "engram_shard_serve_pushed"),
+          served * (4 + 2 * stride), "per served row: its id, the row read from the shard and written")
+    del send, req_ids, rix
+    # the legacy pulled stage at W = 2 (both owners' shards the same buffer, local rows g / 2 < its rows): rows of
+    # the other rank copied in
+    W2 = 2
+    n_stage = 1 << 14
+    shard_ptrs = torch.tensor([shard.data_ptr()] * W2, dtype=torch.int64, device=device)
+    sb = int(lib.engram_stage_bytes(C.byref(addr.ctable), n_stage))
+    stage = torch.empty(sb, dtype=torch.uint8, device=device)
+    hid = torch.empty(n_stage * 16, dtype=torch.int32, device=device)
+    L.check(lib.engram_hash(C.byref(addr.ctable), toks.data_ptr(), None, 0, n_stage, hid.data_ptr(), stream), "hash")
+    torch.cuda.synchronize()
+    remote = int(((hid.long() % W2) != 0).sum().item())
+    timed("engram_stage_sharded (k_stage_sharded, W=2)",
+          lambda: L.check(lib.engram_stage_sharded(C.byref(addr.ctable), C.byref(no_ov), toks.data_ptr(), None, 0,
+                                                   n_stage, shard_ptrs.data_ptr(), W2, 0, stage.data_ptr(), 0, stream),
+                          "engram_stage_sharded"),
+          n_stage * 4 + remote * 2 * stride, "tokens in, each remote row read and written")
+    del shard, stage, hid
+    # PLE block backward at the reference's width: 2048 positions, hc = 4, n_embd = 2560
+    hc, n, Kc, dil, Tp = 4, 2560, 4, 3, 2048
+    r_ = lambda *sh: torch.randn(*sh, generator=g, device=device) * 0.1  # noqa: E731
+    kvs = hc * n + n
+    kv, hidden, dout, dnormed = r_(Tp, kvs), r_(Tp, hc, n), r_(Tp, hc, n), r_(Tp, hc, n)
+    nk, nq, nc, conv_w = 1 + r_(hc * n), 1 + r_(hc * n), 1 + r_(hc * n), r_(hc * n, Kc)
+    gate, s_ = torch.rand(Tp, hc, generator=g, device=device), r_(Tp, hc)
+    normed, hist = r_(Tp, hc, n), r_((Kc - 1) * dil, hc, n)
+    dkv, dhidden = torch.empty(Tp, kvs, device=device), torch.empty(Tp, hc, n, device=device)
+    dconv, dnorm_out = torch.empty(Tp, hc, n, device=device), torch.empty(Tp, hc, n, device=device)
+    Cb = Tp * hc * n * 4
+    timed("engram_ple_gate_backward (k_ple_gate_bwd)",
+          lambda: L.check(lib.engram_ple_gate_backward(
+              kv.data_ptr(), kvs, kv[:, hc * n:].data_ptr(), kvs, hidden.data_ptr(), nk.data_ptr(), nq.data_ptr(),
+              nc.data_ptr(), gate.data_ptr(), s_.data_ptr(), dout.data_ptr(), dnormed.data_ptr(), Tp, hc, n, 1e-6, 0, 0,
+              dkv.data_ptr(), kvs, dkv[:, hc * n:].data_ptr(), kvs, dhidden.data_ptr(), stream),
+              "engram_ple_gate_backward"),
+          4 * Cb + Tp * n * 4 + 2 * Cb + Tp * n * 4,
+          "key, hidden, dout, dnormed and value read; dkey, dhidden and dvalue written")
+    timed("engram_ple_conv_backward (k_ple_dconv + k_ple_dx)",
+          lambda: L.check(lib.engram_ple_conv_backward(
+              normed.data_ptr(), hist.data_ptr(), hist.shape[0], conv_w.data_ptr(), Kc, dil, Tp, hc, n,
+              dout.data_ptr(), None, 0, dconv.data_ptr(), dnorm_out.data_ptr(), None, stream),
+              "engram_ple_conv_backward"),
+          3 * Cb, "normed and dout read, dnormed written (the silu'-scaled gradient is a scratch pass)")
+    line = {"metric": "per-kernel HBM GB/s of the kernels off the config-5 step",
+            "unit": "GB/s", "peak_gbs": peak, "peak_source": peak_kind, "launches_timed": K, "kernels": out,
+            "config": {"workload": "micro: engram_hash over 16 M positions; row sets over the 320 M-row table; "
+                                   "a 400 k x 160 .pleo accumulation; the pushed exchange at W=4 and the pulled "
+                                   "stage at W=2 emulated on one GPU with config 5's batch; the PLE backward at "
+                                   "2048 x hc 4 x 2560"}}
+    print(json.dumps(line), flush=True)
+
+
 def shard_text(cfg):
     if not cfg.get("shard"):
         return ""
@@ -1063,9 +1258,9 @@ START = time.perf_counter()
 
 def main():
     args = parse()
-    if args.config in ("scan", "ple"):
+    if args.config in ("scan", "ple", "micro"):
         import torch
-        run = run_scan if args.config == "scan" else run_ple
+        run = {"scan": run_scan, "ple": run_ple, "micro": run_micro}[args.config]
         run(args, torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
         return
     cfg = dict(CONFIGS[args.config])

@@ -121,8 +121,8 @@ SIGNATURES = {
                                         C.c_int64, C.c_void_p]),
     "engram_rowset_index": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                                       C.c_void_p, C.c_void_p]),
-    "engram_overlay_accumulate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
-                                            C.c_void_p]),
+    "engram_overlay_accumulate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
+                                            C.c_int32, C.c_void_p]),
     "engram_backward_to_owners": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                             C.c_int32, C.c_int64, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                             C.c_int64, C.c_void_p]),

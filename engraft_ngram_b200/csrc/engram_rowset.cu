@@ -224,6 +224,31 @@ __global__ void k_overlay_accumulate(float* __restrict__ acc, const int32_t* __r
     }
 }
 
+// The same with repeated targets, in one launch: order lists the rows k sorted
+// by index[k], stable (ascending k among equal targets).  The thread of
+// (j, c) with j the first of a run of equal targets adds the run's rows to
+// column c one after another, in file order, as np.add.at applies them.
+__global__ void k_overlay_accumulate_runs(float* __restrict__ acc, const int32_t* __restrict__ index,
+                                          const int64_t* __restrict__ order, const float* __restrict__ data,
+                                          const float* __restrict__ base, int64_t n, int dim) {
+    const int64_t total = n * dim;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = e / dim;
+        const int c = (int)(e - j * dim);
+        const int32_t r = __ldg(index + __ldg(order + j));
+        if (r < 0 || (j > 0 && __ldg(index + __ldg(order + j - 1)) == r)) continue;
+        float* a = acc + (int64_t)r * dim + c;
+        float v = *a;
+        for (int64_t q = j; q < n; q++) {
+            const int64_t k = __ldg(order + q);
+            if (q > j && __ldg(index + k) != r) break;
+            v = __fadd_rn(v, __fsub_rn(__ldg(data + k * dim + c), __ldg(base + k * dim + c)));
+        }
+        *a = v;
+    }
+}
+
 int grid_for(int64_t work) {
     const int64_t want = (work + 255) / 256, cap = (int64_t)sm_count() * 8;
     return (int)(want < 1 ? 1 : (want < cap ? want : cap));
@@ -304,12 +329,16 @@ extern "C" int engram_rowset_index(const uint32_t* bitmap, int64_t words, const 
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }
 
-extern "C" int engram_overlay_accumulate(float* acc, const int32_t* index, const float* data, const float* base,
-                                         int64_t n, int32_t dim, void* stream) {
+extern "C" int engram_overlay_accumulate(float* acc, const int32_t* index, const int64_t* order, const float* data,
+                                         const float* base, int64_t n, int32_t dim, void* stream) {
     if (n < 0 || dim <= 0) return ENGRAM_ERR_ARG;
     if (n == 0) return ENGRAM_OK;
     if (!acc || !index || !data || !base) return ENGRAM_ERR_ARG;
-    k_overlay_accumulate<<<grid_for(n * dim), 256, 0, (cudaStream_t)stream>>>(acc, index, data, base, n, dim);
+    if (order)
+        k_overlay_accumulate_runs<<<grid_for(n * dim), 256, 0, (cudaStream_t)stream>>>(acc, index, order, data, base,
+                                                                                       n, dim);
+    else
+        k_overlay_accumulate<<<grid_for(n * dim), 256, 0, (cudaStream_t)stream>>>(acc, index, data, base, n, dim);
     count_launches(1);
     return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
 }

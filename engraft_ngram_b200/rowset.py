@@ -223,25 +223,18 @@ def build_rows_var(table, sequences, policy: str, row_sets: dict, exclude_positi
 
 
 def _accumulate(acc: torch.Tensor, index: torch.Tensor, data: torch.Tensor, base: torch.Tensor) -> None:
-    """acc[index[k]] += data[k] - base[k], repeated indices in order (rounds)."""
-    lib = L.load()
-    dim = acc.shape[1]
-    idx = index.cpu().numpy().astype(np.int64)
-    # occurrence number of each row among equal indices, in file order
-    order = np.argsort(idx, kind="stable")
-    sorted_idx = idx[order]
-    first = np.r_[True, sorted_idx[1:] != sorted_idx[:-1]]
-    start = np.maximum.accumulate(np.where(first, np.arange(idx.size), 0))
-    occ = np.empty(idx.size, dtype=np.int64)
-    occ[order] = np.arange(idx.size) - start
-    for r in range(int(occ.max()) + 1 if idx.size else 0):
-        sel = torch.from_numpy(np.nonzero(occ == r)[0]).to(acc.device)
-        ix = index[sel].contiguous()
-        d = data[sel].contiguous()
-        b = base[sel].contiguous()
-        st = lib.engram_overlay_accumulate(acc.data_ptr(), ix.data_ptr(), d.data_ptr(), b.data_ptr(), ix.numel(),
-                                           dim, L.stream_of(acc.device))
-        L.check(st, "engram_overlay_accumulate")
+    """acc[index[k]] += data[k] - base[k], repeated indices in file order: a
+    stable device sort of the targets, then one launch that adds each run of
+    equal targets in order (engram_overlay_accumulate with `order`)."""
+    n = index.numel()
+    if n == 0:
+        return
+    ix = index.contiguous()
+    order = torch.sort(ix.long(), stable=True).indices.contiguous()
+    d, b = data.contiguous(), base.contiguous()
+    st = L.load().engram_overlay_accumulate(acc.data_ptr(), ix.data_ptr(), order.data_ptr(), d.data_ptr(),
+                                            b.data_ptr(), n, acc.shape[1], L.stream_of(acc.device))
+    L.check(st, "engram_overlay_accumulate")
 
 
 def sum_overlays(table, pleo_paths: list, device=None):

@@ -558,11 +558,13 @@ ENGRAM_API int engram_rowset_index(const uint32_t* bitmap, int64_t words, const 
 
 /* acc[index[k]] += data[k] - base[k] for k < n (rows of dim floats, fp32
  * subtract then add; index -1 skips a row): one .pleo file's deltas added into
- * the sum over the union of rows (engraft/replica/overlay_sum.py:80-96).  The
- * rows of one call must have distinct targets; repeated rows go in later calls,
- * in file order, as np.add.at applies them. */
-ENGRAM_API int engram_overlay_accumulate(float* acc, const int32_t* index, const float* data, const float* base,
-                                         int64_t n, int32_t dim, void* stream);
+ * the sum over the union of rows (engraft/replica/overlay_sum.py:80-96).
+ * order (device int64 [n], nullable): the rows k sorted by index[k], stable;
+ * with it, rows with the same target are added in ascending k (file order), as
+ * np.add.at applies them, all in one launch.  Without it the targets must be
+ * distinct. */
+ENGRAM_API int engram_overlay_accumulate(float* acc, const int32_t* index, const int64_t* order, const float* data,
+                                         const float* base, int64_t n, int32_t dim, void* stream);
 
 /* Host self-test of the division magic: out[i] = x[i] % d using exactly the
  * device code path (host arrays).  Lets CPU-only tests check it. */

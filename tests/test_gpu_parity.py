@@ -1036,6 +1036,30 @@ def test_sum_overlays_matches_reference_golden(eb, golden, fake7, tmp_path):
         assert manifest[k] == pytest.approx(ref[k], rel=1e-12, abs=1e-15), k  # float64 norms, summed in another order
 
 
+def test_overlay_accumulate_adds_repeated_rows_in_file_order(eb):
+    """engram_overlay_accumulate with the stable device sort of the targets
+    (rowset._accumulate): a file whose rows repeat (up to 40 times, index -1
+    skipped) gives bit for bit numpy's np.add.at of the fp32 deltas, which
+    adds repeated rows in file order."""
+    from engraft_ngram_b200 import rowset
+    rng = np.random.default_rng(71)
+    n, R, dim = 6000, 300, 160
+    idx = rng.zipf(1.3, size=n).astype(np.int64) % R
+    idx[rng.random(n) < 0.05] = -1
+    data = (rng.standard_normal((n, dim)) * 1e-2).astype(np.float32)
+    base = (rng.standard_normal((n, dim)) * 1e-2).astype(np.float32)
+    acc0 = (rng.standard_normal((R, dim)) * 1e-3).astype(np.float32)
+    want = acc0.copy()
+    keep = idx >= 0
+    np.add.at(want, idx[keep], data[keep] - base[keep])
+    acc = torch.from_numpy(acc0.copy()).to(DEV)
+    rowset._accumulate(acc, torch.from_numpy(idx.astype(np.int32)).to(DEV), torch.from_numpy(data).to(DEV),
+                       torch.from_numpy(base).to(DEV))
+    torch.cuda.synchronize()
+    assert np.bincount(idx[keep]).max() >= 20
+    assert np.array_equal(acc.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
 def test_write_merged_pleo_matches_reference_golden(eb, golden, fake7, tmp_path):
     import hashlib
     from engraft_ngram_b200 import rowset

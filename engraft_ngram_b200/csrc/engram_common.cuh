@@ -71,10 +71,47 @@ __device__ __forceinline__ TokCtx load_ctx(const engram_table& T, const int32_t*
     return c;
 }
 
+// Flat (position, head) index k -> (k / nh, k % nh).  A 64-bit division is a
+// long emulated sequence; 32-bit unsigned division is far shorter, so it is
+// used whenever k fits (every batch this library sees; k < 2^32).
+__device__ __forceinline__ void split_pair(int64_t k, int nh, int64_t& i, int& h) {
+    if ((uint64_t)k <= 0xffffffffull) {
+        const uint32_t q = (uint32_t)k / (uint32_t)nh;
+        i = (int64_t)q;
+        h = (int)((uint32_t)k - q * (uint32_t)nh);
+    } else {
+        i = k / nh;
+        h = (int)(k - i * nh);
+    }
+}
+
+// The per-head hash constants of a table, copied once per block into shared
+// memory.  Read from the kernel's parameter block with a different head in
+// every lane, they would be indexed constant-bank loads, which a warp
+// serialises (one address at a time); from shared memory the heads of a warp
+// hit distinct banks or the same word.
+struct HeadTab {
+    uint64_t magic[ENGRAM_MAX_HEADS];
+    int64_t offset[ENGRAM_MAX_HEADS];
+    uint32_t size[ENGRAM_MAX_HEADS];
+    uint32_t shift[ENGRAM_MAX_HEADS];
+};
+
+// Every thread of the block calls it; the caller then synchronises the block.
+__device__ __forceinline__ void head_tab_fill(HeadTab& H, const engram_table& T) {
+    for (int h = threadIdx.x; h < T.n_heads && h < ENGRAM_MAX_HEADS; h += blockDim.x) {
+        H.magic[h] = T.head_magic[h];
+        H.offset[h] = T.head_offset[h];
+        H.size[h] = T.head_size[h];
+        H.shift[h] = T.head_shift[h];
+    }
+}
+
 // Global row id of head `h` at position t (engraft/table.py:111-144 + engraft/lens.py:108-110).
 // ctx[0] = x_t; ctx[s] = x_{t-s}, or EOS once a predecessor is missing (before
 // lo, the start of t's segment) or is itself EOS; the current token never cuts.
-__device__ __forceinline__ int32_t hash_ctx(const engram_table& T, const TokCtx& c, int64_t t, int h) {
+__device__ __forceinline__ int32_t hash_ctx(const engram_table& T, const HeadTab& H, const TokCtx& c, int64_t t,
+                                            int h) {
     const int N = T.ngram_size;
     int64_t ctx[ENGRAM_MAX_CTX];
     ctx[0] = (int64_t)c.x[0];
@@ -96,13 +133,13 @@ __device__ __forceinline__ int32_t hash_ctx(const engram_table& T, const TokCtx&
 #pragma unroll
     for (int j = 1; j < ENGRAM_MAX_CTX; j++)
         if (j < n) mixed ^= (uint64_t)ctx[j] * T.mult[j];
-    const uint64_t local = mod_by_magic(mixed, T.head_size[h], T.head_magic[h], T.head_shift[h]);
-    return (int32_t)(T.head_offset[h] + (int64_t)local);
+    const uint64_t local = mod_by_magic(mixed, H.size[h], H.magic[h], H.shift[h]);
+    return (int32_t)(H.offset[h] + (int64_t)local);
 }
 
-__device__ __forceinline__ int32_t hash_row(const engram_table& T, const int32_t* __restrict__ tokens,
+__device__ __forceinline__ int32_t hash_row(const engram_table& T, const HeadTab& H, const int32_t* __restrict__ tokens,
                                             const int32_t* __restrict__ seg_start, int64_t t, int h) {
-    return hash_ctx(T, load_ctx(T, tokens, seg_start, t), t, h);
+    return hash_ctx(T, H, load_ctx(T, tokens, seg_start, t), t, h);
 }
 
 // Overlay map probe (open addressing, linear probing; built by

@@ -91,11 +91,11 @@ struct PosMap {
     }
 };
 
-__device__ __forceinline__ PosHeads heads_of(const engram_table& T, const engram_overlay& OV, const TokCtx& c,
-                                             const PosMap& pm, int64_t i, int lane) {
+__device__ __forceinline__ PosHeads heads_of(const engram_table& T, const HeadTab& H, const engram_overlay& OV,
+                                             const TokCtx& c, const PosMap& pm, int64_t i, int lane) {
     PosHeads r{0, -1, 0};
     if (lane < T.n_heads) {
-        r.gid = hash_ctx(T, c, pm.at(i), lane);
+        r.gid = hash_ctx(T, H, c, pm.at(i), lane);
         r.slot = overlay_slot(OV, r.gid);
         r.row = pm.row(i, lane, T.n_heads, r.gid);
     }
@@ -119,12 +119,16 @@ __device__ __forceinline__ void flush_hits(unsigned long long hits, unsigned lon
 __global__ void __launch_bounds__(256) k_hash(engram_table T, const int32_t* __restrict__ tokens,
                                               const int32_t* __restrict__ seg_start, PosMap pm, int64_t n,
                                               int32_t* __restrict__ ids_out) {
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
+    __syncthreads();
     const int nh = T.n_heads;
     const int64_t total = n * nh;
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t i = k / nh;
-        const int h = (int)(k - i * nh);
-        ids_out[k] = hash_row(T, tokens, seg_start, pm.at(i), h);
+        int64_t i;
+        int h;
+        split_pair(k, nh, i, h);
+        ids_out[k] = hash_row(T, htab, tokens, seg_start, pm.at(i), h);
     }
 }
 
@@ -139,6 +143,9 @@ __global__ void __launch_bounds__(256) k_stage_sharded(engram_table T, engram_ov
                                                        const int32_t* __restrict__ tokens,
                                                        const int32_t* __restrict__ seg_start, PosMap pm, int64_t n,
                                                        uint8_t* __restrict__ stage) {
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
+    __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
     const int nh = T.n_heads;
@@ -150,7 +157,7 @@ __global__ void __launch_bounds__(256) k_stage_sharded(engram_table T, engram_ov
         bool copy = false;  // another rank's row that the overlay does not replace
         if (lane < nh) {
             const int64_t t = pm.at(i);
-            gid = hash_ctx(T, load_ctx(T, tokens, seg_start, t), t, lane);
+            gid = hash_ctx(T, htab, load_ctx(T, tokens, seg_start, t), t, lane);
             uint32_t o, l;
             pm.owner_of(gid, o, l);
             copy = o != pm.rank && overlay_slot(OV, gid) < 0;
@@ -289,7 +296,9 @@ __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engra
                                                            int64_t n, float* __restrict__ out, int32_t* ids_out,
                                                            int32_t* slots_out, unsigned long long* hit_count) {
     __shared__ float s_kv[16];
+    __shared__ HeadTab htab;
     if (threadIdx.x < 16) s_kv[threadIdx.x] = kKvIq4[threadIdx.x];
+    head_tab_fill(htab, T);
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -304,7 +313,7 @@ __global__ void __launch_bounds__(256, 2) k_forward_concat(engram_table T, engra
     if (warp0 < n) nxt = load_ctx(T, tokens, seg_start, pm.at(warp0));
     for (int64_t i = warp0; i < n; i += nwarps) {
         const TokCtx cur = nxt;
-        const PosHeads ph = heads_of(T, OV, cur, pm, i, lane);
+        const PosHeads ph = heads_of(T, htab, OV, cur, pm, i, lane);
         write_heads(ph, i, nh, lane, ids_out, slots_out, hits);
         if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, pm.at(i + nwarps));
         float4* dst = reinterpret_cast<float4*>(out + i * (int64_t)nh * dim);
@@ -381,7 +390,9 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                                                             int32_t* ids_out, int32_t* slots_out,
                                                             unsigned long long* hit_count) {
     __shared__ float s_kv[16];
+    __shared__ HeadTab htab;
     if (threadIdx.x < 16) s_kv[threadIdx.x] = kKvIq4[threadIdx.x];
+    head_tab_fill(htab, T);
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -406,7 +417,7 @@ __global__ void __launch_bounds__(256, 2) k_forward_pairsum(engram_table T, engr
                 if (c < cpp) r[u] = __ldcs(res + c);
             }
             if (base == 0) {
-                ph = heads_of(T, OV, cur, pm, i, lane);
+                ph = heads_of(T, htab, OV, cur, pm, i, lane);
                 write_heads(ph, i, nh, lane, ids_out, slots_out, hits);
                 if (i + nwarps < n) nxt = load_ctx(T, tokens, seg_start, pm.at(i + nwarps));
             }
@@ -541,6 +552,8 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
     extern __shared__ __align__(16) uint8_t smem[];
     float2* pair_tab = reinterpret_cast<float2*>(smem);
     for (int b = threadIdx.x; b < 256; b += blockDim.x) pair_tab[b] = make_float2(kKvIq4[b & 15], kKvIq4[b >> 4]);
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* wbuf = smem + kPairTableBytes + warp * 2 * buf_bytes;
@@ -569,7 +582,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
     };
 
     TokCtx ctx = load_ctx(T, tokens, seg_start, pm.at(i));
-    int32_t gid = lane < nh ? hash_ctx(T, ctx, pm.at(i), lane) : 0;
+    int32_t gid = lane < nh ? hash_ctx(T, htab, ctx, pm.at(i), lane) : 0;
     issue(i, lane < nh ? pm.row(i, lane, nh, gid) : 0, 0);
     int32_t slot = lane < nh ? overlay_slot(OV, gid) : -1;
     int64_t inext = i + nw;
@@ -580,7 +593,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32) k_forward_pairsum_staged(
         const bool has_next = inext < n;
         int32_t gid_n = 0;
         if (has_next) {
-            gid_n = lane < nh ? hash_ctx(T, ctx, pm.at(inext), lane) : 0;
+            gid_n = lane < nh ? hash_ctx(T, htab, ctx, pm.at(inext), lane) : 0;
             issue(inext, lane < nh ? pm.row(inext, lane, nh, gid_n) : 0, b ^ 1);
             if (inext + nw < n) ctx = load_ctx(T, tokens, seg_start, pm.at(inext + nw));
         } else {
@@ -639,7 +652,9 @@ template <int FMT>
 __global__ void __launch_bounds__(256) k_gather_rows(engram_table T, const int32_t* __restrict__ ids, int64_t n,
                                                      float* __restrict__ out) {
     __shared__ float s_kv[16];
+    __shared__ HeadTab htab;
     if (threadIdx.x < 16) s_kv[threadIdx.x] = kKvIq4[threadIdx.x];
+    head_tab_fill(htab, T);
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -757,7 +772,9 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     using G = XsGeom<FMT, DIM>;
     extern __shared__ __align__(16) uint8_t smem[];
     float* kv = reinterpret_cast<float*>(smem);
+    __shared__ HeadTab htab;
     if (threadIdx.x < 16) kv[threadIdx.x] = kKvIq4[threadIdx.x];
+    head_tab_fill(htab, T);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* wbuf = smem + 64 + warp * 2 * G::BUF;
@@ -791,7 +808,7 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     // pipeline state: position k (gid, slot), k+1 (gid, probe in flight), k+2 (tokens in flight)
     int64_t i = first;
     TokCtx c0 = load_ctx(T, tokens, seg_start, pm.at(i));
-    int32_t gid = head_lane ? hash_ctx(T, c0, pm.at(i), lane) : 0;
+    int32_t gid = head_lane ? hash_ctx(T, htab, c0, pm.at(i), lane) : 0;
     int32_t slot = head_lane ? probe_finish(OV, gid, probe_start(OV, gid)) : -1;
     issue(i, head_lane ? pm.row(i, lane, G::NH, gid) : 0, slot, 0);
     int64_t i1 = i + nw;
@@ -799,7 +816,7 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     ProbeState pr1{0u, -1, -1};
     if (i1 < n) {
         const TokCtx c1 = load_ctx(T, tokens, seg_start, pm.at(i1));
-        gid1 = head_lane ? hash_ctx(T, c1, pm.at(i1), lane) : 0;
+        gid1 = head_lane ? hash_ctx(T, htab, c1, pm.at(i1), lane) : 0;
         if (head_lane) pr1 = probe_start(OV, gid1);
     }
     int32_t row1 = head_lane && i1 < n ? pm.row(i1, lane, G::NH, gid1) : 0;
@@ -896,7 +913,7 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         slot = slot1;
         const int64_t i2 = inext + nw;
         if (i2 < n) {
-            gid1 = head_lane ? hash_ctx(T, c2, pm.at(i2), lane) : 0;
+            gid1 = head_lane ? hash_ctx(T, htab, c2, pm.at(i2), lane) : 0;
             if (head_lane) pr1 = probe_start(OV, gid1);
             row1 = pm.rix ? (r2 < 0 ? 0 : r2) : gid1;
             if (i2 + nw < n) {

@@ -65,15 +65,19 @@ __device__ __forceinline__ void set_bit(uint32_t* bitmap, int64_t g) {
 __global__ void k_mark_positions(engram_table T, const int32_t* __restrict__ tokens, int64_t n_tokens,
                                  const int32_t* __restrict__ seg_start, const int64_t* __restrict__ positions,
                                  int64_t n, uint32_t* bitmap) {
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
+    __syncthreads();
     const int nh = T.n_heads;
     const int64_t total = n * nh;
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total;
          k += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t i = k / nh;
-        const int h = (int)(k - i * nh);
+        int64_t i;
+        int h;
+        split_pair(k, nh, i, h);
         int64_t t = positions ? __ldg(positions + i) : i;
         t = t < 0 ? 0 : (t >= n_tokens ? n_tokens - 1 : t);
-        const int32_t g = hash_row(T, tokens, seg_start, t, h);
+        const int32_t g = hash_row(T, htab, tokens, seg_start, t, h);
         if (g >= 0 && g < T.n_rows) set_bit(bitmap, g);
     }
 }

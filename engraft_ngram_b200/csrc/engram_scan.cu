@@ -79,7 +79,9 @@ __global__ void __launch_bounds__(256) k_scan_score(engram_table T, engram_overl
                                                     const float* __restrict__ dnorm,
                                                     unsigned long long* __restrict__ read_count, ScanWs w) {
     __shared__ uint32_t s_cnt;
+    __shared__ HeadTab htab;
     if (threadIdx.x == 0) s_cnt = 0;
+    head_tab_fill(htab, T);
     __syncthreads();
     const int lane = threadIdx.x & 31, sub = lane & 15, grp = threadIdx.x >> 4;  // 16 groups of 16 lanes
     const int nh = T.n_heads;
@@ -92,7 +94,7 @@ __global__ void __launch_bounds__(256) k_scan_score(engram_table T, engram_overl
         float v = 0.0f;
         bool match = false;
         if (live && sub < nh) {
-            const int32_t gid = hash_row(T, tokens, nullptr, t, sub);
+            const int32_t gid = hash_row(T, htab, tokens, nullptr, t, sub);
             const int32_t slot = overlay_slot(OV, gid);
             match = slot >= 0;
             if (match) {

@@ -169,12 +169,16 @@ __global__ void k_row_index(const int32_t* __restrict__ ids, const int32_t* __re
 __global__ void k_plan_ids(engram_table T, engram_overlay OV, const int32_t* __restrict__ tokens,
                            const int32_t* __restrict__ seg_start, int64_t t0, int64_t n, int world, int rank,
                            int32_t* __restrict__ out) {
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
+    __syncthreads();
     const int nh = T.n_heads;
     const int64_t total = n * nh;
     for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < total; k += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t i = k / nh;
-        const int h = (int)(k - i * nh);
-        const int32_t g = hash_row(T, tokens, seg_start, t0 + i, h);
+        int64_t i;
+        int h;
+        split_pair(k, nh, i, h);
+        const int32_t g = hash_row(T, htab, tokens, seg_start, t0 + i, h);
         const bool remote = (int)((uint32_t)g % (uint32_t)world) != rank;
         out[k] = (remote && overlay_slot(OV, g) < 0) ? g : -1;
     }
@@ -235,7 +239,9 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_count(engram_table T, e
                                                                int64_t n, int world, int rank,
                                                                int32_t* __restrict__ ids, uint32_t* __restrict__ tile_cnt) {
     __shared__ uint32_t cnt[kMaxWorld];
+    __shared__ HeadTab htab;
     for (int o = threadIdx.x; o < world; o += blockDim.x) cnt[o] = 0;
+    head_tab_fill(htab, T);
     __syncthreads();
     const int nh = T.n_heads;
     const int64_t total = n * nh;
@@ -244,9 +250,10 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_count(engram_table T, e
     for (int it = 0; it < kRouteItems; it++) {
         const int64_t k = base + it * kRouteThreads + threadIdx.x;
         if (k >= total) break;
-        const int64_t i = k / nh;
-        const int h = (int)(k - i * nh);
-        const int32_t g = hash_row(T, tokens, seg_start, t0 + i, h);
+        int64_t i;
+        int h;
+        split_pair(k, nh, i, h);
+        const int32_t g = hash_row(T, htab, tokens, seg_start, t0 + i, h);
         const int o = (int)((uint32_t)g % (uint32_t)world);
         const bool req = o != rank && overlay_slot(OV, g) < 0;
         ids[k] = req ? g : -1;
@@ -306,12 +313,13 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_scatter(const int32_t* 
 // engram_shard_route_push: the requests of a batch written straight into their
 // owners' memory.  Requester `rank` owns region `rank` of every owner's request
 // buffer (region entries of int32 ids) and of its send buffer (region rows).
-// k_route_push hashes a tile of (position, head) pairs, counts each owner's
-// requests in shared memory, reserves the tile's slots with one atomic per
-// owner on the global counters, then stores every requested id into its
-// owner's region (a plain store over NVLink) and tags the pair with
-// owner * region + slot.  k_route_finish turns the tags into rows of the
-// receive buffer (owners' blocks in ascending owner order, so row = the
+// k_route_push hashes a tile of (position, head) pairs and counts each owner's
+// requests in shared memory; the tile's ids are staged there grouped by owner,
+// one atomic per owner on the global counters reserves the tile's slots, and
+// the block then writes each owner's ids as one contiguous run (consecutive
+// threads, consecutive addresses: coalesced stores over NVLink).  Each pair is
+// tagged with owner * region + slot.  k_route_finish turns the tags into rows
+// of the receive buffer (owners' blocks in ascending owner order, so row = the
 // counts of lower owners + slot) and block 0 stores each count into its
 // owner's count array (entry `rank`).  The order inside an owner's block
 // depends on which tile reserved first; the forward reads every pair's own
@@ -326,8 +334,13 @@ __global__ void __launch_bounds__(kPushThreads) k_route_push(engram_table T, eng
                                                              int64_t region, unsigned long long* __restrict__ cnt,
                                                              int32_t* __restrict__ row_index) {
     __shared__ uint32_t tile_cnt[kMaxWorld];
-    __shared__ unsigned long long first[kMaxWorld];
+    __shared__ uint32_t tile_off[kMaxWorld + 1];        // first staged entry of each owner
+    __shared__ unsigned long long first[kMaxWorld];     // first slot of each owner's run in its region
+    __shared__ int32_t staged[kPushTile];
+    __shared__ uint8_t staged_owner[kPushTile];
+    __shared__ HeadTab htab;
     for (int o = threadIdx.x; o < world; o += blockDim.x) tile_cnt[o] = 0;
+    head_tab_fill(htab, T);
     __syncthreads();
     const int nh = T.n_heads;
     const int64_t total = n * nh;
@@ -339,9 +352,10 @@ __global__ void __launch_bounds__(kPushThreads) k_route_push(engram_table T, eng
         const int64_t k = base + it * kPushThreads + threadIdx.x;
         g[it] = -1;
         if (k < total) {
-            const int64_t i = k / nh;
-            const int h = (int)(k - i * nh);
-            const int32_t id = hash_row(T, tokens, seg_start, t0 + i, h);
+            int64_t i;
+            int h;
+            split_pair(k, nh, i, h);
+            const int32_t id = hash_row(T, htab, tokens, seg_start, t0 + i, h);
             const int o = (int)((uint32_t)id % (uint32_t)world);
             if (o != rank && overlay_slot(OV, id) < 0) {
                 g[it] = id;
@@ -350,6 +364,14 @@ __global__ void __launch_bounds__(kPushThreads) k_route_push(engram_table T, eng
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t acc = 0;
+        for (int o = 0; o < world; o++) {
+            tile_off[o] = acc;
+            acc += tile_cnt[o];
+        }
+        tile_off[world] = acc;
+    }
     for (int o = threadIdx.x; o < world; o += blockDim.x)
         first[o] = tile_cnt[o] ? atomicAdd(cnt + o, (unsigned long long)tile_cnt[o]) : 0ull;
     __syncthreads();
@@ -360,11 +382,19 @@ __global__ void __launch_bounds__(kPushThreads) k_route_push(engram_table T, eng
         int32_t tag = -1;
         if (g[it] >= 0) {
             const int o = (int)((uint32_t)g[it] % (uint32_t)world);
-            const int64_t slot = (int64_t)first[o] + loc[it];  // < region: a batch has at most region pairs
-            reinterpret_cast<int32_t*>(id_ptrs[o])[(int64_t)rank * region + slot] = g[it];
-            tag = (int32_t)(o * region + slot);
+            const uint32_t e = tile_off[o] + loc[it];
+            staged[e] = g[it];
+            staged_owner[e] = (uint8_t)o;
+            tag = (int32_t)(o * region + (int64_t)first[o] + loc[it]);  // slot < region: at most region pairs
         }
         row_index[k] = tag;
+    }
+    __syncthreads();
+    const uint32_t staged_n = tile_off[world];
+    for (uint32_t e = threadIdx.x; e < staged_n; e += blockDim.x) {
+        const int o = staged_owner[e];
+        const int64_t slot = (int64_t)first[o] + (e - tile_off[o]);
+        reinterpret_cast<int32_t*>(id_ptrs[o])[(int64_t)rank * region + slot] = staged[e];
     }
 }
 

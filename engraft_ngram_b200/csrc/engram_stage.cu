@@ -59,12 +59,13 @@ __device__ __forceinline__ TokCtx load_ctx_cg(const engram_table& T, const int32
 }
 
 // Owner of each head of output row i, 4 bits per head (heads 0..15 in lo, 16..31 in hi).
-__device__ __forceinline__ void head_owners(const engram_table& T, const TokCtx& c, int64_t t, const Owners& ow,
+__device__ __forceinline__ void head_owners(const engram_table& T, const HeadTab& H, const TokCtx& c, int64_t t,
+                                            const Owners& ow,
                                             unsigned long long& lo, unsigned long long& hi) {
     lo = hi = 0ull;
     for (int h = 0; h < T.n_heads; h++) {
         uint32_t o, l;
-        ow.of(hash_ctx(T, c, t, h), o, l);
+        ow.of(hash_ctx(T, H, c, t, h), o, l);
         if (h < 16) lo |= (unsigned long long)o << (4 * h);
         else hi |= (unsigned long long)o << (4 * (h - 16));
     }
@@ -95,12 +96,15 @@ __global__ void __launch_bounds__(kPlanWarps * 32) k_plan_count(engram_table T, 
                                                                 const int32_t* __restrict__ seg_start, int64_t t0,
                                                                 int64_t n, Owners ow, int64_t tiles,
                                                                 int32_t* __restrict__ plan) {
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
+    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int64_t tile = (int64_t)blockIdx.x * kPlanWarps + warp; tile < tiles;
          tile += (int64_t)gridDim.x * kPlanWarps) {
         const int64_t i = tile * 32 + lane;
         unsigned long long lo = 0, hi = 0;
-        if (i < n) head_owners(T, load_ctx(T, tokens, seg_start, t0 + i), t0 + i, ow, lo, hi);
+        if (i < n) head_owners(T, htab, load_ctx(T, tokens, seg_start, t0 + i), t0 + i, ow, lo, hi);
         for (uint32_t o = 0; o < ow.world; o++) {
             const unsigned m = i < n ? owned_mask(lo, hi, T.n_heads, o) : 0u;
             int c = __popc(m);
@@ -154,13 +158,16 @@ __global__ void __launch_bounds__(kPlanWarps * 32) k_plan_index(engram_table T, 
                                                                 int64_t n, Owners ow, int64_t tiles,
                                                                 const int32_t* __restrict__ plan,
                                                                 int32_t* __restrict__ row_index) {
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
+    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nh = T.n_heads;
     for (int64_t tile = (int64_t)blockIdx.x * kPlanWarps + warp; tile < tiles;
          tile += (int64_t)gridDim.x * kPlanWarps) {
         const int64_t i = tile * 32 + lane;
         unsigned long long lo = 0, hi = 0;
-        if (i < n) head_owners(T, load_ctx(T, tokens, seg_start, t0 + i), t0 + i, ow, lo, hi);
+        if (i < n) head_owners(T, htab, load_ctx(T, tokens, seg_start, t0 + i), t0 + i, ow, lo, hi);
         for (uint32_t o = 0; o < ow.world; o++) {
             const unsigned m = i < n ? owned_mask(lo, hi, nh, o) : 0u;
             int total;
@@ -185,6 +192,9 @@ __global__ void __launch_bounds__(kPushWarps * 32) k_stage_push(engram_table T, 
                                                                uint8_t* const* stages, Owners ow, int rank,
                                                                int first_r) {
     extern __shared__ int32_t plist[];
+    __shared__ HeadTab htab;
+    head_tab_fill(htab, T);
+    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nh = T.n_heads;
     int32_t* list = plist + warp * 32 * nh;
@@ -230,14 +240,14 @@ __global__ void __launch_bounds__(kPushWarps * 32) k_stage_push(engram_table T, 
         if (i < n)
             for (int h = 0; h < nh; h++) {
                 uint32_t o, l;
-                ow.of(hash_ctx(T, cur, t0 + i, h), o, l);
+                ow.of(hash_ctx(T, htab, cur, t0 + i, h), o, l);
                 if ((int)o == rank) m |= 1u << h;
             }
         int total;
         int k = warp_exclusive(__popc(m), lane, total);
         for (unsigned b = m; b; b &= b - 1) {  // their local rows, in head order (the hash again: no local array)
             uint32_t o, l;
-            ow.of(hash_ctx(T, cur, t0 + i, __ffs(b) - 1), o, l);
+            ow.of(hash_ctx(T, htab, cur, t0 + i, __ffs(b) - 1), o, l);
             list[k++] = (int32_t)l;
         }
         __syncwarp();

@@ -77,6 +77,19 @@ struct PosMap {
             reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(shard) + o));
         return base + (int64_t)l * stride;
     }
+    // row_ptr with the exchanged-read row index srix[i * nh + h] already loaded
+    // (k_pre; ignored for every other layout).
+    __device__ __forceinline__ const uint8_t* row_ptr_pre(const uint8_t* rows, int64_t stride, int32_t r, int32_t k_pre,
+                                                          int64_t i, int h, int nh) const {
+        if (srix == nullptr || !sharded()) return row_ptr(rows, stride, r, i, h, nh);
+        uint32_t o, l;
+        owner_of(r, o, l);
+        if (o != rank) return stage + (int64_t)(k_pre < 0 ? 0 : k_pre) * stride;
+        if (local != nullptr) return local + (int64_t)l * stride;
+        const uint8_t* base =
+            reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(shard) + o));
+        return base + (int64_t)l * stride;
+    }
     // Row number in T.rows that serves head h of output row i (the global id
     // unless the rows were gathered into a local buffer, see engram_forward_indirect).
     __device__ __forceinline__ int32_t row(int64_t i, int h, int nh, int32_t gid) const {
@@ -786,7 +799,9 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
 
     // Copies position pos's residual and the table rows of its heads that the
     // overlay does not serve (slot < 0; an overlay head reads its fp32 row instead).
-    auto issue = [&](int64_t pos, int32_t gid, int32_t slot, int b) {
+    // gid: the head lane's row in T.rows; with SHARD, hp: the head lane's row address
+    // (computed when the position was hashed, its row index loaded an iteration earlier).
+    auto issue = [&](int64_t pos, int32_t gid, unsigned long long hp, int32_t slot, int b) {
         uint8_t* bb = wbuf + b * G::BUF;
         const uint4* src = reinterpret_cast<const uint4*>(out + pos * (G::HPN * DIM));
 #pragma unroll
@@ -796,11 +811,15 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
             const int j = j0 + lane;
             const int h = j / G::PIECES;
             const int p = j - h * G::PIECES;
-            const int32_t g = __shfl_sync(kFull, gid, h < G::NH ? h : 0);
             const int32_t sl = __shfl_sync(kFull, slot, h < G::NH ? h : 0);
-            if (j < G::NH * G::PIECES && sl < 0)
-                cp_async16_f(bb + G::RES + h * G::ROW + p * 16,
-                             (SHARD ? pm.row_ptr(rows, G::ROW, g, pos, h, G::NH) : rows + (int64_t)g * G::ROW) + p * 16);
+            const uint8_t* src;
+            if (SHARD) {
+                src = reinterpret_cast<const uint8_t*>(__shfl_sync(kFull, hp, h < G::NH ? h : 0));
+            } else {
+                const int32_t g = __shfl_sync(kFull, gid, h < G::NH ? h : 0);
+                src = rows + (int64_t)g * G::ROW;
+            }
+            if (j < G::NH * G::PIECES && sl < 0) cp_async16_f(bb + G::RES + h * G::ROW + p * 16, src + p * 16);
         }
         cp_async_commit_f();
     };
@@ -810,7 +829,15 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
     TokCtx c0 = load_ctx(T, tokens, seg_start, pm.at(i));
     int32_t gid = head_lane ? hash_ctx(T, htab, c0, pm.at(i), lane) : 0;
     int32_t slot = head_lane ? probe_finish(OV, gid, probe_start(OV, gid)) : -1;
-    issue(i, head_lane ? pm.row(i, lane, G::NH, gid) : 0, slot, 0);
+    auto head_ptr = [&](int64_t pos, int32_t g, int32_t k_pre) -> unsigned long long {
+        return SHARD && head_lane
+                   ? reinterpret_cast<unsigned long long>(pm.row_ptr_pre(rows, G::ROW, g, k_pre, pos, lane, G::NH))
+                   : 0ull;
+    };
+    auto srix_of = [&](int64_t pos) -> int32_t {
+        return SHARD && pm.srix && head_lane ? __ldg(pm.srix + pos * G::NH + lane) : 0;
+    };
+    issue(i, head_lane ? pm.row(i, lane, G::NH, gid) : 0, head_ptr(i, gid, srix_of(i)), slot, 0);
     int64_t i1 = i + nw;
     int32_t gid1 = 0;
     ProbeState pr1{0u, -1, -1};
@@ -820,12 +847,14 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         if (head_lane) pr1 = probe_start(OV, gid1);
     }
     int32_t row1 = head_lane && i1 < n ? pm.row(i1, lane, G::NH, gid1) : 0;
-    // tokens (and gathered-row indices) of position k+2 load one iteration ahead
+    unsigned long long hp1 = i1 < n ? head_ptr(i1, gid1, srix_of(i1)) : 0ull;
+    // tokens (and gathered-row or exchanged-row indices) of position k+2 load one iteration ahead
     TokCtx c2{};
-    int32_t r2 = 0;
+    int32_t r2 = 0, s2 = 0;
     if (i1 + nw < n) {
         c2 = load_ctx(T, tokens, seg_start, pm.at(i1 + nw));
         if (pm.rix && head_lane) r2 = __ldg(pm.rix + (i1 + nw) * G::NH + lane);
+        s2 = srix_of(i1 + nw);
     }
     unsigned long long hits = 0;
     int b = 0;
@@ -833,7 +862,7 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
         const int64_t inext = i + nw;
         // the next position's probe (its key loads were issued an iteration ago) decides which rows to copy
         const int32_t slot1 = (inext < n && head_lane) ? probe_finish(OV, gid1, pr1) : -1;
-        if (inext < n) issue(inext, row1, slot1, b ^ 1);
+        if (inext < n) issue(inext, row1, hp1, slot1, b ^ 1);
         else cp_async_commit_f();
         if (slot1 >= 0) {  // the next position's overlay row: pull it into L1 while this position computes
             const char* orow_p = reinterpret_cast<const char*>(OV.rows + (int64_t)slot1 * DIM);
@@ -916,9 +945,11 @@ __global__ void __launch_bounds__(kXsWarps * 32) k_forward_pairsum_fixed(
             gid1 = head_lane ? hash_ctx(T, htab, c2, pm.at(i2), lane) : 0;
             if (head_lane) pr1 = probe_start(OV, gid1);
             row1 = pm.rix ? (r2 < 0 ? 0 : r2) : gid1;
+            hp1 = head_ptr(i2, gid1, s2);
             if (i2 + nw < n) {
                 c2 = load_ctx(T, tokens, seg_start, pm.at(i2 + nw));
                 if (pm.rix && head_lane) r2 = __ldg(pm.rix + (i2 + nw) * G::NH + lane);
+                s2 = srix_of(i2 + nw);
             }
         }
         b ^= 1;

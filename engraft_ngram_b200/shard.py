@@ -468,8 +468,9 @@ class ExchangeStage:
       barrier: a 4-byte all-reduce.  Once it completes, every rank's route of
         this call is visible to its owners (served next call) and every
         owner's gather of this call is done (fetched next call);
-    and on the side stream, at the start of the next prefetch() call (after
-    the barrier of the call that served it):
+    and on the side stream, at the end of the next prefetch() call (after
+    its barrier, so the copies overlap the forward that follows rather than
+    the gathers and the route, which move more bytes per unit time):
       fetch: the batch's rows, one copy-engine transfer per owner from the
         owner's send buffer (the host reads this rank's counts, copied two
         calls earlier, so it does not wait).  Queued behind the forward
@@ -562,8 +563,10 @@ class ExchangeStage:
         if n > self.n_max:
             raise ValueError(f"{n} positions exceed n_tokens_max {self.n_max}")
         cur = torch.cuda.current_stream(t.device)
-        for b in self._oldest("served"):  # the next forward waits for the oldest of them
-            self._fetch(b)
+        fetch_now = self._oldest("served")  # the next forward waits for the oldest of them
+        if not self.push:
+            for b in fetch_now:
+                self._fetch(b)
         served = self._oldest("routed")
         for b in served:
             self._serve(b, cur)
@@ -595,6 +598,8 @@ class ExchangeStage:
             done.record(cur)
             for s_ in served:
                 self.ev_barrier[s_] = done
+            for s_ in fetch_now:  # behind this call's gathers and route, so the copies overlap the forward
+                self._fetch(s_)
             self._routed(b, key, ov, omap)
             return
         t_route = self._mark(cur)

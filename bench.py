@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="cfg5", choices=sorted(CONFIGS) + ["scan", "ple", "micro"])
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--projection", choices=["3xtf32", "tcgen05", "fp32"], default=None,
+                    help="--config ple: the projections' engine (default: engraft_ngram_b200.ple.PROJECTION)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-latency", action="store_true",
@@ -966,6 +968,8 @@ def run_ple(args, device):
     lib = L.load()
     stream = torch.cuda.current_stream(device).cuda_stream
     from engraft_ngram_b200 import ple as P
+    if args.projection:
+        P.PROJECTION = args.projection
     kv = torch.empty(T, hc * n + n, device=device)
     value = kv[:, hc * n:]
     gate, normed, out = (torch.empty(T, hc, device=device), torch.empty(T, hc, n, device=device),
@@ -1032,7 +1036,9 @@ def run_micro(args, device):
     headline table's size, timed with CUDA events over K launches after three
     warm-up launches: achieved GB/s = the bytes the call must move (stated per
     kernel) / its mean time, against the measured copy peak.  One JSON line.
-    Also the command the per-kernel ncu summaries are captured from."""
+    Also the command the per-kernel ncu summaries are captured from
+    (--table-rows shrinks the table and the hashed stream for multi-pass
+    captures)."""
     import ctypes as C
     import torch
     import engraft_ngram_b200 as eb
@@ -1045,12 +1051,13 @@ def run_micro(args, device):
     g = torch.Generator(device=device)
     g.manual_seed(args.seed)
     cdf = zipf_cdf(torch, device)
-    sizes = synthetic_head_sizes(FULL_ROWS)
+    n_rows = args.table_rows or FULL_ROWS
+    sizes = synthetic_head_sizes(n_rows)
     offs = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
     mult = synthetic_multipliers(args.seed)
     fmt, dim = L.FMT_IQ4_XS, 256
     addr = eb.DeviceTable(torch.zeros(64, dtype=torch.uint8, device=device), fmt, dim, sizes, offs, mult, EOS,
-                          n_rows=FULL_ROWS, hash_only=True)
+                          n_rows=n_rows, hash_only=True)
     stride = addr.row_stride
     out = {}
 
@@ -1069,7 +1076,7 @@ def run_micro(args, device):
         out[name] = {"ms": ms, "bytes": int(nbytes), "gbs": gbs, "frac": gbs / peak, "bytes_are": note}
 
     # engram_hash: 16 M positions of a Zipf stream, 16 heads each
-    T = 1 << 24
+    T = 1 << 24 if n_rows == FULL_ROWS else 1 << 22
     toks = zipf_tokens(torch, T, g, cdf)
     ids = torch.empty(T * 16, dtype=torch.int32, device=device)
     timed("engram_hash (k_hash)", lambda: L.check(lib.engram_hash(C.byref(addr.ctable), toks.data_ptr(), None, 0, T,
@@ -1077,7 +1084,7 @@ def run_micro(args, device):
           T * (4 + 64), "4 B token in + 16 x 4 B ids out per position")
     del ids
     # row sets over the 320 M-row table: a 40 MB bitmap (it fits in L2, as in the descent's own use)
-    words = int(lib.engram_rowset_words(FULL_ROWS))
+    words = int(lib.engram_rowset_words(n_rows))
     bm_a = torch.zeros(words, dtype=torch.int32, device=device)
     bm_b = torch.zeros(words, dtype=torch.int32, device=device)
     bm_c = torch.empty(words, dtype=torch.int32, device=device)
@@ -1086,9 +1093,9 @@ def run_micro(args, device):
           lambda: L.check(lib.engram_rowset_mark(C.byref(addr.ctable), toks.data_ptr(), T, None, None, n_mark,
                                                  bm_a.data_ptr(), stream), "engram_rowset_mark"),
           n_mark * (4 + 16 * 4), "4 B token in + one 4 B bitmap word per head, per position")
-    some = torch.randint(0, FULL_ROWS, (1 << 22,), generator=g, device=device, dtype=torch.int32)
+    some = torch.randint(0, n_rows, (1 << 22,), generator=g, device=device, dtype=torch.int32)
     timed("engram_rowset_mark_ids (k_mark_ids)",
-          lambda: L.check(lib.engram_rowset_mark_ids(some.data_ptr(), some.numel(), FULL_ROWS, bm_b.data_ptr(),
+          lambda: L.check(lib.engram_rowset_mark_ids(some.data_ptr(), some.numel(), n_rows, bm_b.data_ptr(),
                                                      stream), "engram_rowset_mark_ids"),
           some.numel() * 8, "4 B id in + one 4 B bitmap word per id")
     timed("engram_rowset_combine (k_combine, union)",
@@ -1152,10 +1159,10 @@ def run_micro(args, device):
                           "engram_shard_route_push"),
           n5 * 4 + region * 4 * 2 + int(region * (W - 1) / W) * 4,
           "tokens in, row_index written then rewritten, one 4 B id per remote pair")
-    n_local = (FULL_ROWS + W - 1) // W
+    n_local = (n_rows + W - 1) // W
     # one buffer of a W=2 shard's rows (23 GB): a W=4 owner's shard below, every owner's shard of the W=2 stage;
     # its contents do not change the timing
-    shard = torch.empty(((FULL_ROWS + 1) // 2) * stride, dtype=torch.uint8, device=device)
+    shard = torch.empty(((n_rows + 1) // 2) * stride, dtype=torch.uint8, device=device)
     owner = (me + 1) % W
     for r in range(W):  # every other requester's ids of this batch for `owner`
         if r != owner:
@@ -1215,6 +1222,7 @@ def run_micro(args, device):
           3 * Cb, "normed and dout read, dnormed written (the silu'-scaled gradient is a scratch pass)")
     line = {"metric": "per-kernel HBM GB/s of the kernels off the config-5 step",
             "unit": "GB/s", "peak_gbs": peak, "peak_source": peak_kind, "launches_timed": K, "kernels": out,
+            "table_rows": n_rows,
             "config": {"workload": "micro: engram_hash over 16 M positions; row sets over the 320 M-row table; "
                                    "a 400 k x 160 .pleo accumulation; the pushed exchange at W=4 and the pulled "
                                    "stage at W=2 emulated on one GPU with config 5's batch; the PLE backward at "

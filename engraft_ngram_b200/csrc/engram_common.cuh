@@ -75,7 +75,10 @@ __device__ __forceinline__ TokCtx load_ctx(const engram_table& T, const int32_t*
 // long emulated sequence; 32-bit unsigned division is far shorter, so it is
 // used whenever k fits (every batch this library sees; k < 2^32).
 __device__ __forceinline__ void split_pair(int64_t k, int nh, int64_t& i, int& h) {
-    if ((uint64_t)k <= 0xffffffffull) {
+    if (nh == 16) {  // the reference's head count: shifts
+        i = k >> 4;
+        h = (int)(k & 15);
+    } else if ((uint64_t)k <= 0xffffffffull) {
         const uint32_t q = (uint32_t)k / (uint32_t)nh;
         i = (int64_t)q;
         h = (int)((uint32_t)k - q * (uint32_t)nh);
@@ -95,6 +98,7 @@ struct HeadTab {
     int64_t offset[ENGRAM_MAX_HEADS];
     uint32_t size[ENGRAM_MAX_HEADS];
     uint32_t shift[ENGRAM_MAX_HEADS];
+    int32_t order[ENGRAM_MAX_HEADS];  // n of the n-gram head h hashes: 2 + h / heads_per_ngram
 };
 
 // Every thread of the block calls it; the caller then synchronises the block.
@@ -104,6 +108,7 @@ __device__ __forceinline__ void head_tab_fill(HeadTab& H, const engram_table& T)
         H.offset[h] = T.head_offset[h];
         H.size[h] = T.head_size[h];
         H.shift[h] = T.head_shift[h];
+        H.order[h] = 2 + h / T.heads_per_ngram;
     }
 }
 
@@ -128,7 +133,7 @@ __device__ __forceinline__ int32_t hash_ctx(const engram_table& T, const HeadTab
             ctx[s] = tok;
         }
     }
-    const int n = 2 + h / T.heads_per_ngram;  // heads (n-2)*hpn .. hold the n-gram of order n
+    const int n = H.order[h];  // heads (n-2)*hpn .. hold the n-gram of order n
     uint64_t mixed = (uint64_t)ctx[0] * T.mult[0];
 #pragma unroll
     for (int j = 1; j < ENGRAM_MAX_CTX; j++)

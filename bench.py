@@ -1363,7 +1363,12 @@ def main():
             "roofline": {"kernel": "engram_forward (k_forward_pairsum_fixed<IQ4_XS,256>)" if pairsum else "engram_forward (k_forward_concat)",
                          "bound": "hbm", "achieved": fwd_gbs, "peak": peak, "unit": "GB/s", "frac": fwd_gbs / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s",
-                         "traffic": traffic, "traffic_source": tfile, "algorithmic_bytes_per_launch": nbytes["fwd"],
+                         "traffic": traffic, "traffic_source": tfile,
+                         "traffic_note": ("DRAM read + write bytes per launch from the committed ncu capture of the same "
+                                          "kernel on the same 131,072 positions with a 2^24-row table (a launch moves "
+                                          "what its positions and rows need, whatever the table size), not measured "
+                                          "in this run") if traffic is not None else None,
+                         "algorithmic_bytes_per_launch": nbytes["fwd"],
                          "avg_launch_ms": fwd_ms},
             "gpu_launches": int(launches),
             "clocks": clk.summary(),

@@ -165,3 +165,47 @@ def test_sharded_staged_and_ple_entry_points_reject_bad_arguments(lib):
     assert lib.engram_ple_conv(*conv, None, 0, 0x5004, 4, 3, 4, 4, 2560, 0x6000, None) == L.ERR_ARG  # taps misaligned
     assert lib.engram_ple_conv(0x1000, 1 << 27, 0x2000, 0x3000, 0x4000, None, 0, 0x5000, 4, 3, 4, 8, 1 << 27,
                                0x6000, None) == L.ERR_RANGE  # hc * n too large for the kernel's indexing
+
+
+def test_pushed_exchange_gemm_and_accumulate_entry_points_reject_bad_arguments(lib):
+    """The pushed row exchange, the tcgen05 GEMMs and the ordered overlay
+    accumulation refuse bad arguments with the documented codes before any
+    CUDA call (these calls never reach the GPU)."""
+    st, t = _init(lib)
+    assert st == 0
+    ov = L.EngramOverlay(None, 0, None, None, 0)
+    tok, seg, idp, cnp, cnt, rix = 0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 0x6000
+    # engram_shard_route_push: n = 10 positions x 16 heads = 160 entries
+    assert lib.engram_shard_route_push(None, C.byref(ov), tok, seg, 0, 10, 2, 0, idp, cnp, 160, cnt, rix,
+                                       None) == L.ERR_ARG
+    assert lib.engram_shard_route_push(C.byref(t), C.byref(ov), tok, seg, 0, 10, 2, 2, idp, cnp, 160, cnt, rix,
+                                       None) == L.ERR_ARG  # rank outside the world
+    assert lib.engram_shard_route_push(C.byref(t), C.byref(ov), tok, seg, 0, 10, 2, 0, None, cnp, 160, cnt, rix,
+                                       None) == L.ERR_ARG  # no request buffers
+    assert lib.engram_shard_route_push(C.byref(t), C.byref(ov), tok, seg, 0, 10, 2, 0, idp, cnp, 159, cnt, rix,
+                                       None) == L.ERR_RANGE  # a region smaller than the batch
+    assert lib.engram_shard_route_push(C.byref(t), C.byref(ov), tok, seg, 0, 10, 64, 0, idp, cnp, 1 << 26, cnt, rix,
+                                       None) == L.ERR_RANGE  # world x region beyond the int32 row tags
+    # engram_shard_serve_pushed
+    shard, ids, counts, send = 0x10000, 0x20000, 0x30000, 0x40000
+    assert lib.engram_shard_serve_pushed(shard, 144, 100, 0, 0, ids, counts, 160, send, None) == L.ERR_ARG
+    assert lib.engram_shard_serve_pushed(shard, 136, 100, 2, 0, ids, counts, 160, send, None) == L.ERR_ARG  # stride % 16
+    assert lib.engram_shard_serve_pushed(shard, 144, 100, 2, 0, ids, counts, 160, send + 8, None) == L.ERR_ARG
+    assert lib.engram_shard_serve_pushed(shard, 144, 100, 2, 0, None, counts, 160, send, None) == L.ERR_ARG
+    assert lib.engram_shard_serve_pushed(shard, 144, 100, 1, 0, ids, counts, 160, send, None) == 0  # one rank
+    # engram_gemm_3xtf32 / engram_gemm_tf32
+    a, b, c = 0x100000, 0x200000, 0x300000
+    assert lib.engram_gemm_3xtf32(a, a, b, b, 128, 256, 30, 30, 30, c, 256, None, None) == L.ERR_ARG  # K % 4
+    assert lib.engram_gemm_3xtf32(a, a, b, b, 128, 256, 32, 16, 32, c, 256, None, None) == L.ERR_ARG  # lda < K
+    assert lib.engram_gemm_3xtf32(a + 4, a, b, b, 128, 256, 32, 32, 32, c, 256, None, None) == L.ERR_ARG
+    assert lib.engram_gemm_3xtf32(a, a, b, b, 128, 256, 32, 32, 32, None, 256, None, None) == L.ERR_ARG
+    assert lib.engram_gemm_3xtf32(a, a, b, b, 0, 256, 32, 32, 32, c, 256, None, None) == 0  # empty output
+    ptrs = (C.c_void_p * 4)(a, a, a, a)
+    assert lib.engram_gemm_tf32(0, ptrs, ptrs, 128, 256, 32, 32, 32, c, 256, None, None) == L.ERR_ARG
+    assert lib.engram_gemm_tf32(4, ptrs, ptrs, 128, 256, 32, 32, 32, c, 256, None, None) == L.ERR_ARG
+    # engram_overlay_accumulate (with and without the stable order of the targets)
+    acc, index, order, data, base = 0x400000, 0x500000, 0x600000, 0x700000, 0x800000
+    assert lib.engram_overlay_accumulate(acc, index, order, data, base, -1, 160, None) == L.ERR_ARG
+    assert lib.engram_overlay_accumulate(acc, index, order, data, base, 10, 0, None) == L.ERR_ARG
+    assert lib.engram_overlay_accumulate(None, index, order, data, base, 10, 160, None) == L.ERR_ARG
+    assert lib.engram_overlay_accumulate(acc, index, None, data, base, 0, 160, None) == 0  # nothing to add

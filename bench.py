@@ -1541,6 +1541,7 @@ def run_e2e(wl, args, device, ddist, world):
                + ("NCCL all-reduce of the row gradients + " if ddist is not None else "") + "OverlayAdam.step")
     hits = torch.zeros(1, dtype=torch.int64, device=device)
     pending = []  # staged sharded reads: the next step's inputs, copied and prefetched one step ahead
+    h2d = torch.cuda.Stream(device)  # the token copies, apart from the exchange's row copies
 
     def one():
         residual = wl.out.detach()
@@ -1549,11 +1550,11 @@ def run_e2e(wl, args, device, ddist, world):
                 pending.append((tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True)))
             tok, ss = pending.pop(0)
             xs = getattr(wl.table, "xstage", None)
-            if xs is not None:  # copied on the staging stream: the exchange waits for the copy, not for the step
-                with torch.cuda.stream(xs.side):
+            if xs is not None:  # copied on a stream of their own: the exchange waits for the copy, not for the step
+                with torch.cuda.stream(h2d):
                     nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
                     ready = torch.cuda.Event()
-                    ready.record(xs.side)
+                    ready.record(h2d)
                 for x in nxt:
                     x.record_stream(torch.cuda.current_stream(device))
                 wl.table.prefetch(nxt[0], nxt[1], omap=wl.omap, ready=ready)

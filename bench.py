@@ -1408,10 +1408,12 @@ def sharded_stats(wl, ms, fwd_ms, bwd_ms, ddist, world, device):
     nv_bytes = int(rr[0]) * wl.shard.stride  # the exchange moves one row per remote (position, head) pair
     phases = None
     xs = getattr(wl.shard, "xstage", None)
-    if xs is not None:  # a few more steps with the exchange's phases timed (after the timed region)
+    if xs is not None:  # more steps with the exchange's phases timed (after the timed region and 3 plain steps)
         import torch
+        for _ in range(3):
+            wl.step(ddist)
         xs.timing = {}
-        for _ in range(5):
+        for _ in range(9):
             wl.step(ddist)
         wl.join_stage()
         torch.cuda.synchronize()
@@ -1421,7 +1423,7 @@ def sharded_stats(wl, ms, fwd_ms, bwd_ms, ddist, world, device):
         t = torch.tensor([ph[k] for k in keys], dtype=torch.float64, device=device)
         ddist.all_reduce(t, op=ddist.ReduceOp.MAX)
         phases = {k: float(v) for k, v in zip(keys, t.tolist())}
-        phases["note"] = ("ms per step, max over ranks: route (ids pushed to their owners), serve (the owner's "
+        phases["note"] = ("ms per step, the median of 9 steps, max over ranks: route (ids pushed to their owners), serve (the owner's "
                           "local gather) and barrier (a 4-byte all-reduce) on the step's stream before the forward, "
                           "fetch (copy-engine transfers) on the side stream, wait = the forward's stream blocked on "
                           "its rows")

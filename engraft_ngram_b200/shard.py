@@ -547,10 +547,15 @@ class ExchangeStage:
             self.timing.setdefault(name, []).append((e0, self._mark(stream)))
 
     def phase_ms(self) -> dict:
-        """Mean ms per batch of each timed phase (after a synchronize): route,
+        """Median ms per batch of each timed phase (after a synchronize): route,
         serve and barrier on the caller's stream, fetch on the side stream,
         wait = how long the forward's stream waited for its rows."""
-        return {k: sum(a.elapsed_time(b) for a, b in v) / len(v) for k, v in (self.timing or {}).items() if v}
+        out = {}
+        for k, v in (self.timing or {}).items():
+            if v:
+                ms = sorted(a.elapsed_time(b) for a, b in v)
+                out[k] = ms[len(ms) // 2]
+        return out
 
     def _oldest(self, state):
         return sorted((k for k in range(self.SETS) if self.state[k] == state), key=lambda k: self.seq[k])

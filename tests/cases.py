@@ -89,6 +89,29 @@ def shard_plan_ref(ids, ov_ids, world: int, rank: int):
     return send.astype(np.int32), counts, rix
 
 
+def shard_route_push_ref(ids, ov_ids, world: int, rank: int):
+    """The contract of engram_shard_route_push restated in numpy (a test
+    reference): every (position, head) pair of `ids` ([n, n_heads]) whose owner
+    id % world is another rank and which the overlay (ov_ids) does not serve
+    sends its id to its owner; requests[o] lists owner o's ids in slot order
+    (ascending pair index here; the kernel leaves the order open), counts[o]
+    their number, and row_index each pair's row in the receive buffer (owners'
+    blocks in ascending owner order: the counts of lower owners + its slot),
+    -1 when not requested."""
+    flat = np.asarray(ids, dtype=np.int64).reshape(-1)
+    req = (flat % world != rank) & ~np.isin(flat, np.asarray(ov_ids, dtype=np.int64))
+    owner = flat % world
+    counts = np.bincount(owner[req], minlength=world).astype(np.int64)
+    base = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    rix = np.full(flat.shape, -1, dtype=np.int64)
+    requests = {}
+    for o in range(world):
+        sel = np.flatnonzero(req & (owner == o))
+        requests[o] = flat[sel].astype(np.int32)
+        rix[sel] = base[o] + np.arange(sel.size)
+    return requests, counts, rix
+
+
 def ple_block_torch(emb, hidden, w, hist, hc: int, n: int, eps: float, dil: int, detach_value: bool = False,
                     detach_gate: bool = False):
     """The PLE block's formula (engraft/replica/layers.py:565-626) restated in

@@ -380,6 +380,88 @@ __global__ void __launch_bounds__(256) k_ple_dx(const float* __restrict__ dconv,
     }
 }
 
+// The two steps above for the reference's K = 4 with 16-byte aligned rows: a
+// thread owns a channel quad (its 16 tap weights stay in registers) and walks
+// positions with a grid stride, so every row access is one float4 load and no
+// index needs a division.  The per-channel arithmetic and its order are those
+// of the scalar kernels.
+__global__ void __launch_bounds__(256) k_ple_dconv4(const float* __restrict__ normed, const float* __restrict__ hist,
+                                                    int64_t hist_len, const float* __restrict__ conv_w, int dilation,
+                                                    int64_t T, int C, const float* __restrict__ dout,
+                                                    float* __restrict__ dconv) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;  // channel quad: channels 4q..4q+3
+    if (q >= (C >> 2)) return;
+    float w[4][4];  // w[channel][tap]
+#pragma unroll
+    for (int ch = 0; ch < 4; ch++) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(conv_w) + (4 * q + ch));
+        w[ch][0] = v.x, w[ch][1] = v.y, w[ch][2] = v.z, w[ch][3] = v.w;
+    }
+    for (int64_t t = blockIdx.y; t < T; t += gridDim.y) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t src = t - (int64_t)(3 - k) * dilation;
+            const float* row = src >= 0 ? normed + src * C : (hist_len + src >= 0 ? hist + (hist_len + src) * C : nullptr);
+            if (row == nullptr) continue;
+            const float4 x = __ldg(reinterpret_cast<const float4*>(row) + q);
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(x.x, w[0][k]));
+            acc[1] = __fadd_rn(acc[1], __fmul_rn(x.y, w[1][k]));
+            acc[2] = __fadd_rn(acc[2], __fmul_rn(x.z, w[2][k]));
+            acc[3] = __fadd_rn(acc[3], __fmul_rn(x.w, w[3][k]));
+        }
+        const float4 d = __ldg(reinterpret_cast<const float4*>(dout + t * C) + q);
+        const float dd[4] = {d.x, d.y, d.z, d.w};
+        float o[4];
+#pragma unroll
+        for (int ch = 0; ch < 4; ch++) {
+            const float sg = sigmoidf_(acc[ch]);
+            o[ch] = dd[ch] * (sg * (1.0f + acc[ch] * (1.0f - sg)));
+        }
+        reinterpret_cast<float4*>(dconv + t * C)[q] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+__global__ void __launch_bounds__(256) k_ple_dx4(const float* __restrict__ dconv, const float* __restrict__ conv_w,
+                                                 int dilation, int64_t T, int C, int64_t hist_len,
+                                                 const float* __restrict__ dtail, int64_t tail_len,
+                                                 float* __restrict__ dnormed, float* __restrict__ dhist) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= (C >> 2)) return;
+    float w[4][4];
+#pragma unroll
+    for (int ch = 0; ch < 4; ch++) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(conv_w) + (4 * q + ch));
+        w[ch][0] = v.x, w[ch][1] = v.y, w[ch][2] = v.z, w[ch][3] = v.w;
+    }
+    const int64_t rows = hist_len + T;
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+        const int64_t u = r - hist_len;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 3; k >= 0; k--) {
+            const int64_t t = u + (int64_t)(3 - k) * dilation;
+            if (t < 0 || t >= T) continue;
+            const float4 g = __ldg(reinterpret_cast<const float4*>(dconv + t * C) + q);
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(w[0][k], g.x));
+            acc[1] = __fadd_rn(acc[1], __fmul_rn(w[1][k], g.y));
+            acc[2] = __fadd_rn(acc[2], __fmul_rn(w[2][k], g.z));
+            acc[3] = __fadd_rn(acc[3], __fmul_rn(w[3][k], g.w));
+        }
+        const int64_t tr = r - (rows - tail_len);
+        if (dtail && tr >= 0) {
+            const float4 d = __ldg(reinterpret_cast<const float4*>(dtail + tr * C) + q);
+            acc[0] = __fadd_rn(acc[0], d.x);
+            acc[1] = __fadd_rn(acc[1], d.y);
+            acc[2] = __fadd_rn(acc[2], d.z);
+            acc[3] = __fadd_rn(acc[3], d.w);
+        }
+        const float4 o = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (u >= 0) reinterpret_cast<float4*>(dnormed + u * C)[q] = o;
+        else if (dhist) reinterpret_cast<float4*>(dhist + r * C)[q] = o;
+    }
+}
+
 }  // namespace
 
 extern "C" int engram_ple_gate(const float* key, int64_t key_stride, const float* value, int64_t value_stride,
@@ -474,6 +556,27 @@ extern "C" int engram_ple_conv_backward(const float* normed, const float* hist, 
     const int64_t cap = (int64_t)sm_count() * 8;
     cudaStream_t st = (cudaStream_t)stream;
     int launched = 0;
+    const bool vec = K == 4 && aligned16(conv_w) && (T == 0 || (aligned16(normed) && aligned16(dout) &&
+                                                              aligned16(dconv) && aligned16(dnormed))) &&
+                     (hist_len == 0 || aligned16(hist)) && (!dhist || aligned16(dhist)) &&
+                     (tail_len == 0 || aligned16(dtail));
+    if (vec) {  // channel quads x strided positions, as k_ple_conv<4>
+        const int gx = (C / 4 + 255) / 256;
+        const int64_t want_y = ((int64_t)sm_count() * 8 + gx - 1) / gx;
+        if (T > 0) {
+            const int64_t gy = T < want_y ? T : (want_y < 65535 ? want_y : 65535);
+            k_ple_dconv4<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(normed, hist, hist_len, conv_w, dilation, T, C, dout,
+                                                                 dconv);
+            launched++;
+        }
+        const int64_t rows = hist_len + T;
+        const int64_t gy = rows < want_y ? rows : (want_y < 65535 ? want_y : 65535);
+        k_ple_dx4<<<dim3(gx, (unsigned)gy), 256, 0, st>>>(dconv, conv_w, dilation, T, C, hist_len, dtail, tail_len,
+                                                          dnormed, dhist);
+        launched++;
+        count_launches(launched);
+        return cudaGetLastError() == cudaSuccess ? ENGRAM_OK : ENGRAM_ERR_CUDA;
+    }
     if (T > 0) {
         const int64_t want = (T * (int64_t)C + 255) / 256;
         k_ple_dconv<<<(int)(want < cap ? want : cap), 256, 0, st>>>(normed, hist, hist_len, conv_w, K, dilation, T, C,

@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
 // KT = 4: the reference's 4 taps, unrolled, two positions per iteration (t and
 // t + gridDim.y) so that their loads are in flight together; KT = 0: any K.
 template <int KT>
-__global__ void __launch_bounds__(256) k_ple_conv(const float* __restrict__ value, int64_t value_stride,
+__global__ void __launch_bounds__(256, KT == 4 ? 3 : 1) k_ple_conv(const float* __restrict__ value, int64_t value_stride,
                                                   const float* __restrict__ hidden, const float* __restrict__ gate,
                                                   const float* __restrict__ normed, const float* __restrict__ hist,
                                                   int64_t hist_len, const float* __restrict__ conv_w, int K,
@@ -212,6 +212,7 @@ __global__ void __launch_bounds__(256) k_ple_conv(const float* __restrict__ valu
 //   d_value_c  = sum_j d_gated_jc g_j
 // (rmsnorm's backward: d x = r w dy - x r^3 sum(x w dy) / n).  detach_gate
 // zeroes d_gate (gated = value * gate.detach()), detach_value zeroes d_value.
+template <int MAXHC>
 __global__ void __launch_bounds__(kGateThreads) k_ple_gate_bwd(
     const float* __restrict__ key, int64_t key_stride, const float* __restrict__ value, int64_t value_stride,
     const float* __restrict__ hidden, const float* __restrict__ norm_key, const float* __restrict__ norm_query,
@@ -219,9 +220,9 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate_bwd(
     const float* __restrict__ dout, const float* __restrict__ dnormed, int64_t T, int hc, int n, float eps,
     int detach_value, int detach_gate, float* __restrict__ dkey, int64_t dkey_stride, float* __restrict__ dvalue,
     int64_t dvalue_stride, float* __restrict__ dhidden) {
-    constexpr int kSums = 5 * kPleMaxHc + 1;
+    constexpr int kSums = 5 * MAXHC + 1;
     __shared__ float part[kGateThreads / 32][kSums];
-    __shared__ float coef[8 * kPleMaxHc];  // per stream: g, rg, cg, ck1, ck2, ch1, ch2
+    __shared__ float coef[8 * MAXHC];  // per stream: g, rg, cg, ck1, ck2, ch1, ch2
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n4 = n >> 2;
     const float fn = (float)n;
@@ -236,9 +237,9 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate_bwd(
         for (int q = 0; q < kSums; q++) acc[q] = 0.f;
         for (int c = tid; c < n4; c += kGateThreads) {
             const float4 v = __ldg(v4 + c);
-            acc[5 * kPleMaxHc] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            acc[5 * MAXHC] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
 #pragma unroll
-            for (int j = 0; j < kPleMaxHc; j++) {
+            for (int j = 0; j < MAXHC; j++) {
                 if (j < hc) {
                     const float4 k = __ldg(k4 + j * n4 + c), h = __ldg(h4 + j * n4 + c);
                     const float4 a = __ldg(reinterpret_cast<const float4*>(norm_key + (int64_t)j * n) + c);
@@ -272,7 +273,7 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate_bwd(
                 Cq += part[w][5 * j + 2];
                 E += part[w][5 * j + 3];
                 F += part[w][5 * j + 4];
-                V += part[w][5 * kPleMaxHc];
+                V += part[w][5 * MAXHC];
             }
             const float rk = 1.0f / sqrtf(A / fn + eps);
             const float rq = 1.0f / sqrtf(B / fn + eps);
@@ -533,7 +534,12 @@ extern "C" int engram_ple_gate_backward(const float* key, int64_t key_stride, co
         return ENGRAM_ERR_ARG;
     const int64_t cap = (int64_t)sm_count() * 8;
     const int blocks = (int)(T < cap ? T : cap);
-    k_ple_gate_bwd<<<blocks, kGateThreads, 0, (cudaStream_t)stream>>>(
+    if (hc <= 4)  // the reference's hc: a quarter of the accumulators live, twice the resident blocks
+        k_ple_gate_bwd<4><<<blocks, kGateThreads, 0, (cudaStream_t)stream>>>(
+        key, key_stride, value, value_stride, hidden, norm_key, norm_query, norm_conv, gate, s, dout, dnormed, T, hc,
+        n_embd, eps, detach_value, detach_gate, dkey, dkey_stride, dvalue, dvalue_stride, dhidden);
+    else
+        k_ple_gate_bwd<kPleMaxHc><<<blocks, kGateThreads, 0, (cudaStream_t)stream>>>(
         key, key_stride, value, value_stride, hidden, norm_key, norm_query, norm_conv, gate, s, dout, dnormed, T, hc,
         n_embd, eps, detach_value, detach_gate, dkey, dkey_stride, dvalue, dvalue_stride, dhidden);
     count_launches(1);

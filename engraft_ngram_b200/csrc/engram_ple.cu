@@ -26,6 +26,7 @@ constexpr int kGateThreads = 256;
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+template <int MAXHC>
 __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restrict__ key, int64_t key_stride,
                                                            const float* __restrict__ value, int64_t value_stride,
                                                            const float* __restrict__ hidden,
@@ -35,9 +36,9 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
                                                            int n, float eps, float* __restrict__ gate_out,
                                                            float* __restrict__ s_out, float* __restrict__ normed) {
     // per stream j: sum key^2, sum hidden^2, sum (key*nk)(hidden*nq); then sum value^2
-    constexpr int kSums = 3 * kPleMaxHc + 1;
+    constexpr int kSums = 3 * MAXHC + 1;
     __shared__ float part[kGateThreads / 32][kSums];
-    __shared__ float coef[2 * kPleMaxHc];  // per stream: gate, rsqrt of the gated mean square
+    __shared__ float coef[2 * MAXHC];  // per stream: gate, rsqrt of the gated mean square
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n4 = n >> 2;
     for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
@@ -49,9 +50,9 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
         for (int q = 0; q < kSums; q++) acc[q] = 0.f;
         for (int c = tid; c < n4; c += kGateThreads) {
             const float4 v = __ldg(v4 + c);
-            acc[3 * kPleMaxHc] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            acc[3 * MAXHC] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
 #pragma unroll
-            for (int j = 0; j < kPleMaxHc; j++) {
+            for (int j = 0; j < MAXHC; j++) {
                 if (j < hc) {
                     const float4 k = __ldg(k4 + j * n4 + c), h = __ldg(h4 + j * n4 + c);
                     const float4 a = __ldg(reinterpret_cast<const float4*>(norm_key + (int64_t)j * n) + c);
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(kGateThreads) k_ple_gate(const float* __restri
                 ssk += part[w][3 * j];
                 ssq += part[w][3 * j + 1];
                 dot += part[w][3 * j + 2];
-                ssv += part[w][3 * kPleMaxHc];
+                ssv += part[w][3 * MAXHC];
             }
             const float rk = 1.0f / sqrtf(ssk / (float)n + eps);
             const float rq = 1.0f / sqrtf(ssq / (float)n + eps);
@@ -479,7 +480,12 @@ extern "C" int engram_ple_gate(const float* key, int64_t key_stride, const float
         return ENGRAM_ERR_ARG;
     const int64_t cap = (int64_t)sm_count() * 8;
     const int blocks = (int)(T < cap ? T : cap);
-    k_ple_gate<<<blocks, kGateThreads, 0, (cudaStream_t)stream>>>(key, key_stride, value, value_stride, hidden,
+    if (hc <= 4)  // the reference's hc: fewer sums live and no skipped streams in the unrolled loops
+        k_ple_gate<4><<<blocks, kGateThreads, 0, (cudaStream_t)stream>>>(key, key_stride, value, value_stride, hidden,
+                                                                   norm_key, norm_query, norm_conv, T, hc, n_embd, eps,
+                                                                   gate, s_out, normed);
+    else
+        k_ple_gate<kPleMaxHc><<<blocks, kGateThreads, 0, (cudaStream_t)stream>>>(key, key_stride, value, value_stride, hidden,
                                                                    norm_key, norm_query, norm_conv, T, hc, n_embd, eps,
                                                                    gate, s_out, normed);
     count_launches(1);

@@ -1542,7 +1542,7 @@ def run_e2e(wl, args, device, ddist, world):
         api = ("engraft_ngram_b200.engram_residual_add + autograd backward + "
                + ("NCCL all-reduce of the row gradients + " if ddist is not None else "") + "OverlayAdam.step")
     hits = torch.zeros(1, dtype=torch.int64, device=device)
-    pending = []  # staged sharded reads: the next step's inputs, copied and prefetched one step ahead
+    pending = []  # the next steps' inputs, copied (and for sharded reads prefetched) ahead
     h2d = torch.cuda.Stream(device)  # the token copies, apart from the exchange's row copies
 
     def one():
@@ -1564,9 +1564,18 @@ def run_e2e(wl, args, device, ddist, world):
                 nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
                 wl.table.prefetch(nxt[0], nxt[1], max_blocks=wl.stage_blocks, omap=wl.omap)
             pending.append(nxt)
-        else:
-            tok = tok_h.to(device, non_blocking=True)
-            ss = ss_h.to(device, non_blocking=True)
+        else:  # copied one step ahead on a stream of their own: the copy overlaps the step before
+            cur = torch.cuda.current_stream(device)
+            while len(pending) < 2:
+                with torch.cuda.stream(h2d):
+                    nxt = (tok_h.to(device, non_blocking=True), ss_h.to(device, non_blocking=True))
+                    ready = torch.cuda.Event()
+                    ready.record(h2d)
+                for x in nxt:
+                    x.record_stream(cur)
+                pending.append((nxt[0], nxt[1], ready))
+            tok, ss, ready = pending.pop(0)
+            cur.wait_event(ready)
         hits.zero_()
         opt.zero_grad()
         if wl.mode == wl.L.MODE_PAIRSUM_ADD_BF16:
